@@ -1,0 +1,217 @@
+// extern "C" entry points of include/ancha_b200.h: argument validation with the
+// reference's rules (fused/mod.rs:20-176), status codes and the per-thread last error.
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "attention.cuh"
+#include "dsp.cuh"
+#include "gemm.cuh"
+#include "model.hpp"
+
+namespace ancha {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+int fail(int code, const std::string& msg) {
+    g_last_error = msg;
+    return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+    return fail(ANCHA_E_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return cuda_fail(e, what);
+    return ANCHA_OK;
+}
+
+}  // namespace ancha
+
+using namespace ancha;
+
+extern "C" {
+
+const char* ancha_last_error(void) { return g_last_error.c_str(); }
+
+const char* ancha_version(void) { return "ancha-b200 0.1.0 (sm_100a)"; }
+
+int ancha_available(int device) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(ANCHA_E_CUDA, std::string("no CUDA device: ") + cudaGetErrorString(e));
+        return 0;
+    }
+    if (device < 0 || device >= count) {
+        fail(ANCHA_E_INVALID, "CUDA device " + std::to_string(device) + " not found");
+        return 0;
+    }
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, device) != cudaSuccess || p.major != 10) {
+        fail(ANCHA_E_UNSUPPORTED, "device is not an sm_100 (B200-class) GPU");
+        return 0;
+    }
+    return 1;
+}
+
+int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, const void* v,
+                        const void* gate, void* out, void* stream) {
+    if (!d || !q || !k || !v || !out) return fail(ANCHA_E_INVALID, "attention: null argument");
+    if (d->head_dim != 64) return fail(ANCHA_E_UNSUPPORTED, "attention: head_dim must be 64");
+    if (d->groups < 0 || d->tokens < 0 || d->heads <= 0)
+        return fail(ANCHA_E_INVALID, "attention: negative shape");
+    if (d->dtype != ANCHA_F32 && d->dtype != ANCHA_BF16)
+        return fail(ANCHA_E_INVALID, "attention: unknown dtype");
+    if (d->group_inner <= 0 || d->token_stride < 0 || d->ld <= 0 || d->out_ld <= 0)
+        return fail(ANCHA_E_INVALID, "attention: invalid strides");
+    const int64_t span = (int64_t)d->heads * 64;
+    if (d->q_col < 0 || d->k_col < 0 || d->v_col < 0 || d->out_col < 0 ||
+        d->q_col + span > d->ld || d->k_col + span > d->ld || d->v_col + span > d->ld ||
+        d->out_col + span > d->out_ld || (gate && (d->gate_col < 0 || d->gate_col + d->heads > d->ld)))
+        return fail(ANCHA_E_INVALID, "attention: q / k / v column ranges do not fit the rows");
+    AttnArgs a{};
+    a.q = q; a.k = k; a.v = v; a.gate = gate; a.out = out;
+    a.groups = d->groups; a.tokens = d->tokens; a.heads = d->heads; a.head_dim = 64;
+    a.ld = d->ld; a.out_ld = d->out_ld;
+    a.group_inner = d->group_inner; a.group_inner_stride = d->group_inner_stride;
+    a.group_outer_stride = d->group_outer_stride; a.token_stride = d->token_stride;
+    a.q_col = d->q_col; a.k_col = d->k_col; a.v_col = d->v_col;
+    a.gate_col = gate ? d->gate_col : 0; a.out_col = d->out_col;
+    a.bf16 = d->dtype == ANCHA_BF16;
+    cudaStream_t s = as_stream(stream);
+    if (a.bf16) {
+        int st = attention_tc(a, s);
+        if (st != ANCHA_E_UNSUPPORTED) return st;
+    }
+    return attention_ffma(a, s);
+}
+
+int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, const float* bias,
+                     const float* residual, const float* rope, void* out, void* stream) {
+    if (!d || !x || !w || !out) return fail(ANCHA_E_INVALID, "linear: null argument");
+    if (d->m < 0 || d->n <= 0 || d->k <= 0) return fail(ANCHA_E_UNSUPPORTED, "linear: empty shape");
+    if (d->dtype != ANCHA_F32 && d->dtype != ANCHA_BF16)
+        return fail(ANCHA_E_INVALID, "linear: unknown dtype");
+    if (d->act < ANCHA_ACT_NONE || d->act > ANCHA_ACT_GLU) return fail(ANCHA_E_INVALID, "linear: unknown activation");
+    if (d->act == ANCHA_ACT_GLU && (d->n % 2 || residual || d->rope_width))
+        return fail(ANCHA_E_INVALID, "linear: GLU needs an even n and no residual / rotary");
+    const int wl = d->weight_layout;
+    if (wl != ANCHA_W_KN && wl != ANCHA_W_NK) return fail(ANCHA_E_INVALID, "linear: unknown weight layout");
+    if (d->ldx < d->k || d->ldw < (wl == ANCHA_W_NK ? d->k : d->n))
+        return fail(ANCHA_E_INVALID, "linear: leading dimension too small");
+    const int n_out = d->act == ANCHA_ACT_GLU ? d->n / 2 : d->n;
+    if (d->ldout < n_out || (residual && d->ldres < d->n))
+        return fail(ANCHA_E_INVALID, "linear: output / residual leading dimension too small");
+    if (d->rope_width) {
+        // fused/mod.rs:114-124: [4, tokens, 64] table, whole token rows, width % 64, 2w <= n.
+        if (!rope || d->rope_tokens <= 0 || d->rope_div <= 0 || d->rope_width % 64 ||
+            2 * d->rope_width > d->n)
+            return fail(ANCHA_E_UNSUPPORTED, "linear: rotary epilogue shape not supported");
+    }
+    GemmGroup g{};
+    g.a = x; g.b = w; g.bias = bias; g.residual = residual; g.out = out;
+    g.m = d->m; g.n = d->n; g.k = d->k;
+    g.lda = d->ldx; g.ldb = d->ldw; g.ldr = d->ldres; g.ldo = d->ldout;
+    GemmEpilogue e{};
+    e.act = d->act;
+    e.out_bf16 = d->out_dtype == ANCHA_BF16;
+    e.rope = d->rope_width ? rope : nullptr;
+    e.rope_width = d->rope_width;
+    e.rope_tokens = d->rope_tokens > 0 ? d->rope_tokens : 1;
+    e.rope_div = d->rope_div > 0 ? d->rope_div : 1;
+    e.rope_hd = 64;
+    cudaStream_t s = as_stream(stream);
+    const int bf = d->dtype == ANCHA_BF16;
+    if (bf && wl == ANCHA_W_NK) {
+        int st = gemm_tc(g, e, s);
+        if (st != ANCHA_E_UNSUPPORTED) return st;
+    }
+    return gemm_ffma(g, nullptr, 1, d->m, d->n, bf, bf, wl == ANCHA_W_NK, e, s);
+}
+
+int ancha_stft_fwd(const float* audio, int chunks, int samples, int hop, float* packed, void* stream) {
+    if (!audio || !packed || chunks < 0) return fail(ANCHA_E_INVALID, "stft: invalid arguments");
+    if (reinterpret_cast<uintptr_t>(packed) % 16)
+        return fail(ANCHA_E_INVALID, "stft: packed spectrum must be 16-byte aligned");
+    return stft_forward(audio, chunks, samples, hop, packed, as_stream(stream));
+}
+
+int ancha_istft_masked(const float* packed, const float* masks, int chunks, int stems, int samples,
+                       int hop, int zero_dc, float* scratch, float* out, void* stream) {
+    if (!packed || !masks || !scratch || !out || chunks < 0 || stems < 0 || hop <= 0)
+        return fail(ANCHA_E_INVALID, "istft: invalid arguments");
+    if (reinterpret_cast<uintptr_t>(packed) % 16 || reinterpret_cast<uintptr_t>(scratch) % 8)
+        return fail(ANCHA_E_INVALID, "istft: packed must be 16-byte and scratch 8-byte aligned");
+    // The status word sits after the frame scratch; bit 2 = an uncovered sample.
+    const int frames = samples / hop + 1;
+    int* flag = reinterpret_cast<int*>(scratch + (int64_t)chunks * stems * 2 * frames * 2048);
+    cudaStream_t s = as_stream(stream);
+    ANCHA_CUDA(cudaMemsetAsync(flag, 0, sizeof(int), s));
+    return istft_masked(packed, masks, chunks, stems, samples, hop, zero_dc, scratch, out, flag, s);
+}
+
+int ancha_ola_add(const float* y, int chunks, int planes, int chunk, int overlap,
+                  const int64_t* starts, int64_t length, float* sums, float* weights, void* stream) {
+    if (!y || !starts || !sums || !weights || chunks < 0 || planes <= 0 || chunk <= 0 || overlap <= 0)
+        return fail(ANCHA_E_INVALID, "ola: invalid arguments");
+    if (chunks > kMaxChunksPerCall) return fail(ANCHA_E_INVALID, "ola: too many chunks per call");
+    ChunkStarts cs{};
+    for (int c = 0; c < chunks; ++c) {
+        if (starts[c] < 0 || starts[c] >= length || (c && starts[c] < starts[c - 1]))
+            return fail(ANCHA_E_INVALID, "ola: chunk starts must be ascending and inside the output");
+        cs.v[c] = starts[c];
+    }
+    return ola_add(y, chunks, planes, chunk, cs, length, 0, length, sums, weights, as_stream(stream));
+}
+
+int ancha_model_load(const char* package_dir, int device, int precision, ancha_model** out) {
+    if (!package_dir || !out) return fail(ANCHA_E_INVALID, "model_load: null argument");
+    *out = nullptr;
+    try {
+        auto m = Model::load(package_dir, device, precision);
+        *out = new ancha_model{std::move(m)};
+        return ANCHA_OK;
+    } catch (const std::exception& e) {
+        const std::string msg = e.what();
+        const bool io = msg.rfind("read ", 0) == 0;
+        return fail(io ? ANCHA_E_IO : ANCHA_E_INVALID, msg);
+    }
+}
+
+int ancha_model_info(const ancha_model* model, int* stems, int* bands, int* dim, int* bins,
+                     int* chunk_samples, int* hop, int* overlap) {
+    if (!model) return fail(ANCHA_E_INVALID, "model_info: null model");
+    const ModelConfig& c = model->impl->manifest.config;
+    if (stems) *stems = (int)c.stems.size();
+    if (bands) *bands = (int)c.bands.size();
+    if (dim) *dim = c.dim;
+    if (bins) *bins = c.n_fft / 2 + 1;
+    if (chunk_samples) *chunk_samples = (int)c.chunk_samples;
+    if (hop) *hop = c.hop;
+    if (overlap) *overlap = c.overlap;
+    return ANCHA_OK;
+}
+
+int ancha_model_forward(ancha_model* model, const float* spectrum, int chunks, int frames,
+                        float* masks, const volatile int* cancel, void* stream) {
+    if (!model || !spectrum || !masks) return fail(ANCHA_E_INVALID, "model_forward: null argument");
+    try {
+        return model->impl->forward(spectrum, chunks, frames, masks, cancel, as_stream(stream));
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_CUDA, e.what());
+    }
+}
+
+void ancha_model_free(ancha_model* model) { delete model; }
+
+void ancha_free_string(char* s) { std::free(s); }
+
+}  // extern "C"

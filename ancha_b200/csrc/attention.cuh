@@ -1,0 +1,28 @@
+// Attention operand addressing shared by the attention kernels.
+#pragma once
+#include "common.cuh"
+
+namespace ancha {
+
+struct AttnArgs {
+    const void* q;
+    const void* k;
+    const void* v;
+    const void* gate;  // null: ungated
+    void* out;
+    int groups, tokens, heads, head_dim;  // head_dim <= 64 (FFMA) or == 64 (tcgen05)
+    int64_t ld, out_ld;
+    int64_t group_inner, group_inner_stride, group_outer_stride, token_stride;
+    int q_col, k_col, v_col, gate_col, out_col;
+    int bf16;  // q/k/v/gate/out element type
+};
+
+// First row of group g (see ancha_attn_desc).
+__host__ __device__ __forceinline__ int64_t attn_group_row(const AttnArgs& a, int64_t g) {
+    return (g / a.group_inner) * a.group_outer_stride + (g % a.group_inner) * a.group_inner_stride;
+}
+
+int attention_ffma(const AttnArgs& a, cudaStream_t stream);
+int attention_tc(const AttnArgs& a, cudaStream_t stream);
+
+}  // namespace ancha

@@ -1,0 +1,28 @@
+// Spectral DSP kernels (see dsp.cu).
+#pragma once
+#include "common.cuh"
+
+namespace ancha {
+
+constexpr int kMaxChunksPerCall = 128;
+
+// Chunk start samples passed by value to the gather / overlap-add kernels.
+struct ChunkStarts {
+    int64_t v[kMaxChunksPerCall];
+};
+
+int dsp_prepare(cudaStream_t s);
+int stft_forward(const float* audio, int chunks, int samples, int hop, float* packed,
+                 cudaStream_t s);
+int istft_masked(const float* packed, const float* masks, int chunks, int stems, int samples,
+                 int hop, int zero_dc, float* scratch, float* out, int* flag, cudaStream_t s);
+int gather_chunks(const float* planes, int64_t samples, const ChunkStarts& starts, int chunks,
+                  int chunk, int64_t border, int64_t length, float* out, cudaStream_t s);
+int ola_add(const float* y, int chunks, int planes, int chunk, const ChunkStarts& starts,
+            int64_t length, int64_t base, int64_t span, float* sums, float* weights,
+            cudaStream_t s);
+int ola_finish(const float* sums, const float* weights, int planes, int64_t length,
+               int64_t border, int64_t samples, const float* input, float* stems,
+               float* residual, int* flag, cudaStream_t s);
+
+}  // namespace ancha

@@ -1,0 +1,41 @@
+// GEMM problem descriptors shared by the FFMA and tcgen05 GEMM kernels.
+#pragma once
+#include "common.cuh"
+
+namespace ancha {
+
+// One GEMM problem: out[m, n'] = epilogue(sum_k a[m, k] · b(k, n)).
+// b(k, n) = b[n·ldb + k] (NK, PyTorch [out, in]) or b[k·ldb + n] (KN, Burn [in, out]).
+struct GemmGroup {
+    const void* a;
+    const void* b;
+    const float* bias;      // [n] or null
+    const float* residual;  // [m, n] f32 or null (row stride ldr)
+    void* out;              // [m, n] (n/2 for GLU), row stride ldo
+    int m, n, k;
+    int64_t lda, ldb, ldr, ldo;
+};
+
+// Epilogue shared by every group of one launch.
+struct GemmEpilogue {
+    int act;            // ANCHA_ACT_*
+    int out_bf16;       // 1: out is bf16, 0: f32
+    const float* rope;  // [4, rope_tokens, 64] or null
+    int rope_width;     // rotate columns [0, 2·rope_width)
+    int rope_tokens;
+    int rope_div;       // token = (row / rope_div) % rope_tokens
+    int rope_hd;        // head width of the table (columns per head)
+};
+
+// FFMA GEMM (fp32 accumulation). `groups` is a device array of `count` problems when
+// non-null, else `single` is the one problem. TA / TB are float or __nv_bfloat16.
+int gemm_ffma(const GemmGroup& single, const GemmGroup* groups, int count, int max_m,
+              int max_n, int a_bf16, int b_bf16, int b_nk, const GemmEpilogue& epi,
+              cudaStream_t stream);
+
+// tcgen05 / TMA GEMM (bf16 operands, fp32 accumulation in TMEM) for one problem with
+// NK weights. Returns ANCHA_E_UNSUPPORTED when the operands do not meet its alignment
+// rules (16-byte rows, k % 8 == 0), so the caller can use gemm_ffma instead.
+int gemm_tc(const GemmGroup& g, const GemmEpilogue& epi, cudaStream_t stream);
+
+}  // namespace ancha

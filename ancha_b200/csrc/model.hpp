@@ -1,0 +1,140 @@
+// RoFormer model on one device: strict package loading with the reference's load-time
+// folding, and the forward pass over this library's kernels.
+#pragma once
+
+#include <array>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "gemm.cuh"
+#include "hostio.hpp"
+
+namespace ancha {
+
+// Owned device allocation (moved, never copied).
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), bytes(o.bytes) { o.p = nullptr; o.bytes = 0; }
+    DevBuf& operator=(DevBuf&& o) noexcept {
+        if (this != &o) { release(); p = o.p; bytes = o.bytes; o.p = nullptr; o.bytes = 0; }
+        return *this;
+    }
+    ~DevBuf() { release(); }
+    void release();
+    void alloc(size_t n);  // throws std::runtime_error on failure
+    template <typename T> T* as() const { return reinterpret_cast<T*>(p); }
+};
+
+// crates/ancha-models/src/config.rs::ModelConfig.
+struct ModelConfig {
+    std::string family;
+    int dim = 0, depth = 0, heads = 0, head_dim = 0, ff_mult = 0, mask_depth = 0,
+        mask_expansion = 0, sample_rate = 0, n_fft = 0, hop = 0, overlap = 0;
+    int64_t chunk_samples = 0;
+    bool zero_dc = false;
+    std::vector<std::string> stems;
+    std::vector<std::vector<int>> bands;
+    bool mel() const { return family == "mel-band-roformer"; }
+    void validate() const;  // throws std::runtime_error (config.rs:36-121)
+    static ModelConfig from_json(const Json& j);
+    Json to_json() const;
+};
+
+struct Manifest {
+    int schema_version = 0;
+    std::string model_id, weights_sha256, checkpoint_sha256, source_url, forward_revision,
+        weight_license;
+    ModelConfig config;
+    static Manifest from_json(const Json& j);  // strict keys (deny_unknown_fields)
+    void validate() const;
+};
+
+struct TransformerWeights {
+    DevBuf wqkvg, bqkvg;  // [3·inner + heads, dim] (norm folded) + bias (0 for q/k/v)
+    DevBuf wout;          // [dim, inner]
+    DevBuf w1, b1;        // [hidden, dim] (norm folded) + bias
+    DevBuf w2, b2;        // [dim, hidden] + bias
+    DevBuf out_scale;     // f32 [dim], Mel SourceNorm sqrt(dim)·gamma
+    int rope_set = 0;     // index into Model::rope_freqs
+};
+
+struct MaskWeights {
+    std::vector<DevBuf> w, b;  // hidden layers: [bands, out, in], [bands, out]
+    DevBuf glu_w, glu_b;       // [bands, 2·max_width, in] rows interleaved (value, gate)
+};
+
+struct Workspace {
+    int chunks = 0, frames = 0;
+    DevBuf x, xn, qkvg, att, hidden, h2, z, glu;
+    DevBuf split_groups, mask_groups, glu_groups;
+    std::vector<DevBuf> rope;  // per rope set: [time table, band table]
+};
+
+// Device buffers of the chunk pipeline (gather → STFT → model → iSTFT → overlap-add),
+// allocated on first use and reused while the batch and chunk length fit.
+struct PipelineBuffers {
+    int batch = 0;
+    int64_t chunk = 0;
+    DevBuf audio, packed, masks, scratch, y, flag, acc;
+};
+
+class Model {
+public:
+    static std::unique_ptr<Model> load(const std::string& package, int device, int precision);
+    ~Model();
+    // With check = false the non-finite status is left on the device (read_flag) and the
+    // call does not synchronise.
+    int forward(const float* spectrum, int chunks, int frames, float* masks,
+                const volatile int* cancel, cudaStream_t stream, bool check = true);
+    int reset_flag(cudaStream_t s);
+    int read_flag(cudaStream_t s, int* flag);  // synchronises `s`
+
+    PipelineBuffers pipe;
+
+    Manifest manifest;
+    int device = 0, precision = 0;
+    size_t tensor_count = 0;
+    int bands = 0, bins = 0, total_width = 0, max_width = 0, max_cover = 0;
+    int ldq = 0;  // row stride of the packed q|k|v|gate projection
+    std::string device_name;
+
+    // Kernel choices actually used (run.json attention_kernel / gemm_kernel).
+    bool tc_gemm() const;
+    bool tc_attention() const;
+
+private:
+    Model() = default;
+    int ensure_workspace(int chunks, int frames, cudaStream_t s);
+    int linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias,
+               const float* residual, int64_t ldr, void* out, int64_t ldo, int out_bf16,
+               int64_t m, int n, int k, int act, const float* rope, int rope_tokens,
+               int rope_div, cudaStream_t s);
+    int transformer(const TransformerWeights& t, bool time_axis, cudaStream_t s);
+
+    std::vector<int> width_, offset_;
+    DevBuf zcols_, zoffsets_, wsplit_, bsplit_;
+    std::vector<int64_t> wsplit_off_;
+    std::vector<std::array<TransformerWeights, 2>> layers_;
+    DevBuf final_scale_;
+    std::vector<MaskWeights> masks_;
+    DevBuf cover_count_, cover_entries_;
+    std::vector<std::vector<float>> rope_freqs_;
+    Workspace ws_;
+    DevBuf flag_;  // non-finite model output (sticky until reset_flag)
+    int elt_bf16_ = 0;  // activations / weights of the GEMMs in bf16
+    int cur_chunks_ = 0;  // chunks of the forward in progress
+};
+
+}  // namespace ancha
+
+// The opaque handle of the C ABI.
+struct ancha_model {
+    std::unique_ptr<ancha::Model> impl;
+};

@@ -1,0 +1,17 @@
+// Row-wise and gather kernels of the RoFormer stack (see rowops.cu).
+#pragma once
+#include "common.cuh"
+
+namespace ancha {
+
+int norm_rows(float* x, int64_t ldx, const float* scale, void* xn, int xn_bf16, int64_t ldn,
+              int64_t rows, int dim, cudaStream_t s);
+int cast_rows(const float* x, int64_t ldx, void* y, int y_bf16, int64_t ldy, int64_t rows,
+              int dim, cudaStream_t s);
+int band_gather(const float* spec, int chunks, int frames, int columns, const int* cols,
+                const int* offsets, int bands, int total, float* z, cudaStream_t s);
+int mask_assemble(const float* glu, int64_t ldg, int bands, int frames, int rows,
+                  const int* count, const int2* entries, int max_cover, int stems, int stem,
+                  float* masks, int chunks, int* nonfinite, cudaStream_t s);
+
+}  // namespace ancha

@@ -1,0 +1,340 @@
+"""×realtime of the Mel-Band RoFormer separation path on 1..8 B200s (one process per GPU).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (BASELINE.json configs[0] model, native context): Mel-Band RoFormer dim 384, depth 6,
+8×64 heads, 60 mel bands, n_fft 2048, hop 441, chunk 352800, overlap 4, one stem, seeded
+N(0, 0.02) weights; each GPU separates its own synthetic stereo track (Gaussian σ = 0.1,
+44.1 kHz, ``--seconds`` long, seed = 1000 + rank). A step is the whole pipeline over that
+track: chunk gather → STFT → model → complex mask + iSTFT → overlap-add → crop. Chunks are
+independent, so ranks shard the work with no collective ("scaling": "weak").
+
+* ``value``: audio seconds separated per wall second over all ranks, with the PCM already in
+  HBM (``ancha_separate_device``), timed with CUDA events on the launch stream, max over
+  ranks. The working set (≈0.5 GB of weights, ≈0.7 GB of activations per chunk) exceeds the
+  126 MB L2, so no extra flush runs between steps.
+* ``e2e``: the same through ``ancha_separate_pcm`` (host PCM in, host stems out, host↔device
+  copies inside the timed region).
+* ``roofline``: the dominant kernel re-launched alone with CUDA events.
+* ``cpu_baseline``: the numpy oracle (f32, all host cores) on one native chunk (rank 0, N=1).
+* ``--impl reference`` times that CPU port per step instead (the reference itself is Rust and
+  cannot be built offline).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "×realtime (audio s/wall s) Mel-RoFormer at 1/2/4/8 B200; fused-attn TFLOP/s vs peak"
+SR, CHUNK, OVERLAP, HOP = 44100, 352800, 4, 441
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--precision", default="bf16", choices=["bf16", "f32"])
+    p.add_argument("--seconds", type=float, default=30.0)
+    p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--package", default=os.environ.get("ANCHA_BENCH_PACKAGE", "/tmp/ancha_bench/mel-seed0"))
+    return p.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            m = json.load(fh)
+        return m["hbm_gbs"], m["bf16_tflops"], m.get("bf16_tflops_sustained", m["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def ensure_package(path: str, rank: int):
+    from ancha_b200 import synthetic
+    from ancha_b200.config import ModelConfig
+    done = os.path.join(path, "manifest.json")
+    if rank == 0 and not os.path.exists(done):
+        tmp = path + f".tmp{os.getpid()}"
+        synthetic.seeded_package(tmp, ModelConfig.mel_karaoke())
+        os.makedirs(os.path.dirname(path), exist_ok=True)
+        os.replace(tmp, path)
+    while not os.path.exists(done):
+        time.sleep(0.5)
+
+
+def track(seconds: float, seed: int):
+    n = int(round(seconds * SR))
+    return (np.random.default_rng(seed).standard_normal((2, n)) * 0.1).astype(np.float32)
+
+
+def plan_chunks(samples: int, chunk=CHUNK, overlap=OVERLAP):
+    step = chunk // overlap
+    border = chunk - step
+    border = border if samples > 2 * border else 0
+    length = samples + 2 * border
+    return len(range(0, length, step)), length
+
+
+def launches_per_step(chunks: int, batch: int, depth=6, stems=1, mask_layers=2, mel=True, bf16=True):
+    """Kernels of this library launched per step (from the pipeline structure)."""
+    per_transformer = 7 + (1 if mel else 0)
+    model = 2 + 2 * depth * per_transformer + (0 if mel else 1) + (1 if bf16 else 0) + stems * (mask_layers + 2)
+    per_batch = 2 + model + 2 + 1          # gather + stft, model, istft (2), ola
+    batches = -(-chunks // batch)
+    return batches * per_batch + 1        # + finish
+
+
+class Clocks:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self._stop = index, [], threading.Event()
+        self._proc = None
+
+    def __enter__(self):
+        q = "clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active," \
+            "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown," \
+            "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+        try:
+            self._proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
+                                           "--format=csv,noheader,nounits", "-lms", "200"],
+                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except Exception:
+            self._proc = None
+        return self
+
+    def _read(self):
+        for line in self._proc.stdout:
+            self.samples.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self._proc:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except Exception:
+                self._proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 4 + i and s[4 + i].lower().startswith("active")})
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(self.samples)}
+
+
+def cpu_oracle_chunk(package: str, seconds_audio: float = CHUNK / SR):
+    """Time the numpy oracle (f32) on one native chunk: gather → STFT → model → iSTFT → OLA."""
+    from oracle import dsp, roformer, runtime
+    model = roformer.Roformer(package, dtype=np.float32)
+    planes = track(CHUNK / SR, 7)
+    st = dsp.Stft(2048, HOP, dtype=np.float32)
+
+    def one():
+        t0 = time.perf_counter()
+        spectra = [st.forward(p) for p in planes]
+        masks = model.forward(runtime.pack_spectrum(spectra).astype(np.float32))
+        y = runtime.apply_masks(spectra, masks, st, CHUNK, True)
+        acc = dsp.Accumulator(2, CHUNK)
+        acc.add(dsp.ChunkPlan(CHUNK, OVERLAP), 0, y[0])
+        return time.perf_counter() - t0
+    return model, one
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ensure_package(a.package, 0)
+    _, one = cpu_oracle_chunk(a.package)
+    advance = CHUNK / OVERLAP / SR  # new audio per native chunk (s)
+    for _ in range(a.warmup):
+        one()
+    times = [one() for _ in range(a.steps)]
+    t = float(np.mean(times))
+    value = advance / t
+    cores = os.cpu_count()
+    sample = (f"one native-context chunk (8 s window, {advance:.0f} s of new audio) of the Mel-Band "
+              f"RoFormer per step through the numpy f32 port of the reference CPU path")
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "×realtime",
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": t * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": {"workload": "mel-band-roformer native context, CPU port"},
+        "cpu_baseline": {"value": value, "unit": "×realtime", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "×realtime", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    a = parse()
+    if a.impl == "reference":
+        return run_reference(a)
+    import ctypes as C
+
+    import torch
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from ancha_b200 import _native as N
+    from ancha_b200.model import Roformer, separate_pcm
+
+    ensure_package(a.package, rank if world == 1 else int(os.environ.get("LOCAL_RANK", "0")))
+    model = Roformer(a.package, local, a.precision)
+    planes = track(a.seconds, 1000 + rank)
+    samples = planes.shape[1]
+    chunks, length = plan_chunks(samples)
+    d_planes = torch.from_numpy(planes).to(f"cuda:{local}")
+    d_stems = torch.empty((model.stems, 2, samples), dtype=torch.float32, device=f"cuda:{local}")
+    stream = torch.cuda.Stream()
+    L = N.lib()
+
+    def step():
+        N.check(L.ancha_separate_device(model.handle, d_planes.data_ptr(), samples, CHUNK, OVERLAP,
+                                        a.batch, d_stems.data_ptr(), C.c_void_p(stream.cuda_stream)))
+
+    def barrier():
+        if dist:
+            dist.barrier()
+
+    with torch.cuda.stream(stream):
+        for _ in range(a.warmup):
+            step()
+        N.check(L.ancha_separate_status(model.handle, C.c_void_p(stream.cuda_stream)))
+        torch.cuda.synchronize()
+        barrier()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk:
+            ev0.record(stream)
+            for _ in range(a.steps):
+                step()
+            ev1.record(stream)
+            torch.cuda.synchronize()
+        N.check(L.ancha_separate_status(model.handle, C.c_void_p(stream.cuda_stream)))
+        barrier()
+    ms = ev0.elapsed_time(ev1) / a.steps
+    t = torch.tensor([ms], device=f"cuda:{local}")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    audio_s = samples / SR
+    value = world * audio_s / (ms / 1e3)
+
+    # End to end through the public host API (host PCM in, host stems out).
+    for _ in range(1):
+        separate_pcm([model], planes, CHUNK, OVERLAP, a.batch)
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(max(1, a.steps // 2)):
+        _, secs = separate_pcm([model], planes, CHUNK, OVERLAP, a.batch)
+    e2e_s = (time.perf_counter() - t0) / max(1, a.steps // 2)
+    te = torch.tensor([e2e_s], device=f"cuda:{local}")
+    if dist:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_s = float(te.item())
+    span_planes = model.stems * 2 + 1
+    e2e = {"value": world * audio_s / e2e_s, "unit": "×realtime",
+           "h2d_bytes_per_step": int(planes.nbytes), "d2h_bytes_per_step": int(span_planes * length * 4)}
+
+    # Dominant kernel alone: the FFN-in projection (rows = 60·801, 384 → 1536, GELU epilogue).
+    hbm, tc_peak, tc_sus, peak_kind = peaks()
+    from ancha_b200 import fused
+    rows = 60 * 801
+    x = torch.randn(rows, 384, device=f"cuda:{local}").to(torch.bfloat16 if a.precision == "bf16" else torch.float32)
+    w = (torch.randn(1536, 384, device=f"cuda:{local}") * 0.02).to(x.dtype)
+    b = torch.zeros(1536, device=f"cuda:{local}")
+    ep = fused.Epilogue(bias=b, gelu=True)
+    for _ in range(3):
+        fused.linear(x, w, ep, weight_layout=N.W_NK)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 20
+    e0.record()
+    for _ in range(reps):
+        fused.linear(x, w, ep, weight_layout=N.W_NK)
+    e1.record()
+    torch.cuda.synchronize()
+    kms = e0.elapsed_time(e1) / reps
+    flops = 2.0 * rows * 384 * 1536
+    achieved = flops / (kms / 1e3) / 1e12
+    roofline = {"kernel": "ffn_in linear (gemm, bias+GELU epilogue)", "bound": "tensor",
+                "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s", "frac": achieved / tc_peak,
+                "peak_kind": peak_kind, "traffic": None,
+                "algorithmic": f"2·{rows}·384·1536 flop per launch"}
+
+    # Fused attention alone (time axis T=801).
+    q = torch.randn(60, 801, 8, 64, device=f"cuda:{local}").to(x.dtype)
+    for _ in range(3):
+        fused.attention(q, q, q)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        fused.attention(q, q, q)
+    e1.record()
+    torch.cuda.synchronize()
+    ams = e0.elapsed_time(e1) / reps
+    attn_tf = 4.0 * 60 * 8 * 801 * 801 * 64 / (ams / 1e3) / 1e12
+    attention = {"shape": "[B=60, H=8, T=801, D=64]", "ms": ams, "tflops": attn_tf,
+                 "frac": attn_tf / tc_peak, "peak_kind": peak_kind}
+
+    cpu = None
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        _, one = cpu_oracle_chunk(a.package)
+        one()
+        tcpu = one()
+        cpu = {"value": (CHUNK / OVERLAP / SR) / tcpu, "unit": "×realtime", "cores": os.cpu_count(),
+               "kind": "port",
+               "sample": "one native-context chunk (8 s window, 2 s of new audio) through the numpy "
+                         f"f32 oracle, {tcpu:.1f} s"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "×realtime", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": a.precision,
+            "data": "synthetic (Gaussian sigma 0.1 stereo 44.1 kHz; seeded N(0,0.02) weights)",
+            "config": {"workload": f"mel-band-roformer dim384 depth6 60 bands, native context "
+                                   f"(chunk {CHUNK}, overlap {OVERLAP}), {a.seconds:.0f} s track "
+                                   f"= {chunks} chunks per GPU",
+                       "chunks_per_gpu": chunks, "batch_chunks": a.batch,
+                       "l2": "working set > 126 MB L2 (no flush)", "parallelism": f"chunk-shard x{world}"},
+            "clocks": clk.summary(), "e2e": e2e,
+            "gpu_launches": launches_per_step(chunks, a.batch, bf16=a.precision == "bf16") * a.steps,
+            "roofline": roofline, "attention": attention, "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,218 @@
+/*
+ * ancha_b200.h -- C ABI of the B200-native RoFormer separation engine.
+ *
+ * This is the drop-in boundary for the hot path of 3tic-project/Ancha: the kernel plug-in
+ * API of crates/ancha-models/src/fused/mod.rs, the model API of
+ * crates/ancha-models/src/network.rs and the task API of src/backend.rs / src/runtime.rs.
+ * Every entry point takes plain pointers and sizes. Device pointers are CUDA device
+ * addresses on the calling thread's current device; `stream` is a cudaStream_t passed as
+ * void* (NULL = the legacy default stream). The caller owns every buffer: kernel entry
+ * points never allocate.
+ *
+ * Status codes: ANCHA_OK, or a negative code. ANCHA_E_UNSUPPORTED is the reference's
+ * `None` ("shape or backend not handled here, use your fallback"); the reference panics
+ * inside `launch` on invalid operands, which maps to ANCHA_E_INVALID. After any non-zero
+ * status, ancha_last_error() returns a message for the calling thread.
+ */
+#ifndef ANCHA_B200_H
+#define ANCHA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ANCHA_API __attribute__((visibility("default")))
+#else
+#define ANCHA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    ANCHA_OK = 0,
+    ANCHA_E_UNSUPPORTED = -1, /* the reference's `None`: caller falls back            */
+    ANCHA_E_INVALID = -2,     /* invalid arguments (the reference asserts / errors)     */
+    ANCHA_E_CUDA = -3,        /* a CUDA runtime or launch error                         */
+    ANCHA_E_CANCELLED = -4,   /* the cancel flag was set (runtime.rs:44,118)           */
+    ANCHA_E_IO = -5,          /* file or package error                                  */
+    ANCHA_E_TIMEOUT = -6,     /* a bounded device-side wait gave up                     */
+    ANCHA_E_NONFINITE = -7    /* non-finite model output (runtime.rs:173-176)           */
+};
+
+/* Element types of kernel operands. */
+enum { ANCHA_F32 = 0, ANCHA_BF16 = 1 };
+
+/* Model arithmetic: F32 = fp32 FFMA kernels throughout; BF16 = bf16 tcgen05 tensor-core
+ * GEMMs and attention with fp32 accumulation, fp32 residual stream and DSP. */
+enum { ANCHA_PRECISION_F32 = 0, ANCHA_PRECISION_BF16 = 1 };
+
+/* Message of the last failure on the calling thread ("" if none). */
+ANCHA_API const char* ancha_last_error(void);
+
+/* Library version string. */
+ANCHA_API const char* ancha_version(void);
+
+/* 1 when `device` is an sm_100 GPU this library can run on, else 0 (with a message).
+ * Replaces fused::available::<B>() (fused/mod.rs:249-255) and src/cuda.rs::probe (19-46). */
+ANCHA_API int ancha_available(int device);
+
+/* ------------------------------------------------------------------------------------ *
+ * Kernel plug-in API (replaces crates/ancha-models/src/fused/mod.rs)                   *
+ * ------------------------------------------------------------------------------------ */
+
+/* Attention operand layout. Token `i` of group `g` lives at row
+ *     row(g, i) = (g / group_inner) * group_outer_stride + (g % group_inner) * group_inner_stride
+ *                 + i * token_stride
+ * of a row-major matrix whose rows are `ld` elements apart; head `h` of q / k / v starts at
+ * column q_col / k_col / v_col + 64·h and the output head at out_col + 64·h of rows
+ * `out_ld` apart. With gate_col >= 0 each output row of head h is scaled by
+ * sigmoid(q[row, gate_col + h]) (the gated form). The reference's dense [groups, tokens,
+ * heads, 64] layout is group_inner = groups, group_inner_stride = tokens, token_stride = 1,
+ * ld = out_ld = heads·64. */
+typedef struct {
+    int groups, tokens, heads;
+    int head_dim;                 /* must be 64 (ATTENTION_HEAD_DIM, fused/mod.rs:18) */
+    int dtype;                    /* ANCHA_F32 or ANCHA_BF16 for q/k/v/gate and out    */
+    int64_t ld, out_ld;           /* row strides in elements                           */
+    int64_t group_inner, group_inner_stride, group_outer_stride, token_stride; /* rows */
+    int q_col, k_col, v_col, gate_col, out_col;
+} ancha_attn_desc;
+
+/* softmax(q·kᵀ)·v per (group, head), non-causal, q pre-scaled by 1/sqrt(64); optionally
+ * gated. Replaces fused::attention (fused/mod.rs:20-41) and fused::gated_attention
+ * (fused/mod.rs:43-55), whose kernel is fused/attention.rs:24-298. */
+ANCHA_API int ancha_attention_fwd(const ancha_attn_desc* desc, const void* q, const void* k,
+                        const void* v, const void* gate, void* out, void* stream);
+
+/* Weight layouts accepted by ancha_linear_fwd. */
+enum {
+    ANCHA_W_KN = 0, /* weight[k][n]: Burn's Linear layout, the reference's fused::linear */
+    ANCHA_W_NK = 1  /* weight[n][k]: PyTorch's [out, in]                                 */
+};
+
+/* Epilogue activations (applied after the bias, fused/gemm.rs:44-82 order). */
+enum { ANCHA_ACT_NONE = 0, ANCHA_ACT_GELU = 1, ANCHA_ACT_TANH = 2, ANCHA_ACT_GLU = 3 };
+
+/* out[m, n] = epilogue(sum_k x[m, k] · w(k, n)).
+ * Epilogue, in order: + bias[n]; activation; interleaved RoPE on columns [0, 2·rope_width)
+ * (queries then keys, token = (m / rope_div) % rope_tokens, table [4, rope_tokens, 64] =
+ * query cos / signed sin (carrying 1/sqrt(64)), key cos / signed sin, as AxisRope::packed,
+ * roformer.rs:281-302); + residual[m, n]. ANCHA_ACT_GLU pairs columns (2j, 2j+1) as
+ * (value, gate) and writes value·sigmoid(gate) to column j (n_out = n / 2).
+ * Replaces fused::linear + Epilogue (fused/mod.rs:57-176, kernel fused/gemm.rs:84-311).
+ * x, w: `dtype` (F32 → fp32 FFMA kernel; BF16 → tcgen05 kernel, requires ANCHA_W_NK);
+ * bias, residual, rope: f32; out: out_dtype. `workspace` may be NULL (none is needed). */
+typedef struct {
+    int m, n, k;
+    int dtype, out_dtype, weight_layout;
+    int64_t ldx, ldw, ldout, ldres;
+    int act;
+    int rope_width, rope_tokens, rope_div;  /* rope_width = 0: no rotary epilogue */
+} ancha_linear_desc;
+
+ANCHA_API int ancha_linear_fwd(const ancha_linear_desc* desc, const void* x, const void* w,
+                     const float* bias, const float* residual, const float* rope,
+                     void* out, void* stream);
+
+/* ------------------------------------------------------------------------------------ *
+ * Spectral DSP (replaces crates/ancha-audio/src/dsp.rs and chunk.rs on the device)     *
+ * ------------------------------------------------------------------------------------ */
+
+/* Centered periodic-Hann STFT (n_fft 2048, reflect padding, unnormalised FFT) of `chunks`
+ * stereo chunks `audio[c][ch][samples]` into the model layout
+ * `packed[c][frame][(bin·2 + ch)·2 + re/im]`, frames = samples / hop + 1 (dsp.rs:52-79,
+ * runtime.rs:148-162). */
+ANCHA_API int ancha_stft_fwd(const float* audio, int chunks, int samples, int hop, float* packed,
+                   void* stream);
+
+/* Complex-mask multiply + inverse STFT: for every chunk, stem and channel, multiply the
+ * packed spectrum by masks[c][stem][bin·2+ch][re/im][frame] and invert (zero Im at DC and
+ * Nyquist, zero Re at DC if zero_dc, 1/n scale, window-square normalised overlap-add,
+ * dsp.rs:82-133, runtime.rs:181-201) into out[c][stem][ch][samples]. `scratch` holds
+ * chunks·stems·2·frames·2048 floats followed by one int status word that the call sets to
+ * a non-zero value if a sample had no window support ("iSTFT has an uncovered sample"). */
+ANCHA_API int ancha_istft_masked(const float* packed, const float* masks, int chunks, int stems,
+                       int samples, int hop, int zero_dc, float* scratch, float* out,
+                       void* stream);
+
+/* Linear-fade overlap-add of `chunks` chunk outputs y[c][planes][chunk] starting at
+ * starts[c] (host array, ascending) into sums[planes][length] and weights[length], in
+ * chunk order (chunk.rs:26-75). */
+ANCHA_API int ancha_ola_add(const float* y, int chunks, int planes, int chunk, int overlap,
+                  const int64_t* starts, int64_t length, float* sums, float* weights,
+                  void* stream);
+
+/* ------------------------------------------------------------------------------------ *
+ * Model API (replaces Roformer::load / forward, crates/ancha-models/src/network.rs)   *
+ * ------------------------------------------------------------------------------------ */
+
+typedef struct ancha_model ancha_model;
+
+/* Load `package_dir/manifest.json` + `model.safetensors` (strict schema-1 checks, SHA-256
+ * verification, load-time folding) onto `device` (network.rs:80-278, weights.rs:29-176). */
+ANCHA_API int ancha_model_load(const char* package_dir, int device, int precision, ancha_model** out);
+
+/* Model shape queries. */
+ANCHA_API int ancha_model_info(const ancha_model* model, int* stems, int* bands, int* dim,
+                     int* bins, int* chunk_samples, int* hop, int* overlap);
+
+/* Masks for `chunks` spectra: spectrum[c][frames][bins·4] (device, packed as above) →
+ * masks[c][stem][bins·2][2][frames] (device) (network.rs:301-400). Checks *cancel (host
+ * memory, may be NULL) between layers (network.rs:334,367). The handle is bound to its
+ * device and is not re-entrant. */
+ANCHA_API int ancha_model_forward(ancha_model* model, const float* spectrum, int chunks, int frames,
+                        float* masks, const volatile int* cancel, void* stream);
+
+ANCHA_API void ancha_model_free(ancha_model* model);
+
+/* ------------------------------------------------------------------------------------ *
+ * Task API (replaces backend::separate / runtime::separate, src/backend.rs:145-199)    *
+ * ------------------------------------------------------------------------------------ */
+
+typedef struct {
+    const char* input;         /* WAV path (PCM16/24/32 or float32, mono or stereo, 44.1 kHz) */
+    const char* model;         /* package directory                                           */
+    const char* output;        /* output directory (published atomically)                     */
+    int64_t chunk_samples;     /* 0 = manifest value (runtime.rs:52-57)                       */
+    int overlap;               /* 0 = manifest value                                          */
+    int precision;             /* ANCHA_PRECISION_*                                           */
+    int batch_chunks;          /* chunks per model call on each device (0 = automatic)        */
+    double start_seconds;      /* decode window (DecodeOptions)                                */
+    double duration_seconds;   /* <= 0: to the end                                             */
+} ancha_separate_opts;
+
+/* Separate a track on `n_devices` GPUs (chunks sharded in contiguous ranges, one host
+ * thread per GPU). Writes <stem>.wav and run.json into opts->output and returns the run
+ * report JSON in *run_json (free with ancha_free_string). `progress(done, total, user)` may
+ * be NULL. */
+ANCHA_API int ancha_separate(const ancha_separate_opts* opts, int n_devices, const int* devices,
+                   void (*progress)(size_t done, size_t total, void* user), void* user,
+                   const volatile int* cancel, char** run_json);
+
+/* In-memory form of ancha_separate for host PCM: planes[2][samples] (host, f32) →
+ * stems_out[stems][2][samples] (host, f32). Used by benchmarks and the SDK. */
+ANCHA_API int ancha_separate_pcm(ancha_model* const* models, int n_models, const float* planes,
+                       int64_t samples, int64_t chunk_samples, int overlap, int batch_chunks,
+                       const volatile int* cancel, float* stems_out, double* seconds_out);
+
+/* Device-resident form for one model: planes[2][samples] (device) → stems[stems][2][samples]
+ * (device), everything enqueued on `stream` without a host synchronisation (the model's
+ * pipeline buffers are allocated on the first call and reused). Status words (non-finite
+ * output, uncovered sample) stay on the device until ancha_separate_status. Replaces the
+ * per-chunk loop of src/runtime.rs:117-225 for inputs already in HBM. */
+ANCHA_API int ancha_separate_device(ancha_model* model, const float* planes, int64_t samples,
+                                    int64_t chunk_samples, int overlap, int batch_chunks,
+                                    float* stems, void* stream);
+
+/* Synchronise `stream` and report the status words of the last ancha_separate_device. */
+ANCHA_API int ancha_separate_status(ancha_model* model, void* stream);
+
+ANCHA_API void ancha_free_string(char* s);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ANCHA_B200_H */

@@ -1,0 +1,63 @@
+"""The C-ABI library without a GPU: it loads, exports every symbol the header declares, and
+fails with a status (not a crash) when no GPU is present. No compute call runs here."""
+import ctypes as C
+import os
+import re
+
+import pytest
+
+from ancha_b200 import _native as N
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "ancha_b200.h")).read()
+    return sorted(set(re.findall(r"ANCHA_API\s+[\w\s\*]+?\b(ancha_\w+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = N.lib()
+    declared = header_functions()
+    assert declared == sorted(N.EXPORTS)
+    for name in declared:
+        assert hasattr(lib, name), name
+
+
+def test_exported_symbols_are_exactly_the_header():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", N.LIB_PATH], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("nm unavailable")
+    syms = sorted(l.split()[-1] for l in out.stdout.splitlines() if " T " in l and "ancha_" in l)
+    assert syms == header_functions()
+
+
+def test_version_and_status_without_gpu():
+    lib = N.lib()
+    assert b"sm_100a" in lib.ancha_version()
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    assert lib.ancha_available(0) == 0
+    assert N.last_error()
+
+
+def test_struct_layouts_match_header():
+    # The ctypes mirrors must match the C layout (sizes of the packed descriptors).
+    assert C.sizeof(N.AttnDesc) == 5 * 4 + 4 + 6 * 8 + 5 * 4 + 4  # + padding to 8
+    assert C.sizeof(N.LinearDesc) == 6 * 4 + 4 * 8 + 4 * 4
+    assert C.sizeof(N.SeparateOpts) == 3 * 8 + 8 + 4 * 4 + 2 * 8
+
+
+def test_invalid_arguments_are_rejected_before_any_launch():
+    lib = N.lib()
+    assert lib.ancha_attention_fwd(None, None, None, None, None, None, None) == N.E_INVALID
+    d = N.AttnDesc(1, 1, 1, 32, N.F32, 64, 64, 1, 1, 0, 1, 0, 0, 0, -1, 0)
+    # head_dim 32 is the reference's `None` (cuda_contracts.rs:249-250).
+    assert lib.ancha_attention_fwd(C.byref(d), 1, 1, 1, None, 1, None) == N.E_UNSUPPORTED
+    ld = N.LinearDesc(4, 128, 12, N.F32, N.F32, N.W_KN, 12, 128, 128, 0, N.ACT_NONE, 0, 1, 1)
+    assert lib.ancha_linear_fwd(C.byref(ld), 1, 1, None, None, None, 1, None) != N.OK
+    h = C.c_void_p()
+    assert lib.ancha_model_load(b"/nonexistent-package", 0, 0, C.byref(h)) != N.OK
+    assert not h.value
