@@ -13,8 +13,9 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "lib", "liba
 
 OK, E_UNSUPPORTED, E_INVALID, E_CUDA, E_CANCELLED, E_IO, E_TIMEOUT, E_NONFINITE = \
     0, -1, -2, -3, -4, -5, -6, -7
-F32, BF16 = 0, 1
-PRECISION_F32, PRECISION_BF16 = 0, 1
+F32, BF16, F16 = 0, 1, 2
+PRECISION_F32, PRECISION_BF16, PRECISION_F16 = 0, 1, 2
+PRECISIONS = {"f32": PRECISION_F32, "bf16": PRECISION_BF16, "f16": PRECISION_F16}
 W_KN, W_NK = 0, 1
 ACT_NONE, ACT_GELU, ACT_TANH, ACT_GLU = 0, 1, 2, 3
 

@@ -68,7 +68,7 @@ int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, 
     if (d->head_dim != 64) return fail(ANCHA_E_UNSUPPORTED, "attention: head_dim must be 64");
     if (d->groups < 0 || d->tokens < 0 || d->heads <= 0)
         return fail(ANCHA_E_INVALID, "attention: negative shape");
-    if (d->dtype != ANCHA_F32 && d->dtype != ANCHA_BF16)
+    if (d->dtype != ANCHA_F32 && d->dtype != ANCHA_BF16 && d->dtype != ANCHA_F16)
         return fail(ANCHA_E_INVALID, "attention: unknown dtype");
     if (d->group_inner <= 0 || d->token_stride < 0 || d->ld <= 0 || d->out_ld <= 0)
         return fail(ANCHA_E_INVALID, "attention: invalid strides");
@@ -85,9 +85,9 @@ int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, 
     a.group_outer_stride = d->group_outer_stride; a.token_stride = d->token_stride;
     a.q_col = d->q_col; a.k_col = d->k_col; a.v_col = d->v_col;
     a.gate_col = gate ? d->gate_col : 0; a.out_col = d->out_col;
-    a.bf16 = d->dtype == ANCHA_BF16;
+    a.elt = d->dtype;
     cudaStream_t s = as_stream(stream);
-    if (a.bf16) {
+    if (a.elt != ELT_F32) {
         int st = attention_tc(a, s);
         if (st != ANCHA_E_UNSUPPORTED) return st;
     }
@@ -98,8 +98,10 @@ int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, c
                      const float* residual, const float* rope, void* out, void* stream) {
     if (!d || !x || !w || !out) return fail(ANCHA_E_INVALID, "linear: null argument");
     if (d->m < 0 || d->n <= 0 || d->k <= 0) return fail(ANCHA_E_UNSUPPORTED, "linear: empty shape");
-    if (d->dtype != ANCHA_F32 && d->dtype != ANCHA_BF16)
+    if (d->dtype != ANCHA_F32 && d->dtype != ANCHA_BF16 && d->dtype != ANCHA_F16)
         return fail(ANCHA_E_INVALID, "linear: unknown dtype");
+    if (d->out_dtype != ANCHA_F32 && d->out_dtype != ANCHA_BF16 && d->out_dtype != ANCHA_F16)
+        return fail(ANCHA_E_INVALID, "linear: unknown output dtype");
     if (d->act < ANCHA_ACT_NONE || d->act > ANCHA_ACT_GLU) return fail(ANCHA_E_INVALID, "linear: unknown activation");
     if (d->act == ANCHA_ACT_GLU && (d->n % 2 || residual || d->rope_width))
         return fail(ANCHA_E_INVALID, "linear: GLU needs an even n and no residual / rotary");
@@ -122,19 +124,18 @@ int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, c
     g.lda = d->ldx; g.ldb = d->ldw; g.ldr = d->ldres; g.ldo = d->ldout;
     GemmEpilogue e{};
     e.act = d->act;
-    e.out_bf16 = d->out_dtype == ANCHA_BF16;
+    e.out_type = d->out_dtype;
     e.rope = d->rope_width ? rope : nullptr;
     e.rope_width = d->rope_width;
     e.rope_tokens = d->rope_tokens > 0 ? d->rope_tokens : 1;
     e.rope_div = d->rope_div > 0 ? d->rope_div : 1;
     e.rope_hd = 64;
     cudaStream_t s = as_stream(stream);
-    const int bf = d->dtype == ANCHA_BF16;
-    if (bf && wl == ANCHA_W_NK) {
-        int st = gemm_tc(g, e, s);
+    if (d->dtype != ANCHA_F32 && wl == ANCHA_W_NK) {
+        int st = gemm_tc(g, d->dtype, e, s);
         if (st != ANCHA_E_UNSUPPORTED) return st;
     }
-    return gemm_ffma(g, nullptr, 1, d->m, d->n, bf, bf, wl == ANCHA_W_NK, e, s);
+    return gemm_ffma(g, nullptr, 1, d->m, d->n, d->dtype, d->dtype, wl == ANCHA_W_NK, e, s);
 }
 
 int ancha_stft_fwd(const float* audio, int chunks, int samples, int hop, float* packed, void* stream) {

@@ -14,7 +14,7 @@ struct AttnArgs {
     int64_t ld, out_ld;
     int64_t group_inner, group_inner_stride, group_outer_stride, token_stride;
     int q_col, k_col, v_col, gate_col, out_col;
-    int bf16;  // q/k/v/gate/out element type
+    int elt;  // q/k/v/gate/out element type (ELT_*)
 };
 
 // First row of group g (see ancha_attn_desc).

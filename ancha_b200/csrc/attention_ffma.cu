@@ -112,7 +112,8 @@ int attention_ffma(const AttnArgs& a, cudaStream_t stream) {
     if (a.head_dim <= 0 || a.head_dim > 64 || a.head_dim % 4)
         return fail(ANCHA_E_UNSUPPORTED, "attention: head_dim must be a multiple of 4 up to 64");
     dim3 grid((unsigned)ceil_div(a.tokens, TQ), (unsigned)a.heads, (unsigned)a.groups);
-    if (a.bf16) attention_ffma_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(a);
+    if (a.elt == ELT_BF16) attention_ffma_kernel<__nv_bfloat16><<<grid, 128, 0, stream>>>(a);
+    else if (a.elt == ELT_F16) attention_ffma_kernel<__half><<<grid, 128, 0, stream>>>(a);
     else attention_ffma_kernel<float><<<grid, 128, 0, stream>>>(a);
     return check_launch("attention_ffma");
 }

@@ -19,7 +19,7 @@ struct GemmGroup {
 // Epilogue shared by every group of one launch.
 struct GemmEpilogue {
     int act;            // ANCHA_ACT_*
-    int out_bf16;       // 1: out is bf16, 0: f32
+    int out_type;       // ELT_F32 / ELT_BF16 / ELT_F16
     const float* rope;  // [4, rope_tokens, 64] or null
     int rope_width;     // rotate columns [0, 2·rope_width)
     int rope_tokens;
@@ -28,14 +28,14 @@ struct GemmEpilogue {
 };
 
 // FFMA GEMM (fp32 accumulation). `groups` is a device array of `count` problems when
-// non-null, else `single` is the one problem. TA / TB are float or __nv_bfloat16.
+// non-null, else `single` is the one problem. A and B are f32, or both bf16, or both f16.
 int gemm_ffma(const GemmGroup& single, const GemmGroup* groups, int count, int max_m,
-              int max_n, int a_bf16, int b_bf16, int b_nk, const GemmEpilogue& epi,
+              int max_n, int a_type, int b_type, int b_nk, const GemmEpilogue& epi,
               cudaStream_t stream);
 
-// tcgen05 / TMA GEMM (bf16 operands, fp32 accumulation in TMEM) for one problem with
-// NK weights. Returns ANCHA_E_UNSUPPORTED when the operands do not meet its alignment
+// tcgen05 / TMA GEMM (bf16 or f16 operands, fp32 accumulation in TMEM) for one problem
+// with NK weights; `ab_type` is the operand type of both A and B. Returns ANCHA_E_UNSUPPORTED when the operands do not meet its alignment
 // rules (16-byte rows, k % 8 == 0), so the caller can use gemm_ffma instead.
-int gemm_tc(const GemmGroup& g, const GemmEpilogue& epi, cudaStream_t stream);
+int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& epi, cudaStream_t stream);
 
 }  // namespace ancha

@@ -54,9 +54,7 @@ __device__ __forceinline__ void finish4(const GemmGroup& g, const GemmEpilogue& 
             const int c = c0 + j;
             if (c + 1 < g.n) {
                 const float o = v[j] * sigmoidf_(v[j + 1]);
-                const int64_t idx = (int64_t)row * g.ldo + c / 2;
-                if (e.out_bf16) store_f(reinterpret_cast<__nv_bfloat16*>(g.out) + idx, o);
-                else store_f(reinterpret_cast<float*>(g.out) + idx, o);
+                store_elt(g.out, (int64_t)row * g.ldo + c / 2, o, e.out_type);
             }
         }
         return;
@@ -67,9 +65,7 @@ __device__ __forceinline__ void finish4(const GemmGroup& g, const GemmEpilogue& 
         if (c >= g.n) break;
         float o = v[j];
         if (g.residual) o += g.residual[(int64_t)row * g.ldr + c];
-        const int64_t idx = (int64_t)row * g.ldo + c;
-        if (e.out_bf16) store_f(reinterpret_cast<__nv_bfloat16*>(g.out) + idx, o);
-        else store_f(reinterpret_cast<float*>(g.out) + idx, o);
+        store_elt(g.out, (int64_t)row * g.ldo + c, o, e.out_type);
     }
 }
 
@@ -168,17 +164,17 @@ void launch_typed(dim3 grid, cudaStream_t s, int b_nk, const GemmGroup& single,
 }  // namespace
 
 int gemm_ffma(const GemmGroup& single, const GemmGroup* groups, int count, int max_m,
-              int max_n, int a_bf16, int b_bf16, int b_nk, const GemmEpilogue& epi,
+              int max_n, int a_type, int b_type, int b_nk, const GemmEpilogue& epi,
               cudaStream_t stream) {
     if (count <= 0 || max_m <= 0 || max_n <= 0) return ANCHA_OK;
     if (count > 65535 || ceil_div(max_m, BM) > 65535)
         return fail(ANCHA_E_INVALID, "gemm: grid too large");
     dim3 grid((unsigned)ceil_div(max_n, BN), (unsigned)ceil_div(max_m, BM), (unsigned)count);
     using bf = __nv_bfloat16;
-    if (a_bf16 && b_bf16) launch_typed<bf, bf>(grid, stream, b_nk, single, groups, epi);
-    else if (a_bf16) launch_typed<bf, float>(grid, stream, b_nk, single, groups, epi);
-    else if (b_bf16) launch_typed<float, bf>(grid, stream, b_nk, single, groups, epi);
-    else launch_typed<float, float>(grid, stream, b_nk, single, groups, epi);
+    if (a_type == ELT_F32 && b_type == ELT_F32) launch_typed<float, float>(grid, stream, b_nk, single, groups, epi);
+    else if (a_type == ELT_BF16 && b_type == ELT_BF16) launch_typed<bf, bf>(grid, stream, b_nk, single, groups, epi);
+    else if (a_type == ELT_F16 && b_type == ELT_F16) launch_typed<__half, __half>(grid, stream, b_nk, single, groups, epi);
+    else return fail(ANCHA_E_UNSUPPORTED, "gemm: mixed operand types");
     return check_launch("gemm_ffma");
 }
 

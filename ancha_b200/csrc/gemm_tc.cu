@@ -2,7 +2,7 @@
 #include "gemm.cuh"
 
 namespace ancha {
-int gemm_tc(const GemmGroup&, const GemmEpilogue&, cudaStream_t) {
+int gemm_tc(const GemmGroup&, int, const GemmEpilogue&, cudaStream_t) {
     return fail(ANCHA_E_UNSUPPORTED, "tcgen05 GEMM not built");
 }
 }  // namespace ancha

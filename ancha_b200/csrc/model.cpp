@@ -55,19 +55,16 @@ void upload(DevBuf& d, const std::vector<T>& v) {
     if (e != cudaSuccess) bad(std::string("cudaMemcpy: ") + cudaGetErrorString(e));
 }
 
-uint16_t to_bf16(float f) {  // round to nearest even
-    uint32_t u;
-    std::memcpy(&u, &f, 4);
-    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
-    u += 0x7fffu + ((u >> 16) & 1u);
-    return (uint16_t)(u >> 16);
-}
-
-// Upload f32 host weights as f32 or bf16.
-void upload_weights(DevBuf& d, const std::vector<float>& v, bool bf16) {
-    if (!bf16) return upload(d, v);
-    std::vector<uint16_t> h(v.size());
-    for (size_t i = 0; i < v.size(); ++i) h[i] = to_bf16(v[i]);
+// Upload f32 host weights as f32, bf16 or f16 (round to nearest even).
+void upload_weights(DevBuf& d, const std::vector<float>& v, int elt) {
+    if (elt == ELT_F32) return upload(d, v);
+    if (elt == ELT_BF16) {
+        std::vector<__nv_bfloat16> h(v.size());
+        for (size_t i = 0; i < v.size(); ++i) h[i] = __float2bfloat16_rn(v[i]);
+        return upload(d, h);
+    }
+    std::vector<__half> h(v.size());
+    for (size_t i = 0; i < v.size(); ++i) h[i] = __float2half_rn(v[i]);
     upload(d, h);
 }
 
@@ -218,22 +215,23 @@ void Manifest::validate() const {
 }
 
 // --------------------------------------------------------------------------- model loading
-bool Model::tc_gemm() const { return false; }
-bool Model::tc_attention() const { return false; }
+bool Model::tc_gemm() const { return elt_ != ELT_F32; }
+bool Model::tc_attention() const { return elt_ != ELT_F32; }
 
 Model::~Model() {
     if (device >= 0) cudaSetDevice(device);
 }
 
 std::unique_ptr<Model> Model::load(const std::string& package, int device, int precision) {
-    if (precision != ANCHA_PRECISION_F32 && precision != ANCHA_PRECISION_BF16)
+    if (precision != ANCHA_PRECISION_F32 && precision != ANCHA_PRECISION_BF16 &&
+        precision != ANCHA_PRECISION_F16)
         bad("unknown precision");
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) bad(std::string("cudaSetDevice: ") + cudaGetErrorString(e));
     std::unique_ptr<Model> m(new Model());
     m->device = device;
     m->precision = precision;
-    m->elt_bf16_ = precision == ANCHA_PRECISION_BF16;
+    m->elt_ = precision == ANCHA_PRECISION_BF16 ? ELT_BF16 : precision == ANCHA_PRECISION_F16 ? ELT_F16 : ELT_F32;
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) m->device_name = prop.name;
     m->manifest = Manifest::from_json(Json::parse(read_file(package + "/manifest.json")));
@@ -247,7 +245,7 @@ std::unique_ptr<Model> Model::load(const std::string& package, int device, int p
     try {
         SafeTensors w(bytes);
         const ModelConfig& c = m->manifest.config;
-        const bool bf = m->elt_bf16_;
+        const int bf = m->elt_;
         const int dim = c.dim, inner = c.heads * c.head_dim, hidden = c.dim * c.ff_mult;
         const int nb = (int)c.bands.size();
         m->bands = nb;
@@ -419,7 +417,7 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
         w.chunks = chunks;
         w.frames = frames;
         const int64_t R = (int64_t)chunks * bands * frames;
-        const size_t e = elt_bf16_ ? 2 : 4;
+        const size_t e = elt_size(elt_);
         const int inner = c.heads * c.head_dim, hidden = c.dim * c.ff_mult;
         const int mh = c.dim * c.mask_expansion;
         w.x.alloc(R * c.dim * 4);
@@ -459,7 +457,7 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
         for (size_t st = 0; st < masks_.size(); ++st) {
             const MaskWeights& mw = masks_[st];
             int in = c.dim;
-            const char* a_base = (const char*)(elt_bf16_ ? w.xn.p : w.x.p);
+            const char* a_base = (const char*)(elt_ != ELT_F32 ? w.xn.p : w.x.p);
             for (int l = 0; l <= hidden_layers; ++l) {
                 const bool glu = l == hidden_layers;
                 const char* out_base = glu ? (const char*)w.glu.p
@@ -530,7 +528,7 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
 }
 
 int Model::linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias,
-                  const float* residual, int64_t ldr, void* out, int64_t ldo, int out_bf16,
+                  const float* residual, int64_t ldr, void* out, int64_t ldo, int out_type,
                   int64_t m, int n, int k, int act, const float* rope, int rope_tokens,
                   int rope_div, cudaStream_t s) {
     GemmGroup g{};
@@ -548,14 +546,18 @@ int Model::linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias
     g.k = k;
     GemmEpilogue e{};
     e.act = act;
-    e.out_bf16 = out_bf16;
+    e.out_type = out_type;
     e.rope = rope;
     const ModelConfig& c = manifest.config;
     e.rope_width = rope ? c.heads * c.head_dim : 0;
     e.rope_tokens = rope_tokens;
     e.rope_div = rope_div;
     e.rope_hd = c.head_dim;
-    return gemm_ffma(g, nullptr, 1, (int)m, n, elt_bf16_, elt_bf16_, 1, e, s);
+    if (elt_ != ELT_F32) {
+        const int st = gemm_tc(g, elt_, e, s);
+        if (st != ANCHA_E_UNSUPPORTED) return st;
+    }
+    return gemm_ffma(g, nullptr, 1, (int)m, n, elt_, elt_, 1, e, s);
 }
 
 int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t s) {
@@ -563,7 +565,7 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
     const int T = ws_.frames, C = cur_chunks_;
     const int64_t R = (int64_t)C * bands * T;
     const int dim = c.dim, inner = c.heads * c.head_dim, hidden = c.dim * c.ff_mult;
-    const int bf = elt_bf16_;
+    const int bf = elt_;
     float* x = ws_.x.as<float>();
     const DevBuf& rope = ws_.rope[(size_t)t.rope_set * 2 + (time_axis ? 0 : 1)];
     // Packed q | k | v | gate projection of unit_norm(x), RoPE in the epilogue.
@@ -584,7 +586,7 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
     a.v_col = 2 * inner;
     a.gate_col = 3 * inner;
     a.out_col = 0;
-    a.bf16 = bf;
+    a.elt = bf;
     if (time_axis) {
         a.groups = C * bands;
         a.tokens = T;
@@ -600,14 +602,16 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
         a.group_outer_stride = (int64_t)bands * T;
         a.token_stride = T;
     }
-    ANCHA_TRY(attention_ffma(a, s));
+    int ast = bf != ELT_F32 ? attention_tc(a, s) : ANCHA_E_UNSUPPORTED;
+    if (ast == ANCHA_E_UNSUPPORTED) ast = attention_ffma(a, s);
+    ANCHA_TRY(ast);
     // Output projection + residual, then the GELU feed-forward + residual.
-    ANCHA_TRY(linear(ws_.att.p, inner, t.wout, nullptr, x, dim, x, dim, 0, R, dim, inner,
+    ANCHA_TRY(linear(ws_.att.p, inner, t.wout, nullptr, x, dim, x, dim, ELT_F32, R, dim, inner,
                      ANCHA_ACT_NONE, nullptr, 1, 1, s));
     ANCHA_TRY(norm_rows(x, dim, nullptr, ws_.xn.p, bf, dim, R, dim, s));
     ANCHA_TRY(linear(ws_.xn.p, dim, t.w1, t.b1.as<float>(), nullptr, 0, ws_.hidden.p, hidden, bf,
                      R, hidden, dim, ANCHA_ACT_GELU, nullptr, 1, 1, s));
-    ANCHA_TRY(linear(ws_.hidden.p, hidden, t.w2, t.b2.as<float>(), x, dim, x, dim, 0, R, dim,
+    ANCHA_TRY(linear(ws_.hidden.p, hidden, t.w2, t.b2.as<float>(), x, dim, x, dim, ELT_F32, R, dim,
                      hidden, ANCHA_ACT_NONE, nullptr, 1, 1, s));
     // Mel: SourceNorm of the block output (roformer.rs:516-519).
     if (t.out_scale.p) ANCHA_TRY(norm_rows(x, dim, t.out_scale.as<float>(), nullptr, 0, 0, R, dim, s));
@@ -665,8 +669,8 @@ int Model::forward(const float* spectrum, int chunks, int frames, float* masks,
     float* x = ws_.x.as<float>();
     if (final_scale_.p)  // BS final norm (network.rs:340-342)
         ANCHA_TRY(norm_rows(x, c.dim, final_scale_.as<float>(), nullptr, 0, 0, R, c.dim, s));
-    // Mask estimators (network.rs:364-398): the input is x itself (f32) or its bf16 copy.
-    if (elt_bf16_) ANCHA_TRY(cast_rows(x, c.dim, ws_.xn.p, 1, c.dim, R, c.dim, s));
+    // Mask estimators (network.rs:364-398): the input is x itself (f32) or its bf16 / f16 copy.
+    if (elt_ != ELT_F32) ANCHA_TRY(cast_rows(x, c.dim, ws_.xn.p, elt_, c.dim, R, c.dim, s));
     const int hidden_layers = c.mel() ? c.mask_depth : c.mask_depth - 1;
     const int mh = c.dim * c.mask_expansion;
     const GemmGroup* groups = ws_.mask_groups.as<GemmGroup>();
@@ -676,10 +680,10 @@ int Model::forward(const float* spectrum, int chunks, int frames, float* masks,
             const bool glu = l == hidden_layers;
             GemmEpilogue e{};
             e.act = glu ? ANCHA_ACT_GLU : ANCHA_ACT_TANH;
-            e.out_bf16 = glu ? 0 : elt_bf16_;
+            e.out_type = glu ? ELT_F32 : elt_;
             const GemmGroup* gl = groups + ((size_t)st * (hidden_layers + 1) + l) * (size_t)ws_.chunks * bands;
-            ANCHA_TRY(gemm_ffma(GemmGroup{}, gl, G, frames, glu ? 2 * max_width : mh, elt_bf16_,
-                                elt_bf16_, 1, e, s));
+            ANCHA_TRY(gemm_ffma(GemmGroup{}, gl, G, frames, glu ? 2 * max_width : mh, elt_,
+                                elt_, 1, e, s));
         }
         ANCHA_TRY(mask_assemble(ws_.glu.as<float>(), max_width, bands, frames, 2 * bins,
                                 cover_count_.as<int>(), cover_entries_.as<int2>(), max_cover,

@@ -113,7 +113,7 @@ private:
     Model() = default;
     int ensure_workspace(int chunks, int frames, cudaStream_t s);
     int linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias,
-               const float* residual, int64_t ldr, void* out, int64_t ldo, int out_bf16,
+               const float* residual, int64_t ldr, void* out, int64_t ldo, int out_type,
                int64_t m, int n, int k, int act, const float* rope, int rope_tokens,
                int rope_div, cudaStream_t s);
     int transformer(const TransformerWeights& t, bool time_axis, cudaStream_t s);
@@ -128,7 +128,7 @@ private:
     std::vector<std::vector<float>> rope_freqs_;
     Workspace ws_;
     DevBuf flag_;  // non-finite model output (sticky until reset_flag)
-    int elt_bf16_ = 0;  // activations / weights of the GEMMs in bf16
+    int elt_ = ELT_F32;  // operand type of the GEMMs and attention (ELT_*)
     int cur_chunks_ = 0;  // chunks of the forward in progress
 };
 

@@ -116,28 +116,33 @@ __global__ void mask_assemble_kernel(const float* __restrict__ glu, int64_t ldg,
 
 }  // namespace
 
-int norm_rows(float* x, int64_t ldx, const float* scale, void* xn, int xn_bf16, int64_t ldn,
+int norm_rows(float* x, int64_t ldx, const float* scale, void* xn, int xn_type, int64_t ldn,
               int64_t rows, int dim, cudaStream_t s) {
     if (rows == 0) return ANCHA_OK;
     if (dim > 32 * 16) return fail(ANCHA_E_UNSUPPORTED, "norm_rows: dim > 512");
     const int wpb = 8;
     dim3 grid((unsigned)ceil_div(rows, wpb));
-    if (xn_bf16)
+    if (xn_type == ELT_BF16)
         norm_rows_kernel<__nv_bfloat16, 16><<<grid, 32 * wpb, 0, s>>>(
             x, ldx, scale, reinterpret_cast<__nv_bfloat16*>(xn), ldn, rows, dim);
+    else if (xn_type == ELT_F16)
+        norm_rows_kernel<__half, 16><<<grid, 32 * wpb, 0, s>>>(
+            x, ldx, scale, reinterpret_cast<__half*>(xn), ldn, rows, dim);
     else
         norm_rows_kernel<float, 16><<<grid, 32 * wpb, 0, s>>>(
             x, ldx, scale, reinterpret_cast<float*>(xn), ldn, rows, dim);
     return check_launch("norm_rows");
 }
 
-int cast_rows(const float* x, int64_t ldx, void* y, int y_bf16, int64_t ldy, int64_t rows,
+int cast_rows(const float* x, int64_t ldx, void* y, int y_type, int64_t ldy, int64_t rows,
               int dim, cudaStream_t s) {
     const int64_t n = rows * dim;
     if (n == 0) return ANCHA_OK;
     dim3 grid((unsigned)ceil_div(n, 256));
-    if (y_bf16)
+    if (y_type == ELT_BF16)
         cast_rows_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(x, ldx, reinterpret_cast<__nv_bfloat16*>(y), ldy, rows, dim);
+    else if (y_type == ELT_F16)
+        cast_rows_kernel<__half><<<grid, 256, 0, s>>>(x, ldx, reinterpret_cast<__half*>(y), ldy, rows, dim);
     else
         cast_rows_kernel<float><<<grid, 256, 0, s>>>(x, ldx, reinterpret_cast<float*>(y), ldy, rows, dim);
     return check_launch("cast_rows");

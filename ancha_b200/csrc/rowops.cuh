@@ -4,9 +4,9 @@
 
 namespace ancha {
 
-int norm_rows(float* x, int64_t ldx, const float* scale, void* xn, int xn_bf16, int64_t ldn,
+int norm_rows(float* x, int64_t ldx, const float* scale, void* xn, int xn_type, int64_t ldn,
               int64_t rows, int dim, cudaStream_t s);
-int cast_rows(const float* x, int64_t ldx, void* y, int y_bf16, int64_t ldy, int64_t rows,
+int cast_rows(const float* x, int64_t ldx, void* y, int y_type, int64_t ldy, int64_t rows,
               int dim, cudaStream_t s);
 int band_gather(const float* spec, int chunks, int frames, int columns, const int* cols,
                 const int* offsets, int bands, int total, float* z, cudaStream_t s);

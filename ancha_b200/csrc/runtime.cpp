@@ -528,7 +528,8 @@ extern "C" int ancha_separate(const ancha_separate_opts* o, int n_devices, const
         rep.set("backend", Json::of(std::string("cuda")));
         rep.set("device", Json::of(models[0]->device_name));
         rep.set("gpus", Json::of(n_devices));
-        rep.set("precision", Json::of(std::string(o->precision == ANCHA_PRECISION_BF16 ? "bf16" : "f32")));
+        rep.set("precision", Json::of(std::string(o->precision == ANCHA_PRECISION_BF16 ? "bf16"
+                                                   : o->precision == ANCHA_PRECISION_F16 ? "f16" : "f32")));
         rep.set("dsp_backend", Json::of(std::string("cuda")));
         rep.set("model_id", Json::of(m.model_id));
         rep.set("weights_sha256", Json::of(m.weights_sha256));

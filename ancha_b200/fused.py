@@ -37,6 +37,8 @@ def _dtype_code(t) -> int:
         return N.F32
     if t.dtype == torch.bfloat16:
         return N.BF16
+    if t.dtype == torch.float16:
+        return N.F16
     raise N.AnchaError(N.E_INVALID, f"unsupported dtype {t.dtype}")
 
 

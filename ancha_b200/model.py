@@ -25,7 +25,7 @@ class Roformer:
     """A model package resident on one GPU (not re-entrant; one per device and thread)."""
 
     def __init__(self, package: str, device: int = 0, precision: str = "bf16"):
-        self.precision = {"f32": N.PRECISION_F32, "bf16": N.PRECISION_BF16}[precision]
+        self.precision = N.PRECISIONS[precision]
         handle = C.c_void_p()
         N.check(N.lib().ancha_model_load(package.encode(), device, self.precision, C.byref(handle)))
         self._h = handle
@@ -109,7 +109,7 @@ def separate(options: SeparateOptions, cancelled: Optional[C.c_int] = None,
     """Blocking separation task; returns the ``run.json`` report as a dict."""
     o = N.SeparateOpts(options.input.encode(), options.model.encode(), options.output.encode(),
                        options.chunk_samples or 0, options.overlap or 0,
-                       {"f32": N.PRECISION_F32, "bf16": N.PRECISION_BF16}[options.precision],
+                       N.PRECISIONS[options.precision],
                        options.batch_chunks, options.start_seconds,
                        options.duration_seconds or 0.0)
     devs = (C.c_int * len(options.devices))(*options.devices)

@@ -42,11 +42,12 @@ enum {
 };
 
 /* Element types of kernel operands. */
-enum { ANCHA_F32 = 0, ANCHA_BF16 = 1 };
+enum { ANCHA_F32 = 0, ANCHA_BF16 = 1, ANCHA_F16 = 2 };
 
-/* Model arithmetic: F32 = fp32 FFMA kernels throughout; BF16 = bf16 tcgen05 tensor-core
- * GEMMs and attention with fp32 accumulation, fp32 residual stream and DSP. */
-enum { ANCHA_PRECISION_F32 = 0, ANCHA_PRECISION_BF16 = 1 };
+/* Model arithmetic: F32 = fp32 FFMA kernels throughout; BF16 / F16 = bf16 / f16 operands
+ * on the tcgen05 tensor cores (GEMMs and attention) with fp32 accumulation; the residual
+ * stream, norms, softmax statistics and DSP stay fp32 in every mode. */
+enum { ANCHA_PRECISION_F32 = 0, ANCHA_PRECISION_BF16 = 1, ANCHA_PRECISION_F16 = 2 };
 
 /* Message of the last failure on the calling thread ("" if none). */
 ANCHA_API const char* ancha_last_error(void);
@@ -74,7 +75,7 @@ ANCHA_API int ancha_available(int device);
 typedef struct {
     int groups, tokens, heads;
     int head_dim;                 /* must be 64 (ATTENTION_HEAD_DIM, fused/mod.rs:18) */
-    int dtype;                    /* ANCHA_F32 or ANCHA_BF16 for q/k/v/gate and out    */
+    int dtype;                    /* ANCHA_F32 / ANCHA_BF16 / ANCHA_F16: q/k/v/gate, out */
     int64_t ld, out_ld;           /* row strides in elements                           */
     int64_t group_inner, group_inner_stride, group_outer_stride, token_stride; /* rows */
     int q_col, k_col, v_col, gate_col, out_col;
@@ -102,7 +103,7 @@ enum { ANCHA_ACT_NONE = 0, ANCHA_ACT_GELU = 1, ANCHA_ACT_TANH = 2, ANCHA_ACT_GLU
  * roformer.rs:281-302); + residual[m, n]. ANCHA_ACT_GLU pairs columns (2j, 2j+1) as
  * (value, gate) and writes value·sigmoid(gate) to column j (n_out = n / 2).
  * Replaces fused::linear + Epilogue (fused/mod.rs:57-176, kernel fused/gemm.rs:84-311).
- * x, w: `dtype` (F32 → fp32 FFMA kernel; BF16 → tcgen05 kernel, requires ANCHA_W_NK);
+ * x, w: `dtype` (F32 → fp32 FFMA kernel; BF16 / F16 → tcgen05 kernel with ANCHA_W_NK);
  * bias, residual, rope: f32; out: out_dtype. `workspace` may be NULL (none is needed). */
 typedef struct {
     int m, n, k;
