@@ -38,4 +38,22 @@ int gemm_ffma(const GemmGroup& single, const GemmGroup* groups, int count, int m
 // rules (16-byte rows, k % 8 == 0), so the caller can use gemm_ffma instead.
 int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& epi, cudaStream_t stream);
 
+// A batch of same-shape problems for the tcgen05 GEMM: problem g multiplies depth g of
+// A [groups, m, k] by depth g % b_groups of B [b_groups, n, k] (B group j uses only its
+// first group_n[j] rows when group_n is non-null) into depth g of out [groups, m, ldo].
+struct GroupedGemm {
+    const void* a;
+    int64_t lda, a_group_stride;
+    const void* b;
+    int64_t ldb, b_group_stride;
+    int m, n, k, groups, b_groups;
+    const int* group_n;
+    const float* bias;
+    int64_t bias_group_stride;
+    void* out;
+    int64_t ldo, out_group_stride;
+};
+
+int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& epi, cudaStream_t stream);
+
 }  // namespace ancha

@@ -399,6 +399,9 @@ std::unique_ptr<Model> Model::load(const std::string& package, int device, int p
         }
         upload(m->cover_count_, count);
         upload(m->cover_entries_, ent);
+        std::vector<int> glu_n(nb);
+        for (int b = 0; b < nb; ++b) glu_n[b] = 2 * m->width_[b];
+        upload(m->glu_n_, glu_n);
     } catch (...) {
         hasher.join();
         throw;
@@ -681,9 +684,46 @@ int Model::forward(const float* spectrum, int chunks, int frames, float* masks,
             GemmEpilogue e{};
             e.act = glu ? ANCHA_ACT_GLU : ANCHA_ACT_TANH;
             e.out_type = glu ? ELT_F32 : elt_;
-            const GemmGroup* gl = groups + ((size_t)st * (hidden_layers + 1) + l) * (size_t)ws_.chunks * bands;
-            ANCHA_TRY(gemm_ffma(GemmGroup{}, gl, G, frames, glu ? 2 * max_width : mh, elt_,
-                                elt_, 1, e, s));
+            int gst = ANCHA_E_UNSUPPORTED;
+            if (elt_ != ELT_F32) {
+                // One tcgen05 launch over every (chunk, band) problem of this layer.
+                const MaskWeights& mw = masks_[st];
+                const int in = l == 0 ? c.dim : mh;
+                const void* a = l == 0 ? ws_.xn.p : (l % 2 == 1 ? ws_.hidden.p : ws_.h2.p);
+                GroupedGemm q{};
+                q.a = a;
+                q.lda = in;
+                q.a_group_stride = (int64_t)frames * in;
+                q.m = frames;
+                q.k = in;
+                q.groups = G;
+                q.b_groups = bands;
+                if (glu) {
+                    q.b = mw.glu_w.p;
+                    q.n = 2 * max_width;
+                    q.group_n = glu_n_.as<int>();
+                    q.bias = mw.glu_b.as<float>();
+                    q.out = ws_.glu.p;
+                    q.ldo = max_width;
+                } else {
+                    q.b = mw.w[l].p;
+                    q.n = mh;
+                    q.group_n = nullptr;
+                    q.bias = mw.b[l].as<float>();
+                    q.out = l % 2 == 0 ? ws_.hidden.p : ws_.h2.p;
+                    q.ldo = mh;
+                }
+                q.ldb = in;
+                q.b_group_stride = (int64_t)q.n * in;
+                q.bias_group_stride = q.n;
+                q.out_group_stride = (int64_t)frames * q.ldo;
+                gst = gemm_tc_grouped(q, elt_, e, s);
+            }
+            if (gst == ANCHA_E_UNSUPPORTED) {
+                const GemmGroup* gl = groups + ((size_t)st * (hidden_layers + 1) + l) * (size_t)ws_.chunks * bands;
+                gst = gemm_ffma(GemmGroup{}, gl, G, frames, glu ? 2 * max_width : mh, elt_, elt_, 1, e, s);
+            }
+            ANCHA_TRY(gst);
         }
         ANCHA_TRY(mask_assemble(ws_.glu.as<float>(), max_width, bands, frames, 2 * bins,
                                 cover_count_.as<int>(), cover_entries_.as<int2>(), max_cover,

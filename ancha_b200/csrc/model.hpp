@@ -125,6 +125,7 @@ private:
     DevBuf final_scale_;
     std::vector<MaskWeights> masks_;
     DevBuf cover_count_, cover_entries_;
+    DevBuf glu_n_;  // [bands] GLU weight rows used per band (2·width)
     std::vector<std::vector<float>> rope_freqs_;
     Workspace ws_;
     DevBuf flag_;  // non-finite model output (sticky until reset_flag)

@@ -1,0 +1,75 @@
+// Host side of the tensor-core kernels: the per-device error word that bounded waits report
+// into, and TMA tensor-map encoding through the driver entry point (no libcuda link).
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "tc.cuh"
+
+namespace ancha {
+namespace {
+
+__device__ int g_device_error;
+
+std::mutex g_mu;
+int* g_error_ptr[64];
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+}  // namespace
+
+int* device_error_word() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_error_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+        g_error_ptr[dev] = static_cast<int*>(p);
+    }
+    return g_error_ptr[dev];
+}
+
+int take_device_error(cudaStream_t s) {
+    int* w = device_error_word();
+    if (!w) return ANCHA_OK;
+    int v = 0;
+    ANCHA_CUDA(cudaMemcpyAsync(&v, w, sizeof(int), cudaMemcpyDeviceToHost, s));
+    ANCHA_CUDA(cudaStreamSynchronize(s));
+    if (v) {
+        ANCHA_CUDA(cudaMemsetAsync(w, 0, sizeof(int), s));
+        return fail(ANCHA_E_TIMEOUT, "a bounded device-side wait gave up (kernel aborted)");
+    }
+    return ANCHA_OK;
+}
+
+int make_tma_3d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t rows,
+                int64_t depth, int64_t ld, int64_t depth_stride, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return fail(ANCHA_E_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    if (reinterpret_cast<uintptr_t>(base) % 16 || (ld * 2) % 16 || (depth_stride * 2) % 16 ||
+        cols <= 0 || rows <= 0 || depth <= 0)
+        return fail(ANCHA_E_UNSUPPORTED, "TMA operand not 16-byte aligned");
+    const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)depth};
+    const cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(depth_stride * 2)};
+    const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, elt == ELT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                    3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ANCHA_E_UNSUPPORTED, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return ANCHA_OK;
+}
+
+}  // namespace ancha

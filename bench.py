@@ -45,7 +45,7 @@ def parse():
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--precision", default="bf16", choices=["bf16", "f32"])
+    p.add_argument("--precision", default="f16", choices=["f16", "bf16", "f32"])
     p.add_argument("--seconds", type=float, default=30.0)
     p.add_argument("--batch", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -268,7 +268,7 @@ def main():
     hbm, tc_peak, tc_sus, peak_kind = peaks()
     from ancha_b200 import fused
     rows = 60 * 801
-    x = torch.randn(rows, 384, device=f"cuda:{local}").to(torch.bfloat16 if a.precision == "bf16" else torch.float32)
+    x = torch.randn(rows, 384, device=f"cuda:{local}").to({"bf16": torch.bfloat16, "f16": torch.float16, "f32": torch.float32}[a.precision])
     w = (torch.randn(1536, 384, device=f"cuda:{local}") * 0.02).to(x.dtype)
     b = torch.zeros(1536, device=f"cuda:{local}")
     ep = fused.Epilogue(bias=b, gelu=True)

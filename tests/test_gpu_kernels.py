@@ -233,3 +233,62 @@ def test_overlap_add_matches_oracle():
         acc.add(plan, s, y[i])
     assert max_abs(weights.cpu().numpy(), acc.weights) < 1e-5
     assert max_abs(sums.cpu().numpy(), acc.sums) < 1e-4
+
+
+def linear_abi(x, w_nk, act=N.ACT_NONE, bias=None, residual=None, rope=None, rope_width=0,
+               rope_tokens=1, rope_div=1, layout=N.W_NK, out_dtype=None):
+    """Call ancha_linear_fwd directly; w_nk is [n, k] (transposed here for W_KN)."""
+    import ctypes as C
+    m, k = x.shape
+    n = w_nk.shape[0]
+    w = w_nk if layout == N.W_NK else w_nk.t().contiguous()
+    n_out = n // 2 if act == N.ACT_GLU else n
+    out_dtype = out_dtype or (torch.float32 if act == N.ACT_GLU else x.dtype)
+    out = torch.empty((m, n_out), dtype=out_dtype, device="cuda")
+    code = {torch.float32: N.F32, torch.bfloat16: N.BF16, torch.float16: N.F16}
+    d = N.LinearDesc(m, n, k, code[x.dtype], code[out_dtype], layout, x.stride(0), w.stride(0),
+                     out.stride(0), residual.stride(0) if residual is not None else 0, act,
+                     rope_width, rope_tokens, rope_div)
+    p = lambda t: None if t is None else t.data_ptr()
+    N.check(N.lib().ancha_linear_fwd(C.byref(d), x.data_ptr(), w.data_ptr(), p(bias), p(residual),
+                                     p(rope), out.data_ptr(), None))
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("case", ["plain", "gelu", "tanh", "glu", "rope", "residual"])
+@pytest.mark.parametrize("shape", [(300, 1664, 384), (48060 // 30, 1536, 384), (257, 384, 1536)])
+def test_tensor_core_gemm_matches_ffma(dt, case, shape):
+    """The tcgen05 kernel (NK weights) against the FFMA kernel (KN weights) on the same
+    rounded operands: both accumulate in fp32, so they agree to summation order."""
+    m, n, k = shape
+    g = torch.Generator(device="cuda").manual_seed(m + n + k)
+    x = torch.randn(m, k, device="cuda", generator=g).to(dt)
+    w = (torch.randn(n, k, device="cuda", generator=g) * 0.05).to(dt)
+    bias = torch.randn(n, device="cuda", generator=g)
+    kw = dict(bias=bias)
+    if case == "gelu":
+        kw["act"] = N.ACT_GELU
+    elif case == "tanh":
+        kw["act"] = N.ACT_TANH
+    elif case == "glu":
+        kw["act"] = N.ACT_GLU
+    elif case == "residual":
+        kw["residual"] = torch.randn(m, n, device="cuda", generator=g)
+        kw["out_dtype"] = torch.float32
+    elif case == "rope":
+        if n < 1024:
+            pytest.skip("rotary columns need n >= 2·512")
+        tokens = 10 if m % 10 == 0 else 1
+        freqs = (10000.0 ** (-np.arange(32) / 32.0)).astype(np.float32)
+        qc, qs_ = roformer.rope_tables(freqs, tokens, 1.0 / 8.0)
+        kc, ks_ = roformer.rope_tables(freqs, tokens, 1.0)
+        kw["rope"] = dev(np.stack([qc, qs_, kc, ks_]).astype(np.float32))
+        kw.update(rope_width=512, rope_tokens=tokens, rope_div=1)
+    tc = linear_abi(x, w, layout=N.W_NK, **kw).double()
+    ref = linear_abi(x, w, layout=N.W_KN, **kw).double()
+    scale = ref.abs().max().item()
+    err = (tc - ref).abs().max().item()
+    # 16-bit outputs may differ by one rounding step; f32 outputs only by summation order.
+    assert err <= (8e-3 if kw.get("out_dtype") is None and case != "glu" else 1e-4) * max(scale, 1.0), (case, err, scale)
