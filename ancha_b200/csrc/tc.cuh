@@ -28,6 +28,12 @@ int take_device_error(cudaStream_t s);
 int make_tma_3d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t rows,
                 int64_t depth, int64_t ld, int64_t depth_stride, int box_rows);
 
+// Encode a 4-D tiled tensor map over 2-byte elements: dims {cols, d1, d2, d3} with byte
+// strides of d1..d3 given in elements (`s1..s3`), box {64, b1, b2, 1}, 128-byte swizzle,
+// zero fill out of bounds.
+int make_tma_4d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t d1, int64_t d2,
+                int64_t d3, int64_t s1, int64_t s2, int64_t s3, int b1, int b2);
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -88,6 +94,16 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
         " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
+// 4-D tiled TMA load of one box into shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
+                                            int y, int z, int w) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
         : "memory");
 }
 
@@ -165,10 +181,17 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t smem_addr) {
 }
 
 // Instruction descriptor of kind::f16: fp32 accumulator, A / B both f16 (0) or bf16 (1),
-// both K-major, shape M × N.
-__host__ __device__ constexpr uint32_t umma_idesc_f16(int ab_bf16, int m, int n) {
+// A K-major, B K-major (b_mn = 0) or MN-major (b_mn = 1), shape M × N.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int ab_bf16, int m, int n, int b_mn = 0) {
     return (1u << 4) | ((uint32_t)ab_bf16 << 7) | ((uint32_t)ab_bf16 << 10) |
-           ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+           ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+// exp2 on the MUFU pipe (PTX ex2.approx.f32; ex2(-inf) = +0).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
 }
 
 }  // namespace ancha

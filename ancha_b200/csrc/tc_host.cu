@@ -72,4 +72,23 @@ int make_tma_3d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64
     return ANCHA_OK;
 }
 
+int make_tma_4d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t d1, int64_t d2,
+                int64_t d3, int64_t s1, int64_t s2, int64_t s3, int b1, int b2) {
+    auto fn = encode_fn();
+    if (!fn) return fail(ANCHA_E_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    if (reinterpret_cast<uintptr_t>(base) % 16 || (s1 * 2) % 16 || (s2 * 2) % 16 || (s3 * 2) % 16 ||
+        cols <= 0 || d1 <= 0 || d2 <= 0 || d3 <= 0)
+        return fail(ANCHA_E_UNSUPPORTED, "TMA operand not 16-byte aligned");
+    const cuuint64_t dims[4] = {(cuuint64_t)cols, (cuuint64_t)d1, (cuuint64_t)d2, (cuuint64_t)d3};
+    const cuuint64_t strides[3] = {(cuuint64_t)(s1 * 2), (cuuint64_t)(s2 * 2), (cuuint64_t)(s3 * 2)};
+    const cuuint32_t box[4] = {64, (cuuint32_t)b1, (cuuint32_t)b2, 1};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = fn(map, elt == ELT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                    4, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ANCHA_E_UNSUPPORTED, "cuTensorMapEncodeTiled (4-D) failed: " + std::to_string((int)r));
+    return ANCHA_OK;
+}
+
 }  // namespace ancha

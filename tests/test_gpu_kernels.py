@@ -292,3 +292,51 @@ def test_tensor_core_gemm_matches_ffma(dt, case, shape):
     err = (tc - ref).abs().max().item()
     # 16-bit outputs may differ by one rounding step; f32 outputs only by summation order.
     assert err <= (8e-3 if kw.get("out_dtype") is None and case != "glu" else 1e-4) * max(scale, 1.0), (case, err, scale)
+
+
+def attention_abi(buf, desc_kw, separate_kv=False, out_dtype=None):
+    """ancha_attention_fwd on a packed [rows, ld] buffer; separate_kv copies k / v into their
+    own buffers (which routes 16-bit inputs to the FFMA kernel)."""
+    import ctypes as C
+    rows, ld = buf.shape
+    heads = desc_kw["heads"]
+    out = torch.zeros((rows, heads * 64), dtype=buf.dtype, device="cuda")
+    code = {torch.float32: N.F32, torch.bfloat16: N.BF16, torch.float16: N.F16}[buf.dtype]
+    d = N.AttnDesc(desc_kw["groups"], desc_kw["tokens"], heads, 64, code, ld, heads * 64,
+                   desc_kw["group_inner"], desc_kw["inner_stride"], desc_kw["outer_stride"],
+                   desc_kw["token_stride"], 0, heads * 64, 2 * heads * 64,
+                   3 * heads * 64 if desc_kw.get("gated") else -1, 0)
+    k = buf.clone() if separate_kv else buf
+    v = buf.clone() if separate_kv else buf
+    gate = buf if desc_kw.get("gated") else None
+    N.check(N.lib().ancha_attention_fwd(C.byref(d), buf.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                        None if gate is None else gate.data_ptr(), out.data_ptr(), None))
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("dt,min_db", [(torch.float16, 60.0), (torch.bfloat16, 45.0)])
+@pytest.mark.parametrize("axis", ["time", "band", "short"])
+@pytest.mark.parametrize("gated", [False, True])
+def test_tensor_core_attention_matches_ffma(dt, min_db, axis, gated):
+    """The tcgen05 attention against the FFMA attention on the same 16-bit operands, in the
+    model's layouts: time axis (60 bands × 801 frames, tokens contiguous), band axis (801
+    frames × 60 bands, tokens 801 rows apart, two problems per tile) and a short ragged case."""
+    chunks, bands, frames, heads = (1, 60, 801, 8) if axis != "short" else (2, 3, 37, 2)
+    ld = (3 * heads * 64 + heads + 7) // 8 * 8   # 16-byte rows, as the model's packed projection
+    rows = chunks * bands * frames
+    g = torch.Generator(device="cuda").manual_seed(5)
+    buf = (torch.randn(rows, ld, device="cuda", generator=g) * 0.7).to(dt)
+    if axis in ("time", "short"):
+        kw = dict(groups=chunks * bands, tokens=frames, group_inner=chunks * bands, inner_stride=frames,
+                  outer_stride=0, token_stride=1)
+    else:
+        kw = dict(groups=chunks * frames, tokens=bands, group_inner=frames, inner_stride=1,
+                  outer_stride=bands * frames, token_stride=frames)
+    kw.update(heads=heads, gated=gated)
+    tc = attention_abi(buf, kw).double().cpu().numpy()
+    ref = attention_abi(buf, kw, separate_kv=True).double().cpu().numpy()
+    snr = snr_db(ref, tc)
+    print(f"attention tc vs ffma {axis} {dt} gated={gated}: {snr:.1f} dB")
+    assert np.all(np.isfinite(tc)) and np.abs(ref).max() > 0 and snr >= min_db
+    assert snr < 200.0  # the two kernels really differ (P is rounded to 16 bits on the tensor path)
