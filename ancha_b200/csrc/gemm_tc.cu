@@ -1,16 +1,20 @@
 // tcgen05 GEMM with the RoFormer epilogues: out = epilogue(A · Bᵀ) for f16 / bf16 A [rows, K]
 // and B [N, K] (both K-major, PyTorch [out, in] weights), fp32 accumulation in TMEM.
 //
-// One CTA computes a 128 × BN tile: warp 0 lane 0 streams 64-wide K slabs of A and B with TMA
-// (128-byte swizzle) into a STAGES-deep shared-memory ring, warp 1 lane 0 issues
-// tcgen05.mma (M = 128, N = BN, K = 16 per instruction) into a TMEM accumulator and releases
-// each slab with tcgen05.commit, then all four warps drain TMEM (warp w owns rows
-// 32w..32w+31), apply bias / GELU / tanh / GLU / RoPE / residual and store. Two CTAs fit per
-// SM, so one CTA's epilogue overlaps the other's main loop.
+// Persistent and warp-specialised: each CTA (one per SM) walks the 128 × BN output tiles
+// tile = blockIdx.x + i·gridDim.x (columns fastest, so co-resident CTAs share A rows in L2).
+//   warp 0      TMA producer: 64-wide K slabs of A and B (128-byte swizzle) into a
+//               STAGES-deep shared-memory ring;
+//   warp 1      UMMA issuer: tcgen05.mma M 128 × N BN × K 16 into one of two TMEM
+//               accumulators, tcgen05.commit releasing each slab and, per tile, the
+//               accumulator;
+//   warps 2..9  epilogue: warp w drains TMEM lanes 32·(w % 4).. and half of the columns,
+//               applies bias / GELU / tanh / GLU / RoPE / residual and stores.
+// The two accumulators let the epilogue of tile i overlap the main loop of tile i + 1.
 //
-// Groups (grid z) batch independent problems of the same shape — the per-band mask
-// estimator layers: A group g is depth g of a [groups, rows, K] array, B is depth
-// g % b_groups of [b_groups, N_pad, K], and each group may use fewer than N columns.
+// Groups batch same-shape problems (the per-band mask-estimator layers): problem g takes A
+// from depth g of [groups, rows, K] and B from depth g % b_groups of [b_groups, N_pad, K];
+// B group j may use only its first group_n[j] columns (the others are skipped).
 #include "gemm.cuh"
 #include "tc.cuh"
 
@@ -19,6 +23,8 @@ namespace {
 
 constexpr int BM = 128, BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 
 struct TcParams {
     int m, n, k;          // rows per group, columns (max over groups), depth
@@ -34,6 +40,7 @@ struct TcParams {
     const float* rope;
     int rope_width, rope_tokens, rope_div, rope_hd;
     uint32_t idesc;
+    int m_tiles, n_tiles, tiles;
     int* err;
 };
 
@@ -41,59 +48,49 @@ template <int BN, int STAGES>
 struct Smem {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int TILES = STAGES * (A_BYTES + B_BYTES);
-    static constexpr int BYTES = 1024 + TILES + 8 * (2 * STAGES + 1) + 16;
+    static constexpr int BYTES = 1024 + TILES + 8 * (2 * STAGES + 4) + 16;
 };
 
-__device__ __forceinline__ void store_vec(void* out, int out_type, int64_t idx, const float* v, int n,
-                                          bool vec) {
+// Store 32 consecutive values (n valid) of one row; vectorised when all 32 are valid.
+__device__ __forceinline__ void store32(void* out, int out_type, int64_t idx, const float (&v)[32], int n) {
+    const bool full = n == 32;
     if (out_type == ELT_F32) {
         float* o = reinterpret_cast<float*>(out) + idx;
-        if (vec) {
+        if (full) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                if (j < n) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-            }
+            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
         } else {
-            for (int j = 0; j < n; ++j) o[j] = v[j];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < n) o[j] = v[j];
         }
-    } else if (out_type == ELT_BF16) {
-        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out) + idx;
-        if (vec) {
+        return;
+    }
+    uint32_t h[16];
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-                if (j < n) {
-                    uint4 u;
-                    __nv_bfloat162 h[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) h[q] = __floats2bfloat162_rn(v[j + 2 * q], v[j + 2 * q + 1]);
-                    memcpy(&u, h, 16);
-                    *reinterpret_cast<uint4*>(o + j) = u;
-                }
-            }
+    for (int j = 0; j < 16; ++j) {
+        if (out_type == ELT_BF16) {
+            __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+            h[j] = *reinterpret_cast<uint32_t*>(&t);
         } else {
-            for (int j = 0; j < n; ++j) o[j] = __float2bfloat16_rn(v[j]);
+            __half2 t = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+            h[j] = *reinterpret_cast<uint32_t*>(&t);
         }
+    }
+    uint16_t* o = reinterpret_cast<uint16_t*>(out) + idx;
+    if (full) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(o + 8 * q) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
     } else {
-        __half* o = reinterpret_cast<__half*>(out) + idx;
-        if (vec) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-                if (j < n) {
-                    uint4 u;
-                    __half2 h[4];
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) h[q] = __floats2half2_rn(v[j + 2 * q], v[j + 2 * q + 1]);
-                    memcpy(&u, h, 16);
-                    *reinterpret_cast<uint4*>(o + j) = u;
-                }
-            }
-        } else {
-            for (int j = 0; j < n; ++j) o[j] = __float2half_rn(v[j]);
-        }
+        for (int j = 0; j < 32; ++j)
+            if (j < n) o[j] = (uint16_t)(h[j / 2] >> (16 * (j & 1)));
     }
 }
 
-// Epilogue for 32 consecutive accumulator columns c0.. of one row.
+// Epilogue for 32 consecutive accumulator columns c0.. of one row (bias, activation, RoPE,
+// GLU or residual, store). All indexing of the register arrays is static.
 __device__ __forceinline__ void epilogue32(const TcParams& p, int g, int row, int c0, int n_g,
                                            const uint32_t (&r)[32]) {
     float v[32];
@@ -102,9 +99,17 @@ __device__ __forceinline__ void epilogue32(const TcParams& p, int g, int row, in
     const int nv = min(32, n_g - c0);  // valid columns (> 0)
     if (p.bias) {
         const float* b = p.bias + (int64_t)(g % p.b_groups) * p.bias_group_stride + c0;
+        if (nv == 32) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (j < nv) v[j] += b[j];
+            for (int j = 0; j < 32; j += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(b + j);
+                v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nv) v[j] += b[j];
+        }
     }
     if (p.act == ANCHA_ACT_GELU) {
 #pragma unroll
@@ -120,46 +125,71 @@ __device__ __forceinline__ void epilogue32(const TcParams& p, int g, int row, in
         const float* cs = p.rope + ((int64_t)(key * 2) * p.rope_tokens + token) * p.rope_hd + d;
         const float* sn = cs + (int64_t)p.rope_tokens * p.rope_hd;
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-            const float x0 = v[j], x1 = v[j + 1];
-            v[j] = x0 * cs[j] + x1 * sn[j];
-            v[j + 1] = x1 * cs[j + 1] + x0 * sn[j + 1];
+        for (int j = 0; j < 32; j += 4) {
+            const float4 c4 = *reinterpret_cast<const float4*>(cs + j);
+            const float4 s4 = *reinterpret_cast<const float4*>(sn + j);
+            const float x0 = v[j], x1 = v[j + 1], x2 = v[j + 2], x3 = v[j + 3];
+            v[j] = x0 * c4.x + x1 * s4.x;
+            v[j + 1] = x1 * c4.y + x0 * s4.y;
+            v[j + 2] = x2 * c4.z + x3 * s4.z;
+            v[j + 3] = x3 * c4.w + x2 * s4.w;
         }
     }
     const int64_t obase = (int64_t)g * p.out_group_stride;
-    const bool vec_ok = (nv == 32);
     if (p.act == ANCHA_ACT_GLU) {
         float o[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) o[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
+        for (int j = 0; j < 16; ++j) {
+            o[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
+            o[16 + j] = 0.f;
+        }
         const int no = nv / 2;
         const int64_t idx = obase + (int64_t)row * p.ldo + c0 / 2;
-        if (p.out_type == ELT_F32 && vec_ok) {
+        if (p.out_type == ELT_F32 && no == 16) {
             float* op = reinterpret_cast<float*>(p.out) + idx;
 #pragma unroll
             for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(op + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
         } else {
-            for (int j = 0; j < no; ++j) store_elt(p.out, idx + j, o[j], p.out_type);
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (j < no) store_elt(p.out, idx + j, o[j], p.out_type);
         }
         return;
     }
     if (p.residual) {
         const float* rr = p.residual + (int64_t)row * p.ldr + c0;
-        if (vec_ok) {
+        if (nv == 32) {
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
                 const float4 q = *reinterpret_cast<const float4*>(rr + j);
                 v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
             }
         } else {
-            for (int j = 0; j < nv; ++j) v[j] += rr[j];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nv) v[j] += rr[j];
         }
     }
-    store_vec(p.out, p.out_type, obase + (int64_t)row * p.ldo + c0, v, nv, vec_ok);
+    store32(p.out, p.out_type, obase + (int64_t)row * p.ldo + c0, v, nv);
+}
+
+struct TileCoord {
+    int g, m0, n0, n_g;
+};
+
+__device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int t, int bn) {
+    TileCoord c;
+    const int per_group = p.m_tiles * p.n_tiles;
+    c.g = t / per_group;
+    const int r = t % per_group;
+    c.m0 = (r / p.n_tiles) * BM;
+    c.n0 = (r % p.n_tiles) * bn;
+    c.n_g = p.group_n ? p.group_n[c.g % p.b_groups] : p.n;
+    return c;
 }
 
 template <int BN, int STAGES>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                const TcParams p) {
     using S = Smem<BN, STAGES>;
@@ -169,31 +199,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     uint8_t* b_tiles = smem + STAGES * A_BYTES;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILES);
     uint64_t* empty = full + STAGES;
-    uint64_t* done = empty + STAGES;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    uint64_t* tfull = empty + STAGES;   // [2] accumulator ready
+    uint64_t* tempty = tfull + 2;       // [2] accumulator drained
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
 
-    const int g = blockIdx.z;
-    const int bg = g % p.b_groups;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM;
-    const int n_g = p.group_n ? p.group_n[bg] : p.n;
-    if (n0 >= n_g) return;  // uniform across the CTA, before any barrier or TMEM use
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
-        mbar_init(done, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], EPI_WARPS);
+        }
         *abort = 0;
         fence_barrier_init();
         fence_proxy_async();
         prefetch_tma(&tma_a);
         prefetch_tma(&tma_b);
     }
-    if (warp == 0) {
-        tmem_alloc(tmem_slot, BN);
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -202,83 +231,142 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     const uint32_t tmem = *tmem_slot;
     const int kblocks = (p.k + BK - 1) / BK;
 
-    if (warp == 0 && lane == 0) {
-        // TMA producer.
-        int issued = 0;
-        for (int kb = 0; kb < kblocks; ++kb) {
-            const int s = kb % STAGES;
-            const uint32_t round = kb / STAGES;
-            if (!mbar_wait(&empty[s], (round & 1) ^ 1, abort, p.err)) break;
-            mbar_arrive_expect_tx(&full[s], A_BYTES + S::B_BYTES);
-            tma_load_3d(a_tiles + s * A_BYTES, &tma_a, &full[s], kb * BK, m0, g);
-            tma_load_3d(b_tiles + s * S::B_BYTES, &tma_b, &full[s], kb * BK, n0, bg);
-            ++issued;
-        }
-        if (*abort) {
-            // Let the copies already in flight land before the CTA exits (bounded).
-            const long long t0 = clock64();
-            for (int kb = max(0, issued - STAGES); kb < issued; ++kb)
-                while (!mbar_try_wait(&full[kb % STAGES], (kb / STAGES) & 1) && clock64() - t0 < kWaitCycles) {
+    if (warp == 0) {
+        if (lane == 0) {
+            // TMA producer.
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < p.tiles && !*abort; t += gridDim.x) {
+                const TileCoord c = tile_coord(p, t, BN);
+                if (c.n0 >= c.n_g) continue;
+                const int bg = c.g % p.b_groups;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort, p.err)) break;
+                    mbar_arrive_expect_tx(&full[s], A_BYTES + S::B_BYTES);
+                    tma_load_3d(a_tiles + s * A_BYTES, &tma_a, &full[s], kb * BK, c.m0, c.g);
+                    tma_load_3d(b_tiles + s * S::B_BYTES, &tma_b, &full[s], kb * BK, c.n0, bg);
                 }
+            }
+            if (*abort) {  // let copies in flight land before the CTA exits (bounded)
+                const long long c0 = clock64();
+                for (uint32_t j = it > (uint32_t)STAGES ? it - STAGES : 0; j < it; ++j)
+                    while (!mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1) && clock64() - c0 < kWaitCycles) {
+                    }
+            }
         }
-    } else if (warp == 1 && lane == 0) {
-        // UMMA issuer.
-        for (int kb = 0; kb < kblocks; ++kb) {
-            const int s = kb % STAGES;
-            if (!mbar_wait(&full[s], (kb / STAGES) & 1, abort, p.err)) break;
-            tc_fence_after();
-            const uint32_t a_addr = smem_u32(a_tiles + s * A_BYTES);
-            const uint32_t b_addr = smem_u32(b_tiles + s * S::B_BYTES);
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // UMMA issuer.
+            uint32_t it = 0, local = 0;
+            for (int t = blockIdx.x; t < p.tiles && !*abort; t += gridDim.x) {
+                const TileCoord c = tile_coord(p, t, BN);
+                if (c.n0 >= c.n_g) continue;
+                const int b = local & 1;
+                if (!mbar_wait(&tempty[b], ((local >> 1) & 1) ^ 1, abort, p.err)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + b * BN;
+                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                    const int s = it % STAGES;
+                    if (!mbar_wait(&full[s], (it / STAGES) & 1, abort, p.err)) break;
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(a_tiles + s * A_BYTES);
+                    const uint32_t b_addr = smem_u32(b_tiles + s * S::B_BYTES);
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk)
-                umma_f16(tmem, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), p.idesc,
-                         (kb | kk) != 0);
-            umma_commit(&empty[s]);
+                    for (int kk = 0; kk < BK / 16; ++kk)
+                        umma_f16(acc, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), p.idesc,
+                                 (kb | kk) != 0);
+                    umma_commit(&empty[s]);
+                }
+                umma_commit(&tfull[b]);
+                ++local;
+            }
         }
-        umma_commit(done);
-    }
-    __syncwarp();
-    // Epilogue: all four warps.
-    const bool ok = __all_sync(0xffffffffu, mbar_wait(done, 0, abort, p.err));
-    tc_fence_after();
-    if (ok) {
-        const int row = m0 + warp * 32 + lane;
-        const bool live = row < p.m;
+    } else {
+        // Epilogue warps: lane quarter (warp % 4), column half (warp - 2) / 4.
+        const int quarter = warp % 4;
+        const int half = (warp - 2) / 4;
+        uint32_t local = 0;
+        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
+            const TileCoord c = tile_coord(p, t, BN);
+            if (c.n0 >= c.n_g) continue;
+            const int b = local & 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (local >> 1) & 1, abort, p.err));
+            if (!ok) break;
+            tc_fence_after();
+            const int row = c.m0 + quarter * 32 + lane;
+            const bool live = row < p.m;
+            const uint32_t base = tmem + b * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 32) {
-            uint32_t r[32];
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c, r);
-            tmem_wait_ld();
-            if (live && n0 + c < n_g) epilogue32(p, g, row, n0 + c, n_g, r);
+            for (int col = half * (BN / 2); col < (half + 1) * (BN / 2); col += 32) {
+                uint32_t r[32];
+                tmem_ld32(base + col, r);
+                tmem_wait_ld();
+                if (live && c.n0 + col < c.n_g) epilogue32(p, c.g, row, c.n0 + col, c.n_g, r);
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+            ++local;
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, BN);
+    if (warp == 1) {
+        __syncwarp();
+        tmem_dealloc(tmem, TMEM_COLS);
+    }
 }
 
 template <int BN, int STAGES>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, cudaStream_t s) {
     using S = Smem<BN, STAGES>;
     static bool configured[64] = {};
+    static int sms[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev & 63]) {
         ANCHA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES));
+        ANCHA_CUDA(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
         configured[dev & 63] = true;
     }
-    dim3 grid((unsigned)ceil_div(p.n, BN), (unsigned)ceil_div(p.m, BM), (unsigned)p.groups);
-    gemm_tc_kernel<BN, STAGES><<<grid, 128, S::BYTES, s>>>(ta, tb, p);
+    const int grid = std::max(1, std::min(p.tiles, sms[dev & 63]));
+    gemm_tc_kernel<BN, STAGES><<<grid, THREADS, S::BYTES, s>>>(ta, tb, p);
     return check_launch("gemm_tc");
 }
 
-int run(const CUtensorMap& ta, const CUtensorMap& tb, TcParams p, int ab_type, cudaStream_t s) {
-    constexpr int BN = 128, STAGES = 3;
-    p.idesc = umma_idesc_f16(ab_type == ELT_BF16, BM, BN);
+// Output tile width: the widest of 256 / 192 / 128 that wastes least of the padded N.
+int pick_bn(int n) {
+    int best = 128;
+    int64_t best_pad = ceil_div(n, 128) * 128;
+    for (int bn : {192, 256}) {
+        const int64_t pad = ceil_div(n, bn) * bn;
+        if (pad <= best_pad) {
+            best = bn;
+            best_pad = pad;
+        }
+    }
+    return best;
+}
+
+int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64_t ldb,
+        int64_t b_group_stride, TcParams p, int ab_type, cudaStream_t s) {
+    const int bn = p.group_n ? 128 : pick_bn(p.n);
+    CUtensorMap ta, tb;
+    ANCHA_TRY(make_tma_3d(&ta, a, ab_type, p.k, p.m, p.groups, lda, a_group_stride, BM));
+    ANCHA_TRY(make_tma_3d(&tb, b, ab_type, p.k, p.n, p.b_groups, ldb, b_group_stride, bn));
+    p.idesc = umma_idesc_f16(ab_type == ELT_BF16, BM, bn);
     p.err = device_error_word();
-    if (p.groups > 65535 || ceil_div(p.m, BM) > 65535) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: grid too large");
-    return launch<BN, STAGES>(ta, tb, p, s);
+    p.m_tiles = (int)ceil_div(p.m, BM);
+    p.n_tiles = (int)ceil_div(p.n, bn);
+    const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles * p.groups;
+    if (tiles > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: too many tiles");
+    p.tiles = (int)tiles;
+    switch (bn) {
+        case 256: return launch<256, 4>(ta, tb, p, s);
+        case 192: return launch<192, 4>(ta, tb, p, s);
+        default: return launch<128, 6>(ta, tb, p, s);
+    }
 }
 
 bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
@@ -290,11 +378,8 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     if (g.m <= 0 || g.n <= 0 || g.k <= 0) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: empty problem");
     const size_t oe = elt_size(e.out_type);
     if (!aligned16(g.out) || (g.ldo * oe) % 16 || (g.residual && (!aligned16(g.residual) || (g.ldr * 4) % 16)) ||
-        (e.rope && (!aligned16(e.rope) || e.rope_hd % 32)))
+        (g.bias && !aligned16(g.bias)) || (e.rope && (!aligned16(e.rope) || e.rope_hd % 32)))
         return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: epilogue operands not 16-byte aligned");
-    CUtensorMap ta, tb;
-    ANCHA_TRY(make_tma_3d(&ta, g.a, ab_type, g.k, g.m, 1, g.lda, (int64_t)g.m * g.lda, BM));
-    ANCHA_TRY(make_tma_3d(&tb, g.b, ab_type, g.k, g.n, 1, g.ldb, (int64_t)g.n * g.ldb, 128));
     TcParams p{};
     p.m = g.m; p.n = g.n; p.k = g.k; p.groups = 1; p.b_groups = 1; p.group_n = nullptr;
     p.out = g.out; p.ldo = g.ldo; p.out_group_stride = 0;
@@ -303,18 +388,15 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     p.act = e.act; p.out_type = e.out_type;
     p.rope = e.rope; p.rope_width = e.rope_width; p.rope_tokens = e.rope_tokens;
     p.rope_div = e.rope_div; p.rope_hd = e.rope_hd;
-    return run(ta, tb, p, ab_type, s);
+    return run(g.a, g.lda, (int64_t)g.m * g.lda, g.b, g.ldb, (int64_t)g.n * g.ldb, p, ab_type, s);
 }
 
 int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& e, cudaStream_t s) {
     if (ab_type != ELT_BF16 && ab_type != ELT_F16) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: operand type");
     const size_t oe = elt_size(e.out_type);
-    const int64_t ldo_out = q.ldo;
-    if (!aligned16(q.out) || (ldo_out * oe) % 16 || (q.out_group_stride * oe) % 16)
+    if (!aligned16(q.out) || (q.ldo * oe) % 16 || (q.out_group_stride * oe) % 16 ||
+        (q.bias && (!aligned16(q.bias) || (q.bias_group_stride * 4) % 16)))
         return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: output not 16-byte aligned");
-    CUtensorMap ta, tb;
-    ANCHA_TRY(make_tma_3d(&ta, q.a, ab_type, q.k, q.m, q.groups, q.lda, q.a_group_stride, BM));
-    ANCHA_TRY(make_tma_3d(&tb, q.b, ab_type, q.k, q.n, q.b_groups, q.ldb, q.b_group_stride, 128));
     TcParams p{};
     p.m = q.m; p.n = q.n; p.k = q.k; p.groups = q.groups; p.b_groups = q.b_groups;
     p.group_n = q.group_n;
@@ -323,7 +405,7 @@ int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& e, cu
     p.residual = nullptr; p.ldr = 0;
     p.act = e.act; p.out_type = e.out_type;
     p.rope = nullptr; p.rope_width = 0; p.rope_tokens = 1; p.rope_div = 1; p.rope_hd = 64;
-    return run(ta, tb, p, ab_type, s);
+    return run(q.a, q.lda, q.a_group_stride, q.b, q.ldb, q.b_group_stride, p, ab_type, s);
 }
 
 }  // namespace ancha
