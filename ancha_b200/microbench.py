@@ -38,7 +38,6 @@ def gemm_cases(rows=60 * 801):
 
 
 def run_gemm(dtype, reps):
-    import numpy as np
     import torch
     from . import _native as N
     from .fused import Epilogue, linear
@@ -51,13 +50,14 @@ def run_gemm(dtype, reps):
             ep.gelu = True
         elif kind == "residual":
             ep = Epilogue(residual=torch.randn(m, n, device="cuda"))
+        if kind == "tanh":
+            fn = _abi_linear(x, w, N.ACT_TANH)
         elif kind == "rope":
-            freqs = (10000.0 ** (-np.arange(32) / 32.0))
+            # n = 1544 is not a multiple of 128, where fused.linear returns the reference's None;
+            # the model calls the ABI directly with the rotary table.
             tab = torch.zeros(4, 801, 64, device="cuda")
             tab[0] = tab[2] = 1.0
-            ep.rotary = (tab, 512)
-        if kind == "tanh":
-            fn = _tanh_linear(x, w)
+            fn = _abi_linear(x, w, N.ACT_NONE, rope=tab)
         else:
             fn = (lambda x=x, w=w, ep=ep: linear(x, w, ep, weight_layout=N.W_NK))
         ms = _time(fn, reps)
@@ -66,7 +66,8 @@ def run_gemm(dtype, reps):
     return out
 
 
-def _tanh_linear(x, w):
+def _abi_linear(x, w, act, rope=None):
+    """ancha_linear_fwd with NK weights and a bias (and the RoPE epilogue when given)."""
     import ctypes as C
 
     import torch
@@ -76,9 +77,11 @@ def _tanh_linear(x, w):
     y = torch.empty(m, n, dtype=x.dtype, device="cuda")
     b = torch.zeros(n, device="cuda")
     code = N.BF16 if x.dtype == torch.bfloat16 else N.F16
-    d = N.LinearDesc(m, n, k, code, code, N.W_NK, k, k, n, 0, N.ACT_TANH, 0, 1, 1)
+    tokens = rope.shape[1] if rope is not None else 1
+    d = N.LinearDesc(m, n, k, code, code, N.W_NK, k, k, n, 0, act, 512 if rope is not None else 0, tokens, 1)
+    rp = None if rope is None else rope.data_ptr()
     return lambda: N.check(N.lib().ancha_linear_fwd(C.byref(d), x.data_ptr(), w.data_ptr(), b.data_ptr(),
-                                                    None, None, y.data_ptr(), None))
+                                                    None, rp, y.data_ptr(), None))
 
 
 def run_attention(dtype, reps):
