@@ -282,6 +282,260 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     }
 }
 
+// Time-axis kernel (tokens > 64): two 128-row query tiles of the same (group, head) per CTA
+// share every K / V block. Warps 0–3 and 4–7 are the softmax warpgroups of tile 0 and 1
+// (two warps per SM sub-partition), warp 8 issues TMA, warp 9 issues UMMA. Per tile S, O
+// (TMEM) and P (shared memory) are single-buffered; the two tiles alternate on the tensor
+// cores, so one warpgroup's softmax overlaps the other's S = Q·Kᵀ and P·V. Interior key
+// blocks skip masking; only the last, partial block masks keys ≥ tokens.
+constexpr int PP_OFF_Q = 0, PP_OFF_K = 2 * QKV_BYTES, PP_OFF_V = 4 * QKV_BYTES, PP_OFF_P = 6 * QKV_BYTES;
+constexpr int PP_OFF_BAR = PP_OFF_P + 2 * P_BYTES;
+constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + 16 * 8 + 16;
+constexpr int PP_THREADS = 320;
+
+template <bool BF16>
+__global__ void __launch_bounds__(PP_THREADS, 1)
+attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PP_OFF_BAR);
+    uint64_t* q_full = bars;
+    uint64_t* kv_full = bars + 1;   // [2] stages
+    uint64_t* kv_empty = bars + 3;  // [2] stages
+    uint64_t* s_full = bars + 5;    // [2] tiles
+    uint64_t* p_ready = bars + 7;   // [2] tiles
+    uint64_t* o_full = bars + 9;    // [2] tiles
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int pairs = (p.tiles_per_group + 1) / 2;
+    const int pair = blockIdx.x % pairs;
+    const int gi = blockIdx.x / pairs;
+    const int go = blockIdx.z, head = blockIdx.y;
+    const int nkb = p.tiles_per_group;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int q0 = 2 * pair * TILE;                 // first query token of tile 0
+    const bool active1 = q0 + TILE < p.tokens;      // tile 1 holds at least one query
+
+    if (threadIdx.x == 256) {
+        mbar_init(q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+            mbar_init(&s_full[s], 1);
+            mbar_init(&p_ready[s], 128);
+            mbar_init(&o_full[s], 1);
+        }
+        *abort = 0;
+        fence_barrier_init();
+        fence_proxy_async();
+        prefetch_tma(&tmap);
+    }
+    if (warp == 9) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    // TMEM columns: tile t uses S at t·256 + [0, 128) and O at t·256 + [128, 192).
+
+    if (warp == 8) {
+        if (lane == 0) {
+            mbar_arrive_expect_tx(q_full, 2 * QKV_BYTES);
+            tma_load_4d(smem + PP_OFF_Q, &tmap, q_full, p.q_col + head * HD, q0, gi, go);
+            tma_load_4d(smem + PP_OFF_Q + QKV_BYTES, &tmap, q_full, p.q_col + head * HD, q0 + TILE, gi, go);
+            int issued = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int s = kb & 1;
+                if (!mbar_wait(&kv_empty[s], ((kb >> 1) & 1) ^ 1, abort, p.err)) break;
+                mbar_arrive_expect_tx(&kv_full[s], 2 * QKV_BYTES);
+                tma_load_4d(smem + PP_OFF_K + s * QKV_BYTES, &tmap, &kv_full[s], p.k_col + head * HD, kb * TILE, gi, go);
+                tma_load_4d(smem + PP_OFF_V + s * QKV_BYTES, &tmap, &kv_full[s], p.v_col + head * HD, kb * TILE, gi, go);
+                ++issued;
+            }
+            if (*abort) {  // let copies in flight land before the CTA exits (bounded)
+                const long long c0 = clock64();
+                while (!mbar_try_wait(q_full, 0) && clock64() - c0 < kWaitCycles) {
+                }
+                for (int kb = max(0, issued - 2); kb < issued; ++kb)
+                    while (!mbar_try_wait(&kv_full[kb & 1], (kb >> 1) & 1) && clock64() - c0 < kWaitCycles) {
+                    }
+            }
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            const int ntiles = active1 ? 2 : 1;
+            auto issue_pv = [&](int t, int j) -> bool {
+                if (!mbar_wait(&p_ready[t], j & 1, abort, p.err)) return false;
+                tc_fence_after();
+                const uint32_t p_addr = smem_u32(smem + PP_OFF_P + t * P_BYTES);
+                const uint32_t v_addr = smem_u32(smem + PP_OFF_V + (j & 1) * QKV_BYTES);
+#pragma unroll
+                for (int kk = 0; kk < TILE / 16; ++kk)
+                    umma_f16(tmem + t * 256 + 128,
+                             umma_desc_sw128(p_addr + (kk >> 2) * (TILE * 128) + (kk & 3) * 32),
+                             umma_desc_sw128(v_addr + kk * 16 * 128), p.idesc_o, kk != 0);
+                umma_commit(&o_full[t]);
+                return true;
+            };
+            bool ok = mbar_wait(q_full, 0, abort, p.err);
+            for (int kb = 0; ok && kb < nkb; ++kb) {
+                const int s = kb & 1;
+                if (!mbar_wait(&kv_full[s], (kb >> 1) & 1, abort, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t k_addr = smem_u32(smem + PP_OFF_K + s * QKV_BYTES);
+                for (int t = 0; t < ntiles && ok; ++t) {
+                    if (kb >= 1 && !issue_pv(t, kb - 1)) { ok = false; break; }
+                    const uint32_t q_addr = smem_u32(smem + PP_OFF_Q + t * QKV_BYTES);
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk)
+                        umma_f16(tmem + t * 256, umma_desc_sw128(q_addr + kk * 32),
+                                 umma_desc_sw128(k_addr + kk * 32), p.idesc_s, kk != 0);
+                    umma_commit(&s_full[t]);
+                }
+                if (ok && kb >= 1) umma_commit(&kv_empty[(kb - 1) & 1]);
+            }
+            for (int t = 0; ok && t < ntiles; ++t) ok = issue_pv(t, nkb - 1);
+            if (ok) umma_commit(&kv_empty[(nkb - 1) & 1]);
+        }
+    } else {
+        const int t = warp / 4;  // tile of this softmax warpgroup
+        const int row = threadIdx.x % 128;
+        const int tok = q0 + t * TILE + row;
+        const bool valid = tok < p.tokens;
+        const uint32_t lane_base = tmem + t * 256 + ((uint32_t)((warp % 4) * 32) << 16);
+        if (t == 0 || active1) {
+            float o[HD];
+#pragma unroll
+            for (int d = 0; d < HD; ++d) o[d] = 0.f;
+            float m_run = -INFINITY, l = 0.f, m_acc = -INFINITY, m_prev = 0.f;
+            bool ok = true;
+            uint8_t* pbuf = smem + PP_OFF_P + t * P_BYTES;
+            auto fold = [&](int j) -> bool {
+                if (!__all_sync(0xffffffffu, mbar_wait(&o_full[t], j & 1, abort, p.err))) return false;
+                tc_fence_after();
+                const float sc = m_acc == -INFINITY ? 0.f : ex2_approx(m_acc - m_prev);
+#pragma unroll
+                for (int c = 0; c < HD; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(lane_base + 128 + c, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int d = 0; d < 32; ++d) o[c + d] = o[c + d] * sc + __uint_as_float(r[d]);
+                }
+                m_acc = m_prev;
+                return true;
+            };
+            for (int kb = 0; kb < nkb; ++kb) {
+                ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], kb & 1, abort, p.err));
+                if (!ok) break;
+                tc_fence_after();
+                const int nvalid = min(TILE, p.tokens - kb * TILE);  // valid keys in this block
+                float mx = -INFINITY;
+                if (nvalid == TILE) {
+#pragma unroll
+                    for (int c = 0; c < TILE; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld32(lane_base + c, r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[j]));
+                    }
+                } else {
+#pragma unroll
+                    for (int c = 0; c < TILE; c += 32) {
+                        uint32_t r[32];
+                        tmem_ld32(lane_base + c, r);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (c + j < nvalid) mx = fmaxf(mx, __uint_as_float(r[j]));
+                    }
+                }
+                const float m_new = fmaxf(m_run, mx * LOG2E);
+                const float m_use = m_new == -INFINITY ? 0.f : m_new;
+                if (kb >= 1) {
+                    ok = fold(kb - 1);
+                    if (!ok) break;
+                }
+                float rowsum = 0.f;
+#pragma unroll
+                for (int c = 0; c < TILE; c += 32) {
+                    uint32_t r[32];
+                    tmem_ld32(lane_base + c, r);
+                    tmem_wait_ld();
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        float e0 = ex2_approx(fmaf(__uint_as_float(r[j]), LOG2E, -m_use));
+                        float e1 = ex2_approx(fmaf(__uint_as_float(r[j + 1]), LOG2E, -m_use));
+                        if (nvalid < TILE) {
+                            if (c + j >= nvalid) e0 = 0.f;
+                            if (c + j + 1 >= nvalid) e1 = 0.f;
+                        }
+                        rowsum += e0 + e1;
+                        pk[j / 2] = pack2<BF16>(e0, e1);
+                    }
+                    uint8_t* half_base = pbuf + (c / 64) * (TILE * 128) + row * 128;
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const int chunk = ((c % 64) / 8 + q) ^ (row & 7);
+                        *reinterpret_cast<uint4*>(half_base + chunk * 16) =
+                            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                    }
+                }
+                l = (m_run == -INFINITY ? 0.f : l * ex2_approx(m_run - m_use)) + rowsum;
+                m_run = m_new == -INFINITY ? -INFINITY : m_use;
+                m_prev = m_use;
+                fence_proxy_async();
+                tc_fence_before();
+                mbar_arrive(&p_ready[t]);
+            }
+            if (ok) ok = fold(nkb - 1);
+            if (ok && valid) {
+                const int64_t orow = (int64_t)go * p.group_outer_stride + (int64_t)gi * p.group_inner_stride +
+                                     (int64_t)tok * p.token_stride;
+                float scale = 1.f / l;
+                if (p.gate_col >= 0) {
+                    const float gl = BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[orow * p.ld + p.gate_col + head])
+                                          : __half2float(reinterpret_cast<const __half*>(p.q)[orow * p.ld + p.gate_col + head]);
+                    scale /= 1.f + __expf(-gl);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) +
+                                                      (orow * p.out_ld + p.out_col + head * HD) * 2);
+#pragma unroll
+                for (int q = 0; q < HD / 8; ++q)
+                    dst[q] = make_uint4(pack2<BF16>(o[8 * q] * scale, o[8 * q + 1] * scale),
+                                        pack2<BF16>(o[8 * q + 2] * scale, o[8 * q + 3] * scale),
+                                        pack2<BF16>(o[8 * q + 4] * scale, o[8 * q + 5] * scale),
+                                        pack2<BF16>(o[8 * q + 6] * scale, o[8 * q + 7] * scale));
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 9) {
+        __syncwarp();
+        tmem_dealloc(tmem, 512);
+    }
+}
+
+template <bool BF16>
+int launch_pp(const CUtensorMap& map, const AttnTcParams& p, dim3 grid, cudaStream_t s) {
+    static bool configured[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!configured[dev & 63]) {
+        ANCHA_CUDA(cudaFuncSetAttribute(attention_pp_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        PP_SMEM_BYTES));
+        configured[dev & 63] = true;
+    }
+    attention_pp_kernel<BF16><<<grid, PP_THREADS, PP_SMEM_BYTES, s>>>(map, p);
+    return check_launch("attention_pp");
+}
+
 template <int BT, bool BF16>
 int launch(const CUtensorMap& map, const AttnTcParams& p, dim3 grid, cudaStream_t s) {
     static bool configured[64] = {};
@@ -338,13 +592,19 @@ int attention_tc(const AttnArgs& a, cudaStream_t stream) {
     CUtensorMap map;
     ANCHA_TRY(make_tma_4d(&map, a.q, a.elt, a.ld, a.tokens, a.group_inner, p.group_outer,
                           s1 > 0 ? s1 : a.ld, s2 > 0 ? s2 : a.ld, s3 > 0 ? s3 : a.ld, BT, BG));
+    if (BT == 128) {
+        // Time axis: two query tiles of one (group, head) per CTA.
+        const int64_t gx = (int64_t)((p.tiles_per_group + 1) / 2) * a.group_inner;
+        if (gx > 0x7fffffff || a.heads > 65535 || p.group_outer > 65535)
+            return fail(ANCHA_E_UNSUPPORTED, "attention_tc: grid too large");
+        dim3 grid((unsigned)gx, (unsigned)a.heads, (unsigned)p.group_outer);
+        return a.elt == ELT_BF16 ? launch_pp<true>(map, p, grid, stream) : launch_pp<false>(map, p, grid, stream);
+    }
     const int64_t gx = (int64_t)p.tiles_per_group * ceil_div(a.group_inner, BG);
     if (gx > 0x7fffffff || a.heads > 65535 || p.group_outer > 65535)
         return fail(ANCHA_E_UNSUPPORTED, "attention_tc: grid too large");
     dim3 grid((unsigned)gx, (unsigned)a.heads, (unsigned)p.group_outer);
-    if (a.elt == ELT_BF16)
-        return BT == 64 ? launch<64, true>(map, p, grid, stream) : launch<128, true>(map, p, grid, stream);
-    return BT == 64 ? launch<64, false>(map, p, grid, stream) : launch<128, false>(map, p, grid, stream);
+    return a.elt == ELT_BF16 ? launch<64, true>(map, p, grid, stream) : launch<64, false>(map, p, grid, stream);
 }
 
 }  // namespace ancha
