@@ -9,7 +9,9 @@
 //               accumulators, tcgen05.commit releasing each slab and, per tile, the
 //               accumulator;
 //   warps 2..9  epilogue: warp w drains TMEM lanes 32·(w % 4).. and half of the columns,
-//               applies bias / GELU / tanh / GLU / RoPE / residual and stores.
+//               applies bias / GELU / tanh / GLU / RoPE / residual, stages each 32 × 32
+//               chunk in swizzled shared memory and writes it with a TMA tensor store
+//               (coalesced, asynchronous, clipped at the matrix edges by the hardware).
 // The two accumulators let the epilogue of tile i overlap the main loop of tile i + 1.
 //
 // Groups batch same-shape problems (the per-band mask-estimator layers): problem g takes A
@@ -44,56 +46,21 @@ struct TcParams {
     int* err;
 };
 
+constexpr int STAGE_BYTES = 4096;  // one 32-row × 128-byte epilogue staging buffer
+
 template <int BN, int STAGES>
 struct Smem {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int TILES = STAGES * (A_BYTES + B_BYTES);
-    static constexpr int BYTES = 1024 + TILES + 8 * (2 * STAGES + 4) + 16;
+    static constexpr int STAGING = EPI_WARPS * 2 * STAGE_BYTES;
+    static constexpr int BYTES = 1024 + TILES + STAGING + 8 * (2 * STAGES + 4) + 16;
 };
 
-// Store 32 consecutive values (n valid) of one row; vectorised when all 32 are valid.
-__device__ __forceinline__ void store32(void* out, int out_type, int64_t idx, const float (&v)[32], int n) {
-    const bool full = n == 32;
-    if (out_type == ELT_F32) {
-        float* o = reinterpret_cast<float*>(out) + idx;
-        if (full) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(o + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (j < n) o[j] = v[j];
-        }
-        return;
-    }
-    uint32_t h[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-        if (out_type == ELT_BF16) {
-            __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
-            h[j] = *reinterpret_cast<uint32_t*>(&t);
-        } else {
-            __half2 t = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
-            h[j] = *reinterpret_cast<uint32_t*>(&t);
-        }
-    }
-    uint16_t* o = reinterpret_cast<uint16_t*>(out) + idx;
-    if (full) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            *reinterpret_cast<uint4*>(o + 8 * q) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-    } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-            if (j < n) o[j] = (uint16_t)(h[j / 2] >> (16 * (j & 1)));
-    }
-}
-
-// Epilogue for 32 consecutive accumulator columns c0.. of one row (bias, activation, RoPE,
-// GLU or residual, store). All indexing of the register arrays is static.
-__device__ __forceinline__ void epilogue32(const TcParams& p, int g, int row, int c0, int n_g,
-                                           const uint32_t (&r)[32]) {
-    float v[32];
+// Bias, activation, RoPE and residual for 32 consecutive accumulator columns c0.. of one
+// row, in registers. Returns the number of output values (32, or 16 for GLU). All indexing
+// of the register arrays is static.
+__device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, bool live, int c0, int n_g,
+                                          const uint32_t (&r)[32], float (&v)[32]) {
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
     const int nv = min(32, n_g - c0);  // valid columns (> 0)
@@ -135,28 +102,12 @@ __device__ __forceinline__ void epilogue32(const TcParams& p, int g, int row, in
             v[j + 3] = x3 * c4.w + x2 * s4.w;
         }
     }
-    const int64_t obase = (int64_t)g * p.out_group_stride;
     if (p.act == ANCHA_ACT_GLU) {
-        float o[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-            o[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
-            o[16 + j] = 0.f;
-        }
-        const int no = nv / 2;
-        const int64_t idx = obase + (int64_t)row * p.ldo + c0 / 2;
-        if (p.out_type == ELT_F32 && no == 16) {
-            float* op = reinterpret_cast<float*>(p.out) + idx;
-#pragma unroll
-            for (int j = 0; j < 16; j += 4) *reinterpret_cast<float4*>(op + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
-        } else {
-#pragma unroll
-            for (int j = 0; j < 16; ++j)
-                if (j < no) store_elt(p.out, idx + j, o[j], p.out_type);
-        }
-        return;
+        for (int j = 0; j < 16; ++j) v[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
+        return 16;
     }
-    if (p.residual) {
+    if (p.residual && live) {
         const float* rr = p.residual + (int64_t)row * p.ldr + c0;
         if (nv == 32) {
 #pragma unroll
@@ -170,7 +121,51 @@ __device__ __forceinline__ void epilogue32(const TcParams& p, int g, int row, in
                 if (j < nv) v[j] += rr[j];
         }
     }
-    store32(p.out, p.out_type, obase + (int64_t)row * p.ldo + c0, v, nv);
+    return 32;
+}
+
+// Write this lane's row of a 32-row staging buffer in the TMA swizzled layout: rows of
+// 128 bytes (f32 × 32) use the 128-byte swizzle, rows of 64 bytes (16-bit × 32, or f32 × 16
+// for GLU) the 64-byte swizzle.
+__device__ __forceinline__ void stage_row(uint8_t* buf, int lane, int out_type, int count, const float (&v)[32]) {
+    if (out_type == ELT_F32 && count == 32) {
+        uint8_t* row = buf + lane * 128;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(row + ((q ^ (lane & 7)) * 16)) =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        return;
+    }
+    uint8_t* row = buf + lane * 64;
+    if (out_type == ELT_F32) {  // 16 f32 (GLU)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<float4*>(row + ((q ^ ((lane >> 1) & 3)) * 16)) =
+                make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+        return;
+    }
+    uint32_t h[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+        if (out_type == ELT_BF16) {
+            __nv_bfloat162 t = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+            h[j] = *reinterpret_cast<uint32_t*>(&t);
+        } else {
+            __half2 t = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+            h[j] = *reinterpret_cast<uint32_t*>(&t);
+        }
+    }
+    if (count == 32) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            *reinterpret_cast<uint4*>(row + ((q ^ ((lane >> 1) & 3)) * 16)) =
+                make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+    } else {  // 16 values of 16 bits (GLU with a 16-bit output): 32-byte rows are not staged
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+            *reinterpret_cast<uint4*>(row + ((q ^ ((lane >> 1) & 3)) * 16)) =
+                make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+    }
 }
 
 struct TileCoord {
@@ -191,13 +186,14 @@ __device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int t, int bn
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-               const TcParams p) {
+               const __grid_constant__ CUtensorMap tma_out, const TcParams p) {
     using S = Smem<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_tiles = smem;
     uint8_t* b_tiles = smem + STAGES * A_BYTES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILES);
+    uint8_t* staging = smem + S::TILES;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILES + S::STAGING);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;   // [2] accumulator ready
     uint64_t* tempty = tfull + 2;       // [2] accumulator drained
@@ -220,6 +216,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         fence_proxy_async();
         prefetch_tma(&tma_a);
         prefetch_tma(&tma_b);
+        prefetch_tma(&tma_out);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, TMEM_COLS);
@@ -285,7 +282,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         // Epilogue warps: lane quarter (warp % 4), column half (warp - 2) / 4.
         const int quarter = warp % 4;
         const int half = (warp - 2) / 4;
-        uint32_t local = 0;
+        uint8_t* my_stage = staging + (warp - 2) * 2 * STAGE_BYTES;
+        const bool glu = p.act == ANCHA_ACT_GLU;
+        uint32_t local = 0, chunks = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
             const TileCoord c = tile_coord(p, t, BN);
             if (c.n0 >= c.n_g) continue;
@@ -293,7 +292,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (local >> 1) & 1, abort, p.err));
             if (!ok) break;
             tc_fence_after();
-            const int row = c.m0 + quarter * 32 + lane;
+            const int row0 = c.m0 + quarter * 32;
+            const int row = row0 + lane;
             const bool live = row < p.m;
             const uint32_t base = tmem + b * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
@@ -301,13 +301,30 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 uint32_t r[32];
                 tmem_ld32(base + col, r);
                 tmem_wait_ld();
-                if (live && c.n0 + col < c.n_g) epilogue32(p, c.g, row, c.n0 + col, c.n_g, r);
+                if (c.n0 + col >= c.n_g) continue;  // warp-uniform
+                float v[32];
+                const int count = epilogue32(p, c.g, row, live, c.n0 + col, c.n_g, r, v);
+                uint8_t* buf = my_stage + (chunks & 1) * STAGE_BYTES;
+                if (chunks >= 2) {
+                    if (lane == 0) bulk_wait_read<1>();
+                    __syncwarp();
+                }
+                stage_row(buf, lane, p.out_type, count, v);
+                fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_3d(&tma_out, buf, glu ? (c.n0 + col) / 2 : c.n0 + col, row0, c.g);
+                    bulk_commit();
+                }
+                ++chunks;
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&tempty[b]);
             ++local;
         }
+        if (lane == 0) bulk_wait<0>();
+        __syncwarp();
     }
     tc_fence_before();
     __syncthreads();
@@ -318,7 +335,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
 }
 
 template <int BN, int STAGES>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, cudaStream_t s) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const TcParams& p, cudaStream_t s) {
     using S = Smem<BN, STAGES>;
     static bool configured[64] = {};
     static int sms[64] = {};
@@ -331,7 +348,7 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const TcParams& p, cuda
         configured[dev & 63] = true;
     }
     const int grid = std::max(1, std::min(p.tiles, sms[dev & 63]));
-    gemm_tc_kernel<BN, STAGES><<<grid, THREADS, S::BYTES, s>>>(ta, tb, p);
+    gemm_tc_kernel<BN, STAGES><<<grid, THREADS, S::BYTES, s>>>(ta, tb, to, p);
     return check_launch("gemm_tc");
 }
 
@@ -352,9 +369,15 @@ int pick_bn(int n) {
 int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64_t ldb,
         int64_t b_group_stride, TcParams p, int ab_type, cudaStream_t s) {
     const int bn = p.group_n ? 128 : pick_bn(p.n);
-    CUtensorMap ta, tb;
+    CUtensorMap ta, tb, to;
     ANCHA_TRY(make_tma_3d(&ta, a, ab_type, p.k, p.m, p.groups, lda, a_group_stride, BM));
     ANCHA_TRY(make_tma_3d(&tb, b, ab_type, p.k, p.n, p.b_groups, ldb, b_group_stride, bn));
+    const bool glu = p.act == ANCHA_ACT_GLU;
+    if (glu && p.out_type != ELT_F32) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: GLU output must be f32");
+    const int64_t out_cols = glu ? p.n / 2 : p.n;
+    const int64_t ogs = p.groups > 1 ? p.out_group_stride : (int64_t)p.m * p.ldo;
+    ANCHA_TRY(make_tma_store_3d(&to, p.out, p.out_type, std::min<int64_t>(out_cols, p.ldo), p.m, p.groups, p.ldo,
+                                ogs, glu ? 16 : 32, 32));
     p.idesc = umma_idesc_f16(ab_type == ELT_BF16, BM, bn);
     p.err = device_error_word();
     p.m_tiles = (int)ceil_div(p.m, BM);
@@ -363,9 +386,9 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
     if (tiles > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: too many tiles");
     p.tiles = (int)tiles;
     switch (bn) {
-        case 256: return launch<256, 4>(ta, tb, p, s);
-        case 192: return launch<192, 4>(ta, tb, p, s);
-        default: return launch<128, 6>(ta, tb, p, s);
+        case 256: return launch<256, 3>(ta, tb, to, p, s);
+        case 192: return launch<192, 3>(ta, tb, to, p, s);
+        default: return launch<128, 4>(ta, tb, to, p, s);
     }
 }
 

@@ -34,6 +34,12 @@ int make_tma_3d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64
 int make_tma_4d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t d1, int64_t d2,
                 int64_t d3, int64_t s1, int64_t s2, int64_t s3, int b1, int b2);
 
+// Encode a 3-D tiled tensor map for TMA stores from a row-major [depth][rows][cols] array of
+// `elt` (ELT_F32 / ELT_BF16 / ELT_F16) with box {box_cols, box_rows, 1}; `swizzle_bytes`
+// (64 or 128) must equal the box row size in bytes.
+int make_tma_store_3d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t rows,
+                      int64_t depth, int64_t ld, int64_t depth_stride, int box_cols, int box_rows);
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -105,6 +111,25 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
         " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w)
         : "memory");
+}
+
+// TMA store of one box from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+    asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups still read their shared-memory source.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+// Wait until at most N committed bulk groups are still in flight.
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+    asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tma(const CUtensorMap* map) {
@@ -192,6 +217,45 @@ __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+// 1/x on the MUFU pipe (PTX rcp.approx.ftz.f32).
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+// Activations of the tensor-core epilogues (f16 / bf16 outputs), built from the MUFU ex2 and
+// rcp instructions plus a few FMAs instead of the libm-accurate erff / tanhf, whose
+// instruction count made the GEMM epilogues issue-bound.
+//
+// erf: Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26 (Hastings'
+// approximation): erf(x) = 1 − (a1·t + a2·t² + a3·t³ + a4·t⁴ + a5·t⁵)·e^(−x²),
+// t = 1 / (1 + p·x) for x ≥ 0, |error| ≤ 1.5e-7; odd symmetry for x < 0.
+__device__ __forceinline__ float erf_as(float x) {
+    const float ax = fabsf(x);
+    const float t = rcp_approx(fmaf(0.3275911f, ax, 1.0f));
+    float poly = fmaf(1.061405429f, t, -1.453152027f);
+    poly = fmaf(poly, t, 1.421413741f);
+    poly = fmaf(poly, t, -0.284496736f);
+    poly = fmaf(poly, t, 0.254829592f);
+    poly *= t;
+    const float e = ex2_approx(-1.4426950408889634f * ax * ax);  // e^(−x²)
+    return copysignf(fmaf(-poly, e, 1.0f), x);
+}
+// GELU(x) = x·Φ(x) = ½·x·(1 + erf(x/√2)).
+__device__ __forceinline__ float gelu_fast(float x) {
+    return 0.5f * x * (1.0f + erf_as(x * 0.70710678118654752f));
+}
+// tanh(x) = sign(x)·(1 − 2 / (e^(2|x|) + 1)); absolute error ~1e-7.
+__device__ __forceinline__ float tanh_fast(float x) {
+    const float e = ex2_approx(2.0f * 1.4426950408889634f * fabsf(x));
+    return copysignf(fmaf(-2.0f, rcp_approx(e + 1.0f), 1.0f), x);
+}
+// σ(x) = 1 / (1 + e^(−x)).
+__device__ __forceinline__ float sigmoid_fast(float x) {
+    return rcp_approx(1.0f + ex2_approx(-1.4426950408889634f * x));
 }
 
 }  // namespace ancha

@@ -72,6 +72,29 @@ int make_tma_3d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64
     return ANCHA_OK;
 }
 
+int make_tma_store_3d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t rows,
+                      int64_t depth, int64_t ld, int64_t depth_stride, int box_cols, int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return fail(ANCHA_E_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    const int es = (int)elt_size(elt);
+    const int row_bytes = box_cols * es;
+    if (reinterpret_cast<uintptr_t>(base) % 16 || (ld * es) % 16 || (depth_stride * es) % 16 || cols <= 0 ||
+        rows <= 0 || depth <= 0 || (row_bytes != 64 && row_bytes != 128))
+        return fail(ANCHA_E_UNSUPPORTED, "TMA store operand not 16-byte aligned");
+    const cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)depth};
+    const cuuint64_t strides[2] = {(cuuint64_t)(ld * es), (cuuint64_t)(depth_stride * es)};
+    const cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapDataType dt = elt == ELT_F32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : elt == ELT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    CUresult r = fn(map, dt, 3, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    row_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                    CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(ANCHA_E_UNSUPPORTED, "cuTensorMapEncodeTiled (store) failed: " + std::to_string((int)r));
+    return ANCHA_OK;
+}
+
 int make_tma_4d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t d1, int64_t d2,
                 int64_t d3, int64_t s1, int64_t s2, int64_t s3, int b1, int b2) {
     auto fn = encode_fn();
