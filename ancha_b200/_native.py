@@ -25,7 +25,7 @@ STATUS_NAMES = {OK: "ok", E_UNSUPPORTED: "unsupported", E_INVALID: "invalid", E_
 
 # Every symbol the header declares (checked by the CPU test suite).
 EXPORTS = ("ancha_last_error", "ancha_version", "ancha_available", "ancha_attention_fwd",
-           "ancha_linear_fwd", "ancha_stft_fwd", "ancha_istft_masked", "ancha_ola_add",
+           "ancha_linear_fwd", "ancha_stft_fwd", "ancha_istft_masked", "ancha_istft_masked_static", "ancha_ola_add",
            "ancha_model_load", "ancha_model_info", "ancha_model_forward", "ancha_model_free",
            "ancha_separate", "ancha_separate_pcm", "ancha_separate_device",
            "ancha_separate_status", "ancha_free_string")
@@ -89,6 +89,7 @@ def lib() -> C.CDLL:
             "ancha_linear_fwd": (i32, [C.POINTER(LinearDesc), vp, vp, vp, vp, vp, vp, vp]),
             "ancha_stft_fwd": (i32, [vp, i32, i32, i32, vp, vp]),
             "ancha_istft_masked": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp]),
+            "ancha_istft_masked_static": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp]),
             "ancha_ola_add": (i32, [vp, i32, i32, i32, i32, C.POINTER(i64), i64, vp, vp, vp]),
             "ancha_model_load": (i32, [C.c_char_p, i32, i32, C.POINTER(vp)]),
             "ancha_model_info": (i32, [vp] + [C.POINTER(i32)] * 7),

@@ -159,6 +159,17 @@ int ancha_istft_masked(const float* packed, const float* masks, int chunks, int 
     return istft_masked(packed, masks, chunks, stems, samples, hop, zero_dc, scratch, out, flag, s);
 }
 
+int ancha_istft_masked_static(const float* packed, const float* masks, int chunks, int stems,
+                              int samples, int hop, int zero_dc, float* out, int* status,
+                              void* stream) {
+    if (!packed || !masks || !out || chunks < 0 || stems < 0 || hop <= 0)
+        return fail(ANCHA_E_INVALID, "istft_static: invalid arguments");
+    if (reinterpret_cast<uintptr_t>(packed) % 16 || reinterpret_cast<uintptr_t>(status) % 4)
+        return fail(ANCHA_E_INVALID, "istft_static: packed must be 16-byte and status 4-byte aligned");
+    return istft_masked_static(packed, masks, chunks, stems, samples, hop, zero_dc, out, status,
+                               as_stream(stream));
+}
+
 int ancha_ola_add(const float* y, int chunks, int planes, int chunk, int overlap,
                   const int64_t* starts, int64_t length, float* sums, float* weights, void* stream) {
     if (!y || !starts || !sums || !weights || chunks < 0 || planes <= 0 || chunk <= 0 || overlap <= 0)

@@ -322,4 +322,82 @@ int ola_finish(const float* sums, const float* weights, int planes, int64_t leng
     return check_launch("ola_finish");
 }
 
+// ---- Masked iSTFT with library-owned scratch (ancha_istft_masked_static) -------------------
+//
+// The frame scratch lives in a fixed device array of this module instead of caller memory, so
+// the call allocates nothing. Its contents need not start at zero: every element the overlap
+// kernel reads was written by the frames kernel earlier in the same batch. The status word is
+// zeroed by the call itself. The buffer is shared by every call on a device, so calls that may
+// overlap in time (different streams, or different host threads without ordering) race on it.
+namespace {
+
+__device__ __align__(256) float g_static_scratch[kStaticIstftScratchFloats];
+__device__ __align__(256) int g_static_status;
+
+struct StaticScratch {
+    float* frames = nullptr;
+    int* status = nullptr;
+    int rc = ANCHA_OK;
+};
+std::once_flag g_static_once[64];
+StaticScratch g_static[64];
+
+// Resolves the device addresses of the static scratch for the current device, once per device.
+int static_scratch(StaticScratch** out) {
+    int dev = 0;
+    ANCHA_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(ANCHA_E_INVALID, "device index out of range");
+    std::call_once(g_static_once[dev], [dev] {
+        StaticScratch& st = g_static[dev];
+        cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.frames), g_static_scratch);
+        if (e == cudaSuccess)
+            e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.status), g_static_status);
+        st.rc = e == cudaSuccess ? ANCHA_OK : cuda_fail(e, "istft_static: scratch symbol lookup");
+    });
+    if (g_static[dev].rc != ANCHA_OK)
+        return fail(g_static[dev].rc, "istft_static: scratch set-up failed on this device");
+    *out = &g_static[dev];
+    return ANCHA_OK;
+}
+
+}  // namespace
+
+int istft_masked_static(const float* packed, const float* masks, int chunks, int stems,
+                        int samples, int hop, int zero_dc, float* out, int* status,
+                        cudaStream_t s) {
+    if (hop <= 0 || hop > NH || samples <= NH)
+        return fail(ANCHA_E_INVALID, "istft_static: require hop in 1..=1024 and samples > 1024");
+    StaticScratch* st = nullptr;
+    ANCHA_TRY(static_scratch(&st));
+    ANCHA_TRY(dsp_prepare(s));
+    const int frames = samples / hop + 1;
+    // One (chunk, stem) pair needs both channels' windowed frames.
+    const int64_t per_pair = 2LL * frames * NFFT;
+    if (per_pair > kStaticIstftScratchFloats)
+        return fail(ANCHA_E_INVALID,
+                    "istft_static: one chunk-stem needs " + std::to_string(per_pair) +
+                        " scratch floats (frames = " + std::to_string(frames) + ") but the static "
+                        "scratch holds " + std::to_string(kStaticIstftScratchFloats) +
+                        " (at most " + std::to_string(kStaticIstftScratchFloats / (2 * NFFT)) +
+                        " frames); use ancha_istft_masked with caller scratch");
+    ANCHA_CUDA(cudaMemsetAsync(st->status, 0, sizeof(int), s));
+    if (chunks > 0 && stems > 0) {
+        const int per_batch = (int)std::min<int64_t>(stems, kStaticIstftScratchFloats / per_pair);
+        const int64_t spec = (int64_t)frames * BINS * 4;       // packed floats per chunk
+        const int64_t mask = (int64_t)2 * BINS * 2 * frames;  // mask floats per (chunk, stem)
+        // Batches run in stream order on the same scratch; within a batch the frames kernel
+        // fills it and the overlap kernel consumes it.
+        for (int c = 0; c < chunks; ++c)
+            for (int s0 = 0; s0 < stems; s0 += per_batch) {
+                const int n = std::min(per_batch, stems - s0);
+                const int64_t q = (int64_t)c * stems + s0;
+                ANCHA_TRY(istft_masked(packed + c * spec, masks + q * mask, 1, n, samples, hop,
+                                       zero_dc, st->frames, out + q * 2 * samples, st->status, s));
+            }
+    }
+    if (status)
+        ANCHA_CUDA(cudaMemcpyAsync(status, st->status, sizeof(int), cudaMemcpyDeviceToDevice, s));
+    return ANCHA_OK;
+}
+
 }  // namespace ancha

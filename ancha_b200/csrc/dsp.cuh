@@ -21,6 +21,12 @@ int gather_chunks(const float* planes, int64_t samples, const ChunkStarts& start
 int ola_add(const float* y, int chunks, int planes, int chunk, const ChunkStarts& starts,
             int64_t length, int64_t base, int64_t span, float* sums, float* weights,
             cudaStream_t s);
+// Static scratch of ancha_istft_masked_static: 6 Mi floats (24 MiB) per device, enough for one
+// chunk-stem of up to 1536 frames.
+constexpr int64_t kStaticIstftScratchFloats = 6LL << 20;
+int istft_masked_static(const float* packed, const float* masks, int chunks, int stems,
+                        int samples, int hop, int zero_dc, float* out, int* status,
+                        cudaStream_t s);
 int ola_finish(const float* sums, const float* weights, int planes, int64_t length,
                int64_t border, int64_t samples, const float* input, float* stems,
                float* residual, int* flag, cudaStream_t s);

@@ -138,6 +138,27 @@ ANCHA_API int ancha_istft_masked(const float* packed, const float* masks, int ch
                        int samples, int hop, int zero_dc, float* scratch, float* out,
                        void* stream);
 
+/* ancha_istft_masked without caller scratch, for callers that cannot allocate device memory:
+ * a host whose allocator owns the whole device (a caching pool or fixed arenas that hand
+ * out no extra buffers), or a real-time audio thread that must not block on cudaMalloc,
+ * which can synchronise the device. No counterpart in the reference (its iSTFT runs on the
+ * host, dsp.rs:82-133); same arguments and results as ancha_istft_masked.
+ *
+ * The frames go through a fixed 24 MiB device array inside the library (6 Mi floats per
+ * device), processed one chunk and as many stems as fit at a time; the call allocates
+ * nothing. Limit: one chunk-stem needs 2·frames·2048 floats, so frames = samples / hop + 1
+ * must be at most 1536; larger calls fail with ANCHA_E_INVALID and a message naming the
+ * sizes. `status` is an optional DEVICE pointer to one int: the call sets it to 0, or to a
+ * non-zero value if a sample had no window support; no other memory needs to start at zero.
+ * The first call on each device (with that device current) looks up the scratch address and
+ * builds the DSP tables, synchronising the stream once: make it before any stream capture.
+ * The scratch is shared by all calls on a device, so calls that can overlap in time (other
+ * streams, or host threads without ordering between them) race; serialise them on one
+ * stream. */
+ANCHA_API int ancha_istft_masked_static(const float* packed, const float* masks, int chunks,
+                       int stems, int samples, int hop, int zero_dc, float* out, int* status,
+                       void* stream);
+
 /* Linear-fade overlap-add of `chunks` chunk outputs y[c][planes][chunk] starting at
  * starts[c] (host array, ascending) into sums[planes][length] and weights[length], in
  * chunk order (chunk.rs:26-75). */
