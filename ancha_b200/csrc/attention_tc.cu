@@ -1,21 +1,18 @@
 // Single-pass attention on the tcgen05 tensor cores for head width 64, f16 / bf16 operands:
 // softmax(q·kᵀ)·v per (group, head), q pre-scaled, optionally gated by sigmoid(gate).
 //
-// One CTA owns a 128-row query tile. Q, K and V tiles are TMA-loaded from the packed q|k|v|gate
-// projection through one 4-D tensor map {columns, tokens, inner groups, outer groups}, so
-// the time axis (tokens contiguous) and the band axis (tokens T rows apart) share the code
-// and nothing is transposed. A tile holds BG = 128 / BT problems of BT token rows: BT = 128
-// for the time axis (T = 801 → 7 query tiles × 7 key blocks), BT = 64 for the band axis
-// (two 60-token problems per tile, one key block, cross-problem scores masked).
+// Q, K and V tiles are TMA-loaded from the packed q|k|v|gate projection through one 4-D
+// tensor map {columns, tokens, inner groups, outer groups}, so the time axis (tokens
+// contiguous) and the band axis (tokens T rows apart) run on the model's one layout and
+// nothing is transposed. Each tile is 128 query rows; S = Q·Kᵀ (M 128, N 128) accumulates in
+// TMEM, the softmax warps (one query row per thread) read it with tcgen05.ld, take base-2
+// exponentials on the MUFU pipe (log2 e folded into the row maximum), write P in f16 / bf16
+// to shared memory in the UMMA K-major 128-byte-swizzled layout, and O = P·V (V as an
+// MN-major operand) accumulates in TMEM.
 //
-// Warp roles (192 threads): warps 0–3 run the softmax, one query row per thread; warp 4
-// issues TMA; warp 5 issues UMMA. Per key block kb: S(kb) = Q·K(kb)ᵀ into TMEM (M 128, N 128);
-// the softmax warps read S twice (row max, then exponentials on the MUFU ex2 pipe), write
-// P(kb) in f16 / bf16 into shared memory in the UMMA K-major 128-byte-swizzled layout, and the
-// UMMA warp computes O(kb) = P(kb)·V(kb) into TMEM (V as an MN-major operand). S, P and O are
-// double-buffered, so S(kb+1) and P(kb−1)·V run on the tensor cores while the softmax works on
-// block kb; O(kb) is folded into a per-thread fp32 accumulator two blocks later with the
-// online-softmax rescale. Scores use base 2 (log2 e folded into the running maximum).
+// Two kernels: attention_pp_kernel for tokens > 64 (the time axis, online softmax over key
+// blocks, two query tiles per CTA) and attention_band_kernel for tokens ≤ 64 (the band axis,
+// two problems per tile, persistent and pipelined across tiles).
 #include "attention.cuh"
 #include "tc.cuh"
 
@@ -26,10 +23,6 @@ constexpr int TILE = 128;           // query rows / keys per block
 constexpr int HD = 64;              // head width
 constexpr int QKV_BYTES = TILE * HD * 2;
 constexpr int P_BYTES = TILE * TILE * 2;
-constexpr int OFF_Q = 0, OFF_K = QKV_BYTES, OFF_V = 3 * QKV_BYTES, OFF_P = 5 * QKV_BYTES;
-constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-constexpr int SMEM_BYTES = 1024 + OFF_BAR + 16 * 8 + 16;
-constexpr uint32_t S_COL = 0, O_COL = 256;  // TMEM columns: S[2] at 0 / 128, O[2] at 256 / 320
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct AttnTcParams {
@@ -53,44 +46,69 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     }
 }
 
-template <int BT, bool BF16>
-__global__ void __launch_bounds__(192, 1)
-attention_tc_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams p) {
-    constexpr int BG = TILE / BT;
+// Band-axis kernel (tokens ≤ 64). A persistent CTA walks tiles of two problems: inner groups
+// gi0 and gi0 + 1 of one outer group and head, 128 query rows against one 128-key block
+// whose cross-problem scores are ignored. Tiles stream through a 4-deep ring of Q | K | V
+// stages so that the loads of later tiles are in flight while earlier ones compute: at 60
+// tokens a tile moves 64 KB for 4 MFLOP and the axis is bound by HBM, not the tensor cores.
+// Warps 0–3 and 4–7 are two softmax warpgroups that take alternate tiles (TMEM slot = tile
+// parity: S at slot·128, O at 256 + slot·64); warp 8 issues TMA, warp 9 UMMA. A stage's Q | K
+// bytes are reused for P once S = Q·Kᵀ has completed, and its V bytes for the output rows
+// once P·V has completed; the output leaves through a TMA store that clips the padding rows
+// (tokens ≥ `tokens`, a second group past the end).
+constexpr int BD_STAGES = 4;
+constexpr int BD_STAGE_BYTES = 3 * QKV_BYTES;
+constexpr int BD_OFF_BAR = BD_STAGES * BD_STAGE_BYTES;
+constexpr int BD_SMEM_BYTES = 1024 + BD_OFF_BAR + 20 * 8 + 16;
+constexpr int BD_THREADS = 320;
+
+template <bool BF16>
+__global__ void __launch_bounds__(BD_THREADS, 1)
+attention_band_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_constant__ CUtensorMap omap,
+                      const AttnTcParams p, const int pairs, const int heads, const int total) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-    uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;   // [2]
-    uint64_t* kv_empty = bars + 3;  // [2]
-    uint64_t* s_full = bars + 5;    // [2]
-    uint64_t* p_ready = bars + 7;   // [2]
-    uint64_t* o_full = bars + 9;    // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BD_OFF_BAR);
+    uint64_t* full = bars;          // [stage] Q | K | V landed
+    uint64_t* empty = bars + 4;     // [stage] output stored, stage reusable
+    uint64_t* s_full = bars + 8;    // [slot] S = Q·Kᵀ done
+    uint64_t* p_ready = bars + 10;  // [slot] P written (128 arrivals)
+    uint64_t* o_full = bars + 12;   // [slot] O = P·V done
+    uint64_t* o_empty = bars + 14;  // [slot] O read (128 arrivals)
+    uint64_t* staged = bars + 16;   // [slot] output rows written (128 arrivals)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
-    const int tile = blockIdx.x % p.tiles_per_group;
-    const int gi0 = (blockIdx.x / p.tiles_per_group) * BG;
-    const int go = blockIdx.z, head = blockIdx.y;
-    const int t0 = tile * BT;
-    const int nkb = p.tiles_per_group;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int my_tiles = (int)blockIdx.x < total ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    // Tile → (outer group, group pair, head); the head varies fastest, so CTAs running at the
+    // same time read neighbouring column slices of the same rows.
+    auto decode = [&](int i, int& go, int& gi0, int& head) {
+        const int tile = (int)blockIdx.x + i * (int)gridDim.x;
+        head = tile % heads;
+        const int r = tile / heads;
+        gi0 = 2 * (r % pairs);
+        go = r / pairs;
+    };
 
-    if (threadIdx.x == 128) {
-        mbar_init(q_full, 1);
+    if (threadIdx.x == 256) {
+        for (int s = 0; s < BD_STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
             mbar_init(&s_full[s], 1);
             mbar_init(&p_ready[s], 128);
             mbar_init(&o_full[s], 1);
+            mbar_init(&o_empty[s], 128);
+            mbar_init(&staged[s], 128);
         }
         *abort = 0;
         fence_barrier_init();
         fence_proxy_async();
         prefetch_tma(&tmap);
+        prefetch_tma(&omap);
     }
-    if (warp == 4) {
+    if (warp == 9) {
         tmem_alloc(tmem_slot, 512);
         tmem_relinquish();
     }
@@ -99,184 +117,160 @@ attention_tc_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == 8) {
         if (lane == 0) {
-            // TMA producer: Q once, then K / V blocks through a 2-deep ring.
-            mbar_arrive_expect_tx(q_full, QKV_BYTES);
-            tma_load_4d(smem + OFF_Q, &tmap, q_full, p.q_col + head * HD, t0, gi0, go);
             int issued = 0;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb & 1;
-                if (!mbar_wait(&kv_empty[s], ((kb >> 1) & 1) ^ 1, abort, p.err)) break;
-                mbar_arrive_expect_tx(&kv_full[s], 2 * QKV_BYTES);
-                tma_load_4d(smem + OFF_K + s * QKV_BYTES, &tmap, &kv_full[s], p.k_col + head * HD, kb * BT, gi0, go);
-                tma_load_4d(smem + OFF_V + s * QKV_BYTES, &tmap, &kv_full[s], p.v_col + head * HD, kb * BT, gi0, go);
+            for (int i = 0; i < my_tiles; ++i) {
+                const int st = i % BD_STAGES;
+                if (!mbar_wait(&empty[st], ((i / BD_STAGES) & 1) ^ 1, abort, p.err)) break;
+                int go, gi0, head;
+                decode(i, go, gi0, head);
+                uint8_t* base = smem + st * BD_STAGE_BYTES;
+                mbar_arrive_expect_tx(&full[st], 3 * QKV_BYTES);
+                tma_load_4d(base, &tmap, &full[st], p.q_col + head * HD, 0, gi0, go);
+                tma_load_4d(base + QKV_BYTES, &tmap, &full[st], p.k_col + head * HD, 0, gi0, go);
+                tma_load_4d(base + 2 * QKV_BYTES, &tmap, &full[st], p.v_col + head * HD, 0, gi0, go);
                 ++issued;
             }
             if (*abort) {  // let copies in flight land before the CTA exits (bounded)
                 const long long c0 = clock64();
-                while (!mbar_try_wait(q_full, 0) && clock64() - c0 < kWaitCycles) {
-                }
-                for (int kb = max(0, issued - 2); kb < issued; ++kb)
-                    while (!mbar_try_wait(&kv_full[kb & 1], (kb >> 1) & 1) && clock64() - c0 < kWaitCycles) {
+                for (int i = max(0, issued - BD_STAGES); i < issued; ++i)
+                    while (!mbar_try_wait(&full[i % BD_STAGES], (i / BD_STAGES) & 1) &&
+                           clock64() - c0 < kWaitCycles) {
                     }
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == 9) {
         if (lane == 0) {
-            // UMMA issuer.
-            const uint32_t q_addr = smem_u32(smem + OFF_Q);
             auto issue_pv = [&](int j) -> bool {
-                const int s = j & 1;
-                if (!mbar_wait(&p_ready[s], (j >> 1) & 1, abort, p.err)) return false;
+                const int slot = j & 1;
+                if (!mbar_wait(&p_ready[slot], (j >> 1) & 1, abort, p.err)) return false;
+                if (j >= 2 && !mbar_wait(&o_empty[slot], ((j - 2) >> 1) & 1, abort, p.err)) return false;
                 tc_fence_after();
-                const uint32_t p_addr = smem_u32(smem + OFF_P + s * P_BYTES);
-                const uint32_t v_addr = smem_u32(smem + OFF_V + s * QKV_BYTES);
+                const uint32_t p_addr = smem_u32(smem + (j % BD_STAGES) * BD_STAGE_BYTES);
+                const uint32_t v_addr = p_addr + 2 * QKV_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < TILE / 16; ++kk)
-                    umma_f16(tmem + O_COL + s * HD,
+                    umma_f16(tmem + 256 + slot * HD,
                              umma_desc_sw128(p_addr + (kk >> 2) * (TILE * 128) + (kk & 3) * 32),
                              umma_desc_sw128(v_addr + kk * 16 * 128), p.idesc_o, kk != 0);
-                umma_commit(&o_full[s]);
-                umma_commit(&kv_empty[s]);
+                umma_commit(&o_full[slot]);
                 return true;
             };
-            bool ok = mbar_wait(q_full, 0, abort, p.err);
-            for (int kb = 0; ok && kb < nkb; ++kb) {
-                const int s = kb & 1;
-                if (!mbar_wait(&kv_full[s], (kb >> 1) & 1, abort, p.err)) break;
-                if (kb >= 2 && !mbar_wait(&p_ready[s], ((kb - 2) >> 1) & 1, abort, p.err)) break;
+            bool ok = true;
+            for (int i = 0; i < my_tiles; ++i) {
+                const int slot = i & 1, st = i % BD_STAGES;
+                if (!mbar_wait(&full[st], (i / BD_STAGES) & 1, abort, p.err)) { ok = false; break; }
+                // S(slot) is free once the softmax of tile i − 2 has read it (its P is ready).
+                if (i >= 2 && !mbar_wait(&p_ready[slot], ((i - 2) >> 1) & 1, abort, p.err)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t k_addr = smem_u32(smem + OFF_K + s * QKV_BYTES);
+                const uint32_t q_addr = smem_u32(smem + st * BD_STAGE_BYTES);
+                const uint32_t k_addr = q_addr + QKV_BYTES;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)
-                    umma_f16(tmem + S_COL + s * TILE, umma_desc_sw128(q_addr + kk * 32),
+                    umma_f16(tmem + slot * TILE, umma_desc_sw128(q_addr + kk * 32),
                              umma_desc_sw128(k_addr + kk * 32), p.idesc_s, kk != 0);
-                umma_commit(&s_full[s]);
-                if (kb >= 1 && !issue_pv(kb - 1)) { ok = false; break; }
+                umma_commit(&s_full[slot]);
+                if (i >= 1 && !issue_pv(i - 1)) { ok = false; break; }
             }
-            if (ok && nkb > 0) issue_pv(nkb - 1);
+            if (ok && my_tiles > 0) issue_pv(my_tiles - 1);
         }
     } else {
-        // Softmax warps: thread `row` owns query row `row` of the tile.
-        const int row = threadIdx.x;
-        const int prob = row / BT;
-        const int tok = t0 + row % BT;
-        const int gi = gi0 + prob;
-        const bool valid = tok < p.tokens && gi < p.group_inner;
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        float o[HD];
-#pragma unroll
-        for (int d = 0; d < HD; ++d) o[d] = 0.f;
-        float m_run = -INFINITY, l = 0.f, m_acc = -INFINITY;
-        float m_pend[2] = {0.f, 0.f};
-        bool ok = true;
-
-        auto fold = [&](int j) -> bool {  // o = o·2^(m_acc − m_j) + O(j); warp-uniform
-            const int s = j & 1;
-            if (!__all_sync(0xffffffffu, mbar_wait(&o_full[s], (j >> 1) & 1, abort, p.err))) return false;
+        const int g = warp / 4, wq = warp % 4;
+        const int row = threadIdx.x % 128;  // query row of the tile
+        const int prob = wq / 2;            // rows 0–63: group gi0, rows 64–127: gi0 + 1
+        const int tok = row % 64;
+        const uint32_t lane_base = tmem + ((uint32_t)(wq * 32) << 16);
+        for (int i = g; i < my_tiles; i += 2) {
+            const int st = i % BD_STAGES, k = i >> 1;
+            int go, gi0, head;
+            decode(i, go, gi0, head);
+            uint8_t* base = smem + st * BD_STAGE_BYTES;
+            if (!__all_sync(0xffffffffu, mbar_wait(&s_full[g], k & 1, abort, p.err))) break;
             tc_fence_after();
-            const float sc = m_acc == -INFINITY ? 0.f : ex2_approx(m_acc - m_pend[s]);
-#pragma unroll
-            for (int c = 0; c < HD; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(lane_base + O_COL + s * HD + c, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int d = 0; d < 32; ++d) o[c + d] = o[c + d] * sc + __uint_as_float(r[d]);
-            }
-            m_acc = m_pend[s];
-            return true;
-        };
-
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb & 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[s], (kb >> 1) & 1, abort, p.err));
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t s_base = lane_base + S_COL + s * TILE;
-            // Pass 1: row maximum over this block's valid keys.
+            // Scores of this row against its own problem's keys (columns prob·64 ..).
+            uint32_t ra[32], rb[32];
+            tmem_ld32(lane_base + g * TILE + prob * 64, ra);
+            tmem_ld32(lane_base + g * TILE + prob * 64 + 32, rb);
+            tmem_wait_ld();
             float mx = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < TILE; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(s_base + c, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int col = c + j;
-                    const bool kv = (col / BT == prob) && (kb * BT + col % BT < p.tokens);
-                    if (kv) mx = fmaxf(mx, __uint_as_float(r[j]));
-                }
+            for (int j = 0; j < 32; ++j) {
+                if (j < p.tokens) mx = fmaxf(mx, __uint_as_float(ra[j]));
+                if (32 + j < p.tokens) mx = fmaxf(mx, __uint_as_float(rb[j]));
             }
-            const float m_new = fmaxf(m_run, mx * LOG2E);
-            const float m_use = m_new == -INFINITY ? 0.f : m_new;
-            // Fold O(kb−2) before its P buffer is overwritten.
-            if (kb >= 2) {
-                ok = fold(kb - 2);
-                if (!ok) break;
-            }
-            // Pass 2: exponentials, row sum and P(kb) into shared memory (swizzled K-major).
-            uint8_t* pbuf = smem + OFF_P + s * P_BYTES;
+            const float m = mx * LOG2E;
             float rowsum = 0.f;
+            uint32_t pk[32];
 #pragma unroll
-            for (int c = 0; c < TILE; c += 32) {
-                uint32_t r[32];
-                tmem_ld32(s_base + c, r);
-                tmem_wait_ld();
-                uint32_t pk[16];
-#pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    float e[2];
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const int col = c + j + u;
-                        const bool kv = (col / BT == prob) && (kb * BT + col % BT < p.tokens);
-                        e[u] = kv ? ex2_approx(__uint_as_float(r[j + u]) * LOG2E - m_use) : 0.f;
-                        rowsum += e[u];
-                    }
-                    pk[j / 2] = pack2<BF16>(e[0], e[1]);
-                }
-                uint8_t* half_base = pbuf + (c / 64) * (TILE * 128) + row * 128;
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const int chunk = ((c % 64) / 8 + q) ^ (row & 7);
-                    *reinterpret_cast<uint4*>(half_base + chunk * 16) =
-                        make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
-                }
+            for (int j = 0; j < 64; j += 2) {
+                const float s0 = __uint_as_float(j < 32 ? ra[j] : rb[j - 32]);
+                const float s1 = __uint_as_float(j + 1 < 32 ? ra[j + 1] : rb[j + 1 - 32]);
+                const float e0 = j < p.tokens ? ex2_approx(fmaf(s0, LOG2E, -m)) : 0.f;
+                const float e1 = j + 1 < p.tokens ? ex2_approx(fmaf(s1, LOG2E, -m)) : 0.f;
+                rowsum += e0 + e1;
+                pk[j / 2] = pack2<BF16>(e0, e1);
             }
-            l = (m_run == -INFINITY ? 0.f : l * ex2_approx(m_run - m_use)) + rowsum;
-            m_run = m_new == -INFINITY ? -INFINITY : m_use;
-            m_pend[s] = m_use;
+            // P row over the tile's 128 keys (K-major, 128-byte swizzle, over Q | K): this
+            // problem's half holds the probabilities, the other half zeros.
+            uint8_t* own = base + prob * (TILE * 128) + row * 128;
+            uint8_t* other = base + (1 - prob) * (TILE * 128) + row * 128;
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                const int chunk = q ^ (row & 7);
+                *reinterpret_cast<uint4*>(own + chunk * 16) = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                *reinterpret_cast<uint4*>(other + chunk * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
             fence_proxy_async();
             tc_fence_before();
-            mbar_arrive(&p_ready[s]);
-        }
-        if (ok) {
-            for (int j = max(0, nkb - 2); j < nkb && ok; ++j) ok = fold(j);
-        }
-        if (ok && valid) {
-            const int64_t orow = (int64_t)go * p.group_outer_stride + (int64_t)gi * p.group_inner_stride +
-                                 (int64_t)tok * p.token_stride;
-            float scale = 1.f / l;
-            if (p.gate_col >= 0) {
+            mbar_arrive(&p_ready[g]);
+
+            if (!__all_sync(0xffffffffu, mbar_wait(&o_full[g], k & 1, abort, p.err))) break;
+            tc_fence_after();
+            tmem_ld32(lane_base + 256 + g * HD, ra);
+            tmem_ld32(lane_base + 256 + g * HD + 32, rb);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(&o_empty[g]);
+            const int gi = gi0 + prob;
+            const bool valid = tok < p.tokens && gi < p.group_inner;
+            float scale = valid ? 1.f / rowsum : 0.f;
+            if (valid && p.gate_col >= 0) {
+                const int64_t orow = (int64_t)go * p.group_outer_stride + (int64_t)gi * p.group_inner_stride +
+                                     (int64_t)tok * p.token_stride;
                 const float gl = BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[orow * p.ld + p.gate_col + head])
                                       : __half2float(reinterpret_cast<const __half*>(p.q)[orow * p.ld + p.gate_col + head]);
                 scale /= 1.f + __expf(-gl);
             }
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) +
-                                                  (orow * p.out_ld + p.out_col + head * HD) * 2);
+            // Output row into the stage's V bytes in the TMA layout (128-byte swizzle).
+            uint8_t* orow_s = base + 2 * QKV_BYTES + row * 128;
 #pragma unroll
-            for (int q = 0; q < HD / 8; ++q)
-                dst[q] = make_uint4(pack2<BF16>(o[8 * q] * scale, o[8 * q + 1] * scale),
-                                    pack2<BF16>(o[8 * q + 2] * scale, o[8 * q + 3] * scale),
-                                    pack2<BF16>(o[8 * q + 4] * scale, o[8 * q + 5] * scale),
-                                    pack2<BF16>(o[8 * q + 6] * scale, o[8 * q + 7] * scale));
+            for (int q = 0; q < 8; ++q) {
+                const int chunk = q ^ (row & 7);
+                float v[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    v[u] = __uint_as_float(q < 4 ? ra[8 * q + u] : rb[8 * (q - 4) + u]) * scale;
+                *reinterpret_cast<uint4*>(orow_s + chunk * 16) =
+                    make_uint4(pack2<BF16>(v[0], v[1]), pack2<BF16>(v[2], v[3]), pack2<BF16>(v[4], v[5]),
+                               pack2<BF16>(v[6], v[7]));
+            }
+            fence_proxy_async();
+            mbar_arrive(&staged[g]);
+            if (row == 0) {
+                if (mbar_wait(&staged[g], k & 1, abort, p.err)) {
+                    tma_store_4d(&omap, base + 2 * QKV_BYTES, p.out_col + head * HD, 0, gi0, go);
+                    bulk_commit();
+                    bulk_wait_read<0>();
+                }
+                mbar_arrive(&empty[st]);
+            }
         }
+        if (row == 0) bulk_wait<0>();
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4) {
+    if (warp == 9) {
         __syncwarp();
         tmem_dealloc(tmem, 512);
     }
@@ -536,18 +530,22 @@ int launch_pp(const CUtensorMap& map, const AttnTcParams& p, dim3 grid, cudaStre
     return check_launch("attention_pp");
 }
 
-template <int BT, bool BF16>
-int launch(const CUtensorMap& map, const AttnTcParams& p, dim3 grid, cudaStream_t s) {
+template <bool BF16>
+int launch_band(const CUtensorMap& map, const CUtensorMap& omap, const AttnTcParams& p, int pairs, int heads,
+                int total, cudaStream_t s) {
     static bool configured[64] = {};
+    static int sms[64] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
+    ANCHA_CUDA(cudaGetDevice(&dev));
     if (!configured[dev & 63]) {
-        ANCHA_CUDA(cudaFuncSetAttribute(attention_tc_kernel<BT, BF16>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        ANCHA_CUDA(cudaFuncSetAttribute(attention_band_kernel<BF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        BD_SMEM_BYTES));
+        ANCHA_CUDA(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
         configured[dev & 63] = true;
     }
-    attention_tc_kernel<BT, BF16><<<grid, 192, SMEM_BYTES, s>>>(map, p);
-    return check_launch("attention_tc");
+    const int grid = std::min(total, sms[dev & 63]);
+    attention_band_kernel<BF16><<<grid, BD_THREADS, BD_SMEM_BYTES, s>>>(map, omap, p, pairs, heads, total);
+    return check_launch("attention_band");
 }
 
 }  // namespace
@@ -600,11 +598,20 @@ int attention_tc(const AttnArgs& a, cudaStream_t stream) {
         dim3 grid((unsigned)gx, (unsigned)a.heads, (unsigned)p.group_outer);
         return a.elt == ELT_BF16 ? launch_pp<true>(map, p, grid, stream) : launch_pp<false>(map, p, grid, stream);
     }
-    const int64_t gx = (int64_t)p.tiles_per_group * ceil_div(a.group_inner, BG);
-    if (gx > 0x7fffffff || a.heads > 65535 || p.group_outer > 65535)
-        return fail(ANCHA_E_UNSUPPORTED, "attention_tc: grid too large");
-    dim3 grid((unsigned)gx, (unsigned)a.heads, (unsigned)p.group_outer);
-    return a.elt == ELT_BF16 ? launch<64, true>(map, p, grid, stream) : launch<64, false>(map, p, grid, stream);
+    // Band axis: persistent CTAs over (outer group, group pair, head) tiles; the output leaves
+    // through a TMA store with the same {columns, tokens, inner groups, outer groups} shape.
+    const int64_t pairs = ceil_div(a.group_inner, 2);
+    const int64_t total = (int64_t)p.group_outer * pairs * a.heads;
+    if (total > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "attention_tc: too many tiles");
+    const int64_t o1 = a.token_stride * a.out_ld;
+    const int64_t o2 = a.group_inner_stride * a.out_ld;
+    const int64_t o3 = p.group_outer > 1 ? a.group_outer_stride * a.out_ld : a.out_ld;
+    CUtensorMap omap;
+    ANCHA_TRY(make_tma_4d(&omap, a.out, a.elt, a.out_col + (int64_t)a.heads * HD, a.tokens, a.group_inner,
+                          p.group_outer, o1 > 0 ? o1 : a.out_ld, o2 > 0 ? o2 : a.out_ld, o3 > 0 ? o3 : a.out_ld,
+                          BT, BG));
+    return a.elt == ELT_BF16 ? launch_band<true>(map, omap, p, (int)pairs, a.heads, (int)total, stream)
+                             : launch_band<false>(map, omap, p, (int)pairs, a.heads, (int)total, stream);
 }
 
 }  // namespace ancha

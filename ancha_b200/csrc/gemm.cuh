@@ -25,6 +25,11 @@ struct GemmEpilogue {
     int rope_tokens;
     int rope_div;       // token = (row / rope_div) % rope_tokens
     int rope_hd;        // head width of the table (columns per head)
+    // Optional pair-major copy of the same table for the tensor-core epilogue:
+    // [2 (query, key)][rope_hd / 2 pairs][rope_tokens] × (cos, sin) float2, where a pair's two
+    // columns share the cosine and carry ∓sin. Lanes of a warp hold consecutive rows, so a
+    // token-fastest table makes their loads coalesce. Null: the tensor-core path reads `rope`.
+    const float* rope_pairs;
 };
 
 // FFMA GEMM (fp32 accumulation). `groups` is a device array of `count` problems when

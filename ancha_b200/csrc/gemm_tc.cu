@@ -40,6 +40,7 @@ struct TcParams {
     int64_t ldr;
     int act, out_type;
     const float* rope;
+    const float2* rope_pairs;
     int rope_width, rope_tokens, rope_div, rope_hd;
     uint32_t idesc;
     int m_tiles, n_tiles, tiles;
@@ -80,12 +81,24 @@ __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, boo
     }
     if (p.act == ANCHA_ACT_GELU) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_erf(v[j]);
+        for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
     } else if (p.act == ANCHA_ACT_TANH) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = tanhf(v[j]);
+        for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j]);
     }
-    if (p.rope && c0 < 2 * p.rope_width) {
+    if (p.rope_pairs && c0 < 2 * p.rope_width) {
+        const int key = c0 >= p.rope_width;
+        const int token = (row / p.rope_div) % p.rope_tokens;
+        const float2* t = p.rope_pairs +
+                          ((int64_t)key * (p.rope_hd / 2) + (c0 % p.rope_hd) / 2) * p.rope_tokens + token;
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+            const float2 cs = t[(int64_t)(j / 2) * p.rope_tokens];
+            const float x0 = v[j], x1 = v[j + 1];
+            v[j] = x0 * cs.x - x1 * cs.y;
+            v[j + 1] = x1 * cs.x + x0 * cs.y;
+        }
+    } else if (p.rope && c0 < 2 * p.rope_width) {
         const int key = c0 >= p.rope_width;
         const int token = (row / p.rope_div) % p.rope_tokens;
         const int d = c0 % p.rope_hd;
@@ -104,7 +117,7 @@ __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, boo
     }
     if (p.act == ANCHA_ACT_GLU) {
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = v[2 * j] * sigmoidf_(v[2 * j + 1]);
+        for (int j = 0; j < 16; ++j) v[j] = v[2 * j] * sigmoid_fast(v[2 * j + 1]);
         return 16;
     }
     if (p.residual && live) {
@@ -401,7 +414,8 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     if (g.m <= 0 || g.n <= 0 || g.k <= 0) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: empty problem");
     const size_t oe = elt_size(e.out_type);
     if (!aligned16(g.out) || (g.ldo * oe) % 16 || (g.residual && (!aligned16(g.residual) || (g.ldr * 4) % 16)) ||
-        (g.bias && !aligned16(g.bias)) || (e.rope && (!aligned16(e.rope) || e.rope_hd % 32)))
+        (g.bias && !aligned16(g.bias)) || (e.rope && (!aligned16(e.rope) || e.rope_hd % 32)) ||
+        (e.rope_pairs && (!aligned16(e.rope_pairs) || e.rope_hd % 32)))
         return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: epilogue operands not 16-byte aligned");
     TcParams p{};
     p.m = g.m; p.n = g.n; p.k = g.k; p.groups = 1; p.b_groups = 1; p.group_n = nullptr;
@@ -410,6 +424,7 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     p.residual = g.residual; p.ldr = g.ldr;
     p.act = e.act; p.out_type = e.out_type;
     p.rope = e.rope; p.rope_width = e.rope_width; p.rope_tokens = e.rope_tokens;
+    p.rope_pairs = reinterpret_cast<const float2*>(e.rope_pairs);
     p.rope_div = e.rope_div; p.rope_hd = e.rope_hd;
     return run(g.a, g.lda, (int64_t)g.m * g.lda, g.b, g.ldb, (int64_t)g.n * g.ldb, p, ab_type, s);
 }
@@ -427,7 +442,7 @@ int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& e, cu
     p.bias = q.bias; p.bias_group_stride = q.bias_group_stride;
     p.residual = nullptr; p.ldr = 0;
     p.act = e.act; p.out_type = e.out_type;
-    p.rope = nullptr; p.rope_width = 0; p.rope_tokens = 1; p.rope_div = 1; p.rope_hd = 64;
+    p.rope = nullptr; p.rope_pairs = nullptr; p.rope_width = 0; p.rope_tokens = 1; p.rope_div = 1; p.rope_hd = 64;
     return run(q.a, q.lda, q.a_group_stride, q.b, q.ldb, q.b_group_stride, p, ab_type, s);
 }
 

@@ -503,7 +503,7 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
         for (auto& freqs : rope_freqs_) {
             for (int axis = 0; axis < 2; ++axis) {
                 const int tokens = axis == 0 ? frames : bands;
-                std::vector<float> tab((size_t)4 * tokens * hd);
+                std::vector<float> tab((size_t)4 * tokens * hd), pairs((size_t)2 * tokens * hd);
                 for (int q = 0; q < 2; ++q) {
                     const float sc = q == 0 ? qscale : 1.f;
                     for (int t = 0; t < tokens; ++t)
@@ -515,10 +515,15 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
                             tab[base_c] = tab[base_c + 1] = (float)(cs * sc);
                             tab[base_s] = (float)(-sn * sc);
                             tab[base_s + 1] = (float)(sn * sc);
+                            const size_t pr = (((size_t)q * (hd / 2) + j) * tokens + t) * 2;
+                            pairs[pr] = (float)(cs * sc);
+                            pairs[pr + 1] = (float)(sn * sc);
                         }
                 }
                 w.rope.emplace_back();
                 upload(w.rope.back(), tab);
+                w.rope_pairs.emplace_back();
+                upload(w.rope_pairs.back(), pairs);
             }
         }
         ws_ = std::move(w);
@@ -532,8 +537,8 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
 
 int Model::linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias,
                   const float* residual, int64_t ldr, void* out, int64_t ldo, int out_type,
-                  int64_t m, int n, int k, int act, const float* rope, int rope_tokens,
-                  int rope_div, cudaStream_t s) {
+                  int64_t m, int n, int k, int act, const float* rope, const float* rope_pairs,
+                  int rope_tokens, int rope_div, cudaStream_t s) {
     GemmGroup g{};
     g.a = x;
     g.lda = ldx;
@@ -551,6 +556,7 @@ int Model::linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias
     e.act = act;
     e.out_type = out_type;
     e.rope = rope;
+    e.rope_pairs = rope_pairs;
     const ModelConfig& c = manifest.config;
     e.rope_width = rope ? c.heads * c.head_dim : 0;
     e.rope_tokens = rope_tokens;
@@ -570,11 +576,13 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
     const int dim = c.dim, inner = c.heads * c.head_dim, hidden = c.dim * c.ff_mult;
     const int bf = elt_;
     float* x = ws_.x.as<float>();
-    const DevBuf& rope = ws_.rope[(size_t)t.rope_set * 2 + (time_axis ? 0 : 1)];
+    const size_t rope_slot = (size_t)t.rope_set * 2 + (time_axis ? 0 : 1);
+    const DevBuf& rope = ws_.rope[rope_slot];
     // Packed q | k | v | gate projection of unit_norm(x), RoPE in the epilogue.
     ANCHA_TRY(norm_rows(x, dim, nullptr, ws_.xn.p, bf, dim, R, dim, s));
     ANCHA_TRY(linear(ws_.xn.p, dim, t.wqkvg, t.bqkvg.as<float>(), nullptr, 0, ws_.qkvg.p, ldq, bf,
                      R, 3 * inner + c.heads, dim, ANCHA_ACT_NONE, rope.as<float>(),
+                     ws_.rope_pairs[rope_slot].as<float>(),
                      time_axis ? T : bands, time_axis ? 1 : T, s));
     // Gated attention within each group.
     AttnArgs a{};
@@ -610,12 +618,12 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
     ANCHA_TRY(ast);
     // Output projection + residual, then the GELU feed-forward + residual.
     ANCHA_TRY(linear(ws_.att.p, inner, t.wout, nullptr, x, dim, x, dim, ELT_F32, R, dim, inner,
-                     ANCHA_ACT_NONE, nullptr, 1, 1, s));
+                     ANCHA_ACT_NONE, nullptr, nullptr, 1, 1, s));
     ANCHA_TRY(norm_rows(x, dim, nullptr, ws_.xn.p, bf, dim, R, dim, s));
     ANCHA_TRY(linear(ws_.xn.p, dim, t.w1, t.b1.as<float>(), nullptr, 0, ws_.hidden.p, hidden, bf,
-                     R, hidden, dim, ANCHA_ACT_GELU, nullptr, 1, 1, s));
+                     R, hidden, dim, ANCHA_ACT_GELU, nullptr, nullptr, 1, 1, s));
     ANCHA_TRY(linear(ws_.hidden.p, hidden, t.w2, t.b2.as<float>(), x, dim, x, dim, ELT_F32, R, dim,
-                     hidden, ANCHA_ACT_NONE, nullptr, 1, 1, s));
+                     hidden, ANCHA_ACT_NONE, nullptr, nullptr, 1, 1, s));
     // Mel: SourceNorm of the block output (roformer.rs:516-519).
     if (t.out_scale.p) ANCHA_TRY(norm_rows(x, dim, t.out_scale.as<float>(), nullptr, 0, 0, R, dim, s));
     return ANCHA_OK;

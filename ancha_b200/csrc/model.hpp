@@ -74,7 +74,8 @@ struct Workspace {
     int chunks = 0, frames = 0;
     DevBuf x, xn, qkvg, att, hidden, h2, z, glu;
     DevBuf split_groups, mask_groups, glu_groups;
-    std::vector<DevBuf> rope;  // per rope set: [time table, band table]
+    std::vector<DevBuf> rope;        // per rope set: [time table, band table], [4, tokens, hd]
+    std::vector<DevBuf> rope_pairs;  // the same tables pair-major: [2, hd / 2, tokens] × float2
 };
 
 // Device buffers of the chunk pipeline (gather → STFT → model → iSTFT → overlap-add),
@@ -114,8 +115,8 @@ private:
     int ensure_workspace(int chunks, int frames, cudaStream_t s);
     int linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias,
                const float* residual, int64_t ldr, void* out, int64_t ldo, int out_type,
-               int64_t m, int n, int k, int act, const float* rope, int rope_tokens,
-               int rope_div, cudaStream_t s);
+               int64_t m, int n, int k, int act, const float* rope, const float* rope_pairs,
+               int rope_tokens, int rope_div, cudaStream_t s);
     int transformer(const TransformerWeights& t, bool time_axis, cudaStream_t s);
 
     std::vector<int> width_, offset_;
