@@ -22,7 +22,6 @@ namespace {
 constexpr int TILE = 128;           // query rows / keys per block
 constexpr int HD = 64;              // head width
 constexpr int QKV_BYTES = TILE * HD * 2;
-constexpr int P_BYTES = TILE * TILE * 2;
 constexpr float LOG2E = 1.4426950408889634f;
 
 struct AttnTcParams {
@@ -277,15 +276,24 @@ attention_band_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
 }
 
 // Time-axis kernel (tokens > 64): two 128-row query tiles of the same (group, head) per CTA
-// share every K / V block. Warps 0–3 and 4–7 are the softmax warpgroups of tile 0 and 1
-// (two warps per SM sub-partition), warp 8 issues TMA, warp 9 issues UMMA. Per tile S, O
-// (TMEM) and P (shared memory) are single-buffered; the two tiles alternate on the tensor
-// cores, so one warpgroup's softmax overlaps the other's S = Q·Kᵀ and P·V. Interior key
-// blocks skip masking; only the last, partial block masks keys ≥ tokens.
-constexpr int PP_OFF_Q = 0, PP_OFF_K = 2 * QKV_BYTES, PP_OFF_V = 4 * QKV_BYTES, PP_OFF_P = 6 * QKV_BYTES;
-constexpr int PP_OFF_BAR = PP_OFF_P + 2 * P_BYTES;
-constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + 16 * 8 + 16;
+// share every K / V block, streamed through a 3-deep ring. Warps 0–3 and 4–7 are the softmax
+// warpgroups of tile 0 and 1 (two warps per SM sub-partition), warp 8 issues TMA, warp 9
+// UMMA.
+//
+// TMEM (512 columns): S of tile t at t·128, its output accumulator O at 256 + t·64 and its
+// P (16-bit pairs, the A operand of P·V) at 384 + t·64. A softmax thread copies its row of
+// S(kb) into registers and releases the S buffer at once, so S(kb+1) = Q·K(kb+1)ᵀ runs on the
+// tensor cores while the exponentials of block kb are computed; it then writes P(kb) and the
+// UMMA warp accumulates O += P(kb)·V(kb). The running maximum is updated lazily: it moves
+// (and O, l are rescaled in TMEM) only when a row's block maximum exceeds it by more than 2^8,
+// so P stays ≤ 256 and the rescale is rare. Interior key blocks skip masking.
+constexpr int PP_KV_STAGES = 3;
+constexpr int PP_OFF_Q = 0, PP_OFF_K = 2 * QKV_BYTES, PP_OFF_V = PP_OFF_K + PP_KV_STAGES * QKV_BYTES;
+constexpr int PP_OFF_BAR = PP_OFF_V + PP_KV_STAGES * QKV_BYTES;
+constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + 20 * 8 + 16;
 constexpr int PP_THREADS = 320;
+constexpr float PP_RESCALE_LOG2 = 8.f;
+constexpr uint32_t PP_O_COL = 256, PP_P_COL = 384;
 
 template <bool BF16>
 __global__ void __launch_bounds__(PP_THREADS, 1)
@@ -294,12 +302,13 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PP_OFF_BAR);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;   // [2] stages
-    uint64_t* kv_empty = bars + 3;  // [2] stages
-    uint64_t* s_full = bars + 5;    // [2] tiles
-    uint64_t* p_ready = bars + 7;   // [2] tiles
-    uint64_t* o_full = bars + 9;    // [2] tiles
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+    uint64_t* kv_full = bars + 1;                  // [stage]
+    uint64_t* kv_empty = bars + 1 + PP_KV_STAGES;  // [stage]
+    uint64_t* s_full = bars + 7;                   // [tile] S(kb) computed
+    uint64_t* s_free = bars + 9;                   // [tile] S(kb) copied to registers (128 arrivals)
+    uint64_t* p_ready = bars + 11;                 // [tile] P(kb) written (128 arrivals)
+    uint64_t* pv_done = bars + 13;                 // [tile] O += P(kb)·V(kb) completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int pairs = (p.tiles_per_group + 1) / 2;
@@ -308,17 +317,20 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     const int go = blockIdx.z, head = blockIdx.y;
     const int nkb = p.tiles_per_group;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int q0 = 2 * pair * TILE;                 // first query token of tile 0
-    const bool active1 = q0 + TILE < p.tokens;      // tile 1 holds at least one query
+    const int q0 = 2 * pair * TILE;             // first query token of tile 0
+    const bool active1 = q0 + TILE < p.tokens;  // tile 1 holds at least one query
 
     if (threadIdx.x == 256) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < PP_KV_STAGES; ++s) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
-            mbar_init(&s_full[s], 1);
-            mbar_init(&p_ready[s], 128);
-            mbar_init(&o_full[s], 1);
+        }
+        for (int t = 0; t < 2; ++t) {
+            mbar_init(&s_full[t], 1);
+            mbar_init(&s_free[t], 128);
+            mbar_init(&p_ready[t], 128);
+            mbar_init(&pv_done[t], 1);
         }
         *abort = 0;
         fence_barrier_init();
@@ -333,7 +345,6 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // TMEM columns: tile t uses S at t·256 + [0, 128) and O at t·256 + [128, 192).
 
     if (warp == 8) {
         if (lane == 0) {
@@ -342,8 +353,8 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             tma_load_4d(smem + PP_OFF_Q + QKV_BYTES, &tmap, q_full, p.q_col + head * HD, q0 + TILE, gi, go);
             int issued = 0;
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb & 1;
-                if (!mbar_wait(&kv_empty[s], ((kb >> 1) & 1) ^ 1, abort, p.err)) break;
+                const int s = kb % PP_KV_STAGES;
+                if (!mbar_wait(&kv_empty[s], ((kb / PP_KV_STAGES) & 1) ^ 1, abort, p.err)) break;
                 mbar_arrive_expect_tx(&kv_full[s], 2 * QKV_BYTES);
                 tma_load_4d(smem + PP_OFF_K + s * QKV_BYTES, &tmap, &kv_full[s], p.k_col + head * HD, kb * TILE, gi, go);
                 tma_load_4d(smem + PP_OFF_V + s * QKV_BYTES, &tmap, &kv_full[s], p.v_col + head * HD, kb * TILE, gi, go);
@@ -353,158 +364,163 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 const long long c0 = clock64();
                 while (!mbar_try_wait(q_full, 0) && clock64() - c0 < kWaitCycles) {
                 }
-                for (int kb = max(0, issued - 2); kb < issued; ++kb)
-                    while (!mbar_try_wait(&kv_full[kb & 1], (kb >> 1) & 1) && clock64() - c0 < kWaitCycles) {
+                for (int kb = max(0, issued - PP_KV_STAGES); kb < issued; ++kb)
+                    while (!mbar_try_wait(&kv_full[kb % PP_KV_STAGES], (kb / PP_KV_STAGES) & 1) &&
+                           clock64() - c0 < kWaitCycles) {
                     }
             }
         }
     } else if (warp == 9) {
         if (lane == 0) {
+            // Fixed issue order per key block j: S(j + 1) of both tiles (each once its softmax
+            // has copied S(j) out), then P(j)·V(j) of both tiles.
             const int ntiles = active1 ? 2 : 1;
-            auto issue_pv = [&](int t, int j) -> bool {
-                if (!mbar_wait(&p_ready[t], j & 1, abort, p.err)) return false;
+            const uint64_t q_desc[2] = {umma_desc_sw128(smem_u32(smem + PP_OFF_Q)),
+                                        umma_desc_sw128(smem_u32(smem + PP_OFF_Q + QKV_BYTES))};
+            auto issue_s = [&](int t, int j) -> bool {
+                if (j >= 1 && !mbar_wait(&s_free[t], (j - 1) & 1, abort, p.err)) return false;
                 tc_fence_after();
-                const uint32_t p_addr = smem_u32(smem + PP_OFF_P + t * P_BYTES);
-                const uint32_t v_addr = smem_u32(smem + PP_OFF_V + (j & 1) * QKV_BYTES);
+                const uint64_t k_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_K + (j % PP_KV_STAGES) * QKV_BYTES));
 #pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk)
-                    umma_f16(tmem + t * 256 + 128,
-                             umma_desc_sw128(p_addr + (kk >> 2) * (TILE * 128) + (kk & 3) * 32),
-                             umma_desc_sw128(v_addr + kk * 16 * 128), p.idesc_o, kk != 0);
-                umma_commit(&o_full[t]);
+                for (int kk = 0; kk < HD / 16; ++kk)  // K step of 16 = 32 bytes = 2 descriptor units
+                    umma_f16(tmem + t * TILE, q_desc[t] + 2 * kk, k_desc + 2 * kk, p.idesc_s, kk != 0);
+                umma_commit(&s_full[t]);
                 return true;
             };
-            bool ok = mbar_wait(q_full, 0, abort, p.err);
-            for (int kb = 0; ok && kb < nkb; ++kb) {
-                const int s = kb & 1;
-                if (!mbar_wait(&kv_full[s], (kb >> 1) & 1, abort, p.err)) { ok = false; break; }
+            auto issue_pv = [&](int t, int k) -> bool {
+                if (!mbar_wait(&p_ready[t], k & 1, abort, p.err)) return false;
                 tc_fence_after();
-                const uint32_t k_addr = smem_u32(smem + PP_OFF_K + s * QKV_BYTES);
-                for (int t = 0; t < ntiles && ok; ++t) {
-                    if (kb >= 1 && !issue_pv(t, kb - 1)) { ok = false; break; }
-                    const uint32_t q_addr = smem_u32(smem + PP_OFF_Q + t * QKV_BYTES);
+                const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_V + (k % PP_KV_STAGES) * QKV_BYTES));
 #pragma unroll
-                    for (int kk = 0; kk < HD / 16; ++kk)
-                        umma_f16(tmem + t * 256, umma_desc_sw128(q_addr + kk * 32),
-                                 umma_desc_sw128(k_addr + kk * 32), p.idesc_s, kk != 0);
-                    umma_commit(&s_full[t]);
+                for (int kk = 0; kk < TILE / 16; ++kk)  // 16 keys = 16 rows of 128 bytes = 128 units
+                    umma_f16_ts(tmem + PP_O_COL + t * HD, tmem + PP_P_COL + t * HD + kk * 8, v_desc + 128 * kk,
+                                p.idesc_o, (k > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(&pv_done[t]);
+                return true;
+            };
+            bool ok = mbar_wait(q_full, 0, abort, p.err) && mbar_wait(&kv_full[0], 0, abort, p.err);
+            for (int t = 0; ok && t < ntiles; ++t) ok = issue_s(t, 0);
+            for (int j = 0; ok && j < nkb; ++j) {
+                if (j + 1 < nkb) {
+                    ok = mbar_wait(&kv_full[(j + 1) % PP_KV_STAGES], ((j + 1) / PP_KV_STAGES) & 1, abort, p.err);
+                    for (int t = 0; ok && t < ntiles; ++t) ok = issue_s(t, j + 1);
                 }
-                if (ok && kb >= 1) umma_commit(&kv_empty[(kb - 1) & 1]);
+                for (int t = 0; ok && t < ntiles; ++t) ok = issue_pv(t, j);
+                if (ok) umma_commit(&kv_empty[j % PP_KV_STAGES]);  // fires once both P·V are done
             }
-            for (int t = 0; ok && t < ntiles; ++t) ok = issue_pv(t, nkb - 1);
-            if (ok) umma_commit(&kv_empty[(nkb - 1) & 1]);
         }
     } else {
         const int t = warp / 4;  // tile of this softmax warpgroup
         const int row = threadIdx.x % 128;
         const int tok = q0 + t * TILE + row;
         const bool valid = tok < p.tokens;
-        const uint32_t lane_base = tmem + t * 256 + ((uint32_t)((warp % 4) * 32) << 16);
+        const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
+        const uint32_t s_addr = tmem + lane_off + t * TILE;
+        const uint32_t o_addr = tmem + lane_off + PP_O_COL + t * HD;
+        const uint32_t p_addr = tmem + lane_off + PP_P_COL + t * HD;
         if (t == 0 || active1) {
-            float o[HD];
-#pragma unroll
-            for (int d = 0; d < HD; ++d) o[d] = 0.f;
-            float m_run = -INFINITY, l = 0.f, m_acc = -INFINITY, m_prev = 0.f;
+            float m_used = -INFINITY, l = 0.f;
             bool ok = true;
-            uint8_t* pbuf = smem + PP_OFF_P + t * P_BYTES;
-            auto fold = [&](int j) -> bool {
-                if (!__all_sync(0xffffffffu, mbar_wait(&o_full[t], j & 1, abort, p.err))) return false;
-                tc_fence_after();
-                const float sc = m_acc == -INFINITY ? 0.f : ex2_approx(m_acc - m_prev);
-#pragma unroll
-                for (int c = 0; c < HD; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(lane_base + 128 + c, r);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int d = 0; d < 32; ++d) o[c + d] = o[c + d] * sc + __uint_as_float(r[d]);
-                }
-                m_acc = m_prev;
-                return true;
-            };
             for (int kb = 0; kb < nkb; ++kb) {
                 ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], kb & 1, abort, p.err));
                 if (!ok) break;
                 tc_fence_after();
+                uint32_t s[4][32];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, s[c]);
+                tmem_wait_ld();
+                tc_fence_before();
+                mbar_arrive(&s_free[t]);  // the tensor cores may compute S(kb + 1) now
                 const int nvalid = min(TILE, p.tokens - kb * TILE);  // valid keys in this block
-                float mx = -INFINITY;
-                if (nvalid == TILE) {
+                if (nvalid < TILE) {
 #pragma unroll
-                    for (int c = 0; c < TILE; c += 32) {
-                        uint32_t r[32];
-                        tmem_ld32(lane_base + c, r);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) mx = fmaxf(mx, __uint_as_float(r[j]));
-                    }
-                } else {
-#pragma unroll
-                    for (int c = 0; c < TILE; c += 32) {
-                        uint32_t r[32];
-                        tmem_ld32(lane_base + c, r);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (c + j < nvalid) mx = fmaxf(mx, __uint_as_float(r[j]));
-                    }
+                    for (int c = 0; c < TILE; ++c)
+                        if (c >= nvalid) s[c / 32][c % 32] = __float_as_uint(-INFINITY);
                 }
-                const float m_new = fmaxf(m_run, mx * LOG2E);
-                const float m_use = m_new == -INFINITY ? 0.f : m_new;
-                if (kb >= 1) {
-                    ok = fold(kb - 1);
-                    if (!ok) break;
+                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+                for (int c = 0; c < TILE; c += 4) {
+                    mx0 = fmaxf(mx0, __uint_as_float(s[c / 32][c % 32]));
+                    mx1 = fmaxf(mx1, __uint_as_float(s[c / 32][c % 32 + 1]));
+                    mx2 = fmaxf(mx2, __uint_as_float(s[c / 32][c % 32 + 2]));
+                    mx3 = fmaxf(mx3, __uint_as_float(s[c / 32][c % 32 + 3]));
                 }
-                float rowsum = 0.f;
+                const float m_blk = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * LOG2E;
+                float corr = 1.f;
+                if (m_blk > m_used + PP_RESCALE_LOG2) {  // also the first block (m_used = −∞)
+                    corr = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_blk);
+                    m_used = m_blk;
+                    l *= corr;
+                }
+                // P = 2^(s·log2 e − m_used) as 16-bit pairs, in two halves of 64 keys.
+                float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-                for (int c = 0; c < TILE; c += 32) {
-                    uint32_t r[32];
-                    tmem_ld32(lane_base + c, r);
-                    tmem_wait_ld();
-                    uint32_t pk[16];
+                for (int h = 0; h < 2; ++h) {
+                    uint32_t pk[32];
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
-                        float e0 = ex2_approx(fmaf(__uint_as_float(r[j]), LOG2E, -m_use));
-                        float e1 = ex2_approx(fmaf(__uint_as_float(r[j + 1]), LOG2E, -m_use));
-                        if (nvalid < TILE) {
-                            if (c + j >= nvalid) e0 = 0.f;
-                            if (c + j + 1 >= nvalid) e1 = 0.f;
-                        }
-                        rowsum += e0 + e1;
+                    for (int j = 0; j < 64; j += 2) {
+                        const int c = h * 64 + j;
+                        const float e0 = ex2_approx(fmaf(__uint_as_float(s[c / 32][c % 32]), LOG2E, -m_used));
+                        const float e1 = ex2_approx(fmaf(__uint_as_float(s[c / 32][c % 32 + 1]), LOG2E, -m_used));
+                        sum0 += e0;
+                        sum1 += e1;
                         pk[j / 2] = pack2<BF16>(e0, e1);
                     }
-                    uint8_t* half_base = pbuf + (c / 64) * (TILE * 128) + row * 128;
+                    if (h == 0 && kb > 0) {
+                        // P(kb − 1)·V must have finished reading P before it is overwritten,
+                        // and O must hold it before a rescale.
+                        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (kb - 1) & 1, abort, p.err));
+                        if (!ok) break;
+                        tc_fence_after();
+                        if (__any_sync(0xffffffffu, corr != 1.f)) {
+                            uint32_t o[2][32];
+                            tmem_ld32(o_addr, o[0]);
+                            tmem_ld32(o_addr + 32, o[1]);
+                            tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const int chunk = ((c % 64) / 8 + q) ^ (row & 7);
-                        *reinterpret_cast<uint4*>(half_base + chunk * 16) =
-                            make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
+                            for (int d = 0; d < 32; ++d) {
+                                o[0][d] = __float_as_uint(__uint_as_float(o[0][d]) * corr);
+                                o[1][d] = __float_as_uint(__uint_as_float(o[1][d]) * corr);
+                            }
+                            tmem_st32(o_addr, o[0]);
+                            tmem_st32(o_addr + 32, o[1]);
+                        }
                     }
+                    tmem_st32(p_addr + h * 32, pk);
                 }
-                l = (m_run == -INFINITY ? 0.f : l * ex2_approx(m_run - m_use)) + rowsum;
-                m_run = m_new == -INFINITY ? -INFINITY : m_use;
-                m_prev = m_use;
-                fence_proxy_async();
+                if (!ok) break;
+                l += sum0 + sum1;
+                tmem_wait_st();
                 tc_fence_before();
                 mbar_arrive(&p_ready[t]);
             }
-            if (ok) ok = fold(nkb - 1);
-            if (ok && valid) {
-                const int64_t orow = (int64_t)go * p.group_outer_stride + (int64_t)gi * p.group_inner_stride +
-                                     (int64_t)tok * p.token_stride;
-                float scale = 1.f / l;
-                if (p.gate_col >= 0) {
-                    const float gl = BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[orow * p.ld + p.gate_col + head])
-                                          : __half2float(reinterpret_cast<const __half*>(p.q)[orow * p.ld + p.gate_col + head]);
-                    scale /= 1.f + __expf(-gl);
-                }
-                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) +
-                                                      (orow * p.out_ld + p.out_col + head * HD) * 2);
+            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (nkb - 1) & 1, abort, p.err));
+            if (ok) {
+                tc_fence_after();
+                uint32_t o[2][32];
+                tmem_ld32(o_addr, o[0]);
+                tmem_ld32(o_addr + 32, o[1]);
+                tmem_wait_ld();
+                if (valid) {
+                    const int64_t orow = (int64_t)go * p.group_outer_stride + (int64_t)gi * p.group_inner_stride +
+                                         (int64_t)tok * p.token_stride;
+                    float scale = 1.f / l;
+                    if (p.gate_col >= 0) {
+                        const float gl = BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[orow * p.ld + p.gate_col + head])
+                                              : __half2float(reinterpret_cast<const __half*>(p.q)[orow * p.ld + p.gate_col + head]);
+                        scale /= 1.f + __expf(-gl);
+                    }
+                    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) +
+                                                          (orow * p.out_ld + p.out_col + head * HD) * 2);
 #pragma unroll
-                for (int q = 0; q < HD / 8; ++q)
-                    dst[q] = make_uint4(pack2<BF16>(o[8 * q] * scale, o[8 * q + 1] * scale),
-                                        pack2<BF16>(o[8 * q + 2] * scale, o[8 * q + 3] * scale),
-                                        pack2<BF16>(o[8 * q + 4] * scale, o[8 * q + 5] * scale),
-                                        pack2<BF16>(o[8 * q + 6] * scale, o[8 * q + 7] * scale));
+                    for (int q = 0; q < HD / 8; ++q) {
+                        float v[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) v[u] = __uint_as_float(o[q / 4][(q % 4) * 8 + u]) * scale;
+                        dst[q] = make_uint4(pack2<BF16>(v[0], v[1]), pack2<BF16>(v[2], v[3]),
+                                            pack2<BF16>(v[4], v[5]), pack2<BF16>(v[6], v[7]));
+                    }
+                }
             }
         }
     }

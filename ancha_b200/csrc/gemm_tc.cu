@@ -8,9 +8,9 @@
 //   warp 1      UMMA issuer: tcgen05.mma M 128 × N BN × K 16 into one of two TMEM
 //               accumulators, tcgen05.commit releasing each slab and, per tile, the
 //               accumulator;
-//   warps 2..9  epilogue: warp w drains TMEM lanes 32·(w % 4).. and half of the columns,
-//               applies bias / GELU / tanh / GLU / RoPE / residual, stages each 32 × 32
-//               chunk in swizzled shared memory and writes it with a TMA tensor store
+//   warps 2..9  epilogue: warp w drains TMEM lanes 32·(w % 4).. and every other 32-column
+//               chunk, applies bias / GELU / tanh / GLU / RoPE / residual, stages each
+//               32 × 32 chunk in swizzled shared memory and writes it with a TMA tensor store
 //               (coalesced, asynchronous, clipped at the matrix edges by the hardware).
 // The two accumulators let the epilogue of tile i overlap the main loop of tile i + 1.
 //
@@ -25,7 +25,8 @@ namespace {
 
 constexpr int BM = 128, BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int EPI_WARPS = 8;
+constexpr int EPI_WARPS = 8;        // a multiple of 4: EPI_WARPS / 4 warps per TMEM lane quarter
+constexpr int STAGE_BUFS = 1;       // staging buffers per epilogue warp
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 
 struct TcParams {
@@ -53,7 +54,7 @@ template <int BN, int STAGES>
 struct Smem {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int TILES = STAGES * (A_BYTES + B_BYTES);
-    static constexpr int STAGING = EPI_WARPS * 2 * STAGE_BYTES;
+    static constexpr int STAGING = EPI_WARPS * STAGE_BUFS * STAGE_BYTES;
     static constexpr int BYTES = 1024 + TILES + STAGING + 8 * (2 * STAGES + 4) + 16;
 };
 
@@ -292,10 +293,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             }
         }
     } else {
-        // Epilogue warps: lane quarter (warp % 4), column half (warp - 2) / 4.
+        // Epilogue warps: lane quarter (warp % 4); the quarter's warps take its 32-column
+        // chunks in turn.
+        constexpr int PER_QUARTER = EPI_WARPS / 4;
         const int quarter = warp % 4;
-        const int half = (warp - 2) / 4;
-        uint8_t* my_stage = staging + (warp - 2) * 2 * STAGE_BYTES;
+        const int first = (warp - 2) / 4;
+        uint8_t* my_stage = staging + (warp - 2) * STAGE_BUFS * STAGE_BYTES;
         const bool glu = p.act == ANCHA_ACT_GLU;
         uint32_t local = 0, chunks = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
@@ -310,16 +313,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             const bool live = row < p.m;
             const uint32_t base = tmem + b * BN + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll 1
-            for (int col = half * (BN / 2); col < (half + 1) * (BN / 2); col += 32) {
+            for (int col = first * 32; col < BN; col += PER_QUARTER * 32) {
                 uint32_t r[32];
                 tmem_ld32(base + col, r);
                 tmem_wait_ld();
                 if (c.n0 + col >= c.n_g) continue;  // warp-uniform
                 float v[32];
                 const int count = epilogue32(p, c.g, row, live, c.n0 + col, c.n_g, r, v);
-                uint8_t* buf = my_stage + (chunks & 1) * STAGE_BYTES;
-                if (chunks >= 2) {
-                    if (lane == 0) bulk_wait_read<1>();
+                uint8_t* buf = my_stage + (chunks % STAGE_BUFS) * STAGE_BYTES;
+                if (chunks >= STAGE_BUFS) {  // the store that last read this buffer is done with it
+                    if (lane == 0) bulk_wait_read<STAGE_BUFS - 1>();
                     __syncwarp();
                 }
                 stage_row(buf, lane, p.out_type, count, v);

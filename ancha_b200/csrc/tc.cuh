@@ -65,6 +65,19 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Non-blocking probe of a phase (mbarrier.test_wait), for issuers that poll several barriers.
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -174,6 +187,18 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t adesc, uint64
         : "memory");
 }
 
+// D (TMEM, f32) (+)= A·B with A read from TMEM (K-major: lane = row, 16-bit pairs along the
+// columns, so a K step of 16 elements is 8 columns) and B from shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread has completed.
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -199,6 +224,23 @@ __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// Store 32 consecutive 32-bit TMEM columns of this thread's lane (same lane rule as loads).
+__device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+        "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+        "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(addr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+        "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+        "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+        "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // UMMA shared-memory descriptor of a K-major operand tile stored as rows of 128 bytes with
 // the 128-byte swizzle (TMA SWIZZLE_128B): start address >> 4, leading byte offset unused
 // (1), stride byte offset = 1024 B between 8-row groups, version 1 (sm_100), layout type 2.
@@ -219,10 +261,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_f16(int ab_bf16, int m, int n,
            ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
 }
 
-// exp2 on the MUFU pipe (PTX ex2.approx.f32; ex2(-inf) = +0).
+// exp2 on the MUFU pipe (PTX ex2.approx.ftz.f32: one instruction, subnormal results flush to
+// zero; ex2(-inf) = +0).
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
-    asm("ex2.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
 }
 
@@ -238,22 +281,22 @@ __device__ __forceinline__ float rcp_approx(float x) {
 // instruction count made the GEMM epilogues issue-bound.
 //
 // erf: Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26 (Hastings'
-// approximation): erf(x) = 1 − (a1·t + a2·t² + a3·t³ + a4·t⁴ + a5·t⁵)·e^(−x²),
-// t = 1 / (1 + p·x) for x ≥ 0, |error| ≤ 1.5e-7; odd symmetry for x < 0.
-__device__ __forceinline__ float erf_as(float x) {
-    const float ax = fabsf(x);
-    const float t = rcp_approx(fmaf(0.3275911f, ax, 1.0f));
-    float poly = fmaf(1.061405429f, t, -1.453152027f);
-    poly = fmaf(poly, t, 1.421413741f);
-    poly = fmaf(poly, t, -0.284496736f);
-    poly = fmaf(poly, t, 0.254829592f);
-    poly *= t;
-    const float e = ex2_approx(-1.4426950408889634f * ax * ax);  // e^(−x²)
-    return copysignf(fmaf(-poly, e, 1.0f), x);
-}
-// GELU(x) = x·Φ(x) = ½·x·(1 + erf(x/√2)).
+// approximation): erf(z) = 1 − (a1·t + a2·t² + a3·t³ + a4·t⁴ + a5·t⁵)·e^(−z²),
+// t = 1 / (1 + p·z) for z ≥ 0, |error| ≤ 1.5e-7.
+//
+// GELU(x) = x·Φ(x). With 7.1.26 at z = |x|/√2: 1 − Φ(|x|) = ½·erfc(z) = h,
+// h = ½·poly(t)·e^(−x²/2), t = 1 / (1 + p·z); Φ(x) = 1 − h for x ≥ 0 and h for x < 0.
 __device__ __forceinline__ float gelu_fast(float x) {
-    return 0.5f * x * (1.0f + erf_as(x * 0.70710678118654752f));
+    constexpr float kP = 0.3275911f * 0.70710678118654752f;
+    const float t = rcp_approx(fmaf(kP, fabsf(x), 1.0f));
+    float q = fmaf(0.5f * 1.061405429f, t, 0.5f * -1.453152027f);
+    q = fmaf(q, t, 0.5f * 1.421413741f);
+    q = fmaf(q, t, 0.5f * -0.284496736f);
+    q = fmaf(q, t, 0.5f * 0.254829592f);
+    q *= t;
+    const float h = q * ex2_approx(x * x * (-0.5f * 1.4426950408889634f));
+    const float xh = x * h;
+    return x >= 0.f ? x - xh : xh;
 }
 // tanh(x) = sign(x)·(1 − 2 / (e^(2|x|) + 1)); absolute error ~1e-7.
 __device__ __forceinline__ float tanh_fast(float x) {
