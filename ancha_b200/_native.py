@@ -28,7 +28,8 @@ EXPORTS = ("ancha_last_error", "ancha_version", "ancha_available", "ancha_attent
            "ancha_linear_fwd", "ancha_stft_fwd", "ancha_istft_masked", "ancha_istft_masked_static", "ancha_ola_add",
            "ancha_model_load", "ancha_model_info", "ancha_model_forward", "ancha_model_free",
            "ancha_separate", "ancha_separate_pcm", "ancha_separate_device",
-           "ancha_separate_status", "ancha_free_string")
+           "ancha_separate_status", "ancha_chunk_plan", "ancha_chunk_span", "ancha_separate_span",
+           "ancha_free_string")
 
 
 class AnchaError(RuntimeError):
@@ -101,6 +102,9 @@ def lib() -> C.CDLL:
                                          C.POINTER(i32), fp, C.POINTER(C.c_double)]),
             "ancha_separate_device": (i32, [vp, vp, i64, i64, i32, i32, vp, vp]),
             "ancha_separate_status": (i32, [vp, vp]),
+            "ancha_chunk_plan": (i32, [i64, i64, i32, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
+            "ancha_chunk_span": (i32, [i64, i64, i32, i64, i64, C.POINTER(i64), C.POINTER(i64)]),
+            "ancha_separate_span": (i32, [vp, fp, i64, i64, i32, i32, i64, i64, vp, fp, fp]),
             "ancha_free_string": (None, [vp]),
         }
         for name, (res, args) in sig.items():

@@ -346,6 +346,65 @@ extern "C" int ancha_separate_pcm(ancha_model* const* models, int n_models, cons
     return r.status;
 }
 
+extern "C" int ancha_chunk_plan(int64_t samples, int64_t chunk_samples, int overlap, int64_t* chunks,
+                                int64_t* border, int64_t* length) {
+    if (samples <= 0) return fail(ANCHA_E_INVALID, "audio is empty");
+    try {
+        const TrackPlan plan = make_plan(samples, chunk_samples, overlap);
+        if (chunks) *chunks = (int64_t)plan.starts.size();
+        if (border) *border = plan.border;
+        if (length) *length = plan.length;
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
+    }
+    return ANCHA_OK;
+}
+
+extern "C" int ancha_chunk_span(int64_t samples, int64_t chunk_samples, int overlap, int64_t first,
+                                int64_t last, int64_t* lo, int64_t* hi) {
+    if (samples <= 0 || !lo || !hi) return fail(ANCHA_E_INVALID, "chunk_span: invalid arguments");
+    try {
+        const TrackPlan plan = make_plan(samples, chunk_samples, overlap);
+        const int64_t n = (int64_t)plan.starts.size();
+        if (first < 0 || last > n || first > last) return fail(ANCHA_E_INVALID, "chunk_span: chunk range outside the plan");
+        if (first == last) {
+            *lo = *hi = 0;
+        } else {
+            *lo = plan.starts[first];
+            *hi = std::min(plan.starts[last - 1] + plan.chunk, plan.length);
+        }
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
+    }
+    return ANCHA_OK;
+}
+
+extern "C" int ancha_separate_span(ancha_model* model, const float* planes, int64_t samples,
+                                   int64_t chunk_samples, int overlap, int batch_chunks, int64_t first,
+                                   int64_t last, const volatile int* cancel, float* sums, float* weights) {
+    if (!model || !planes || !sums || !weights) return fail(ANCHA_E_INVALID, "separate_span: null argument");
+    Model& m = *model->impl;
+    const ModelConfig& c = m.manifest.config;
+    TrackPlan plan;
+    try {
+        plan = make_plan(samples, chunk_samples > 0 ? chunk_samples : c.chunk_samples,
+                         overlap > 0 ? overlap : c.overlap);
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
+    }
+    if (samples <= 0 || plan.chunk <= c.n_fft / 2) return fail(ANCHA_E_INVALID, "invalid chunk settings");
+    if (first < 0 || last > (int64_t)plan.starts.size() || first > last)
+        return fail(ANCHA_E_INVALID, "separate_span: chunk range outside the plan");
+    if (first == last) return ANCHA_OK;
+    int batch = batch_chunks > 0 ? std::min(batch_chunks, kMaxChunksPerCall) : 4;
+    Partial part;
+    run_device(m, planes, plan, (size_t)first, (size_t)last, batch, cancel, part);
+    if (part.status != ANCHA_OK) return fail(part.status, part.error);
+    std::copy(part.sums.begin(), part.sums.end(), sums);
+    std::copy(part.weights.begin(), part.weights.end(), weights);
+    return ANCHA_OK;
+}
+
 extern "C" int ancha_separate_device(ancha_model* model, const float* planes, int64_t samples,
                                      int64_t chunk_samples, int overlap, int batch_chunks,
                                      float* stems, void* stream) {

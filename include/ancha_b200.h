@@ -219,6 +219,28 @@ ANCHA_API int ancha_separate_pcm(ancha_model* const* models, int n_models, const
                        int64_t samples, int64_t chunk_samples, int overlap, int batch_chunks,
                        const volatile int* cancel, float* stems_out, double* seconds_out);
 
+/* Chunk plan of a `samples`-long track (chunk.rs:1-23, runtime.rs:103-111): number of
+ * chunks, reflect border and padded length. chunk_samples / overlap must be explicit here
+ * (the model defaults come from ancha_model_info). Host-only. */
+ANCHA_API int ancha_chunk_plan(int64_t samples, int64_t chunk_samples, int overlap, int64_t* chunks,
+                     int64_t* border, int64_t* length);
+
+/* Padded-track samples [*lo, *hi) covered by chunks [first, last) of that plan (both 0 for
+ * an empty range). Host-only. */
+ANCHA_API int ancha_chunk_span(int64_t samples, int64_t chunk_samples, int overlap, int64_t first,
+                     int64_t last, int64_t* lo, int64_t* hi);
+
+/* One shard of ancha_separate_pcm: chunks [first, last) of the plan of host planes[2][samples]
+ * on `model`'s GPU, returning their weighted overlap-add over the span of
+ * ancha_chunk_span (host sums[stems·2][hi − lo], weights[hi − lo]). Adding the spans of
+ * disjoint chunk ranges at their offsets, dividing by the summed weights and cropping the
+ * border gives the stems (chunk.rs:77-88, runtime.rs:210-225): this is how one track is
+ * split over processes, one per GPU (ancha_b200.distributed). chunk_samples / overlap 0 take
+ * the model defaults. */
+ANCHA_API int ancha_separate_span(ancha_model* model, const float* planes, int64_t samples,
+                        int64_t chunk_samples, int overlap, int batch_chunks, int64_t first,
+                        int64_t last, const volatile int* cancel, float* sums, float* weights);
+
 /* Device-resident form for one model: planes[2][samples] (device) → stems[stems][2][samples]
  * (device), everything enqueued on `stream` without a host synchronisation (the model's
  * pipeline buffers are allocated on the first call and reused). Status words (non-finite

@@ -152,3 +152,40 @@ def test_separate_task_writes_reference_outputs(tmp_path, mel_package):
     with pytest.raises(Exception):
         separate(SeparateOptions(inp, mel_package, str(tmp_path / "cancelled")), cancelled=flag)
     assert not os.path.exists(str(tmp_path / "cancelled"))
+
+
+def test_span_shards_combine_to_separate_pcm(mel_package):
+    """ancha_separate_span on two chunk ranges, placed at their spans and summed, gives the
+    single-call result; through a one-rank process group separate_distributed is identical."""
+    import datetime
+    import socket
+
+    import torch.distributed as dist
+
+    from ancha_b200.distributed import ChunkPlan, gpu_span, separate_distributed, shard
+    rng = np.random.default_rng(12)
+    planes = (rng.standard_normal((2, 132300)) * 0.1).astype(np.float32)
+    model = Roformer(mel_package, 0, "f16")
+    whole, _ = separate_pcm([model], planes, chunk_samples=22050, overlap=2, batch_chunks=3)
+    plan = ChunkPlan.of(planes.shape[1], 22050, 2)
+    span = gpu_span(model, batch_chunks=3)
+    sums = np.zeros((2, plan.length), np.float64)
+    weights = np.zeros(plan.length, np.float64)
+    for r in range(2):
+        first, last = shard(plan.chunks, r, 2)
+        s, w = span(planes, plan, first, last)
+        lo, hi = plan.span(first, last)
+        sums[:, lo:hi] += s
+        weights[lo:hi] += w
+    got = (sums / weights)[:, plan.border:plan.border + plan.samples]
+    assert np.max(np.abs(got - whole[0])) <= 1e-6 * max(1.0, np.max(np.abs(whole)))
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        one = separate_distributed(planes, plan, span, 2)
+    finally:
+        dist.destroy_process_group()
+    assert np.array_equal(one, whole)
