@@ -30,6 +30,24 @@ struct GemmEpilogue {
     // columns share the cosine and carry ∓sin. Lanes of a warp hold consecutive rows, so a
     // token-fastest table makes their loads coalesce. Null: the tensor-core path reads `rope`.
     const float* rope_pairs;
+    // Row-norm fusion (tensor-core path only; null / 0 = off). Sums of squares are kept per
+    // 32-column chunk, chunk-major: ss[c / 32][r] for an m-row output.
+    //   row_ss / row_ss_n: scale row r of A·Bᵀ by 1 / max(√Σ row_ss[r][·], 1e-12) before the
+    //     bias (A holds unnormalised rows; their unit norm is applied here instead);
+    //   res_ss / res_ss_n, res_col: the residual is read as res[r][c] · res_scale[r] · res_col[c]
+    //     with res_scale from res_ss like above (a row normalisation the producer deferred);
+    //   out16 / out16_col: also write the output, times out16_col[c] when set, in the operand
+    //     type (f16 / bf16) as a dense [m][n] copy, the next GEMM's A operand;
+    //   ss_out / ss16_out: write the per-chunk sums of squares of the output / of that copy.
+    const float* row_ss;
+    int row_ss_n;
+    const float* res_ss;
+    int res_ss_n;
+    const float* res_col;
+    void* out16;
+    const float* out16_col;
+    float* ss_out;
+    float* ss16_out;
 };
 
 // FFMA GEMM (fp32 accumulation). `groups` is a device array of `count` problems when

@@ -43,28 +43,44 @@ struct TcParams {
     const float* rope;
     const float2* rope_pairs;
     int rope_width, rope_tokens, rope_div, rope_hd;
+    const float* row_ss;     // row-norm fusion, see GemmEpilogue
+    int row_ss_n;
+    const float* res_ss;
+    int res_ss_n;
+    const float* res_col;
+    void* out16;
+    const float* out16_col;
+    float* ss_out;
+    float* ss16_out;
+    int ab16;                // operand type (ELT_BF16 / ELT_F16) of the out16 copy
     uint32_t idesc;
     int m_tiles, n_tiles, tiles;
     int* err;
 };
 
-constexpr int STAGE_BYTES = 4096;  // one 32-row × 128-byte epilogue staging buffer
+constexpr int STAGE_BYTES = 4096;    // one 32-row × 128-byte epilogue staging buffer
+constexpr int STAGE16_BYTES = 2048;  // one 32-row × 64-byte buffer for the 16-bit copy
+// One buffer per warp: a chunk waits for every store of the previous chunk (the output and the
+// 16-bit copy) to have read its source before it overwrites either buffer.
+static_assert(STAGE_BUFS == 1, "the row-norm copy shares the single-buffer wait");
 
 template <int BN, int STAGES>
 struct Smem {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int TILES = STAGES * (A_BYTES + B_BYTES);
     static constexpr int STAGING = EPI_WARPS * STAGE_BUFS * STAGE_BYTES;
-    static constexpr int BYTES = 1024 + TILES + STAGING + 8 * (2 * STAGES + 4) + 16;
+    static constexpr int STAGING16 = EPI_WARPS * STAGE16_BYTES;  // the row-norm fusion's copy
+    static constexpr int BYTES = 1024 + TILES + STAGING + STAGING16 + 8 * (2 * STAGES + 4) + 16;
 };
 
 // Bias, activation, RoPE and residual for 32 consecutive accumulator columns c0.. of one
 // row, in registers. Returns the number of output values (32, or 16 for GLU). All indexing
 // of the register arrays is static.
 __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, bool live, int c0, int n_g,
-                                          const uint32_t (&r)[32], float (&v)[32]) {
+                                          const uint32_t (&r)[32], float (&v)[32], float row_scale,
+                                          float res_scale) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * row_scale;
     const int nv = min(32, n_g - c0);  // valid columns (> 0)
     if (p.bias) {
         const float* b = p.bias + (int64_t)(g % p.b_groups) * p.bias_group_stride + c0;
@@ -123,19 +139,71 @@ __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, boo
     }
     if (p.residual && live) {
         const float* rr = p.residual + (int64_t)row * p.ldr + c0;
-        if (nv == 32) {
+        if (p.res_col && nv == 32) {
+            const float* rc = p.res_col + c0;
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
                 const float4 q = *reinterpret_cast<const float4*>(rr + j);
-                v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
+                const float4 w = *reinterpret_cast<const float4*>(rc + j);
+                v[j] = fmaf(q.x * res_scale, w.x, v[j]);
+                v[j + 1] = fmaf(q.y * res_scale, w.y, v[j + 1]);
+                v[j + 2] = fmaf(q.z * res_scale, w.z, v[j + 2]);
+                v[j + 3] = fmaf(q.w * res_scale, w.w, v[j + 3]);
+            }
+        } else if (p.res_col) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (j < nv) v[j] = fmaf(rr[j] * res_scale, p.res_col[c0 + j], v[j]);
+        } else if (nv == 32) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                const float4 q = *reinterpret_cast<const float4*>(rr + j);
+                v[j] = fmaf(q.x, res_scale, v[j]);
+                v[j + 1] = fmaf(q.y, res_scale, v[j + 1]);
+                v[j + 2] = fmaf(q.z, res_scale, v[j + 2]);
+                v[j + 3] = fmaf(q.w, res_scale, v[j + 3]);
             }
         } else {
 #pragma unroll
             for (int j = 0; j < 32; ++j)
-                if (j < nv) v[j] += rr[j];
+                if (j < nv) v[j] = fmaf(rr[j], res_scale, v[j]);
         }
     }
     return 32;
+}
+
+// 1 / max(√(Σ_i ss[i·rows]), 1e-12): the unit-norm factor of a row from its per-chunk partial
+// sums of squares, stored chunk-major so a warp's 32 rows read 128 contiguous bytes (the same
+// epsilon as the row-norm kernel).
+__device__ __forceinline__ float inv_norm(const float* ss, int n, int64_t rows) {
+    float t = 0.f;
+    for (int i = 0; i < n; ++i) t += ss[i * rows];
+    return 1.f / fmaxf(sqrtf(t), 1e-12f);
+}
+
+// Row-norm fusion: the sum of squares of 32 values of a row (chunk-major slot, so the warp's
+// 32 rows store 128 contiguous bytes); values past nv do not count.
+__device__ __forceinline__ void store_ss(float* ss, const TcParams& p, int row, bool live, int c0, int nv,
+                                         const float (&v)[32]) {
+    float q = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+        if (j < nv) q = fmaf(v[j], v[j], q);
+    if (live) ss[(int64_t)(c0 / 32) * p.m + row] = q;
+}
+
+// v ⊙ out16_col[c0 ..] in place (the row-norm fusion's copy of the output).
+__device__ __forceinline__ void scale_cols(const float* col, int c0, int nv, float (&v)[32]) {
+    if (nv == 32) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+            const float4 c = *reinterpret_cast<const float4*>(col + c0 + j);
+            v[j] *= c.x; v[j + 1] *= c.y; v[j + 2] *= c.z; v[j + 3] *= c.w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = j < nv ? v[j] * col[c0 + j] : 0.f;
+    }
 }
 
 // Write this lane's row of a 32-row staging buffer in the TMA swizzled layout: rows of
@@ -200,14 +268,15 @@ __device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int t, int bn
 template <int BN, int STAGES>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-               const __grid_constant__ CUtensorMap tma_out, const TcParams p) {
+               const __grid_constant__ CUtensorMap tma_out, const __grid_constant__ CUtensorMap tma_out16,
+               const TcParams p) {
     using S = Smem<BN, STAGES>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_tiles = smem;
     uint8_t* b_tiles = smem + STAGES * A_BYTES;
     uint8_t* staging = smem + S::TILES;
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILES + S::STAGING);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::TILES + S::STAGING + S::STAGING16);
     uint64_t* empty = full + STAGES;
     uint64_t* tfull = empty + STAGES;   // [2] accumulator ready
     uint64_t* tempty = tfull + 2;       // [2] accumulator drained
@@ -231,6 +300,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         prefetch_tma(&tma_a);
         prefetch_tma(&tma_b);
         prefetch_tma(&tma_out);
+        if (p.out16) prefetch_tma(&tma_out16);
     }
     if (warp == 1) {
         tmem_alloc(tmem_slot, TMEM_COLS);
@@ -299,6 +369,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         const int quarter = warp % 4;
         const int first = (warp - 2) / 4;
         uint8_t* my_stage = staging + (warp - 2) * STAGE_BUFS * STAGE_BYTES;
+        uint8_t* my_stage16 = staging + S::STAGING + (warp - 2) * STAGE16_BYTES;
         const bool glu = p.act == ANCHA_ACT_GLU;
         uint32_t local = 0, chunks = 0;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
@@ -312,6 +383,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             const int row = row0 + lane;
             const bool live = row < p.m;
             const uint32_t base = tmem + b * BN + ((uint32_t)(quarter * 32) << 16);
+            const float row_scale = p.row_ss && live ? inv_norm(p.row_ss + row, p.row_ss_n, p.m) : 1.f;
+            const float res_scale = p.res_ss && live ? inv_norm(p.res_ss + row, p.res_ss_n, p.m) : 1.f;
 #pragma unroll 1
             for (int col = first * 32; col < BN; col += PER_QUARTER * 32) {
                 uint32_t r[32];
@@ -319,7 +392,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 tmem_wait_ld();
                 if (c.n0 + col >= c.n_g) continue;  // warp-uniform
                 float v[32];
-                const int count = epilogue32(p, c.g, row, live, c.n0 + col, c.n_g, r, v);
+                const int count = epilogue32(p, c.g, row, live, c.n0 + col, c.n_g, r, v, row_scale, res_scale);
+                const int nv = min(32, c.n_g - (c.n0 + col));
+                if (p.ss_out && count == 32) store_ss(p.ss_out, p, row, live, c.n0 + col, nv, v);
                 uint8_t* buf = my_stage + (chunks % STAGE_BUFS) * STAGE_BYTES;
                 if (chunks >= STAGE_BUFS) {  // the store that last read this buffer is done with it
                     if (lane == 0) bulk_wait_read<STAGE_BUFS - 1>();
@@ -331,6 +406,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 if (lane == 0) {
                     tma_store_3d(&tma_out, buf, glu ? (c.n0 + col) / 2 : c.n0 + col, row0, c.g);
                     bulk_commit();
+                }
+                if (p.out16 && count == 32) {
+                    if (p.out16_col) scale_cols(p.out16_col, c.n0 + col, nv, v);
+                    if (p.ss16_out) store_ss(p.ss16_out, p, row, live, c.n0 + col, nv, v);
+                    uint8_t* buf16 = my_stage16;
+                    stage_row(buf16, lane, p.ab16, 32, v);
+                    fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_3d(&tma_out16, buf16, c.n0 + col, row0, 0);
+                        bulk_commit();
+                    }
                 }
                 ++chunks;
             }
@@ -351,7 +438,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
 }
 
 template <int BN, int STAGES>
-int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const TcParams& p, cudaStream_t s) {
+int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& to16,
+           const TcParams& p, cudaStream_t s) {
     using S = Smem<BN, STAGES>;
     static bool configured[64] = {};
     static int sms[64] = {};
@@ -364,22 +452,19 @@ int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, 
         configured[dev & 63] = true;
     }
     const int grid = std::max(1, std::min(p.tiles, sms[dev & 63]));
-    gemm_tc_kernel<BN, STAGES><<<grid, THREADS, S::BYTES, s>>>(ta, tb, to, p);
+    gemm_tc_kernel<BN, STAGES><<<grid, THREADS, S::BYTES, s>>>(ta, tb, to, to16, p);
     return check_launch("gemm_tc");
 }
 
-// Output tile width: the widest of 256 / 192 / 128 that wastes least of the padded N.
+// Output tile width: the widest of 256 / 192 / 128 whose padded N is within 1/6 of the least
+// padded N. Wider tiles amortise the per-tile main-loop and epilogue overheads; a mostly empty
+// last tile costs its main loop but almost no epilogue work (empty chunks are skipped).
 int pick_bn(int n) {
-    int best = 128;
-    int64_t best_pad = ceil_div(n, 128) * 128;
-    for (int bn : {192, 256}) {
-        const int64_t pad = ceil_div(n, bn) * bn;
-        if (pad <= best_pad) {
-            best = bn;
-            best_pad = pad;
-        }
-    }
-    return best;
+    int64_t least = INT64_MAX;
+    for (int bn : {128, 192, 256}) least = std::min<int64_t>(least, ceil_div(n, bn) * bn);
+    for (int bn : {256, 192, 128})
+        if (ceil_div(n, bn) * bn * 6 <= least * 7) return bn;
+    return 128;
 }
 
 int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64_t ldb,
@@ -394,6 +479,11 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
     const int64_t ogs = p.groups > 1 ? p.out_group_stride : (int64_t)p.m * p.ldo;
     ANCHA_TRY(make_tma_store_3d(&to, p.out, p.out_type, std::min<int64_t>(out_cols, p.ldo), p.m, p.groups, p.ldo,
                                 ogs, glu ? 16 : 32, 32));
+    CUtensorMap to16 = to;  // unused unless the row-norm fusion writes its copy
+    if (p.out16) {
+        if (p.groups != 1) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: row-norm fusion on grouped problems");
+        ANCHA_TRY(make_tma_store_3d(&to16, p.out16, ab_type, p.n, p.m, 1, p.n, (int64_t)p.m * p.n, 32, 32));
+    }
     p.idesc = umma_idesc_f16(ab_type == ELT_BF16, BM, bn);
     p.err = device_error_word();
     p.m_tiles = (int)ceil_div(p.m, BM);
@@ -402,9 +492,9 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
     if (tiles > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: too many tiles");
     p.tiles = (int)tiles;
     switch (bn) {
-        case 256: return launch<256, 3>(ta, tb, to, p, s);
-        case 192: return launch<192, 3>(ta, tb, to, p, s);
-        default: return launch<128, 4>(ta, tb, to, p, s);
+        case 256: return launch<256, 3>(ta, tb, to, to16, p, s);
+        case 192: return launch<192, 3>(ta, tb, to, to16, p, s);
+        default: return launch<128, 4>(ta, tb, to, to16, p, s);
     }
 }
 
@@ -418,8 +508,11 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     const size_t oe = elt_size(e.out_type);
     if (!aligned16(g.out) || (g.ldo * oe) % 16 || (g.residual && (!aligned16(g.residual) || (g.ldr * 4) % 16)) ||
         (g.bias && !aligned16(g.bias)) || (e.rope && (!aligned16(e.rope) || e.rope_hd % 32)) ||
-        (e.rope_pairs && (!aligned16(e.rope_pairs) || e.rope_hd % 32)))
+        (e.rope_pairs && (!aligned16(e.rope_pairs) || e.rope_hd % 32)) ||
+        (e.out16 && (!aligned16(e.out16) || g.n % 8)) || (e.res_col && !aligned16(e.res_col)))
         return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: epilogue operands not 16-byte aligned");
+    if ((e.res_ss && !g.residual) || e.act == ANCHA_ACT_GLU && (e.out16 || e.ss_out))
+        return fail(ANCHA_E_INVALID, "gemm_tc: row-norm fusion operands without their epilogue");
     TcParams p{};
     p.m = g.m; p.n = g.n; p.k = g.k; p.groups = 1; p.b_groups = 1; p.group_n = nullptr;
     p.out = g.out; p.ldo = g.ldo; p.out_group_stride = 0;
@@ -429,6 +522,9 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     p.rope = e.rope; p.rope_width = e.rope_width; p.rope_tokens = e.rope_tokens;
     p.rope_pairs = reinterpret_cast<const float2*>(e.rope_pairs);
     p.rope_div = e.rope_div; p.rope_hd = e.rope_hd;
+    p.row_ss = e.row_ss; p.row_ss_n = e.row_ss_n; p.res_ss = e.res_ss; p.res_ss_n = e.res_ss_n;
+    p.res_col = e.res_col; p.out16 = e.out16; p.out16_col = e.out16_col;
+    p.ss_out = e.ss_out; p.ss16_out = e.ss16_out; p.ab16 = ab_type;
     return run(g.a, g.lda, (int64_t)g.m * g.lda, g.b, g.ldb, (int64_t)g.n * g.ldb, p, ab_type, s);
 }
 

@@ -232,6 +232,7 @@ std::unique_ptr<Model> Model::load(const std::string& package, int device, int p
     m->device = device;
     m->precision = precision;
     m->elt_ = precision == ANCHA_PRECISION_BF16 ? ELT_BF16 : precision == ANCHA_PRECISION_F16 ? ELT_F16 : ELT_F32;
+    m->fuse_norms_ = m->elt_ != ELT_F32 && m->manifest.config.dim % 32 == 0;
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) m->device_name = prop.name;
     m->manifest = Manifest::from_json(Json::parse(read_file(package + "/manifest.json")));
@@ -431,6 +432,11 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
         w.h2.alloc(R * mh * e);
         w.z.alloc((int64_t)chunks * frames * total_width * 4);
         w.glu.alloc(R * max_width * 4);
+        if (fuse_norms_) {
+            w.ss_x.alloc(R * (c.dim / 32) * 4);
+            w.ss_y.alloc(R * (c.dim / 32) * 4);
+            w.ss_yg.alloc(R * (c.dim / 32) * 4);
+        }
         if (!flag_.p) {
             flag_.alloc(16);
             if (cudaMemset(flag_.p, 0, 16) != cudaSuccess) bad("cudaMemset");
@@ -539,6 +545,14 @@ int Model::linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias
                   const float* residual, int64_t ldr, void* out, int64_t ldo, int out_type,
                   int64_t m, int n, int k, int act, const float* rope, const float* rope_pairs,
                   int rope_tokens, int rope_div, cudaStream_t s) {
+    return linear_fused(x, ldx, w, bias, residual, ldr, out, ldo, out_type, m, n, k, act, rope, rope_pairs,
+                        rope_tokens, rope_div, NormFusion{}, s);
+}
+
+int Model::linear_fused(const void* x, int64_t ldx, const DevBuf& w, const float* bias, const float* residual,
+                        int64_t ldr, void* out, int64_t ldo, int out_type, int64_t m, int n, int k, int act,
+                        const float* rope, const float* rope_pairs, int rope_tokens, int rope_div,
+                        const NormFusion& nf, cudaStream_t s) {
     GemmGroup g{};
     g.a = x;
     g.lda = ldx;
@@ -562,9 +576,22 @@ int Model::linear(const void* x, int64_t ldx, const DevBuf& w, const float* bias
     e.rope_tokens = rope_tokens;
     e.rope_div = rope_div;
     e.rope_hd = c.head_dim;
+    const int slots = c.dim / 32;
+    e.row_ss = nf.row_ss;
+    e.row_ss_n = nf.row_ss ? slots : 0;
+    e.res_ss = nf.res_ss;
+    e.res_ss_n = nf.res_ss ? slots : 0;
+    e.res_col = nf.res_col;
+    e.out16 = nf.out16;
+    e.out16_col = nf.out16_col;
+    e.ss_out = nf.ss_out;
+    e.ss16_out = nf.ss16_out;
+    const bool fused = nf.row_ss || nf.res_ss || nf.out16 || nf.ss_out;
     if (elt_ != ELT_F32) {
         const int st = gemm_tc(g, elt_, e, s);
         if (st != ANCHA_E_UNSUPPORTED) return st;
+        // The FFMA kernel has no row-norm fusion: a fused call must not fall back.
+        if (fused) return fail(ANCHA_E_UNSUPPORTED, "linear: row-norm fusion needs the tensor-core GEMM");
     }
     return gemm_ffma(g, nullptr, 1, (int)m, n, elt_, elt_, 1, e, s);
 }
@@ -578,12 +605,19 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
     float* x = ws_.x.as<float>();
     const size_t rope_slot = (size_t)t.rope_set * 2 + (time_axis ? 0 : 1);
     const DevBuf& rope = ws_.rope[rope_slot];
-    // Packed q | k | v | gate projection of unit_norm(x), RoPE in the epilogue.
-    ANCHA_TRY(norm_rows(x, dim, nullptr, ws_.xn.p, bf, dim, R, dim, s));
-    ANCHA_TRY(linear(ws_.xn.p, dim, t.wqkvg, t.bqkvg.as<float>(), nullptr, 0, ws_.qkvg.p, ldq, bf,
-                     R, 3 * inner + c.heads, dim, ANCHA_ACT_NONE, rope.as<float>(),
-                     ws_.rope_pairs[rope_slot].as<float>(),
-                     time_axis ? T : bands, time_axis ? 1 : T, s));
+    // Packed q | k | v | gate projection of unit_norm(x), RoPE in the epilogue. With the
+    // row-norm fusion the previous block left x's operand-type copy in xn and its row norms in
+    // block_ss_, and the GEMM applies the unit norm to its output rows.
+    NormFusion g1;
+    if (fuse_norms_ && block_ss_) {
+        g1.row_ss = block_ss_;
+    } else {
+        ANCHA_TRY(norm_rows(x, dim, nullptr, ws_.xn.p, bf, dim, R, dim, s));
+    }
+    ANCHA_TRY(linear_fused(ws_.xn.p, dim, t.wqkvg, t.bqkvg.as<float>(), nullptr, 0, ws_.qkvg.p, ldq, bf,
+                           R, 3 * inner + c.heads, dim, ANCHA_ACT_NONE, rope.as<float>(),
+                           ws_.rope_pairs[rope_slot].as<float>(), time_axis ? T : bands, time_axis ? 1 : T,
+                           g1, s));
     // Gated attention within each group.
     AttnArgs a{};
     a.q = a.k = a.v = a.gate = ws_.qkvg.p;
@@ -616,7 +650,39 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
     int ast = bf != ELT_F32 ? attention_tc(a, s) : ANCHA_E_UNSUPPORTED;
     if (ast == ANCHA_E_UNSUPPORTED) ast = attention_ffma(a, s);
     ANCHA_TRY(ast);
-    // Output projection + residual, then the GELU feed-forward + residual.
+    // Output projection + residual (with the SourceNorm the previous block deferred), then the
+    // GELU feed-forward + residual.
+    if (fuse_norms_) {
+        NormFusion g2;
+        if (pending_scale_) {
+            g2.res_ss = ws_.ss_y.as<float>();
+            g2.res_col = pending_scale_;
+        }
+        g2.out16 = ws_.xn.p;
+        g2.ss_out = ws_.ss_x.as<float>();
+        ANCHA_TRY(linear_fused(ws_.att.p, inner, t.wout, nullptr, x, dim, x, dim, ELT_F32, R, dim, inner,
+                               ANCHA_ACT_NONE, nullptr, nullptr, 1, 1, g2, s));
+        pending_scale_ = nullptr;
+        NormFusion g3;
+        g3.row_ss = ws_.ss_x.as<float>();
+        ANCHA_TRY(linear_fused(ws_.xn.p, dim, t.w1, t.b1.as<float>(), nullptr, 0, ws_.hidden.p, hidden, bf,
+                               R, hidden, dim, ANCHA_ACT_GELU, nullptr, nullptr, 1, 1, g3, s));
+        // Block output y: stored unnormalised; the next block's operand copy and row norms are
+        // written here, and Mel's SourceNorm (y / ‖y‖ · scale, roformer.rs:516-519) is applied
+        // when y is next read as a residual.
+        NormFusion g4;
+        g4.out16 = ws_.xn.p;
+        g4.ss_out = ws_.ss_y.as<float>();
+        if (t.out_scale.p) {
+            g4.out16_col = t.out_scale.as<float>();
+            g4.ss16_out = ws_.ss_yg.as<float>();
+        }
+        ANCHA_TRY(linear_fused(ws_.hidden.p, hidden, t.w2, t.b2.as<float>(), x, dim, x, dim, ELT_F32, R, dim,
+                               hidden, ANCHA_ACT_NONE, nullptr, nullptr, 1, 1, g4, s));
+        block_ss_ = t.out_scale.p ? ws_.ss_yg.as<float>() : ws_.ss_y.as<float>();
+        pending_scale_ = t.out_scale.p ? t.out_scale.as<float>() : nullptr;
+        return ANCHA_OK;
+    }
     ANCHA_TRY(linear(ws_.att.p, inner, t.wout, nullptr, x, dim, x, dim, ELT_F32, R, dim, inner,
                      ANCHA_ACT_NONE, nullptr, nullptr, 1, 1, s));
     ANCHA_TRY(norm_rows(x, dim, nullptr, ws_.xn.p, bf, dim, R, dim, s));
@@ -672,12 +738,18 @@ int Model::forward(const float* spectrum, int chunks, int frames, float* masks,
                             e, s));
     }
     // Axial stack (network.rs:333-339).
+    block_ss_ = nullptr;
+    pending_scale_ = nullptr;
     for (auto& layer : layers_) {
         if (cancelled()) return fail(ANCHA_E_CANCELLED, "task cancelled");
         ANCHA_TRY(transformer(layer[0], true, s));
         ANCHA_TRY(transformer(layer[1], false, s));
     }
     float* x = ws_.x.as<float>();
+    if (pending_scale_)  // the last block's SourceNorm, deferred by the row-norm fusion
+        ANCHA_TRY(norm_rows(x, c.dim, pending_scale_, nullptr, 0, 0, R, c.dim, s));
+    block_ss_ = nullptr;
+    pending_scale_ = nullptr;
     if (final_scale_.p)  // BS final norm (network.rs:340-342)
         ANCHA_TRY(norm_rows(x, c.dim, final_scale_.as<float>(), nullptr, 0, 0, R, c.dim, s));
     // Mask estimators (network.rs:364-398): the input is x itself (f32) or its bf16 / f16 copy.

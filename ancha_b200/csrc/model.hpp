@@ -73,6 +73,10 @@ struct MaskWeights {
 struct Workspace {
     int chunks = 0, frames = 0;
     DevBuf x, xn, qkvg, att, hidden, h2, z, glu;
+    // Row-norm fusion (16-bit modes): per-row, per-32-column sums of squares [rows][dim / 32]
+    // of x after the attention residual (ss_x), of the block output y (ss_y) and of y ⊙ the
+    // SourceNorm scale (ss_yg).
+    DevBuf ss_x, ss_y, ss_yg;
     DevBuf split_groups, mask_groups, glu_groups;
     std::vector<DevBuf> rope;        // per rope set: [time table, band table], [4, tokens, hd]
     std::vector<DevBuf> rope_pairs;  // the same tables pair-major: [2, hd / 2, tokens] × float2
@@ -118,6 +122,28 @@ private:
                int64_t m, int n, int k, int act, const float* rope, const float* rope_pairs,
                int rope_tokens, int rope_div, cudaStream_t s);
     int transformer(const TransformerWeights& t, bool time_axis, cudaStream_t s);
+
+    // Operands of the row-norm fusion for one linear() call (null = not used); see GemmEpilogue.
+    struct NormFusion {
+        const float* row_ss = nullptr;
+        const float* res_ss = nullptr;
+        const float* res_col = nullptr;
+        void* out16 = nullptr;
+        const float* out16_col = nullptr;
+        float* ss_out = nullptr;
+        float* ss16_out = nullptr;
+    };
+    int linear_fused(const void* x, int64_t ldx, const DevBuf& w, const float* bias, const float* residual,
+                     int64_t ldr, void* out, int64_t ldo, int out_type, int64_t m, int n, int k, int act,
+                     const float* rope, const float* rope_pairs, int rope_tokens, int rope_div,
+                     const NormFusion& nf, cudaStream_t s);
+    // Whether the unit norms run fused into the GEMMs (16-bit modes, dim a multiple of 32),
+    // and the state the fusion carries from one transformer block to the next: ws_.xn holds
+    // the unnormalised next block input (row norms in block_ss_), and x still needs the
+    // deferred SourceNorm (x · 1/‖x‖ · pending_scale_) before it is read as a residual.
+    bool fuse_norms_ = false;
+    const float* block_ss_ = nullptr;
+    const float* pending_scale_ = nullptr;
 
     std::vector<int> width_, offset_;
     DevBuf zcols_, zoffsets_, wsplit_, bsplit_;
