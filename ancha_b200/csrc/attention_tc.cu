@@ -401,11 +401,12 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             bool ok = mbar_wait(q_full, 0, abort, p.err) && mbar_wait(&kv_full[0], 0, abort, p.err);
             for (int t = 0; ok && t < ntiles; ++t) ok = issue_s(t, 0);
             for (int j = 0; ok && j < nkb; ++j) {
-                if (j + 1 < nkb) {
+                if (j + 1 < nkb)
                     ok = mbar_wait(&kv_full[(j + 1) % PP_KV_STAGES], ((j + 1) / PP_KV_STAGES) & 1, abort, p.err);
-                    for (int t = 0; ok && t < ntiles; ++t) ok = issue_s(t, j + 1);
+                for (int t = 0; ok && t < ntiles; ++t) {
+                    if (j + 1 < nkb) ok = issue_s(t, j + 1);
+                    if (ok) ok = issue_pv(t, j);
                 }
-                for (int t = 0; ok && t < ntiles; ++t) ok = issue_pv(t, j);
                 if (ok) umma_commit(&kv_empty[j % PP_KV_STAGES]);  // fires once both P·V are done
             }
         }
@@ -452,42 +453,40 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                     m_used = m_blk;
                     l *= corr;
                 }
-                // P = 2^(s·log2 e − m_used) as 16-bit pairs, in two halves of 64 keys.
+                // P = 2^(s·log2 e − m_used) as 16-bit pairs, all 128 keys in registers before the
+                // wait for P(kb − 1)·V, which then has had the whole exponential pass to finish.
                 float sum0 = 0.f, sum1 = 0.f;
+                uint32_t pk[2][32];
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    uint32_t pk[32];
-#pragma unroll
-                    for (int j = 0; j < 64; j += 2) {
-                        const int c = h * 64 + j;
-                        const float e0 = ex2_approx(fmaf(__uint_as_float(s[c / 32][c % 32]), LOG2E, -m_used));
-                        const float e1 = ex2_approx(fmaf(__uint_as_float(s[c / 32][c % 32 + 1]), LOG2E, -m_used));
-                        sum0 += e0;
-                        sum1 += e1;
-                        pk[j / 2] = pack2<BF16>(e0, e1);
-                    }
-                    if (h == 0 && kb > 0) {
-                        // P(kb − 1)·V must have finished reading P before it is overwritten,
-                        // and O must hold it before a rescale.
-                        ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (kb - 1) & 1, abort, p.err));
-                        if (!ok) break;
-                        tc_fence_after();
-                        if (__any_sync(0xffffffffu, corr != 1.f)) {
-                            uint32_t o[2][32];
-                            tmem_ld32(o_addr, o[0]);
-                            tmem_ld32(o_addr + 32, o[1]);
-                            tmem_wait_ld();
-#pragma unroll
-                            for (int d = 0; d < 32; ++d) {
-                                o[0][d] = __float_as_uint(__uint_as_float(o[0][d]) * corr);
-                                o[1][d] = __float_as_uint(__uint_as_float(o[1][d]) * corr);
-                            }
-                            tmem_st32(o_addr, o[0]);
-                            tmem_st32(o_addr + 32, o[1]);
-                        }
-                    }
-                    tmem_st32(p_addr + h * 32, pk);
+                for (int j = 0; j < TILE; j += 2) {
+                    const float e0 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32]), LOG2E, -m_used));
+                    const float e1 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32 + 1]), LOG2E, -m_used));
+                    sum0 += e0;
+                    sum1 += e1;
+                    pk[j / 64][(j % 64) / 2] = pack2<BF16>(e0, e1);
                 }
+                if (kb > 0) {
+                    // P(kb − 1)·V must have finished reading P before it is overwritten, and O
+                    // must hold it before a rescale.
+                    ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (kb - 1) & 1, abort, p.err));
+                    if (!ok) break;
+                    tc_fence_after();
+                    if (__any_sync(0xffffffffu, corr != 1.f)) {
+                        uint32_t o[2][32];
+                        tmem_ld32(o_addr, o[0]);
+                        tmem_ld32(o_addr + 32, o[1]);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int d = 0; d < 32; ++d) {
+                            o[0][d] = __float_as_uint(__uint_as_float(o[0][d]) * corr);
+                            o[1][d] = __float_as_uint(__uint_as_float(o[1][d]) * corr);
+                        }
+                        tmem_st32(o_addr, o[0]);
+                        tmem_st32(o_addr + 32, o[1]);
+                    }
+                }
+                tmem_st32(p_addr, pk[0]);
+                tmem_st32(p_addr + 32, pk[1]);
                 if (!ok) break;
                 l += sum0 + sum1;
                 tmem_wait_st();

@@ -88,6 +88,7 @@ struct PipelineBuffers {
     int batch = 0;
     int64_t chunk = 0;
     DevBuf audio, packed, masks, scratch, y, flag, acc;
+    DevBuf pcm, span;  // host-PCM separations: the uploaded track and the span accumulators
 };
 
 class Model {

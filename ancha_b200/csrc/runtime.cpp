@@ -136,21 +136,24 @@ void run_device(Model& model, const float* planes, const TrackPlan& plan, size_t
     const int64_t span = out.hi - out.lo;
     int st = ANCHA_OK;
     try {
-        DevBuf d_planes, d_sums, d_weights;
-        d_planes.alloc(2 * plan.samples * 4);
-        d_sums.alloc((size_t)planes_n * span * 4);
-        d_weights.alloc((size_t)span * 4);
-        st = cudaMemcpyAsync(d_planes.p, planes, 2 * plan.samples * 4, cudaMemcpyHostToDevice, s) == cudaSuccess
+        // Device copies of the track and the span accumulators are cached on the model (grown
+        // as needed): a per-call cudaMalloc / cudaFree pair would synchronise the device.
+        PipelineBuffers& pb = model.pipe;
+        if (pb.pcm.bytes < (size_t)(2 * plan.samples * 4)) pb.pcm.alloc(2 * plan.samples * 4);
+        if (pb.span.bytes < (size_t)(planes_n + 1) * span * 4) pb.span.alloc((size_t)(planes_n + 1) * span * 4);
+        float* d_planes = pb.pcm.as<float>();
+        float* d_sums = pb.span.as<float>();
+        float* d_weights = d_sums + (size_t)planes_n * span;
+        st = cudaMemcpyAsync(d_planes, planes, 2 * plan.samples * 4, cudaMemcpyHostToDevice, s) == cudaSuccess
                  ? ANCHA_OK : fail(ANCHA_E_CUDA, "upload PCM");
-        if (!st) st = cudaMemsetAsync(d_sums.p, 0, (size_t)planes_n * span * 4, s) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "memset");
-        if (!st) st = cudaMemsetAsync(d_weights.p, 0, (size_t)span * 4, s) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "memset");
-        if (!st) st = run_chunks(model, d_planes.as<float>(), plan, i0, i1, batch, out.lo, span,
-                                 d_sums.as<float>(), d_weights.as<float>(), cancel, s, &out.model_seconds);
+        if (!st) st = cudaMemsetAsync(d_sums, 0, (size_t)(planes_n + 1) * span * 4, s) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "memset");
+        if (!st) st = run_chunks(model, d_planes, plan, i0, i1, batch, out.lo, span, d_sums, d_weights, cancel, s,
+                                 &out.model_seconds);
         if (!st) {
             out.sums.resize((size_t)planes_n * span);
             out.weights.resize((size_t)span);
-            cudaMemcpyAsync(out.sums.data(), d_sums.p, out.sums.size() * 4, cudaMemcpyDeviceToHost, s);
-            cudaMemcpyAsync(out.weights.data(), d_weights.p, out.weights.size() * 4, cudaMemcpyDeviceToHost, s);
+            cudaMemcpyAsync(out.sums.data(), d_sums, out.sums.size() * 4, cudaMemcpyDeviceToHost, s);
+            cudaMemcpyAsync(out.weights.data(), d_weights, out.weights.size() * 4, cudaMemcpyDeviceToHost, s);
             st = pipeline_status(model, s);
         }
         cudaError_t e = cudaStreamSynchronize(s);

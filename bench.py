@@ -16,6 +16,12 @@ independent, so ranks shard the work with no collective ("scaling": "weak").
 * ``e2e``: the same through ``ancha_separate_pcm`` (host PCM in, host stems out, host↔device
   copies inside the timed region).
 * ``roofline``: the dominant kernel re-launched alone with CUDA events.
+* ``attention``: BASELINE config 2, the fused attention alone (time axis T = 801 / 1601 / 3201
+  and the band axis S = 60) in the bench dtype, and the fp32 (FFMA) variant at T = 801.
+* ``config3``: BASELINE config 3, BS-RoFormer dim 512, depth 12, 8×64 heads, 62 bands, hop 512,
+  bf16, one 180 s track (chunk 352800, overlap 2 → 47 chunks) sharded over the ranks
+  (``ancha_b200.distributed``: each rank separates its chunk range, one reduce of the spans);
+  host PCM in, host stems out on rank 0, wall clock, ``"scaling": "strong"``.
 * ``cpu_baseline``: the numpy oracle (f32, all host cores) on one native chunk (rank 0, N=1).
 * ``--impl reference`` times that CPU port per step instead (the reference itself is Rust and
   cannot be built offline).
@@ -50,7 +56,49 @@ def parse():
     p.add_argument("--batch", type=int, default=4)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--package", default=os.environ.get("ANCHA_BENCH_PACKAGE", "/tmp/ancha_bench/mel-seed0"))
+    p.add_argument("--no-config3", action="store_true")
+    p.add_argument("--pipeline-only", action="store_true",
+                   help="run only the warm-up and timed pipeline steps (for launch-list captures)")
     return p.parse_args()
+
+
+def config3(local: int, world: int, rank: int, dist, steps: int = 2):
+    """BASELINE config 3 (see the module docstring); returns the JSON block on rank 0."""
+    from ancha_b200.config import ModelConfig
+    from ancha_b200.distributed import ChunkPlan, gpu_span, separate_distributed
+    from ancha_b200.model import Roformer
+    pkg = "/tmp/ancha_bench/bs512-seed0"
+    ensure_package(pkg, rank if world == 1 else int(os.environ.get("LOCAL_RANK", "0")),
+                   ModelConfig.bs_roformer_512())
+    model = Roformer(pkg, local, "bf16")
+    planes = track(180.0, 3000)
+    plan = ChunkPlan.of(planes.shape[1], model.chunk_samples, model.overlap)
+    span = gpu_span(model, batch_chunks=4)
+
+    def run():
+        if dist:
+            return separate_distributed(planes, plan, span, model.stems * 2)
+        sums, weights = span(planes, plan, 0, plan.chunks)
+        return (sums / weights)[:, plan.border:plan.border + plan.samples]
+
+    run()
+    times = []
+    for _ in range(steps):
+        if dist:
+            dist.barrier()
+        t0 = time.perf_counter()
+        out = run()
+        times.append(time.perf_counter() - t0)
+    model.close()
+    t = float(np.median(times))  # rank 0's clock includes the reduce, i.e. the slowest rank
+    if rank != 0:
+        return None
+    assert out is not None and np.all(np.isfinite(out))
+    return {"workload": "bs-roformer dim512 depth12 8x64 heads, 62 bands, hop 512, bf16, 180 s track, "
+                        f"chunk {plan.chunk_samples}, overlap {plan.overlap} ({plan.chunks} chunks) sharded "
+                        f"over {world} GPU(s)", "value": 180.0 / t, "unit": "×realtime",
+            "seconds_per_track": t, "steps": steps, "scaling": "strong", "dtype": "bf16",
+            "timing": "wall clock, host PCM in, host stems out on rank 0, median of steps"}
 
 
 def peaks():
@@ -62,13 +110,13 @@ def peaks():
         return 6650.0, 1590.0, 1400.0, "fallback"
 
 
-def ensure_package(path: str, rank: int):
+def ensure_package(path: str, rank: int, config=None):
     from ancha_b200 import synthetic
     from ancha_b200.config import ModelConfig
     done = os.path.join(path, "manifest.json")
     if rank == 0 and not os.path.exists(done):
         tmp = path + f".tmp{os.getpid()}"
-        synthetic.seeded_package(tmp, ModelConfig.mel_karaoke())
+        synthetic.seeded_package(tmp, config or ModelConfig.mel_karaoke())
         os.makedirs(os.path.dirname(path), exist_ok=True)
         os.replace(tmp, path)
     while not os.path.exists(done):
@@ -241,6 +289,14 @@ def main():
         N.check(L.ancha_separate_status(model.handle, C.c_void_p(stream.cuda_stream)))
         barrier()
     ms = ev0.elapsed_time(ev1) / a.steps
+    if a.pipeline_only:
+        if rank == 0:
+            print(json.dumps({"pipeline_only": True, "ms_per_step": ms, "chunks": chunks}), flush=True)
+        model.close()
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     t = torch.tensor([ms], device=f"cuda:{local}")
     if dist:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -287,23 +343,50 @@ def main():
     achieved = flops / (kms / 1e3) / 1e12
     roofline = {"kernel": "ffn_in linear (gemm, bias+GELU epilogue)", "bound": "tensor",
                 "achieved": achieved, "peak": tc_peak, "unit": "TFLOP/s", "frac": achieved / tc_peak,
-                "peak_kind": peak_kind, "traffic": None,
+                "peak_kind": peak_kind,
+                # DRAM bytes of one launch from an ncu capture of the same shape (cold cache);
+                # profiles/gemm_tc_ffn_in_gelu.md has the command and the counters.
+                "traffic": 132.94e6, "traffic_unit": "bytes per launch (dram read + write, ncu)",
                 "algorithmic": f"2·{rows}·384·1536 flop per launch"}
 
-    # Fused attention alone (time axis T=801).
-    q = torch.randn(60, 801, 8, 64, device=f"cuda:{local}").to(x.dtype)
-    for _ in range(3):
-        fused.attention(q, q, q)
-    torch.cuda.synchronize()
-    e0.record()
-    for _ in range(reps):
-        fused.attention(q, q, q)
-    e1.record()
-    torch.cuda.synchronize()
-    ams = e0.elapsed_time(e1) / reps
-    attn_tf = 4.0 * 60 * 8 * 801 * 801 * 64 / (ams / 1e3) / 1e12
-    attention = {"shape": "[B=60, H=8, T=801, D=64]", "ms": ams, "tflops": attn_tf,
-                 "frac": attn_tf / tc_peak, "peak_kind": peak_kind}
+    # Fused attention alone: time axis T = 801 / 1601 / 3201, band axis S = 60
+    # (gated, in the model's packed layout), and the fp32 variant at T = 801.
+    def time_attn(fn, reps=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    sweep = []
+    for T in (801, 1601, 3201):
+        q = torch.randn(60, T, 8, 64, device=f"cuda:{local}").to(x.dtype)
+        ms_t = time_attn(lambda q=q: fused.attention(q, q, q))
+        tf = 4.0 * 60 * 8 * T * T * 64 / (ms_t / 1e3) / 1e12
+        sweep.append({"axis": "time", "shape": f"[B=60, H=8, T={T}, D=64]", "dtype": a.precision, "ms": ms_t,
+                      "tflops": tf, "frac": tf / tc_peak})
+    q = torch.randn(60, 801, 8, 64, device=f"cuda:{local}")
+    ms_t = time_attn(lambda q=q: fused.attention(q, q, q), reps=3)
+    tf = 4.0 * 60 * 8 * 801 * 801 * 64 / (ms_t / 1e3) / 1e12
+    sweep.append({"axis": "time", "shape": "[B=60, H=8, T=801, D=64]", "dtype": "f32 (FFMA)", "ms": ms_t,
+                  "tflops": tf})
+    packed = torch.randn(801, 60, 3 * 512 + 8, device=f"cuda:{local}").to(x.dtype)
+    # Band axis in the model's layout is exercised by the model; standalone, [B=801, S=60] with
+    # the gate columns of the packed projection.
+    ms_t = time_attn(lambda: fused.gated_attention(packed, 8))
+    moved = 801 * 60 * ((3 * 512 + 8) + 512) * 2
+    sweep.append({"axis": "band", "shape": "[B=801, H=8, S=60, D=64] gated", "dtype": a.precision, "ms": ms_t,
+                  "tflops": 4.0 * 801 * 8 * 60 * 60 * 64 / (ms_t / 1e3) / 1e12,
+                  "gbs": moved / (ms_t / 1e3) / 1e9, "hbm_frac": moved / (ms_t / 1e3) / 1e9 / hbm})
+    attention = dict(sweep[0], sweep=sweep[1:])
+
+    c3 = None
+    if not a.no_config3:
+        c3 = config3(local, world, rank, dist)
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -327,7 +410,7 @@ def main():
                        "l2": "working set > 126 MB L2 (no flush)", "parallelism": f"chunk-shard x{world}"},
             "clocks": clk.summary(), "e2e": e2e,
             "gpu_launches": launches_per_step(chunks, a.batch, bf16=a.precision == "bf16") * a.steps,
-            "roofline": roofline, "attention": attention, "cpu_baseline": cpu,
+            "roofline": roofline, "attention": attention, "config3": c3, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     model.close()

@@ -189,3 +189,31 @@ def test_span_shards_combine_to_separate_pcm(mel_package):
     finally:
         dist.destroy_process_group()
     assert np.array_equal(one, whole)
+
+
+@pytest.fixture(scope="session")
+def bs512_package(tmp_path_factory):
+    d = str(tmp_path_factory.mktemp("bs512") / "pkg")
+    synthetic.seeded_package(d, ModelConfig.bs_roformer_512())
+    return d
+
+
+def test_config3_bs_roformer_512_parity(bs512_package):
+    """BASELINE config 3's network (BS-RoFormer dim 512, depth 12, 8×64 heads, the 62-band
+    partition, hop 512, seeded N(0,0.02) weights) on one 1 s chunk (custom context, so the float64
+    oracle finishes in well under a minute): fp32 ≤ 1e-4 / ≥ 80 dB; f16 ≥ 50 dB; bf16 (the config's dtype)
+    reported, with the operand-rounding floor the Mel model shows (≥ 40 dB here)."""
+    rng = np.random.default_rng(3)
+    planes = (rng.standard_normal((2, 44100)) * 0.1).astype(np.float32)
+    oracle = oracle_model.Roformer(bs512_package)
+    ref, _ = oracle_runtime.separate(oracle, planes, chunk=44100, overlap=1)
+    results = {}
+    for precision in ("f32", "f16", "bf16"):
+        model = Roformer(bs512_package, 0, precision)
+        got, _ = separate_pcm([model], planes, chunk_samples=44100, overlap=1)
+        results[precision] = (snr_db(ref, got), max_abs(ref, got))
+        model.close()
+    print("config-3 network parity:", results)
+    assert results["f32"][1] <= 1e-4 and results["f32"][0] >= 80.0
+    assert results["f16"][0] >= 50.0
+    assert results["bf16"][0] >= 40.0
