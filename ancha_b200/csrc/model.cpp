@@ -273,6 +273,18 @@ std::unique_ptr<Model> Model::load(const std::string& package, int device, int p
             m->max_width = std::max(m->max_width, width);
         }
         m->total_width = offsets.back();
+        if (m->elt_ == ELT_F16) {
+            // Tensor-core band split (f16 only: bf16's 8-bit mantissa on these inputs would eat
+            // into the little margin bf16 has left; it keeps the fp32 split).
+            const int kp = (m->max_width + 63) / 64 * 64;
+            std::vector<float> w16((size_t)nb * dim * kp, 0.f);
+            for (int b = 0; b < nb; ++b)
+                for (int o = 0; o < dim; ++o)
+                    for (int i = 0; i < m->width_[b]; ++i)
+                        w16[((size_t)b * dim + o) * kp + i] = wsplit[m->wsplit_off_[b] + (size_t)o * m->width_[b] + i];
+            upload_weights(m->wsplit16_, w16, ELT_F16);
+            m->split_kp_ = kp;
+        }
         upload(m->zcols_, cols);
         upload(m->zoffsets_, offsets);
         upload(m->wsplit_, wsplit);
@@ -431,6 +443,7 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
         w.hidden.alloc(R * std::max(hidden, mh) * e);
         w.h2.alloc(R * mh * e);
         w.z.alloc((int64_t)chunks * frames * total_width * 4);
+        if (split_kp_) w.z16.alloc(R * split_kp_ * 2);
         w.glu.alloc(R * max_width * 4);
         if (fuse_norms_) {
             w.ss_x.alloc(R * (c.dim / 32) * 4);
@@ -729,9 +742,34 @@ int Model::forward(const float* spectrum, int chunks, int frames, float* masks,
     if (check) ANCHA_TRY(reset_flag(s));
     // Band split (network.rs:316-330): gather + unit_norm per band, then one grouped affine
     // per (chunk, band) written straight into x [chunks, bands, frames, dim].
-    ANCHA_TRY(band_gather(spectrum, chunks, frames, 4 * bins, zcols_.as<int>(),
-                          zoffsets_.as<int>(), bands, total_width, ws_.z.as<float>(), s));
-    {
+    if (split_kp_) {
+        ANCHA_TRY(band_gather_padded(spectrum, chunks, frames, 4 * bins, zcols_.as<int>(), zoffsets_.as<int>(),
+                                     bands, split_kp_, ws_.z16.p, s));
+        GroupedGemm q{};
+        q.a = ws_.z16.p;
+        q.lda = split_kp_;
+        q.a_group_stride = (int64_t)frames * split_kp_;
+        q.m = frames;
+        q.k = split_kp_;
+        q.groups = G;
+        q.b = wsplit16_.p;
+        q.ldb = split_kp_;
+        q.b_group_stride = (int64_t)c.dim * split_kp_;
+        q.b_groups = bands;
+        q.n = c.dim;
+        q.group_n = nullptr;
+        q.bias = bsplit_.as<float>();
+        q.bias_group_stride = c.dim;
+        q.out = ws_.x.p;
+        q.ldo = c.dim;
+        q.out_group_stride = (int64_t)frames * c.dim;
+        GemmEpilogue e{};
+        e.act = ANCHA_ACT_NONE;
+        e.out_type = ELT_F32;
+        ANCHA_TRY(gemm_tc_grouped(q, ELT_F16, e, s));
+    } else {
+        ANCHA_TRY(band_gather(spectrum, chunks, frames, 4 * bins, zcols_.as<int>(),
+                              zoffsets_.as<int>(), bands, total_width, ws_.z.as<float>(), s));
         GemmEpilogue e{};
         e.act = ANCHA_ACT_NONE;
         ANCHA_TRY(gemm_ffma(GemmGroup{}, ws_.split_groups.as<GemmGroup>(), G, frames, c.dim, 0, 0, 1,

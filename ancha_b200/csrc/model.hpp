@@ -73,6 +73,7 @@ struct MaskWeights {
 struct Workspace {
     int chunks = 0, frames = 0;
     DevBuf x, xn, qkvg, att, hidden, h2, z, glu;
+    DevBuf z16;  // f16 mode: the band-split input, zero-padded rows of split_kp features
     // Row-norm fusion (16-bit modes): per-row, per-32-column sums of squares [rows][dim / 32]
     // of x after the attention residual (ss_x), of the block output y (ss_y) and of y ⊙ the
     // SourceNorm scale (ss_yg).
@@ -148,6 +149,10 @@ private:
 
     std::vector<int> width_, offset_;
     DevBuf zcols_, zoffsets_, wsplit_, bsplit_;
+    // f16 mode: band-split weights [bands][dim][split_kp_] f16, K zero-padded to a multiple of 64,
+    // for one grouped tensor-core launch over every (chunk, band); 0 = the fp32 FFMA split.
+    DevBuf wsplit16_;
+    int split_kp_ = 0;
     std::vector<int64_t> wsplit_off_;
     std::vector<std::array<TransformerWeights, 2>> layers_;
     DevBuf final_scale_;

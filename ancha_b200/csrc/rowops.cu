@@ -88,6 +88,30 @@ __global__ void band_gather_kernel(const float* __restrict__ spec, int frames, i
     for (int j = o0 + lane; j < o1; j += 32) zr[j] = s[cols[j]] * inv;
 }
 
+// The same gather in the tensor-core GEMM's operand layout: one zero-padded f16 row of kp
+// features per (chunk, band, frame), z[((c·bands + b)·frames + t)·kp + j] (bands of a chunk are
+// consecutive groups of `frames` rows), so one grouped launch covers every (chunk, band).
+__global__ void band_gather_padded_kernel(const float* __restrict__ spec, int frames, int columns,
+                                          const int* __restrict__ cols, const int* __restrict__ offsets,
+                                          int bands, int kp, __half* __restrict__ z, int64_t units) {
+    const int64_t unit = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x % 32;
+    if (unit >= units) return;
+    const int b = (int)(unit % bands);
+    const int64_t ct = unit / bands;  // c·frames + t
+    const int64_t c = ct / frames, t = ct % frames;
+    const float* s = spec + ct * columns;
+    const int o0 = offsets[b], width = offsets[b + 1] - o0;
+    float sq = 0.f;
+    for (int j = lane; j < width; j += 32) {
+        const float v = s[cols[o0 + j]];
+        sq = fmaf(v, v, sq);
+    }
+    const float inv = 1.f / fmaxf(sqrtf(warp_sum(sq)), 1e-12f);
+    __half* zr = z + ((c * bands + b) * frames + t) * kp;
+    for (int j = lane; j < kp; j += 32) zr[j] = __float2half_rn(j < width ? s[cols[o0 + j]] * inv : 0.f);
+}
+
 // masks[c][stem][r][ri][t] = sum over the bands covering spectrum row r of the GLU output
 // glu[(c·bands + band)·frames + t][feature + ri] / coverage. `entries` lists, per row r,
 // `count[r]` (band, feature) pairs in band order.
@@ -156,6 +180,16 @@ int band_gather(const float* spec, int chunks, int frames, int columns, const in
     band_gather_kernel<<<(unsigned)ceil_div(units, wpb), 32 * wpb, 0, s>>>(
         spec, frames, columns, cols, offsets, bands, total, z, units);
     return check_launch("band_gather");
+}
+
+int band_gather_padded(const float* spec, int chunks, int frames, int columns, const int* cols,
+                       const int* offsets, int bands, int kp, void* z, cudaStream_t s) {
+    const int64_t units = (int64_t)chunks * frames * bands;
+    if (units == 0) return ANCHA_OK;
+    const int wpb = 8;
+    band_gather_padded_kernel<<<(unsigned)ceil_div(units, wpb), 32 * wpb, 0, s>>>(
+        spec, frames, columns, cols, offsets, bands, kp, reinterpret_cast<__half*>(z), units);
+    return check_launch("band_gather_padded");
 }
 
 int mask_assemble(const float* glu, int64_t ldg, int bands, int frames, int rows,

@@ -10,6 +10,10 @@ int cast_rows(const float* x, int64_t ldx, void* y, int y_type, int64_t ldy, int
               int dim, cudaStream_t s);
 int band_gather(const float* spec, int chunks, int frames, int columns, const int* cols,
                 const int* offsets, int bands, int total, float* z, cudaStream_t s);
+// band_gather in f16 with each band's row zero-padded to kp features, rows ordered
+// (chunk, band, frame): the A operand of the grouped tensor-core band-split GEMM.
+int band_gather_padded(const float* spec, int chunks, int frames, int columns, const int* cols,
+                       const int* offsets, int bands, int kp, void* z, cudaStream_t s);
 int mask_assemble(const float* glu, int64_t ldg, int bands, int frames, int rows,
                   const int* count, const int2* entries, int max_cover, int stems, int stem,
                   float* masks, int chunks, int* nonfinite, cudaStream_t s);
