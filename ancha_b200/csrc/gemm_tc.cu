@@ -25,9 +25,13 @@ namespace {
 
 constexpr int BM = 128, BK = 64;
 constexpr int A_BYTES = BM * BK * 2;
-constexpr int EPI_WARPS = 8;        // a multiple of 4: EPI_WARPS / 4 warps per TMEM lane quarter
+// Epilogue warps per CTA (a multiple of 4: EPI / 4 warps per TMEM lane quarter): 16 for the
+// GELU / tanh epilogues, whose long dependent chains need the extra latency hiding, 8 for the
+// others, which need the registers (10 warps allow 168 registers a thread, 18 warps 96).
+constexpr int EPI_ACT = 16, EPI_PLAIN = 8;
 constexpr int STAGE_BUFS = 1;       // staging buffers per epilogue warp
-constexpr int THREADS = 64 + 32 * EPI_WARPS;
+template <int EPI>
+constexpr int threads_of() { return 64 + 32 * EPI; }
 
 struct TcParams {
     int m, n, k;          // rows per group, columns (max over groups), depth
@@ -64,12 +68,13 @@ constexpr int STAGE16_BYTES = 2048;  // one 32-row × 64-byte buffer for the 16-
 // 16-bit copy) to have read its source before it overwrites either buffer.
 static_assert(STAGE_BUFS == 1, "the row-norm copy shares the single-buffer wait");
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI_WARPS>
 struct Smem {
     static constexpr int B_BYTES = BN * BK * 2;
     static constexpr int TILES = STAGES * (A_BYTES + B_BYTES);
     static constexpr int STAGING = EPI_WARPS * STAGE_BUFS * STAGE_BYTES;
-    static constexpr int STAGING16 = EPI_WARPS * STAGE16_BYTES;  // the row-norm fusion's copy
+    // The row-norm fusion's 16-bit copy: only the plain (residual) epilogues write one.
+    static constexpr int STAGING16 = EPI_WARPS == EPI_PLAIN ? EPI_WARPS * STAGE16_BYTES : 0;
     static constexpr int BYTES = 1024 + TILES + STAGING + STAGING16 + 8 * (2 * STAGES + 4) + 16;
 };
 
@@ -265,12 +270,12 @@ __device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int t, int bn
     return c;
 }
 
-template <int BN, int STAGES>
-__global__ void __launch_bounds__(THREADS, 1)
+template <int BN, int STAGES, int EPI_WARPS>
+__global__ void __launch_bounds__(threads_of<EPI_WARPS>(), 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                const __grid_constant__ CUtensorMap tma_out, const __grid_constant__ CUtensorMap tma_out16,
                const TcParams p) {
-    using S = Smem<BN, STAGES>;
+    using S = Smem<BN, STAGES, EPI_WARPS>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_tiles = smem;
@@ -437,22 +442,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     }
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI_WARPS>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& to16,
            const TcParams& p, cudaStream_t s) {
-    using S = Smem<BN, STAGES>;
+    using S = Smem<BN, STAGES, EPI_WARPS>;
     static bool configured[64] = {};
     static int sms[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!configured[dev & 63]) {
-        ANCHA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES>,
+        ANCHA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI_WARPS>,
                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES));
         ANCHA_CUDA(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
         configured[dev & 63] = true;
     }
     const int grid = std::max(1, std::min(p.tiles, sms[dev & 63]));
-    gemm_tc_kernel<BN, STAGES><<<grid, THREADS, S::BYTES, s>>>(ta, tb, to, to16, p);
+    gemm_tc_kernel<BN, STAGES, EPI_WARPS><<<grid, threads_of<EPI_WARPS>(), S::BYTES, s>>>(ta, tb, to, to16, p);
     return check_launch("gemm_tc");
 }
 
@@ -491,10 +496,12 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
     const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles * p.groups;
     if (tiles > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: too many tiles");
     p.tiles = (int)tiles;
+    const bool act = p.act == ANCHA_ACT_GELU || p.act == ANCHA_ACT_TANH;
+    if (act && p.out16) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: no 16-bit copy after an activation");
     switch (bn) {
-        case 256: return launch<256, 3>(ta, tb, to, to16, p, s);
-        case 192: return launch<192, 3>(ta, tb, to, to16, p, s);
-        default: return launch<128, 4>(ta, tb, to, to16, p, s);
+        case 256: return act ? launch<256, 3, EPI_ACT>(ta, tb, to, to16, p, s) : launch<256, 3, EPI_PLAIN>(ta, tb, to, to16, p, s);
+        case 192: return act ? launch<192, 3, EPI_ACT>(ta, tb, to, to16, p, s) : launch<192, 3, EPI_PLAIN>(ta, tb, to, to16, p, s);
+        default: return act ? launch<128, 4, EPI_ACT>(ta, tb, to, to16, p, s) : launch<128, 4, EPI_PLAIN>(ta, tb, to, to16, p, s);
     }
 }
 
