@@ -136,10 +136,15 @@ def plan_chunks(samples: int, chunk=CHUNK, overlap=OVERLAP):
     return len(range(0, length, step)), length
 
 
-def launches_per_step(chunks: int, batch: int, depth=6, stems=1, mask_layers=2, mel=True, bf16=True):
-    """Kernels of this library launched per step (from the pipeline structure)."""
-    per_transformer = 7 + (1 if mel else 0)
-    model = 2 + 2 * depth * per_transformer + (0 if mel else 1) + (1 if bf16 else 0) + stems * (mask_layers + 2)
+def launches_per_step(chunks: int, batch: int, depth=6, stems=1, mask_layers=2, mel=True, fused=True):
+    """Kernels of this library launched per step, from the pipeline structure (checked against
+    the ncu launch list in profiles/bench_launches_mel_native.md: 74 per 4-chunk batch + 1)."""
+    if fused:  # 16-bit modes: one row norm before the first block, five launches per block,
+        blocks = 1 + 2 * depth * 5 + (1 if mel else 0)  # the deferred last SourceNorm
+    else:
+        blocks = 2 * depth * (7 + (1 if mel else 0))
+    hidden = mask_layers if mel else mask_layers - 1
+    model = 2 + blocks + (0 if mel else 1) + 1 + stems * (hidden + 1 + 1)  # split, blocks, final norm, cast, masks
     per_batch = 2 + model + 2 + 1          # gather + stft, model, istft (2), ola
     batches = -(-chunks // batch)
     return batches * per_batch + 1        # + finish
@@ -409,7 +414,7 @@ def main():
                        "chunks_per_gpu": chunks, "batch_chunks": a.batch,
                        "l2": "working set > 126 MB L2 (no flush)", "parallelism": f"chunk-shard x{world}"},
             "clocks": clk.summary(), "e2e": e2e,
-            "gpu_launches": launches_per_step(chunks, a.batch, bf16=a.precision == "bf16") * a.steps,
+            "gpu_launches": launches_per_step(chunks, a.batch, fused=a.precision != "f32") * a.steps,
             "roofline": roofline, "attention": attention, "config3": c3, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
