@@ -53,7 +53,7 @@ def parse():
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--precision", default="f16", choices=["f16", "bf16", "f32"])
     p.add_argument("--seconds", type=float, default=30.0)
-    p.add_argument("--batch", type=int, default=4)
+    p.add_argument("--batch", type=int, default=0, help="chunks per model call (0 = the library's balanced default)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--package", default=os.environ.get("ANCHA_BENCH_PACKAGE", "/tmp/ancha_bench/mel-seed0"))
     p.add_argument("--no-config3", action="store_true")
@@ -73,7 +73,7 @@ def config3(local: int, world: int, rank: int, dist, steps: int = 2):
     model = Roformer(pkg, local, "bf16")
     planes = track(180.0, 3000)
     plan = ChunkPlan.of(planes.shape[1], model.chunk_samples, model.overlap)
-    span = gpu_span(model, batch_chunks=4)
+    span = gpu_span(model, batch_chunks=0)
 
     def run():
         if dist:
@@ -134,6 +134,14 @@ def plan_chunks(samples: int, chunk=CHUNK, overlap=OVERLAP):
     border = border if samples > 2 * border else 0
     length = samples + 2 * border
     return len(range(0, length, step)), length
+
+
+def effective_batch(chunks: int, batch: int) -> int:
+    """The chunks per model call the library uses (runtime.cpp default_batch for 0)."""
+    if batch > 0:
+        return batch
+    batches = max(1, -(-chunks // 8))
+    return max(1, -(-chunks // batches))
 
 
 def launches_per_step(chunks: int, batch: int, depth=6, stems=1, mask_layers=2, mel=True, fused=True):
@@ -415,10 +423,11 @@ def main():
             "config": {"workload": f"mel-band-roformer dim384 depth6 60 bands, native context "
                                    f"(chunk {CHUNK}, overlap {OVERLAP}), {a.seconds:.0f} s track "
                                    f"= {chunks} chunks per GPU",
-                       "chunks_per_gpu": chunks, "batch_chunks": a.batch,
+                       "chunks_per_gpu": chunks, "batch_chunks": effective_batch(chunks, a.batch),
                        "l2": "working set > 126 MB L2 (no flush)", "parallelism": f"chunk-shard x{world}"},
             "clocks": clk.summary(), "e2e": e2e,
-            "gpu_launches": launches_per_step(chunks, a.batch, fused=a.precision != "f32") * a.steps,
+            "gpu_launches": launches_per_step(chunks, effective_batch(chunks, a.batch),
+                                              fused=a.precision != "f32") * a.steps,
             "roofline": roofline, "attention": attention, "config3": c3, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
