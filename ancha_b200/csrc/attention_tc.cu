@@ -11,8 +11,8 @@
 // MN-major operand) accumulates in TMEM.
 //
 // Two kernels: attention_pp_kernel for tokens > 64 (the time axis, online softmax over key
-// blocks, two query tiles per CTA) and attention_band_kernel for tokens ≤ 64 (the band axis,
-// two problems per tile, persistent and pipelined across tiles).
+// blocks, one query tile per CTA, two CTAs per SM) and attention_band_kernel for tokens ≤ 64
+// (the band axis, two problems per tile, persistent and pipelined across tiles).
 #include "attention.cuh"
 #include "tc.cuh"
 
@@ -275,28 +275,31 @@ attention_band_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
     }
 }
 
-// Time-axis kernel (tokens > 64): two 128-row query tiles of the same (group, head) per CTA
-// share every K / V block, streamed through a 3-deep ring. Warps 0–3 and 4–7 are the softmax
-// warpgroups of tile 0 and 1 (two warps per SM sub-partition), warp 8 issues TMA, warp 9
-// UMMA.
+// Time-axis kernel (tokens > 64): one 128-row query tile per CTA and two CTAs per SM. Warps
+// 0–3 run the softmax (one query row per thread), warp 4 issues TMA (Q once, then K / V blocks
+// through a 2-deep ring), warp 5 issues UMMA. A tcgen05.mma issue costs a fixed ~80 cycles
+// whatever its N, so one issuing thread cannot keep the tensor cores busy with these small
+// (N = 128 / 64, K = 16) instructions; two co-resident CTAs give each SM two independent issue
+// streams, and the tensor cores interleave them (measured: 18–20 % faster than two query tiles
+// sharing one CTA and one issuer).
 //
-// TMEM (512 columns): S of tile t at t·128, its output accumulator O at 256 + t·64 and its
-// P (16-bit pairs, the A operand of P·V) at 384 + t·64. A softmax thread copies its row of
-// S(kb) into registers and releases the S buffer at once, so S(kb+1) = Q·K(kb+1)ᵀ runs on the
-// tensor cores while the exponentials of block kb are computed; it then writes P(kb) and the
-// UMMA warp accumulates O += P(kb)·V(kb). The running maximum is updated lazily: it moves
-// (and O, l are rescaled in TMEM) only when a row's block maximum exceeds it by more than 2^8,
-// so P stays ≤ 256 and the rescale is rare. Interior key blocks skip masking.
-constexpr int PP_KV_STAGES = 3;
-constexpr int PP_OFF_Q = 0, PP_OFF_K = 2 * QKV_BYTES, PP_OFF_V = PP_OFF_K + PP_KV_STAGES * QKV_BYTES;
+// TMEM (256 columns per CTA): S at 0 (128), the output accumulator O at 128 (64) and P (16-bit
+// pairs, the A operand of P·V) at 192 (64). The softmax copies its row of S(kb) into registers
+// and releases the buffer at once, so S(kb+1) = Q·K(kb+1)ᵀ runs while the exponentials of kb
+// are computed; P(kb) goes back to TMEM and the UMMA warp accumulates O += P(kb)·V(kb). The
+// running maximum is updated lazily: it moves (and O, l are rescaled in TMEM) only when a row's
+// block maximum exceeds it by more than 2^8, so P stays ≤ 256 and the rescale is rare.
+// Interior key blocks skip masking.
+constexpr int PP_KV_STAGES = 2;
+constexpr int PP_OFF_Q = 0, PP_OFF_K = QKV_BYTES, PP_OFF_V = PP_OFF_K + PP_KV_STAGES * QKV_BYTES;
 constexpr int PP_OFF_BAR = PP_OFF_V + PP_KV_STAGES * QKV_BYTES;
-constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + 20 * 8 + 16;
-constexpr int PP_THREADS = 320;
+constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + 12 * 8 + 16;
+constexpr int PP_THREADS = 192;
 constexpr float PP_RESCALE_LOG2 = 8.f;
-constexpr uint32_t PP_O_COL = 256, PP_P_COL = 384;
+constexpr uint32_t PP_TMEM_COLS = 256, PP_O_COL = 128, PP_P_COL = 192;
 
 template <bool BF16>
-__global__ void __launch_bounds__(PP_THREADS, 1)
+__global__ void __launch_bounds__(PP_THREADS, 2)
 attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -304,41 +307,37 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     uint64_t* q_full = bars;
     uint64_t* kv_full = bars + 1;                  // [stage]
     uint64_t* kv_empty = bars + 1 + PP_KV_STAGES;  // [stage]
-    uint64_t* s_full = bars + 7;                   // [tile] S(kb) computed
-    uint64_t* s_free = bars + 9;                   // [tile] S(kb) copied to registers (128 arrivals)
-    uint64_t* p_ready = bars + 11;                 // [tile] P(kb) written (128 arrivals)
-    uint64_t* pv_done = bars + 13;                 // [tile] O += P(kb)·V(kb) completed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+    uint64_t* s_full = bars + 5;                   // S(kb) computed
+    uint64_t* s_free = bars + 6;                   // S(kb) copied to registers (128 arrivals)
+    uint64_t* p_ready = bars + 7;                  // P(kb) written (128 arrivals)
+    uint64_t* pv_done = bars + 8;                  // O += P(kb)·V(kb) completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-    const int pairs = (p.tiles_per_group + 1) / 2;
-    const int pair = blockIdx.x % pairs;
-    const int gi = blockIdx.x / pairs;
+    const int tile = blockIdx.x % p.tiles_per_group;
+    const int gi = blockIdx.x / p.tiles_per_group;
     const int go = blockIdx.z, head = blockIdx.y;
     const int nkb = p.tiles_per_group;
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-    const int q0 = 2 * pair * TILE;             // first query token of tile 0
-    const bool active1 = q0 + TILE < p.tokens;  // tile 1 holds at least one query
+    const int q0 = tile * TILE;  // first query token of the tile
 
-    if (threadIdx.x == 256) {
+    if (threadIdx.x == 128) {
         mbar_init(q_full, 1);
         for (int s = 0; s < PP_KV_STAGES; ++s) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        for (int t = 0; t < 2; ++t) {
-            mbar_init(&s_full[t], 1);
-            mbar_init(&s_free[t], 128);
-            mbar_init(&p_ready[t], 128);
-            mbar_init(&pv_done[t], 1);
-        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 128);
+        mbar_init(p_ready, 128);
+        mbar_init(pv_done, 1);
         *abort = 0;
         fence_barrier_init();
         fence_proxy_async();
         prefetch_tma(&tmap);
     }
-    if (warp == 9) {
-        tmem_alloc(tmem_slot, 512);
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, PP_TMEM_COLS);
         tmem_relinquish();
     }
     tc_fence_before();
@@ -346,11 +345,10 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 8) {
+    if (warp == 4) {
         if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, 2 * QKV_BYTES);
+            mbar_arrive_expect_tx(q_full, QKV_BYTES);
             tma_load_4d(smem + PP_OFF_Q, &tmap, q_full, p.q_col + head * HD, q0, gi, go);
-            tma_load_4d(smem + PP_OFF_Q + QKV_BYTES, &tmap, q_full, p.q_col + head * HD, q0 + TILE, gi, go);
             int issued = 0;
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % PP_KV_STAGES;
@@ -370,164 +368,155 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                     }
             }
         }
-    } else if (warp == 9) {
+    } else if (warp == 5) {
         if (lane == 0) {
-            // Fixed issue order per key block j: S(j + 1) of both tiles (each once its softmax
-            // has copied S(j) out), then P(j)·V(j) of both tiles.
-            const int ntiles = active1 ? 2 : 1;
-            const uint64_t q_desc[2] = {umma_desc_sw128(smem_u32(smem + PP_OFF_Q)),
-                                        umma_desc_sw128(smem_u32(smem + PP_OFF_Q + QKV_BYTES))};
-            auto issue_s = [&](int t, int j) -> bool {
-                if (j >= 1 && !mbar_wait(&s_free[t], (j - 1) & 1, abort, p.err)) return false;
+            // Per key block j: S(j + 1) once the softmax has copied S(j) out, then P(j)·V(j) once
+            // it has written P(j).
+            const uint64_t q_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_Q));
+            auto issue_s = [&](int j) -> bool {
+                if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, abort, p.err)) return false;
                 tc_fence_after();
                 const uint64_t k_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_K + (j % PP_KV_STAGES) * QKV_BYTES));
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)  // K step of 16 = 32 bytes = 2 descriptor units
-                    umma_f16(tmem + t * TILE, q_desc[t] + 2 * kk, k_desc + 2 * kk, p.idesc_s, kk != 0);
-                umma_commit(&s_full[t]);
+                    umma_f16(tmem, q_desc + 2 * kk, k_desc + 2 * kk, p.idesc_s, kk != 0);
+                umma_commit(s_full);
                 return true;
             };
-            auto issue_pv = [&](int t, int k) -> bool {
-                if (!mbar_wait(&p_ready[t], k & 1, abort, p.err)) return false;
+            auto issue_pv = [&](int k) -> bool {
+                if (!mbar_wait(p_ready, k & 1, abort, p.err)) return false;
                 tc_fence_after();
                 const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_V + (k % PP_KV_STAGES) * QKV_BYTES));
 #pragma unroll
                 for (int kk = 0; kk < TILE / 16; ++kk)  // 16 keys = 16 rows of 128 bytes = 128 units
-                    umma_f16_ts(tmem + PP_O_COL + t * HD, tmem + PP_P_COL + t * HD + kk * 8, v_desc + 128 * kk,
-                                p.idesc_o, (k > 0 || kk > 0) ? 1u : 0u);
-                umma_commit(&pv_done[t]);
+                    umma_f16_ts(tmem + PP_O_COL, tmem + PP_P_COL + kk * 8, v_desc + 128 * kk, p.idesc_o,
+                                (k > 0 || kk > 0) ? 1u : 0u);
+                umma_commit(pv_done);
                 return true;
             };
-            bool ok = mbar_wait(q_full, 0, abort, p.err) && mbar_wait(&kv_full[0], 0, abort, p.err);
-            for (int t = 0; ok && t < ntiles; ++t) ok = issue_s(t, 0);
+            bool ok = mbar_wait(q_full, 0, abort, p.err) && mbar_wait(&kv_full[0], 0, abort, p.err) && issue_s(0);
             for (int j = 0; ok && j < nkb; ++j) {
                 if (j + 1 < nkb)
-                    ok = mbar_wait(&kv_full[(j + 1) % PP_KV_STAGES], ((j + 1) / PP_KV_STAGES) & 1, abort, p.err);
-                for (int t = 0; ok && t < ntiles; ++t) {
-                    if (j + 1 < nkb) ok = issue_s(t, j + 1);
-                    if (ok) ok = issue_pv(t, j);
-                }
-                if (ok) umma_commit(&kv_empty[j % PP_KV_STAGES]);  // fires once both P·V are done
+                    ok = mbar_wait(&kv_full[(j + 1) % PP_KV_STAGES], ((j + 1) / PP_KV_STAGES) & 1, abort, p.err) &&
+                         issue_s(j + 1);
+                if (ok) ok = issue_pv(j);
+                if (ok) umma_commit(&kv_empty[j % PP_KV_STAGES]);  // fires once P·V(j) is done
             }
         }
     } else {
-        const int t = warp / 4;  // tile of this softmax warpgroup
-        const int row = threadIdx.x % 128;
-        const int tok = q0 + t * TILE + row;
+        const int row = threadIdx.x;  // query row of the tile (warps 0–3)
+        const int tok = q0 + row;
         const bool valid = tok < p.tokens;
-        const uint32_t lane_off = (uint32_t)((warp % 4) * 32) << 16;
-        const uint32_t s_addr = tmem + lane_off + t * TILE;
-        const uint32_t o_addr = tmem + lane_off + PP_O_COL + t * HD;
-        const uint32_t p_addr = tmem + lane_off + PP_P_COL + t * HD;
-        if (t == 0 || active1) {
-            float m_used = -INFINITY, l = 0.f;
-            bool ok = true;
-            for (int kb = 0; kb < nkb; ++kb) {
-                ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], kb & 1, abort, p.err));
-                if (!ok) break;
-                tc_fence_after();
-                uint32_t s[4][32];
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const uint32_t s_addr = tmem + lane_off;
+        const uint32_t o_addr = tmem + lane_off + PP_O_COL;
+        const uint32_t p_addr = tmem + lane_off + PP_P_COL;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+            ok = __all_sync(0xffffffffu, mbar_wait(s_full, kb & 1, abort, p.err));
+            if (!ok) break;
+            tc_fence_after();
+            uint32_t s[4][32];
 #pragma unroll
-                for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, s[c]);
-                tmem_wait_ld();
-                tc_fence_before();
-                mbar_arrive(&s_free[t]);  // the tensor cores may compute S(kb + 1) now
-                const int nvalid = min(TILE, p.tokens - kb * TILE);  // valid keys in this block
-                if (nvalid < TILE) {
+            for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, s[c]);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(s_free);  // the tensor cores may compute S(kb + 1) now
+            const int nvalid = min(TILE, p.tokens - kb * TILE);  // valid keys in this block
+            if (nvalid < TILE) {
 #pragma unroll
-                    for (int c = 0; c < TILE; ++c)
-                        if (c >= nvalid) s[c / 32][c % 32] = __float_as_uint(-INFINITY);
-                }
-                float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
-#pragma unroll
-                for (int c = 0; c < TILE; c += 4) {
-                    mx0 = fmaxf(mx0, __uint_as_float(s[c / 32][c % 32]));
-                    mx1 = fmaxf(mx1, __uint_as_float(s[c / 32][c % 32 + 1]));
-                    mx2 = fmaxf(mx2, __uint_as_float(s[c / 32][c % 32 + 2]));
-                    mx3 = fmaxf(mx3, __uint_as_float(s[c / 32][c % 32 + 3]));
-                }
-                const float m_blk = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * LOG2E;
-                float corr = 1.f;
-                if (m_blk > m_used + PP_RESCALE_LOG2) {  // also the first block (m_used = −∞)
-                    corr = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_blk);
-                    m_used = m_blk;
-                    l *= corr;
-                }
-                // P = 2^(s·log2 e − m_used) as 16-bit pairs, all 128 keys in registers before the
-                // wait for P(kb − 1)·V, which then has had the whole exponential pass to finish.
-                float sum0 = 0.f, sum1 = 0.f;
-                uint32_t pk[2][32];
-#pragma unroll
-                for (int j = 0; j < TILE; j += 2) {
-                    const float e0 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32]), LOG2E, -m_used));
-                    const float e1 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32 + 1]), LOG2E, -m_used));
-                    sum0 += e0;
-                    sum1 += e1;
-                    pk[j / 64][(j % 64) / 2] = pack2<BF16>(e0, e1);
-                }
-                if (kb > 0) {
-                    // P(kb − 1)·V must have finished reading P before it is overwritten, and O
-                    // must hold it before a rescale.
-                    ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (kb - 1) & 1, abort, p.err));
-                    if (!ok) break;
-                    tc_fence_after();
-                    if (__any_sync(0xffffffffu, corr != 1.f)) {
-                        uint32_t o[2][32];
-                        tmem_ld32(o_addr, o[0]);
-                        tmem_ld32(o_addr + 32, o[1]);
-                        tmem_wait_ld();
-#pragma unroll
-                        for (int d = 0; d < 32; ++d) {
-                            o[0][d] = __float_as_uint(__uint_as_float(o[0][d]) * corr);
-                            o[1][d] = __float_as_uint(__uint_as_float(o[1][d]) * corr);
-                        }
-                        tmem_st32(o_addr, o[0]);
-                        tmem_st32(o_addr + 32, o[1]);
-                    }
-                }
-                tmem_st32(p_addr, pk[0]);
-                tmem_st32(p_addr + 32, pk[1]);
-                if (!ok) break;
-                l += sum0 + sum1;
-                tmem_wait_st();
-                tc_fence_before();
-                mbar_arrive(&p_ready[t]);
+                for (int c = 0; c < TILE; ++c)
+                    if (c >= nvalid) s[c / 32][c % 32] = __float_as_uint(-INFINITY);
             }
-            if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (nkb - 1) & 1, abort, p.err));
-            if (ok) {
+            float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < TILE; c += 4) {
+                mx0 = fmaxf(mx0, __uint_as_float(s[c / 32][c % 32]));
+                mx1 = fmaxf(mx1, __uint_as_float(s[c / 32][c % 32 + 1]));
+                mx2 = fmaxf(mx2, __uint_as_float(s[c / 32][c % 32 + 2]));
+                mx3 = fmaxf(mx3, __uint_as_float(s[c / 32][c % 32 + 3]));
+            }
+            const float m_blk = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * LOG2E;
+            float corr = 1.f;
+            if (m_blk > m_used + PP_RESCALE_LOG2) {  // also the first block (m_used = −∞)
+                corr = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_blk);
+                m_used = m_blk;
+                l *= corr;
+            }
+            // P = 2^(s·log2 e − m_used) as 16-bit pairs, all 128 keys in registers before the
+            // wait for P(kb − 1)·V, which then has had the whole exponential pass to finish.
+            float sum0 = 0.f, sum1 = 0.f;
+            uint32_t pk[2][32];
+#pragma unroll
+            for (int j = 0; j < TILE; j += 2) {
+                const float e0 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32]), LOG2E, -m_used));
+                const float e1 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32 + 1]), LOG2E, -m_used));
+                sum0 += e0;
+                sum1 += e1;
+                pk[j / 64][(j % 64) / 2] = pack2<BF16>(e0, e1);
+            }
+            if (kb > 0) {
+                // P(kb − 1)·V must have finished reading P before it is overwritten, and O must
+                // hold it before a rescale.
+                ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (kb - 1) & 1, abort, p.err));
+                if (!ok) break;
                 tc_fence_after();
-                uint32_t o[2][32];
-                tmem_ld32(o_addr, o[0]);
-                tmem_ld32(o_addr + 32, o[1]);
-                tmem_wait_ld();
-                if (valid) {
-                    const int64_t orow = (int64_t)go * p.group_outer_stride + (int64_t)gi * p.group_inner_stride +
-                                         (int64_t)tok * p.token_stride;
-                    float scale = 1.f / l;
-                    if (p.gate_col >= 0) {
-                        const float gl = BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[orow * p.ld + p.gate_col + head])
-                                              : __half2float(reinterpret_cast<const __half*>(p.q)[orow * p.ld + p.gate_col + head]);
-                        scale /= 1.f + __expf(-gl);
-                    }
-                    uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) +
-                                                          (orow * p.out_ld + p.out_col + head * HD) * 2);
+                if (__any_sync(0xffffffffu, corr != 1.f)) {
+                    uint32_t o[2][32];
+                    tmem_ld32(o_addr, o[0]);
+                    tmem_ld32(o_addr + 32, o[1]);
+                    tmem_wait_ld();
 #pragma unroll
-                    for (int q = 0; q < HD / 8; ++q) {
-                        float v[8];
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) v[u] = __uint_as_float(o[q / 4][(q % 4) * 8 + u]) * scale;
-                        dst[q] = make_uint4(pack2<BF16>(v[0], v[1]), pack2<BF16>(v[2], v[3]),
-                                            pack2<BF16>(v[4], v[5]), pack2<BF16>(v[6], v[7]));
+                    for (int d = 0; d < 32; ++d) {
+                        o[0][d] = __float_as_uint(__uint_as_float(o[0][d]) * corr);
+                        o[1][d] = __float_as_uint(__uint_as_float(o[1][d]) * corr);
                     }
+                    tmem_st32(o_addr, o[0]);
+                    tmem_st32(o_addr + 32, o[1]);
+                }
+            }
+            tmem_st32(p_addr, pk[0]);
+            tmem_st32(p_addr + 32, pk[1]);
+            l += sum0 + sum1;
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_ready);
+        }
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkb - 1) & 1, abort, p.err));
+        if (ok) {
+            tc_fence_after();
+            uint32_t o[2][32];
+            tmem_ld32(o_addr, o[0]);
+            tmem_ld32(o_addr + 32, o[1]);
+            tmem_wait_ld();
+            if (valid) {
+                const int64_t orow = (int64_t)go * p.group_outer_stride + (int64_t)gi * p.group_inner_stride +
+                                     (int64_t)tok * p.token_stride;
+                float scale = 1.f / l;
+                if (p.gate_col >= 0) {
+                    const float gl = BF16 ? __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(p.q)[orow * p.ld + p.gate_col + head])
+                                          : __half2float(reinterpret_cast<const __half*>(p.q)[orow * p.ld + p.gate_col + head]);
+                    scale /= 1.f + __expf(-gl);
+                }
+                uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) +
+                                                      (orow * p.out_ld + p.out_col + head * HD) * 2);
+#pragma unroll
+                for (int q = 0; q < HD / 8; ++q) {
+                    float v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v[u] = __uint_as_float(o[q / 4][(q % 4) * 8 + u]) * scale;
+                    dst[q] = make_uint4(pack2<BF16>(v[0], v[1]), pack2<BF16>(v[2], v[3]),
+                                        pack2<BF16>(v[4], v[5]), pack2<BF16>(v[6], v[7]));
                 }
             }
         }
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 9) {
+    if (warp == 5) {
         __syncwarp();
-        tmem_dealloc(tmem, 512);
+        tmem_dealloc(tmem, PP_TMEM_COLS);
     }
 }
 
@@ -606,8 +595,8 @@ int attention_tc(const AttnArgs& a, cudaStream_t stream) {
     ANCHA_TRY(make_tma_4d(&map, a.q, a.elt, a.ld, a.tokens, a.group_inner, p.group_outer,
                           s1 > 0 ? s1 : a.ld, s2 > 0 ? s2 : a.ld, s3 > 0 ? s3 : a.ld, BT, BG));
     if (BT == 128) {
-        // Time axis: two query tiles of one (group, head) per CTA.
-        const int64_t gx = (int64_t)((p.tiles_per_group + 1) / 2) * a.group_inner;
+        // Time axis: one query tile of one (group, head) per CTA, two CTAs per SM.
+        const int64_t gx = (int64_t)p.tiles_per_group * a.group_inner;
         if (gx > 0x7fffffff || a.heads > 65535 || p.group_outer > 65535)
             return fail(ANCHA_E_UNSUPPORTED, "attention_tc: grid too large");
         dim3 grid((unsigned)gx, (unsigned)a.heads, (unsigned)p.group_outer);
