@@ -9,6 +9,7 @@
 #include "attention.cuh"
 #include "dsp.cuh"
 #include "gemm.cuh"
+#include "mdx23c_model.hpp"
 #include "model.hpp"
 
 namespace ancha {
@@ -223,6 +224,46 @@ int ancha_model_forward(ancha_model* model, const float* spectrum, int chunks, i
 }
 
 void ancha_model_free(ancha_model* model) { delete model; }
+
+int ancha_mdx23c_load(const char* package_dir, int device, int precision, ancha_mdx23c** out) {
+    if (!package_dir || !out) return fail(ANCHA_E_INVALID, "mdx23c_load: null argument");
+    *out = nullptr;
+    try {
+        auto m = Mdx23c::load(package_dir, device, precision);
+        *out = new ancha_mdx23c{std::move(m)};
+        return ANCHA_OK;
+    } catch (const std::exception& e) {
+        const std::string msg = e.what();
+        const bool io = msg.rfind("read ", 0) == 0;
+        return fail(io ? ANCHA_E_IO : ANCHA_E_INVALID, msg);
+    }
+}
+
+int ancha_mdx23c_info(const ancha_mdx23c* model, int* bins, int* frames, int* n_fft, int* hop, int* overlap,
+                      int* stems, int* tensor_count) {
+    if (!model) return fail(ANCHA_E_INVALID, "mdx23c_info: null model");
+    const Mdx23cConfig& c = model->impl->manifest.config;
+    if (bins) *bins = c.bins;
+    if (frames) *frames = c.frames;
+    if (n_fft) *n_fft = c.n_fft;
+    if (hop) *hop = c.hop;
+    if (overlap) *overlap = c.overlap;
+    if (stems) *stems = (int)c.stems.size();
+    if (tensor_count) *tensor_count = (int)model->impl->tensor_count;
+    return ANCHA_OK;
+}
+
+int ancha_mdx23c_forward(ancha_mdx23c* model, const float* spectrum, int batch, int frames, float* out,
+                         const volatile int* cancel, void* stream) {
+    if (!model || !spectrum || !out) return fail(ANCHA_E_INVALID, "mdx23c_forward: null argument");
+    try {
+        return model->impl->forward(spectrum, batch, frames, out, cancel, as_stream(stream));
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_CUDA, e.what());
+    }
+}
+
+void ancha_mdx23c_free(ancha_mdx23c* model) { delete model; }
 
 void ancha_free_string(char* s) { std::free(s); }
 

@@ -1,0 +1,413 @@
+// MDX23C (TFC-TDF v3) on the device (mdx23c_model.hpp).
+//
+// Layout: NCHW f32 planes, [batch][channels][time][frequency] inside the network (the
+// reference's layout after swap_dims(2, 3), mdx23c.rs:437), so the TDF Linear over the
+// frequency axis is one plain GEMM over rows (batch, channel, time), and its residual x + y
+// (mdx23c.rs:271) is that GEMM's epilogue. Every convolution is a patch gather
+// (mdx_pack: instance norm → GELU → zero padding → K-major patch rows, over a concatenation
+// of two sources) and one GEMM per batch item, out[co][pos] = W[co][k]·P[pos][k]ᵀ, so the
+// output lands in NCHW directly; the second convolution's `+ skip` (mdx23c.rs:272-273) is its
+// epilogue. GEMMs run on the tcgen05 kernel with f16 / bf16 operands (the FFMA kernel when a
+// shape breaks its 16-byte rules, and for f32); accumulation and activations stay f32.
+#include "mdx23c_model.hpp"
+
+#include <algorithm>
+#include <cstring>
+#include <set>
+#include <stdexcept>
+#include <thread>
+
+#include "gemm.cuh"
+
+namespace ancha {
+
+namespace {
+
+[[noreturn]] void bad(const std::string& m) { throw std::runtime_error(m); }
+
+void ensure(bool ok, const char* msg) {
+    if (!ok) bad(msg);
+}
+
+void check_keys(const Json& j, const std::set<std::string>& keys, const char* what) {
+    if (j.kind != Json::Object) bad(std::string(what) + " must be an object");
+    std::set<std::string> seen;
+    for (const auto& kv : j.obj) {
+        if (!keys.count(kv.first)) bad(std::string("unknown field `") + kv.first + "` in " + what);
+        seen.insert(kv.first);
+    }
+    for (const auto& k : keys)
+        if (!seen.count(k)) bad(std::string("missing field `") + k + "` in " + what);
+}
+
+bool is_hex64(const std::string& s) {
+    return s.size() == 64 && std::all_of(s.begin(), s.end(), [](char c) { return isxdigit((unsigned char)c) != 0; });
+}
+
+template <typename T>
+void upload(DevBuf& d, const std::vector<T>& v) {
+    d.alloc(v.size() * sizeof(T));
+    cudaError_t e = cudaMemcpy(d.p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) bad(std::string("cudaMemcpy: ") + cudaGetErrorString(e));
+}
+
+void upload_elt(DevBuf& d, const std::vector<float>& v, int elt) {
+    if (elt == ELT_F32) return upload(d, v);
+    if (elt == ELT_BF16) {
+        std::vector<__nv_bfloat16> h(v.size());
+        for (size_t i = 0; i < v.size(); ++i) h[i] = __float2bfloat16_rn(v[i]);
+        return upload(d, h);
+    }
+    std::vector<__half> h(v.size());
+    for (size_t i = 0; i < v.size(); ++i) h[i] = __float2half_rn(v[i]);
+    upload(d, h);
+}
+
+int64_t round8(int64_t k) { return (k + 7) / 8 * 8; }
+
+constexpr float kNormEps = 1e-5f;  // Preact's InstanceNorm epsilon (mdx23c.rs:204)
+
+}  // namespace
+
+void Mdx23cConfig::validate() const {
+    // mdx23c.rs:76-122.
+    ensure(sample_rate == 44100 && n_fft >= 32 && n_fft <= 8192 && n_fft % 2 == 0 && hop > 0 && hop <= n_fft / 2,
+           "MDX23C requires stereo 44100 Hz and a valid centered STFT");
+    ensure(scales >= 1 && scales <= 6 && scale == std::vector<int>{2, 2},
+           "MDX23C supports 1..=6 scales with 2x2 down/up sampling");
+    const int factor = 1 << scales;
+    ensure(subbands >= 1 && subbands <= 16 && bins > 0 && bins <= n_fft / 2 + 1 && bins % (subbands * factor) == 0 &&
+               frames >= factor && frames <= 2048 && frames % factor == 0,
+           "MDX23C frequency/time dimensions must survive all encoder scales");
+    ensure(channels >= 1 && channels <= 1024 && growth >= 1 && growth <= 1024 && channels + scales * growth <= 2048 &&
+               blocks_per_scale >= 1 && blocks_per_scale <= 4 && bottleneck_factor >= 1 && bottleneck_factor <= 16,
+           "invalid MDX23C network size");
+    const int bottom = bins / subbands / factor;
+    ensure(bottom >= bottleneck_factor && (frames / factor) * bottom > 1,
+           "MDX23C bottleneck is too small for Linear or InstanceNorm");
+    ensure(chunk_samples() > n_fft / 2 && chunk_samples() <= 44100 * 60 && overlap >= 1 && overlap <= 16,
+           "invalid MDX23C context");
+    ensure(stems == std::vector<std::string>{"vocals", "instrumental"},
+           "MDX23C schema 1 requires two native heads in vocals/instrumental order");
+}
+
+Mdx23cConfig Mdx23cConfig::from_json(const Json& j) {
+    check_keys(j, {"family", "sample_rate", "n_fft", "hop", "bins", "frames", "overlap", "subbands", "channels",
+                   "growth", "scales", "blocks_per_scale", "bottleneck_factor", "scale", "stems"},
+               "MDX23C config");
+    ensure(j.at("family").as_string() == "mdx23c", "not an MDX23C package");
+    Mdx23cConfig c;
+    auto i = [&](const char* k) { return (int)j.at(k).as_int(); };
+    c.sample_rate = i("sample_rate"); c.n_fft = i("n_fft"); c.hop = i("hop"); c.bins = i("bins");
+    c.frames = i("frames"); c.overlap = i("overlap"); c.subbands = i("subbands"); c.channels = i("channels");
+    c.growth = i("growth"); c.scales = i("scales"); c.blocks_per_scale = i("blocks_per_scale");
+    c.bottleneck_factor = i("bottleneck_factor");
+    for (const Json& v : j.at("scale").arr) c.scale.push_back((int)v.as_int());
+    for (const Json& v : j.at("stems").arr) c.stems.push_back(v.as_string());
+    return c;
+}
+
+Mdx23cManifest Mdx23cManifest::from_json(const Json& j) {
+    check_keys(j, {"schema_version", "model_id", "weights_sha256", "checkpoint_sha256", "source_url",
+                   "forward_revision", "weight_license", "config"},
+               "manifest");
+    Mdx23cManifest m;
+    m.schema_version = (int)j.at("schema_version").as_int();
+    m.model_id = j.at("model_id").as_string();
+    m.weights_sha256 = j.at("weights_sha256").as_string();
+    m.checkpoint_sha256 = j.at("checkpoint_sha256").as_string();
+    m.source_url = j.at("source_url").as_string();
+    m.forward_revision = j.at("forward_revision").as_string();
+    m.weight_license = j.at("weight_license").as_string();
+    m.config = Mdx23cConfig::from_json(j.at("config"));
+    return m;
+}
+
+void Mdx23cManifest::validate() const {
+    // config.rs:211-221 (validate_metadata), then the network config.
+    ensure(schema_version == 1, "unsupported model package schema");
+    ensure(!model_id.empty(), "model ID is empty");
+    ensure(is_hex64(weights_sha256) && is_hex64(checkpoint_sha256), "invalid SHA256");
+    config.validate();
+}
+
+std::unique_ptr<Mdx23c> Mdx23c::load(const std::string& package, int device, int precision) {
+    if (precision != ANCHA_PRECISION_F32 && precision != ANCHA_PRECISION_BF16 && precision != ANCHA_PRECISION_F16)
+        bad("unknown precision");
+    std::unique_ptr<Mdx23c> m(new Mdx23c());
+    // The manifest is checked before any device work, so a bad package fails the same way
+    // with or without a GPU.
+    m->manifest = Mdx23cManifest::from_json(Json::parse(read_file(package + "/manifest.json")));
+    m->manifest.validate();
+    cudaError_t e = cudaSetDevice(device);
+    if (e != cudaSuccess) bad(std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    m->device = device;
+    m->precision = precision;
+    m->elt_ = precision == ANCHA_PRECISION_BF16 ? ELT_BF16 : precision == ANCHA_PRECISION_F16 ? ELT_F16 : ELT_F32;
+    const std::string bytes = read_file(package + "/model.safetensors");
+    std::string digest;  // SHA-256 on another thread while the weights are converted (weights.rs:29-40)
+    std::thread hasher([&] { digest = sha256_hex(reinterpret_cast<const uint8_t*>(bytes.data()), bytes.size()); });
+    try {
+        SafeTensors w(bytes);
+        const Mdx23cConfig& c = m->manifest.config;
+        const int elt = m->elt_;
+        auto norm = [&](Norm& n, const std::string& p, int ch) {
+            upload(n.gamma, w.take(p + ".weight", {ch}));
+            upload(n.beta, w.take(p + ".bias", {ch}));
+        };
+        // [co][ci][kh][kw] → [co][kp]: PyTorch's flattening is the patch column order
+        // k = (ci·kh + ky)·kw + kx of mdx_pack; columns k..kp−1 are zero.
+        auto conv = [&](Conv& cv, const std::string& name, int co, int ci, int k) {
+            const std::vector<float> src = w.take(name, {co, ci, k, k});
+            cv.co = co; cv.kh = cv.kw = k; cv.k = ci * k * k; cv.kp = (int)round8(cv.k);
+            std::vector<float> dst((size_t)co * cv.kp, 0.f);
+            for (int o = 0; o < co; ++o) std::copy_n(&src[(size_t)o * cv.k], cv.k, &dst[(size_t)o * cv.kp]);
+            upload_elt(cv.w, dst, elt);
+        };
+        auto blocks = [&](std::vector<Block>& out, const std::string& p, int ci, int co, int f) {
+            const int bn = c.bottleneck_factor;
+            for (int i = 0; i < c.blocks_per_scale; ++i) {
+                // Block::load (mdx23c.rs:243-263).
+                const std::string q = p + ".blocks." + std::to_string(i);
+                Block b;
+                b.ci = i == 0 ? ci : co; b.co = co; b.f = f; b.fb = f / bn;
+                norm(b.n1, q + ".tfc1.0", b.ci);
+                conv(b.c1, q + ".tfc1.2.weight", co, b.ci, 3);
+                norm(b.t0, q + ".tdf.0", co);
+                upload_elt(b.tdf1, w.take(q + ".tdf.2.weight", {b.fb, f}), elt);
+                norm(b.t3, q + ".tdf.3", co);
+                upload_elt(b.tdf2, w.take(q + ".tdf.5.weight", {f, b.fb}), elt);
+                norm(b.n2, q + ".tfc2.0", co);
+                conv(b.c2, q + ".tfc2.2.weight", co, co, 3);
+                conv(b.sc, q + ".shortcut.weight", co, b.ci, 1);
+                out.push_back(std::move(b));
+            }
+        };
+        // Mdx23c::build (mdx23c.rs:379-418).
+        const int input = 4 * c.subbands;
+        conv(m->first_, "first_conv.weight", c.channels, input, 1);
+        int ch = c.channels, f = c.bins / c.subbands;
+        for (int i = 0; i < c.scales; ++i) {
+            const std::string p = "encoder_blocks." + std::to_string(i);
+            Down d;
+            blocks(d.blocks, p + ".tfc_tdf", ch, ch, f);
+            norm(d.norm, p + ".downscale.conv.0", ch);
+            conv(d.conv, p + ".downscale.conv.2.weight", ch + c.growth, ch, 2);
+            m->down_.push_back(std::move(d));
+            f /= 2;
+            ch += c.growth;
+        }
+        blocks(m->bottom_, "bottleneck_block", ch, ch, f);
+        for (int i = 0; i < c.scales; ++i) {
+            const std::string p = "decoder_blocks." + std::to_string(i);
+            const int co = ch - c.growth;
+            f *= 2;
+            Up u;
+            u.co = co;
+            norm(u.norm, p + ".upscale.conv.0", ch);
+            // ConvTranspose2d weight [ci][co][2][2] → GEMM rows (co, dy, dx) over K = ci.
+            const std::vector<float> src = w.take(p + ".upscale.conv.2.weight", {ch, co, 2, 2});
+            u.conv.co = 4 * co; u.conv.kh = u.conv.kw = 1; u.conv.k = ch; u.conv.kp = (int)round8(ch);
+            std::vector<float> dst((size_t)4 * co * u.conv.kp, 0.f);
+            for (int ci = 0; ci < ch; ++ci)
+                for (int r = 0; r < 4 * co; ++r) dst[(size_t)r * u.conv.kp + ci] = src[(size_t)ci * 4 * co + r];
+            upload_elt(u.conv.w, dst, elt);
+            blocks(u.blocks, p + ".tfc_tdf", co * 2, co, f);
+            m->up_.push_back(std::move(u));
+            ch = co;
+        }
+        conv(m->final_first_, "final_conv.0.weight", ch, ch + input, 1);
+        conv(m->final_last_, "final_conv.2.weight", (int)c.stems.size() * input, ch, 1);
+        m->tensor_count = w.finish();
+    } catch (...) {
+        hasher.join();
+        throw;
+    }
+    hasher.join();
+    if (digest != m->manifest.weights_sha256) bad("model checksum mismatch");
+    return m;
+}
+
+int Mdx23c::ensure_workspace(int batch, int frames) {
+    if (batch == ws_batch_ && frames == ws_frames_) return ANCHA_OK;
+    const Mdx23cConfig& c = manifest.config;
+    const int64_t b = batch, f0 = c.bins / c.subbands, t0 = frames;
+    const size_t es = elt_size(elt_);
+    int64_t act = 0, patch = 0, rows = 0;
+    auto pos = [&](int l) { return (t0 >> l) * (f0 >> l); };
+    for (int l = 0; l <= c.scales; ++l) {
+        const int64_t cl = c.channels + (int64_t)l * c.growth;
+        act = std::max(act, b * cl * pos(l));
+        rows = std::max(rows, b * cl * pos(l));
+        const int64_t cin = l < c.scales ? 2 * cl : cl;  // decoder blocks read cat(up, skip)
+        patch = std::max(patch, b * pos(l) * round8(9 * std::max(cin, cl)));
+        if (l < c.scales) {
+            patch = std::max(patch, b * pos(l + 1) * round8(4 * cl));                    // down
+            patch = std::max(patch, b * pos(l + 1) * round8(cl + c.growth));              // up
+        }
+    }
+    const int64_t input = 4 * c.subbands;
+    patch = std::max(patch, b * pos(0) * round8(input + c.channels));  // final_first (and first)
+    const size_t fb = sizeof(float);
+    for (DevBuf* d : {&first_f_, &x0_, &z_, &ff_}) d->alloc((size_t)(b * c.channels * pos(0)) * fb);
+    for (DevBuf* d : {&skip_sc_, &h_, &y1_, &s_, &blk_a_, &blk_b_, &up_raw_, &up_out_}) d->alloc((size_t)act * fb);
+    in_.alloc((size_t)act * fb);
+    cur_.alloc((size_t)act * fb);
+    patch_.alloc((size_t)patch * es);
+    rows_.alloc((size_t)rows * es);
+    stats_a_.alloc((size_t)b * 2048 * sizeof(double2));
+    stats_b_.alloc((size_t)b * 2048 * sizeof(double2));
+    skips_.clear();
+    skips_.resize(c.scales);
+    for (int l = 0; l < c.scales; ++l)
+        skips_[l].alloc((size_t)(b * (c.channels + (int64_t)l * c.growth) * pos(l)) * fb);
+    ws_batch_ = batch;
+    ws_frames_ = frames;
+    return ANCHA_OK;
+}
+
+int Mdx23c::gemm(const void* a, int64_t lda, const void* b, int64_t ldb, int m, int n, int k, float* out,
+                 int64_t ldo, const float* residual, cudaStream_t s) {
+    GemmGroup g{};
+    g.a = a; g.b = b; g.bias = nullptr; g.residual = residual; g.out = out;
+    g.m = m; g.n = n; g.k = k;
+    g.lda = lda; g.ldb = ldb; g.ldr = ldo; g.ldo = ldo;
+    GemmEpilogue e{};
+    e.act = ANCHA_ACT_NONE;
+    e.out_type = ELT_F32;
+    e.rope_tokens = 1;
+    e.rope_div = 1;
+    e.rope_hd = 64;
+    if (elt_ != ELT_F32) {
+        const int st = gemm_tc(g, elt_, e, s);
+        if (st != ANCHA_E_UNSUPPORTED) return st;
+    }
+    return gemm_ffma(g, nullptr, 1, m, n, elt_, elt_, 1, e, s);
+}
+
+int Mdx23c::conv(const Conv& w, const PackSource& a, const PackSource& b, int batch, int h, int wd, int stride,
+                 int pad, bool gelu, float* out, const float* residual, cudaStream_t s) {
+    if (a.channels + b.channels != w.k / (w.kh * w.kw)) return fail(ANCHA_E_INVALID, "mdx23c: conv channels");
+    const int ho = (h + 2 * pad - w.kh) / stride + 1, wo = (wd + 2 * pad - w.kw) / stride + 1;
+    const int64_t npos = (int64_t)ho * wo;
+    const size_t es = elt_size(elt_);
+    if ((size_t)(batch * npos * w.kp) * es > patch_.bytes) return fail(ANCHA_E_INVALID, "mdx23c: patch workspace");
+    PackArgs p{};
+    p.a = a; p.b = b;
+    p.batch = batch; p.h = h; p.w = wd; p.ho_n = ho; p.wo_n = wo;
+    p.kh = w.kh; p.kw = w.kw; p.sh = p.sw = stride; p.ph = p.pw = pad;
+    p.gelu = gelu; p.eps = kNormEps; p.kp = w.kp; p.out = patch_.p; p.out_type = elt_;
+    ANCHA_TRY(mdx_pack(p, s));
+    for (int i = 0; i < batch; ++i) {
+        const uint8_t* pb = patch_.as<uint8_t>() + (size_t)(i * npos * w.kp) * es;
+        ANCHA_TRY(gemm(w.w.p, w.kp, pb, w.kp, w.co, (int)npos, w.kp, out + (size_t)i * w.co * npos, npos,
+                       residual ? residual + (size_t)i * w.co * npos : nullptr, s));
+    }
+    return ANCHA_OK;
+}
+
+int Mdx23c::block(const Block& bk, const PackSource& a, const PackSource& b, int batch, int t, int f, float* out,
+                  cudaStream_t s) {
+    // Block::forward (mdx23c.rs:264-274).
+    const int64_t pos = (int64_t)t * f;
+    const int co = bk.co;
+    const PackSource none{nullptr, 0, nullptr, nullptr, nullptr};
+    PackSource ar{a.x, a.channels, nullptr, nullptr, nullptr}, br{b.x, b.channels, nullptr, nullptr, nullptr};
+    ANCHA_TRY(conv(bk.sc, ar, b.channels ? br : none, batch, t, f, 1, 0, false, skip_sc_.as<float>(), nullptr, s));
+    // x = tfc1(x): norm over the channels of the concatenation, per source.
+    double2* sa = stats_a_.as<double2>();
+    double2* sb = stats_b_.as<double2>();
+    ANCHA_TRY(mdx_plane_stats(a.x, (int64_t)batch * a.channels, pos, sa, s));
+    if (b.channels) ANCHA_TRY(mdx_plane_stats(b.x, (int64_t)batch * b.channels, pos, sb, s));
+    const float* g1 = bk.n1.gamma.as<float>();
+    const float* b1 = bk.n1.beta.as<float>();
+    const PackSource an{a.x, a.channels, sa, g1, b1};
+    const PackSource bn{b.x, b.channels, sb, g1 + a.channels, b1 + a.channels};
+    float* h = h_.as<float>();
+    ANCHA_TRY(conv(bk.c1, an, b.channels ? bn : none, batch, t, f, 1, 1, true, h, nullptr, s));
+    // y = tdf2(gelu(norm(tdf1(gelu(norm(x)))))); s = x + y.
+    const int64_t rows = (int64_t)batch * co * t;
+    ANCHA_TRY(mdx_plane_stats(h, (int64_t)batch * co, pos, sa, s));
+    ANCHA_TRY(mdx_norm_act(h, (int64_t)batch * co, pos, co, sa, bk.t0.gamma.as<float>(), bk.t0.beta.as<float>(),
+                           kNormEps, true, rows_.p, elt_, s));
+    float* y1 = y1_.as<float>();
+    ANCHA_TRY(gemm(rows_.p, f, bk.tdf1.p, f, (int)rows, bk.fb, f, y1, bk.fb, nullptr, s));
+    ANCHA_TRY(mdx_plane_stats(y1, (int64_t)batch * co, (int64_t)t * bk.fb, sa, s));
+    ANCHA_TRY(mdx_norm_act(y1, (int64_t)batch * co, (int64_t)t * bk.fb, co, sa, bk.t3.gamma.as<float>(),
+                           bk.t3.beta.as<float>(), kNormEps, true, rows_.p, elt_, s));
+    float* sum = s_.as<float>();
+    ANCHA_TRY(gemm(rows_.p, bk.fb, bk.tdf2.p, bk.fb, (int)rows, f, bk.fb, sum, f, h, s));
+    // out = tfc2(s) + shortcut(x).
+    ANCHA_TRY(mdx_plane_stats(sum, (int64_t)batch * co, pos, sa, s));
+    const PackSource sn{sum, co, sa, bk.n2.gamma.as<float>(), bk.n2.beta.as<float>()};
+    return conv(bk.c2, sn, none, batch, t, f, 1, 1, true, out, skip_sc_.as<float>(), s);
+}
+
+int Mdx23c::forward(const float* spectrum, int batch, int frames, float* out, const volatile int* cancel,
+                    cudaStream_t s) {
+    const Mdx23cConfig& c = manifest.config;
+    const int factor = 1 << c.scales;
+    if (batch <= 0 || batch > 4 || frames < factor || frames % factor)
+        return fail(ANCHA_E_INVALID, "invalid MDX23C spectrum shape");
+    if ((int64_t)frames * c.bins > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "MDX23C spectrum too large");
+    if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
+    ANCHA_CUDA(cudaSetDevice(device));
+    ANCHA_TRY(ensure_workspace(batch, frames));
+    const int input = 4 * c.subbands, f0 = c.bins / c.subbands, ch = c.channels;
+    const PackSource none{nullptr, 0, nullptr, nullptr, nullptr};
+    // mix = spectrum viewed as [batch][4·subbands][bins / subbands][frames] (mdx23c.rs:435).
+    const PackSource mix{spectrum, input, nullptr, nullptr, nullptr};
+    float* first = first_f_.as<float>();
+    ANCHA_TRY(conv(first_, mix, none, batch, f0, frames, 1, 0, false, first, nullptr, s));
+    ANCHA_TRY(mdx_transpose(first, nullptr, (int64_t)batch * ch, f0, frames, x0_.as<float>(), s));
+    auto run_blocks = [&](const std::vector<Block>& blocks, PackSource a, PackSource b, int t, int f,
+                          float* dst) -> int {
+        for (size_t i = 0; i < blocks.size(); ++i) {
+            if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
+            float* o = i + 1 == blocks.size() ? dst : (i % 2 ? blk_b_.as<float>() : blk_a_.as<float>());
+            ANCHA_TRY(block(blocks[i], a, b, batch, t, f, o, s));
+            a = PackSource{o, blocks[i].co, nullptr, nullptr, nullptr};
+            b = none;
+        }
+        return ANCHA_OK;
+    };
+    // Encoder (mdx23c.rs:440-444): blocks, keep the skip, then norm → GELU → 2 × 2 / 2 conv.
+    PackSource x{x0_.as<float>(), ch, nullptr, nullptr, nullptr};
+    int t = frames, f = f0, cl = ch;
+    for (int l = 0; l < c.scales; ++l) {
+        float* skip = skips_[l].as<float>();
+        ANCHA_TRY(run_blocks(down_[l].blocks, x, none, t, f, skip));
+        double2* sa = stats_a_.as<double2>();
+        ANCHA_TRY(mdx_plane_stats(skip, (int64_t)batch * cl, (int64_t)t * f, sa, s));
+        const PackSource sn{skip, cl, sa, down_[l].norm.gamma.as<float>(), down_[l].norm.beta.as<float>()};
+        ANCHA_TRY(conv(down_[l].conv, sn, none, batch, t, f, 2, 0, true, in_.as<float>(), nullptr, s));
+        t /= 2; f /= 2; cl += c.growth;
+        x = PackSource{in_.as<float>(), cl, nullptr, nullptr, nullptr};
+    }
+    ANCHA_TRY(run_blocks(bottom_, x, none, t, f, cur_.as<float>()));
+    // Decoder (Up::forward, mdx23c.rs:330-355): norm → GELU → ConvTranspose2d(2, 2) as a
+    // GEMM over the input positions plus a scatter, then blocks over cat(up, skip).
+    for (int i = 0; i < c.scales; ++i) {
+        const Up& u = up_[i];
+        double2* sa = stats_a_.as<double2>();
+        ANCHA_TRY(mdx_plane_stats(cur_.as<float>(), (int64_t)batch * cl, (int64_t)t * f, sa, s));
+        const PackSource un{cur_.as<float>(), cl, sa, u.norm.gamma.as<float>(), u.norm.beta.as<float>()};
+        ANCHA_TRY(conv(u.conv, un, none, batch, t, f, 1, 0, true, up_raw_.as<float>(), nullptr, s));
+        ANCHA_TRY(mdx_shuffle2x2(up_raw_.as<float>(), batch, u.co, t, f, up_out_.as<float>(), u.co, 0, s));
+        t *= 2; f *= 2; cl = u.co;
+        const int l = c.scales - 1 - i;
+        const PackSource up{up_out_.as<float>(), u.co, nullptr, nullptr, nullptr};
+        const PackSource sk{skips_[l].as<float>(), u.co, nullptr, nullptr, nullptr};
+        ANCHA_TRY(run_blocks(u.blocks, up, sk, t, f, cur_.as<float>()));
+    }
+    if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
+    // x.swap_dims(2, 3) · first, then final_conv = 1×1 → GELU → 1×1 over cat(mix, x)
+    // (mdx23c.rs:475-480).
+    ANCHA_TRY(mdx_transpose(cur_.as<float>(), first, (int64_t)batch * ch, frames, f0, z_.as<float>(), s));
+    const PackSource z{z_.as<float>(), ch, nullptr, nullptr, nullptr};
+    ANCHA_TRY(conv(final_first_, mix, z, batch, f0, frames, 1, 0, false, ff_.as<float>(), nullptr, s));
+    const PackSource ffs{ff_.as<float>(), ch, nullptr, nullptr, nullptr};
+    return conv(final_last_, ffs, none, batch, f0, frames, 1, 0, true, out, nullptr, s);
+}
+
+}  // namespace ancha

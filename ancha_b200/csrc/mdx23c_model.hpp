@@ -1,0 +1,86 @@
+// MDX23C (TFC-TDF v3) network on the device: package loading and the forward pass of
+// crates/ancha-models/src/mdx23c.rs behind ancha_mdx23c_* in the C ABI.
+#pragma once
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "hostio.hpp"
+#include "mdx23c.cuh"
+#include "model.hpp"
+
+namespace ancha {
+
+// crates/ancha-models/src/mdx23c.rs::Config (mdx23c.rs:37-52), checked like Config::validate
+// (mdx23c.rs:76-122).
+struct Mdx23cConfig {
+    int sample_rate = 0, n_fft = 0, hop = 0, bins = 0, frames = 0, overlap = 0, subbands = 0,
+        channels = 0, growth = 0, scales = 0, blocks_per_scale = 0, bottleneck_factor = 0;
+    std::vector<int> scale;
+    std::vector<std::string> stems;
+    int64_t chunk_samples() const { return (int64_t)hop * (frames - 1); }
+    void validate() const;  // throws std::runtime_error
+    static Mdx23cConfig from_json(const Json& j);  // strict keys (deny_unknown_fields)
+};
+
+struct Mdx23cManifest {
+    int schema_version = 0;
+    std::string model_id, weights_sha256, checkpoint_sha256, source_url, forward_revision,
+        weight_license;
+    Mdx23cConfig config;
+    static Mdx23cManifest from_json(const Json& j);
+    void validate() const;
+};
+
+class Mdx23c {
+public:
+    static std::unique_ptr<Mdx23c> load(const std::string& package, int device, int precision);
+    // spectrum [batch][4][bins][frames] → out [batch][stems·4][bins][frames], both device f32
+    // (mdx23c.rs:420-481). Checks *cancel (host, may be null) before every block.
+    int forward(const float* spectrum, int batch, int frames, float* out, const volatile int* cancel,
+                cudaStream_t s);
+
+    Mdx23cManifest manifest;
+    int device = 0, precision = 0;
+    size_t tensor_count = 0;
+
+    struct Norm { DevBuf gamma, beta; };
+    struct Conv { DevBuf w; int co = 0, k = 0, kp = 0, kh = 1, kw = 1; };  // w [co][kp], elt
+    struct Block {
+        Norm n1, t0, t3, n2;
+        Conv c1, c2, sc;
+        DevBuf tdf1, tdf2;  // [f / bn][f], [f][f / bn] (NK), elt
+        int ci = 0, co = 0, f = 0, fb = 0;
+    };
+    struct Down { std::vector<Block> blocks; Norm norm; Conv conv; };
+    struct Up { Norm norm; Conv conv; std::vector<Block> blocks; int co = 0; };  // conv rows (co, dy, dx)
+
+private:
+    // Bias-free convolution of the channel concatenation (a, b) of NCHW [batch][·][h][wd]
+    // planes: patch gather (with the sources' norms and GELU) then one GEMM per batch item,
+    // out[b][co][ho][wo] (+ residual of the same shape).
+    int conv(const Conv& w, const PackSource& a, const PackSource& b, int batch, int h, int wd, int stride,
+             int pad, bool gelu, float* out, const float* residual, cudaStream_t s);
+    int gemm(const void* a, int64_t lda, const void* b, int64_t ldb, int m, int n, int k, float* out,
+             int64_t ldo, const float* residual, cudaStream_t s);
+    int block(const Block& bk, const PackSource& a, const PackSource& b, int batch, int t, int f, float* out,
+              cudaStream_t s);
+    int ensure_workspace(int batch, int frames);
+
+    int elt_ = 0;
+    Conv first_, final_first_, final_last_;
+    std::vector<Down> down_;
+    std::vector<Block> bottom_;
+    std::vector<Up> up_;
+    // Workspace for one (batch, frames) shape.
+    int ws_batch_ = 0, ws_frames_ = 0;
+    DevBuf first_f_, x0_, skip_sc_, h_, y1_, s_, blk_a_, blk_b_, up_raw_, up_out_, z_, ff_, in_, cur_, patch_,
+        rows_, stats_a_, stats_b_;
+    std::vector<DevBuf> skips_;
+};
+
+}  // namespace ancha
+
+struct ancha_mdx23c {
+    std::unique_ptr<ancha::Mdx23c> impl;
+};

@@ -8,7 +8,7 @@ config 2 (time axis [B=60, H=8, T, 64] for T ∈ {801, 1601, 3201}; band axis
 [B=801, H=8, S=60, 64]). Times are CUDA-event averages after warm-up; FLOPs are algorithmic
 (attention 4·B·H·T²·D, GEMM 2·M·N·K with unpadded N).
 
-    python -m ancha_b200.microbench [--kernel all|gemm|attention] [--reps N] [--dtype f16]
+    python -m ancha_b200.microbench [--kernel all|gemm|attention|mdx23c] [--reps N] [--dtype f16]
 """
 from __future__ import annotations
 
@@ -111,10 +111,34 @@ def run_attention(dtype, reps):
     return out
 
 
+def run_mdx23c(dtype_name, reps):
+    """MDX23C inst_voc_hq2 forward (BASELINE config 4's network, synthetic seeded weights) on
+    one chunk: [1, 4, 4096, 256] → [1, 8, 4096, 256]."""
+    import shutil
+    import tempfile
+
+    import torch
+
+    from .mdx23c import Mdx23c, forward_flops, inst_voc_hq2, random_tensors, write_package
+    c = inst_voc_hq2()
+    d = tempfile.mkdtemp(prefix="mdx23c-bench-")
+    try:
+        write_package(d, c, random_tensors(c))
+        m = Mdx23c(d, 0, dtype_name)
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
+    x = torch.randn(1, 4, c["bins"], c["frames"], device="cuda")
+    ms = _time(lambda: m.forward(x), reps)
+    flops = forward_flops(c, 1, c["frames"])
+    step_s = c["hop"] * (c["frames"] - 1) / c["overlap"] / c["sample_rate"]  # new audio per chunk
+    return [{"kernel": "mdx23c_forward", "case": "inst_voc_hq2 batch 1 frames 256", "dtype": dtype_name,
+             "ms": ms, "tflops": flops / (ms / 1e3) / 1e12, "x_realtime_model_only": step_s / (ms / 1e3)}]
+
+
 def main(argv=None):
     import torch
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("--kernel", default="all", choices=["all", "gemm", "attention"])
+    p.add_argument("--kernel", default="all", choices=["all", "gemm", "attention", "mdx23c"])
     p.add_argument("--reps", type=int, default=20)
     p.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
     a = p.parse_args(argv)
@@ -124,6 +148,8 @@ def main(argv=None):
         res += run_gemm(dt, a.reps)
     if a.kernel in ("all", "attention"):
         res += run_attention(dt, a.reps)
+    if a.kernel == "mdx23c":
+        res += run_mdx23c(a.dtype, a.reps)
     for r in res:
         print(json.dumps(r))
 

@@ -190,6 +190,34 @@ ANCHA_API int ancha_model_forward(ancha_model* model, const float* spectrum, int
 ANCHA_API void ancha_model_free(ancha_model* model);
 
 /* ------------------------------------------------------------------------------------ *
+ * MDX23C model API (replaces Mdx23c::load / forward, crates/ancha-models/src/mdx23c.rs) *
+ * ------------------------------------------------------------------------------------ */
+
+typedef struct ancha_mdx23c ancha_mdx23c;
+
+/* Load an MDX23C (TFC-TDF v3) package: `package_dir/manifest.json` (strict schema-1
+ * manifest whose config has family "mdx23c", checked like Config::validate,
+ * mdx23c.rs:76-122) + `model.safetensors` (F32, SHA-256 verified, every tensor used) onto
+ * `device` (Mdx23c::load / build, mdx23c.rs:372-418). */
+ANCHA_API int ancha_mdx23c_load(const char* package_dir, int device, int precision, ancha_mdx23c** out);
+
+/* Shape queries: bins, native frames, n_fft, hop, overlap, stems, and the number of
+ * tensors the package held (Mdx23c::tensor_count). Any pointer may be NULL. */
+ANCHA_API int ancha_mdx23c_info(const ancha_mdx23c* model, int* bins, int* frames, int* n_fft, int* hop,
+                      int* overlap, int* stems, int* tensor_count);
+
+/* spectrum[batch][4][bins][frames] (device f32: L.re, L.im, R.re, R.im) →
+ * out[batch][stems·4][bins][frames] (device f32 spectra, not masks) (Mdx23c::forward,
+ * mdx23c.rs:420-481). batch 1..4; frames a multiple of 2^scales (any such count, not only
+ * the manifest's); ANCHA_E_INVALID otherwise. Checks *cancel (host memory, may be NULL)
+ * before every block (mdx23c.rs:307). The handle is bound to its device and is not
+ * re-entrant. */
+ANCHA_API int ancha_mdx23c_forward(ancha_mdx23c* model, const float* spectrum, int batch, int frames,
+                         float* out, const volatile int* cancel, void* stream);
+
+ANCHA_API void ancha_mdx23c_free(ancha_mdx23c* model);
+
+/* ------------------------------------------------------------------------------------ *
  * Task API (replaces backend::separate / runtime::separate, src/backend.rs:145-199)    *
  * ------------------------------------------------------------------------------------ */
 
