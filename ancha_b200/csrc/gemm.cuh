@@ -79,4 +79,23 @@ struct GroupedGemm {
 
 int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& epi, cudaStream_t stream);
 
+// Implicit-GEMM convolution on the tcgen05 kernel, no patch matrix:
+// out[co][y·w + x] = Σ_tap Σ_c weight[co][tap·channels + c] · act[image][y + dy][x + dx][c]
+// (+ residual[co][y·w + x]) over a channels-last activation act[batch][h][w][channels]
+// (operand type), taps 9 = the 3 × 3 stencil (dy, dx) ∈ {−1, 0, 1}² row-major with zero
+// padding 1, taps 1 = a 1 × 1 convolution. channels % 64 == 0; w a multiple or a divisor of
+// 256. Epilogue: no activation / rotary / row-norm fusion.
+struct ConvGemm {
+    const void* weight;  // [co][taps · channels] (row stride ldw)
+    int64_t ldw;
+    int co;
+    const void* x;       // [batch][h][w][channels]
+    int batch, h, w, channels, image, taps;
+    const float* residual;  // [co][ldo] f32 or null
+    void* out;           // [co][ldo] of the epilogue's out_type
+    int64_t ldo;
+};
+
+int gemm_tc_conv(const ConvGemm& q, int ab_type, const GemmEpilogue& epi, cudaStream_t stream);
+
 }  // namespace ancha

@@ -60,6 +60,12 @@ struct TcParams {
     uint32_t idesc;
     int m_tiles, n_tiles, tiles;
     int* err;
+    // Implicit-GEMM convolution (0 taps = off): B is read straight from a channels-last
+    // activation [batch][h][w][channels] through a 4-D tensor map; k block kb is tap
+    // kb / conv_cblocks (a 3 × 3 stencil with zero padding 1 for 9 taps, the centre for 1),
+    // channels 64·(kb % conv_cblocks); output column n is position n = y·conv_w + x of image
+    // conv_b.
+    int conv_taps, conv_cblocks, conv_w, conv_b;
 };
 
 constexpr int STAGE_BYTES = 4096;    // one 32-row × 128-byte epilogue staging buffer
@@ -330,7 +336,16 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                     if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort, p.err)) break;
                     mbar_arrive_expect_tx(&full[s], A_BYTES + S::B_BYTES);
                     tma_load_3d(a_tiles + s * A_BYTES, &tma_a, &full[s], kb * BK, c.m0, c.g);
-                    tma_load_3d(b_tiles + s * S::B_BYTES, &tma_b, &full[s], kb * BK, c.n0, bg);
+                    if (p.conv_taps) {
+                        // The tap's shifted window; rows or columns outside the image load as
+                        // zeros (the convolution's padding).
+                        const int tap = kb / p.conv_cblocks, cb = kb - tap * p.conv_cblocks;
+                        const int dy = p.conv_taps == 9 ? tap / 3 - 1 : 0, dx = p.conv_taps == 9 ? tap % 3 - 1 : 0;
+                        const int y0 = c.n0 / p.conv_w, x0 = c.n0 - y0 * p.conv_w;
+                        tma_load_4d(b_tiles + s * S::B_BYTES, &tma_b, &full[s], cb * BK, x0 + dx, y0 + dy, p.conv_b);
+                    } else {
+                        tma_load_3d(b_tiles + s * S::B_BYTES, &tma_b, &full[s], kb * BK, c.n0, bg);
+                    }
                 }
             }
             if (*abort) {  // let copies in flight land before the CTA exits (bounded)
@@ -533,6 +548,45 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     p.res_col = e.res_col; p.out16 = e.out16; p.out16_col = e.out16_col;
     p.ss_out = e.ss_out; p.ss16_out = e.ss16_out; p.ab16 = ab_type;
     return run(g.a, g.lda, (int64_t)g.m * g.lda, g.b, g.ldb, (int64_t)g.n * g.ldb, p, ab_type, s);
+}
+
+int gemm_tc_conv(const ConvGemm& q, int ab_type, const GemmEpilogue& e, cudaStream_t s) {
+    if (ab_type != ELT_BF16 && ab_type != ELT_F16) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: operand type");
+    if (q.taps != 1 && q.taps != 9) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: taps");
+    if (q.channels <= 0 || q.channels % BK || q.co <= 0 || q.h <= 0 || q.w <= 0 || q.batch <= 0 ||
+        q.image < 0 || q.image >= q.batch)
+        return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: shape");
+    constexpr int bn = 256;
+    // A tile of 256 output positions is a box of whole rows (w ≤ 256) or a run inside one row.
+    if (!(q.w % bn == 0 || bn % q.w == 0)) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: row width");
+    const size_t oe = elt_size(e.out_type);
+    if (!aligned16(q.out) || (q.ldo * oe) % 16 || (q.residual && (!aligned16(q.residual) || (q.ldo * 4) % 16)))
+        return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: output not 16-byte aligned");
+    if (e.act != ANCHA_ACT_NONE || e.rope || e.rope_pairs || e.row_ss || e.res_ss || e.out16 || e.ss_out)
+        return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: epilogue");
+    TcParams p{};
+    p.m = q.co; p.n = q.h * q.w; p.k = q.taps * q.channels; p.groups = 1; p.b_groups = 1; p.group_n = nullptr;
+    p.out = q.out; p.ldo = q.ldo; p.out_group_stride = 0;
+    p.bias = nullptr; p.bias_group_stride = 0;
+    p.residual = q.residual; p.ldr = q.ldo;
+    p.act = ANCHA_ACT_NONE; p.out_type = e.out_type;
+    p.rope_tokens = 1; p.rope_div = 1; p.rope_hd = 64; p.ab16 = ab_type;
+    p.conv_taps = q.taps; p.conv_cblocks = q.channels / BK; p.conv_w = q.w; p.conv_b = q.image;
+    CUtensorMap ta, tb, to;
+    ANCHA_TRY(make_tma_3d(&ta, q.weight, ab_type, p.k, p.m, 1, q.ldw, (int64_t)p.m * q.ldw, BM));
+    const int bw = std::min(q.w, bn);
+    ANCHA_TRY(make_tma_4d(&tb, q.x, ab_type, q.channels, q.w, q.h, q.batch, q.channels, (int64_t)q.w * q.channels,
+                          (int64_t)q.h * q.w * q.channels, bw, bn / bw));
+    ANCHA_TRY(make_tma_store_3d(&to, p.out, p.out_type, std::min<int64_t>(p.n, p.ldo), p.m, 1, p.ldo,
+                                (int64_t)p.m * p.ldo, 32, 32));
+    p.idesc = umma_idesc_f16(ab_type == ELT_BF16, BM, bn);
+    p.err = device_error_word();
+    p.m_tiles = (int)ceil_div(p.m, BM);
+    p.n_tiles = (int)ceil_div(p.n, bn);
+    const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+    if (tiles > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: too many tiles");
+    p.tiles = (int)tiles;
+    return launch<bn, 3, EPI_PLAIN>(ta, tb, to, to, p, s);
 }
 
 int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& e, cudaStream_t s) {

@@ -1,4 +1,4 @@
-// Device kernels of the MDX23C (TFC-TDF v3) network: per-plane instance-norm statistics,
+// Device kernels of the MDX23C (TFC-TDF v3) network: per-plane instance-norm coefficients,
 // the fused norm → GELU → patch gather that feeds every convolution's GEMM, the row-wise
 // norm → GELU that feeds the TDF GEMMs, plane transposes and the 2 × 2 transpose-convolution
 // scatter. Activations are NCHW f32 planes; GEMM operands are f32, f16 or bf16.
@@ -7,40 +7,46 @@
 
 namespace ancha {
 
-// Sums and sums of squares (f64) of each contiguous plane of `n` floats, accumulated into
-// `stats[plane]` (zeroed here first). The consumers derive mean and 1/sqrt(var + eps).
-int mdx_plane_stats(const float* x, int64_t planes, int64_t n, double2* stats, cudaStream_t s);
+// Instance-norm coefficients of `planes` contiguous planes of `n` floats: with the plane's
+// mean and biased variance (f64 sums), coef[p] = (γ[c]/√(var + eps), β[c] − mean·γ[c]/√(var + eps))
+// for channel c = p % channels, so normalising is one FMA. `scratch` holds planes · 32
+// doubles2 of partial sums.
+int mdx_norm_coef(const float* x, int64_t planes, int64_t n, int channels, const float* gamma,
+                  const float* beta, float eps, double2* scratch, float2* coef, cudaStream_t s);
 
-// One NCHW source of a patch gather: `channels` planes of [h][w] per batch item, optional
-// instance norm (stats from mdx_plane_stats over the same planes, gamma / beta per channel).
+// One NCHW source of a patch gather: `channels` planes of [h][w] per batch item and, when
+// `coef` is set, their instance norm as per-plane (scale, shift) from mdx_norm_coef.
 struct PackSource {
     const float* x;
     int channels;
-    const double2* stats;  // [batch][channels] or null (no norm)
-    const float* gamma;
-    const float* beta;
+    const float2* coef;  // [batch · channels] or null (no norm)
 };
 
 // Patch matrix of a bias-free convolution: P[b][ho·wo_n + wo][k], k = (c·kh + ky)·kw + kx
 // over the channels of `a` then `b` (a channel concatenation), value = act(norm(x)) at input
 // (ho·sh − ph + ky, wo·sw − pw + kx) or 0 outside the plane; columns K..kp−1 are 0. `gelu`
-// applies the exact erf GELU after the norm. P is of element type `out_type`.
+// applies the exact erf GELU after the norm. P is of element type `out_type`. Geometries:
+// 1×1 / stride 1, 3×3 / stride 1 and 2×2 / stride 2 (the network's three); kp % 8 == 0.
 struct PackArgs {
     PackSource a, b;
     int batch, h, w, ho_n, wo_n;
     int kh, kw, sh, sw, ph, pw;
     bool gelu;
-    float eps;
     int64_t kp;
     void* out;
     int out_type;
 };
 int mdx_pack(const PackArgs& a, cudaStream_t s);
 
-// out[i] = act(norm(x[i])) over `planes` contiguous planes of `n` floats (plane index
-// i / n, channel (i / n) % channels), written as `out_type`; the TDF GEMM input.
-int mdx_norm_act(const float* x, int64_t planes, int64_t n, int channels, const double2* stats,
-                 const float* gamma, const float* beta, float eps, bool gelu, void* out,
+// Channels-last copy for the implicit-GEMM convolution: out[b][pos][c] (f16 / bf16) =
+// act(norm(x)) over the channel concatenation of `a` and `b` (NCHW planes of `pos` values);
+// a.channels + b.channels must be a multiple of 64.
+int mdx_preact_nhwc(const PackSource& a, const PackSource& b, int batch, int64_t pos, bool gelu, void* out,
+                    int out_type, cudaStream_t s);
+
+// out[i] = act(x[i]·coef[p].x + coef[p].y) over `planes` contiguous planes of `n` floats
+// (p = i / n), written as `out_type`; the TDF GEMM input.
+int mdx_norm_act(const float* x, int64_t planes, int64_t n, const float2* coef, bool gelu, void* out,
                  int out_type, cudaStream_t s);
 
 // out[p][c][r] = x[p][r][c] · (mul ? mul[p][c][r] : 1) for `planes` planes of rows × cols.

@@ -156,12 +156,24 @@ std::unique_ptr<Mdx23c> Mdx23c::load(const std::string& package, int device, int
             upload(n.beta, w.take(p + ".bias", {ch}));
         };
         // [co][ci][kh][kw] → [co][kp]: PyTorch's flattening is the patch column order
-        // k = (ci·kh + ky)·kw + kx of mdx_pack; columns k..kp−1 are zero.
-        auto conv = [&](Conv& cv, const std::string& name, int co, int ci, int k) {
+        // k = (ci·kh + ky)·kw + kx of mdx_pack; columns k..kp−1 are zero. A 3 × 3 layer over
+        // planes `width` wide that the implicit-GEMM kernel can run (16-bit operands, channels
+        // in 64s, width a multiple or divisor of its 256-position tile) is stored tap-major.
+        auto conv = [&](Conv& cv, const std::string& name, int co, int ci, int k, int width = 0) {
             const std::vector<float> src = w.take(name, {co, ci, k, k});
             cv.co = co; cv.kh = cv.kw = k; cv.k = ci * k * k; cv.kp = (int)round8(cv.k);
+            cv.tap_major = k == 3 && elt != ELT_F32 && ci % 64 == 0 && width > 0 &&
+                           (width % 256 == 0 || 256 % width == 0);
             std::vector<float> dst((size_t)co * cv.kp, 0.f);
-            for (int o = 0; o < co; ++o) std::copy_n(&src[(size_t)o * cv.k], cv.k, &dst[(size_t)o * cv.kp]);
+            for (int o = 0; o < co; ++o) {
+                if (cv.tap_major) {
+                    for (int c = 0; c < ci; ++c)
+                        for (int t = 0; t < k * k; ++t)
+                            dst[(size_t)o * cv.kp + (size_t)t * ci + c] = src[((size_t)o * ci + c) * k * k + t];
+                } else {
+                    std::copy_n(&src[(size_t)o * cv.k], cv.k, &dst[(size_t)o * cv.kp]);
+                }
+            }
             upload_elt(cv.w, dst, elt);
         };
         auto blocks = [&](std::vector<Block>& out, const std::string& p, int ci, int co, int f) {
@@ -172,13 +184,13 @@ std::unique_ptr<Mdx23c> Mdx23c::load(const std::string& package, int device, int
                 Block b;
                 b.ci = i == 0 ? ci : co; b.co = co; b.f = f; b.fb = f / bn;
                 norm(b.n1, q + ".tfc1.0", b.ci);
-                conv(b.c1, q + ".tfc1.2.weight", co, b.ci, 3);
+                conv(b.c1, q + ".tfc1.2.weight", co, b.ci, 3, f);
                 norm(b.t0, q + ".tdf.0", co);
                 upload_elt(b.tdf1, w.take(q + ".tdf.2.weight", {b.fb, f}), elt);
                 norm(b.t3, q + ".tdf.3", co);
                 upload_elt(b.tdf2, w.take(q + ".tdf.5.weight", {f, b.fb}), elt);
                 norm(b.n2, q + ".tfc2.0", co);
-                conv(b.c2, q + ".tfc2.2.weight", co, co, 3);
+                conv(b.c2, q + ".tfc2.2.weight", co, co, 3, f);
                 conv(b.sc, q + ".shortcut.weight", co, b.ci, 1);
                 out.push_back(std::move(b));
             }
@@ -255,8 +267,9 @@ int Mdx23c::ensure_workspace(int batch, int frames) {
     cur_.alloc((size_t)act * fb);
     patch_.alloc((size_t)patch * es);
     rows_.alloc((size_t)rows * es);
-    stats_a_.alloc((size_t)b * 2048 * sizeof(double2));
-    stats_b_.alloc((size_t)b * 2048 * sizeof(double2));
+    sums_.alloc((size_t)b * 2048 * 32 * sizeof(double2));
+    coef_a_.alloc((size_t)b * 2048 * sizeof(float2));
+    coef_b_.alloc((size_t)b * 2048 * sizeof(float2));
     skips_.clear();
     skips_.resize(c.scales);
     for (int l = 0; l < c.scales; ++l)
@@ -291,12 +304,39 @@ int Mdx23c::conv(const Conv& w, const PackSource& a, const PackSource& b, int ba
     const int ho = (h + 2 * pad - w.kh) / stride + 1, wo = (wd + 2 * pad - w.kw) / stride + 1;
     const int64_t npos = (int64_t)ho * wo;
     const size_t es = elt_size(elt_);
+    const int cin = a.channels + b.channels;
+    const bool implicit = elt_ != ELT_F32 && stride == 1 && cin % 64 == 0 && (wd % 256 == 0 || 256 % wd == 0) &&
+                          ((w.kh == 1 && pad == 0) || (w.kh == 3 && pad == 1 && w.tap_major));
+    if (implicit) {
+        // Channels-last act(norm(x)) once, then the GEMM reads each tap's shifted window
+        // through TMA (zero fill at the borders is the padding).
+        if ((size_t)(batch * npos * cin) * es > patch_.bytes) return fail(ANCHA_E_INVALID, "mdx23c: patch workspace");
+        ANCHA_TRY(mdx_preact_nhwc(a, b, batch, npos, gelu, patch_.p, elt_, s));
+        GemmEpilogue e{};
+        e.act = ANCHA_ACT_NONE;
+        e.out_type = ELT_F32;
+        e.rope_tokens = 1;
+        e.rope_div = 1;
+        e.rope_hd = 64;
+        for (int i = 0; i < batch; ++i) {
+            ConvGemm q{};
+            q.weight = w.w.p; q.ldw = w.kp; q.co = w.co;
+            q.x = patch_.p; q.batch = batch; q.h = h; q.w = wd; q.channels = cin; q.image = i;
+            q.taps = w.kh * w.kw;
+            q.residual = residual ? residual + (size_t)i * w.co * npos : nullptr;
+            q.out = out + (size_t)i * w.co * npos;
+            q.ldo = npos;
+            ANCHA_TRY(gemm_tc_conv(q, elt_, e, s));
+        }
+        return ANCHA_OK;
+    }
+    if (w.tap_major) return fail(ANCHA_E_INVALID, "mdx23c: tap-major weights need the implicit-GEMM path");
     if ((size_t)(batch * npos * w.kp) * es > patch_.bytes) return fail(ANCHA_E_INVALID, "mdx23c: patch workspace");
     PackArgs p{};
     p.a = a; p.b = b;
     p.batch = batch; p.h = h; p.w = wd; p.ho_n = ho; p.wo_n = wo;
     p.kh = w.kh; p.kw = w.kw; p.sh = p.sw = stride; p.ph = p.pw = pad;
-    p.gelu = gelu; p.eps = kNormEps; p.kp = w.kp; p.out = patch_.p; p.out_type = elt_;
+    p.gelu = gelu; p.kp = w.kp; p.out = patch_.p; p.out_type = elt_;
     ANCHA_TRY(mdx_pack(p, s));
     for (int i = 0; i < batch; ++i) {
         const uint8_t* pb = patch_.as<uint8_t>() + (size_t)(i * npos * w.kp) * es;
@@ -311,36 +351,39 @@ int Mdx23c::block(const Block& bk, const PackSource& a, const PackSource& b, int
     // Block::forward (mdx23c.rs:264-274).
     const int64_t pos = (int64_t)t * f;
     const int co = bk.co;
-    const PackSource none{nullptr, 0, nullptr, nullptr, nullptr};
-    PackSource ar{a.x, a.channels, nullptr, nullptr, nullptr}, br{b.x, b.channels, nullptr, nullptr, nullptr};
+    const PackSource none{nullptr, 0, nullptr};
+    const PackSource ar{a.x, a.channels, nullptr}, br{b.x, b.channels, nullptr};
     ANCHA_TRY(conv(bk.sc, ar, b.channels ? br : none, batch, t, f, 1, 0, false, skip_sc_.as<float>(), nullptr, s));
     // x = tfc1(x): norm over the channels of the concatenation, per source.
-    double2* sa = stats_a_.as<double2>();
-    double2* sb = stats_b_.as<double2>();
-    ANCHA_TRY(mdx_plane_stats(a.x, (int64_t)batch * a.channels, pos, sa, s));
-    if (b.channels) ANCHA_TRY(mdx_plane_stats(b.x, (int64_t)batch * b.channels, pos, sb, s));
+    float2* ka = coef_a_.as<float2>();
+    float2* kb = coef_b_.as<float2>();
     const float* g1 = bk.n1.gamma.as<float>();
     const float* b1 = bk.n1.beta.as<float>();
-    const PackSource an{a.x, a.channels, sa, g1, b1};
-    const PackSource bn{b.x, b.channels, sb, g1 + a.channels, b1 + a.channels};
+    ANCHA_TRY(norm_coef(a.x, batch, a.channels, pos, g1, b1, ka, s));
+    if (b.channels) ANCHA_TRY(norm_coef(b.x, batch, b.channels, pos, g1 + a.channels, b1 + a.channels, kb, s));
+    const PackSource an{a.x, a.channels, ka}, bn{b.x, b.channels, kb};
     float* h = h_.as<float>();
     ANCHA_TRY(conv(bk.c1, an, b.channels ? bn : none, batch, t, f, 1, 1, true, h, nullptr, s));
     // y = tdf2(gelu(norm(tdf1(gelu(norm(x)))))); s = x + y.
     const int64_t rows = (int64_t)batch * co * t;
-    ANCHA_TRY(mdx_plane_stats(h, (int64_t)batch * co, pos, sa, s));
-    ANCHA_TRY(mdx_norm_act(h, (int64_t)batch * co, pos, co, sa, bk.t0.gamma.as<float>(), bk.t0.beta.as<float>(),
-                           kNormEps, true, rows_.p, elt_, s));
+    ANCHA_TRY(norm_coef(h, batch, co, pos, bk.t0.gamma.as<float>(), bk.t0.beta.as<float>(), ka, s));
+    ANCHA_TRY(mdx_norm_act(h, (int64_t)batch * co, pos, ka, true, rows_.p, elt_, s));
     float* y1 = y1_.as<float>();
     ANCHA_TRY(gemm(rows_.p, f, bk.tdf1.p, f, (int)rows, bk.fb, f, y1, bk.fb, nullptr, s));
-    ANCHA_TRY(mdx_plane_stats(y1, (int64_t)batch * co, (int64_t)t * bk.fb, sa, s));
-    ANCHA_TRY(mdx_norm_act(y1, (int64_t)batch * co, (int64_t)t * bk.fb, co, sa, bk.t3.gamma.as<float>(),
-                           bk.t3.beta.as<float>(), kNormEps, true, rows_.p, elt_, s));
+    ANCHA_TRY(norm_coef(y1, batch, co, (int64_t)t * bk.fb, bk.t3.gamma.as<float>(), bk.t3.beta.as<float>(), ka, s));
+    ANCHA_TRY(mdx_norm_act(y1, (int64_t)batch * co, (int64_t)t * bk.fb, ka, true, rows_.p, elt_, s));
     float* sum = s_.as<float>();
     ANCHA_TRY(gemm(rows_.p, bk.fb, bk.tdf2.p, bk.fb, (int)rows, f, bk.fb, sum, f, h, s));
     // out = tfc2(s) + shortcut(x).
-    ANCHA_TRY(mdx_plane_stats(sum, (int64_t)batch * co, pos, sa, s));
-    const PackSource sn{sum, co, sa, bk.n2.gamma.as<float>(), bk.n2.beta.as<float>()};
+    ANCHA_TRY(norm_coef(sum, batch, co, pos, bk.n2.gamma.as<float>(), bk.n2.beta.as<float>(), ka, s));
+    const PackSource sn{sum, co, ka};
     return conv(bk.c2, sn, none, batch, t, f, 1, 1, true, out, skip_sc_.as<float>(), s);
+}
+
+int Mdx23c::norm_coef(const float* x, int batch, int channels, int64_t n, const float* gamma, const float* beta,
+                      float2* coef, cudaStream_t s) {
+    return mdx_norm_coef(x, (int64_t)batch * channels, n, channels, gamma, beta, kNormEps, sums_.as<double2>(), coef,
+                         s);
 }
 
 int Mdx23c::forward(const float* spectrum, int batch, int frames, float* out, const volatile int* cancel,
@@ -354,9 +397,9 @@ int Mdx23c::forward(const float* spectrum, int batch, int frames, float* out, co
     ANCHA_CUDA(cudaSetDevice(device));
     ANCHA_TRY(ensure_workspace(batch, frames));
     const int input = 4 * c.subbands, f0 = c.bins / c.subbands, ch = c.channels;
-    const PackSource none{nullptr, 0, nullptr, nullptr, nullptr};
+    const PackSource none{nullptr, 0, nullptr};
     // mix = spectrum viewed as [batch][4·subbands][bins / subbands][frames] (mdx23c.rs:435).
-    const PackSource mix{spectrum, input, nullptr, nullptr, nullptr};
+    const PackSource mix{spectrum, input, nullptr};
     float* first = first_f_.as<float>();
     ANCHA_TRY(conv(first_, mix, none, batch, f0, frames, 1, 0, false, first, nullptr, s));
     ANCHA_TRY(mdx_transpose(first, nullptr, (int64_t)batch * ch, f0, frames, x0_.as<float>(), s));
@@ -366,47 +409,49 @@ int Mdx23c::forward(const float* spectrum, int batch, int frames, float* out, co
             if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
             float* o = i + 1 == blocks.size() ? dst : (i % 2 ? blk_b_.as<float>() : blk_a_.as<float>());
             ANCHA_TRY(block(blocks[i], a, b, batch, t, f, o, s));
-            a = PackSource{o, blocks[i].co, nullptr, nullptr, nullptr};
+            a = PackSource{o, blocks[i].co, nullptr};
             b = none;
         }
         return ANCHA_OK;
     };
     // Encoder (mdx23c.rs:440-444): blocks, keep the skip, then norm → GELU → 2 × 2 / 2 conv.
-    PackSource x{x0_.as<float>(), ch, nullptr, nullptr, nullptr};
+    PackSource x{x0_.as<float>(), ch, nullptr};
     int t = frames, f = f0, cl = ch;
     for (int l = 0; l < c.scales; ++l) {
         float* skip = skips_[l].as<float>();
         ANCHA_TRY(run_blocks(down_[l].blocks, x, none, t, f, skip));
-        double2* sa = stats_a_.as<double2>();
-        ANCHA_TRY(mdx_plane_stats(skip, (int64_t)batch * cl, (int64_t)t * f, sa, s));
-        const PackSource sn{skip, cl, sa, down_[l].norm.gamma.as<float>(), down_[l].norm.beta.as<float>()};
+        float2* ka = coef_a_.as<float2>();
+        ANCHA_TRY(norm_coef(skip, batch, cl, (int64_t)t * f, down_[l].norm.gamma.as<float>(),
+                            down_[l].norm.beta.as<float>(), ka, s));
+        const PackSource sn{skip, cl, ka};
         ANCHA_TRY(conv(down_[l].conv, sn, none, batch, t, f, 2, 0, true, in_.as<float>(), nullptr, s));
         t /= 2; f /= 2; cl += c.growth;
-        x = PackSource{in_.as<float>(), cl, nullptr, nullptr, nullptr};
+        x = PackSource{in_.as<float>(), cl, nullptr};
     }
     ANCHA_TRY(run_blocks(bottom_, x, none, t, f, cur_.as<float>()));
     // Decoder (Up::forward, mdx23c.rs:330-355): norm → GELU → ConvTranspose2d(2, 2) as a
     // GEMM over the input positions plus a scatter, then blocks over cat(up, skip).
     for (int i = 0; i < c.scales; ++i) {
         const Up& u = up_[i];
-        double2* sa = stats_a_.as<double2>();
-        ANCHA_TRY(mdx_plane_stats(cur_.as<float>(), (int64_t)batch * cl, (int64_t)t * f, sa, s));
-        const PackSource un{cur_.as<float>(), cl, sa, u.norm.gamma.as<float>(), u.norm.beta.as<float>()};
+        float2* ka = coef_a_.as<float2>();
+        ANCHA_TRY(norm_coef(cur_.as<float>(), batch, cl, (int64_t)t * f, u.norm.gamma.as<float>(),
+                            u.norm.beta.as<float>(), ka, s));
+        const PackSource un{cur_.as<float>(), cl, ka};
         ANCHA_TRY(conv(u.conv, un, none, batch, t, f, 1, 0, true, up_raw_.as<float>(), nullptr, s));
         ANCHA_TRY(mdx_shuffle2x2(up_raw_.as<float>(), batch, u.co, t, f, up_out_.as<float>(), u.co, 0, s));
         t *= 2; f *= 2; cl = u.co;
         const int l = c.scales - 1 - i;
-        const PackSource up{up_out_.as<float>(), u.co, nullptr, nullptr, nullptr};
-        const PackSource sk{skips_[l].as<float>(), u.co, nullptr, nullptr, nullptr};
+        const PackSource up{up_out_.as<float>(), u.co, nullptr};
+        const PackSource sk{skips_[l].as<float>(), u.co, nullptr};
         ANCHA_TRY(run_blocks(u.blocks, up, sk, t, f, cur_.as<float>()));
     }
     if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
     // x.swap_dims(2, 3) · first, then final_conv = 1×1 → GELU → 1×1 over cat(mix, x)
     // (mdx23c.rs:475-480).
     ANCHA_TRY(mdx_transpose(cur_.as<float>(), first, (int64_t)batch * ch, frames, f0, z_.as<float>(), s));
-    const PackSource z{z_.as<float>(), ch, nullptr, nullptr, nullptr};
+    const PackSource z{z_.as<float>(), ch, nullptr};
     ANCHA_TRY(conv(final_first_, mix, z, batch, f0, frames, 1, 0, false, ff_.as<float>(), nullptr, s));
-    const PackSource ffs{ff_.as<float>(), ch, nullptr, nullptr, nullptr};
+    const PackSource ffs{ff_.as<float>(), ch, nullptr};
     return conv(final_last_, ffs, none, batch, f0, frames, 1, 0, true, out, nullptr, s);
 }
 

@@ -45,7 +45,9 @@ public:
     size_t tensor_count = 0;
 
     struct Norm { DevBuf gamma, beta; };
-    struct Conv { DevBuf w; int co = 0, k = 0, kp = 0, kh = 1, kw = 1; };  // w [co][kp], elt
+    // w [co][kp] (elt): patch-column order (c, ky, kx) for the patch-matrix path, or
+    // (ky, kx, c) when tap_major (3 × 3 layers that run as implicit GEMMs).
+    struct Conv { DevBuf w; int co = 0, k = 0, kp = 0, kh = 1, kw = 1; bool tap_major = false; };
     struct Block {
         Norm n1, t0, t3, n2;
         Conv c1, c2, sc;
@@ -65,6 +67,9 @@ private:
              int64_t ldo, const float* residual, cudaStream_t s);
     int block(const Block& bk, const PackSource& a, const PackSource& b, int batch, int t, int f, float* out,
               cudaStream_t s);
+    // Instance-norm (scale, shift) per plane of batch · channels planes of n values.
+    int norm_coef(const float* x, int batch, int channels, int64_t n, const float* gamma, const float* beta,
+                  float2* coef, cudaStream_t s);
     int ensure_workspace(int batch, int frames);
 
     int elt_ = 0;
@@ -75,7 +80,7 @@ private:
     // Workspace for one (batch, frames) shape.
     int ws_batch_ = 0, ws_frames_ = 0;
     DevBuf first_f_, x0_, skip_sc_, h_, y1_, s_, blk_a_, blk_b_, up_raw_, up_out_, z_, ff_, in_, cur_, patch_,
-        rows_, stats_a_, stats_b_;
+        rows_, sums_, coef_a_, coef_b_;
     std::vector<DevBuf> skips_;
 };
 

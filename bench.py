@@ -22,6 +22,9 @@ independent, so ranks shard the work with no collective ("scaling": "weak").
   bf16, one 180 s track (chunk 352800, overlap 2 → 47 chunks) sharded over the ranks
   (``ancha_b200.distributed``: each rank separates its chunk range, one reduce of the spans);
   host PCM in, host stems out on rank 0, wall clock, ``"scaling": "strong"``.
+* ``config4``: BASELINE config 4, the MDX23C inst_voc_hq2 forward in bf16, 16 chunks per GPU
+  (4 calls of batch 4) on spectra in HBM: ms, TFLOP/s against the measured bf16 peak, and
+  model-only ×realtime (0.74 s of new audio per chunk at overlap 8).
 * ``cpu_baseline``: the numpy oracle (f32, all host cores) on one native chunk (rank 0, N=1).
 * ``--impl reference`` times that CPU port per step instead (the reference itself is Rust and
   cannot be built offline).
@@ -57,6 +60,7 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--package", default=os.environ.get("ANCHA_BENCH_PACKAGE", "/tmp/ancha_bench/mel-seed0"))
     p.add_argument("--no-config3", action="store_true")
+    p.add_argument("--no-config4", action="store_true")
     p.add_argument("--pipeline-only", action="store_true",
                    help="run only the warm-up and timed pipeline steps (for launch-list captures)")
     return p.parse_args()
@@ -99,6 +103,61 @@ def config3(local: int, world: int, rank: int, dist, steps: int = 2):
                         f"over {world} GPU(s)", "value": 180.0 / t, "unit": "×realtime",
             "seconds_per_track": t, "steps": steps, "scaling": "strong", "dtype": "bf16",
             "timing": "wall clock, host PCM in, host stems out on rank 0, median of steps"}
+
+
+def config4(local: int, world: int, rank: int, dist, steps: int = 3):
+    """the MDX23C inst_voc_hq2 forward (TFC-TDF v3 U-Net, 128 channels,
+    growth 128, 5 scales, 2 blocks per scale, bottleneck factor 4; dim_f 4096 × dim_t 256),
+    bf16, seeded synthetic weights, 16 chunks per GPU as 4 calls of batch 4 (the reference's
+    batch limit, mdx23c.rs:428-431) on spectra already in HBM; CUDA events, max over ranks."""
+    import torch
+    from ancha_b200.mdx23c import Mdx23c, forward_flops, inst_voc_hq2, random_tensors, write_package
+    c = inst_voc_hq2()
+    pkg = "/tmp/ancha_bench/mdx23c-seed0"
+    if rank == 0 or int(os.environ.get("LOCAL_RANK", "0")) == 0:
+        if not os.path.exists(os.path.join(pkg, "manifest.json")):
+            write_package(pkg + ".tmp", c, random_tensors(c, seed=0))
+            os.replace(pkg + ".tmp", pkg)
+    if dist:
+        dist.barrier()
+    model = Mdx23c(pkg, local, "bf16")
+    g = torch.Generator(device="cuda").manual_seed(4000 + rank)
+    x = torch.randn(16, 4, c["bins"], c["frames"], device="cuda", generator=g) * 0.1
+    out = torch.empty(16, 8, c["bins"], c["frames"], device="cuda")
+
+    def step():
+        for i in range(0, 16, 4):
+            out[i:i + 4] = model.forward(x[i:i + 4])
+
+    step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    assert bool(torch.isfinite(out).all())
+    model.close()
+    if rank != 0:
+        return None
+    flops = forward_flops(c, 16, c["frames"])
+    new_audio = 16 * c["hop"] * (c["frames"] - 1) / c["overlap"] / c["sample_rate"]
+    return {"workload": "mdx23c inst_voc_hq2 forward, bf16, 16 chunks [4, 4096, 256] per GPU as 4 calls "
+                        f"of batch 4, x{world} GPU(s)",
+            "ms_per_16_chunks": ms, "chunks_per_s": 16 * world / (ms / 1e3),
+            "tflops_per_gpu": flops / (ms / 1e3) / 1e12,
+            "tflops_frac": flops / (ms / 1e3) / 1e12 / peaks()[1],
+            "x_realtime_model_only": new_audio * world / (ms / 1e3),
+            "note": "x_realtime_model_only counts the 0.74 s of new audio per chunk at overlap 8; "
+                    "STFT / iSTFT / overlap-add not included", "scaling": "weak", "dtype": "bf16"}
 
 
 def peaks():
@@ -405,6 +464,10 @@ def main():
     if not a.no_config3:
         c3 = config3(local, world, rank, dist)
 
+    c4 = None
+    if not a.no_config4:
+        c4 = config4(local, world, rank, dist)
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         _, one = cpu_oracle_chunk(a.package)
@@ -428,7 +491,7 @@ def main():
             "clocks": clk.summary(), "e2e": e2e,
             "gpu_launches": launches_per_step(chunks, effective_batch(chunks, a.batch),
                                               fused=a.precision != "f32") * a.steps,
-            "roofline": roofline, "attention": attention, "config3": c3, "cpu_baseline": cpu,
+            "roofline": roofline, "attention": attention, "config3": c3, "config4": c4, "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     model.close()

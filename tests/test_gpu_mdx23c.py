@@ -113,6 +113,49 @@ def test_mid_network_matches_oracle(torch_cuda, mid, precision):
         assert s >= SNR_FLOOR[precision]
 
 
+def wide_config():
+    """Planes 1024 / 512 / 256 wide with channels in 64s: every 3 × 3 and 1 × 1 layer of the
+    16-bit paths runs as an implicit GEMM, with 256-position tiles inside one row."""
+    return dict(family="mdx23c", sample_rate=44100, n_fft=2048, hop=256, bins=1024, frames=8, overlap=4,
+                subbands=1, channels=64, growth=64, scales=2, blocks_per_scale=1, bottleneck_factor=4,
+                scale=[2, 2], stems=["vocals", "instrumental"])
+
+
+@pytest.mark.parametrize("precision", ["f32", "f16", "bf16"])
+def test_wide_network_matches_oracle(torch_cuda, tmp_path, precision):
+    from ancha_b200.mdx23c import random_tensors
+    c = wide_config()
+    M.validate(c)
+    w = random_tensors(c, seed=3)
+    write_package(str(tmp_path), c, w)
+    x = np.random.default_rng(13).standard_normal((1, 4, c["bins"], c["frames"])).astype(np.float32)
+    ref = M.forward(c, w, x)
+    y = Mdx23c(str(tmp_path), 0, precision).forward(torch_cuda.from_numpy(x).cuda()).cpu().numpy()
+    s = snr_db(ref, y)
+    print(f"wide {precision}: {s:.1f} dB")
+    if precision == "f32":
+        assert np.abs(y - ref).max() / np.abs(ref).max() < 1e-5
+    else:
+        assert s >= SNR_FLOOR[precision]
+
+
+@pytest.mark.parametrize("precision", ["f16", "bf16"])
+def test_full_size_reduced_precision_against_f32(torch_cuda, tmp_path, precision):
+    """inst_voc_hq2 at its native size (BASELINE config 4's network, synthetic weights): the
+    16-bit implicit-GEMM forward against this library's f32 forward (FFMA GEMMs and patch
+    matrices, checked against the oracle above), a size-independent SNR check."""
+    from ancha_b200.mdx23c import inst_voc_hq2, random_tensors
+    c = inst_voc_hq2()
+    write_package(str(tmp_path), c, random_tensors(c, seed=1))
+    x = torch_cuda.randn(1, 4, c["bins"], c["frames"], generator=torch_cuda.Generator().manual_seed(2)).cuda()
+    ref = Mdx23c(str(tmp_path), 0, "f32").forward(x).cpu().numpy()
+    y = Mdx23c(str(tmp_path), 0, precision).forward(x).cpu().numpy()
+    assert np.isfinite(y).all()
+    s = snr_db(ref, y)
+    print(f"inst_voc_hq2 {precision} vs f32: {s:.1f} dB")
+    assert s >= SNR_FLOOR[precision]
+
+
 def test_batch_and_frame_count_other_than_the_manifest(torch_cuda, mid):
     c, w, d = mid
     rng = np.random.default_rng(5)
