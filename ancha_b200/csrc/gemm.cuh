@@ -48,6 +48,10 @@ struct GemmEpilogue {
     const float* out16_col;
     float* ss_out;
     float* ss16_out;
+    // Per-plane statistics of the output (tensor-core path, one group): Σ v and Σ v² of rows
+    // r are added (f64 atomics) into stats[r / stats_div]; the caller zeroes them. Null = off.
+    double2* stats;
+    int stats_div;
 };
 
 // FFMA GEMM (fp32 accumulation). `groups` is a device array of `count` problems when

@@ -66,7 +66,34 @@ struct TcParams {
     // channels 64·(kb % conv_cblocks); output column n is position n = y·conv_w + x of image
     // conv_b.
     int conv_taps, conv_cblocks, conv_w, conv_b;
+    // Per-plane output statistics (null = off): Σ v and Σ v² of the final output values of
+    // rows r, r + 1, … are added into stats[r / stats_div] (f64), for the instance norm that
+    // follows this GEMM. Single-group problems only.
+    double2* stats;
+    int stats_div;
 };
+
+// Adds a lane's accumulated (Σ v, Σ v²) into stats[plane]; lanes of a warp that share one
+// plane are combined first, so a warp over consecutive rows of one plane issues one pair of
+// atomics.
+__device__ __forceinline__ void flush_stats(double2* stats, int plane, double& sum, double& sq, int lane) {
+    const int first = __shfl_sync(0xffffffffu, plane, 0), last = __shfl_sync(0xffffffffu, plane, 31);
+    if (first == last) {
+        for (int o = 16; o > 0; o >>= 1) {
+            sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        }
+        if (lane == 0 && plane >= 0) {
+            atomicAdd(&stats[plane].x, sum);
+            atomicAdd(&stats[plane].y, sq);
+        }
+    } else if (plane >= 0) {
+        atomicAdd(&stats[plane].x, sum);
+        atomicAdd(&stats[plane].y, sq);
+    }
+    sum = 0.0;
+    sq = 0.0;
+}
 
 constexpr int STAGE_BYTES = 4096;    // one 32-row × 128-byte epilogue staging buffer
 constexpr int STAGE16_BYTES = 2048;  // one 32-row × 64-byte buffer for the 16-bit copy
@@ -392,6 +419,10 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         uint8_t* my_stage16 = staging + S::STAGING + (warp - 2) * STAGE16_BYTES;
         const bool glu = p.act == ANCHA_ACT_GLU;
         uint32_t local = 0, chunks = 0;
+        // Output statistics, accumulated over every tile of the same rows (a persistent CTA
+        // usually keeps its rows) and flushed when the plane changes.
+        double st_sum = 0.0, st_sq = 0.0;
+        int st_plane = -1;
         for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
             const TileCoord c = tile_coord(p, t, BN);
             if (c.n0 >= c.n_g) continue;
@@ -402,6 +433,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             const int row0 = c.m0 + quarter * 32;
             const int row = row0 + lane;
             const bool live = row < p.m;
+            if (p.stats) {
+                const int plane = live ? row / p.stats_div : -1;
+                if (__any_sync(0xffffffffu, plane != st_plane)) {
+                    flush_stats(p.stats, st_plane, st_sum, st_sq, lane);
+                    st_plane = plane;
+                }
+            }
             const uint32_t base = tmem + b * BN + ((uint32_t)(quarter * 32) << 16);
             const float row_scale = p.row_ss && live ? inv_norm(p.row_ss + row, p.row_ss_n, p.m) : 1.f;
             const float res_scale = p.res_ss && live ? inv_norm(p.res_ss + row, p.res_ss_n, p.m) : 1.f;
@@ -414,6 +452,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 float v[32];
                 const int count = epilogue32(p, c.g, row, live, c.n0 + col, c.n_g, r, v, row_scale, res_scale);
                 const int nv = min(32, c.n_g - (c.n0 + col));
+                if (p.stats && live) {
+                    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j < nv) {
+                            s1 += v[j];
+                            s2 = fmaf(v[j], v[j], s2);
+                        }
+                    st_sum += s1;
+                    st_sq += s2;
+                }
                 if (p.ss_out && count == 32) store_ss(p.ss_out, p, row, live, c.n0 + col, nv, v);
                 uint8_t* buf = my_stage + (chunks % STAGE_BUFS) * STAGE_BYTES;
                 if (chunks >= STAGE_BUFS) {  // the store that last read this buffer is done with it
@@ -446,6 +495,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             if (lane == 0) mbar_arrive(&tempty[b]);
             ++local;
         }
+        if (p.stats) flush_stats(p.stats, st_plane, st_sum, st_sq, lane);
         if (lane == 0) bulk_wait<0>();
         __syncwarp();
     }
@@ -547,6 +597,8 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     p.row_ss = e.row_ss; p.row_ss_n = e.row_ss_n; p.res_ss = e.res_ss; p.res_ss_n = e.res_ss_n;
     p.res_col = e.res_col; p.out16 = e.out16; p.out16_col = e.out16_col;
     p.ss_out = e.ss_out; p.ss16_out = e.ss16_out; p.ab16 = ab_type;
+    p.stats = e.stats; p.stats_div = e.stats_div > 0 ? e.stats_div : 1;
+    if (e.stats && e.act == ANCHA_ACT_GLU) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: statistics of a GLU output");
     return run(g.a, g.lda, (int64_t)g.m * g.lda, g.b, g.ldb, (int64_t)g.n * g.ldb, p, ab_type, s);
 }
 
@@ -572,6 +624,7 @@ int gemm_tc_conv(const ConvGemm& q, int ab_type, const GemmEpilogue& e, cudaStre
     p.act = ANCHA_ACT_NONE; p.out_type = e.out_type;
     p.rope_tokens = 1; p.rope_div = 1; p.rope_hd = 64; p.ab16 = ab_type;
     p.conv_taps = q.taps; p.conv_cblocks = q.channels / BK; p.conv_w = q.w; p.conv_b = q.image;
+    p.stats = e.stats; p.stats_div = e.stats_div > 0 ? e.stats_div : 1;
     CUtensorMap ta, tb, to;
     ANCHA_TRY(make_tma_3d(&ta, q.weight, ab_type, p.k, p.m, 1, q.ldw, (int64_t)p.m * q.ldw, BM));
     const int bw = std::min(q.w, bn);

@@ -1,10 +1,11 @@
 // MDX23C device kernels (declared in mdx23c.cuh). All of them are HBM-bound gathers and
 // elementwise passes around the network's GEMMs:
 //
-// * mdx_norm_coef: f64 sum and sum of squares per NCHW plane, folded with gamma / beta into
-//   one (scale, shift) per plane (the instance norms of mdx23c.rs:200-213 reduce over a whole
-//   (batch, channel) plane, so the statistics must be complete before any element is
-//   normalised);
+// * mdx_plane_sums: f64 sum and sum of squares per NCHW plane for tensors no GEMM produced
+//   (the GEMM epilogues accumulate them for their own outputs); every consumer turns a plane's
+//   sums into one (scale, shift) pair, so normalising is one FMA (the instance norms of
+//   mdx23c.rs:200-213 reduce over a whole (batch, channel) plane, so the statistics must be
+//   complete before any element is normalised);
 // * mdx_pack: norm → GELU → zero-padded patch gather into the K-major patch matrix of a
 //   convolution (the B operand of out[co][pos] = W[co][k]·P[pos][k]ᵀ), over a channel
 //   concatenation of two sources so the decoder's cat(up, skip) and the final cat(mix, x)
@@ -16,16 +17,18 @@
 
 #include <type_traits>
 
+#include "tc.cuh"  // gelu_fast
+
 namespace ancha {
 namespace {
 
 constexpr int kPackCols = 32;   // output columns per CTA
 constexpr int kPackChans = 32;  // channels per CTA
-constexpr int kSplits = 32;     // partial sums per plane in mdx_norm_coef
+constexpr int kSplits = 32;     // at most this many CTAs per plane in mdx_plane_sums
 
-__global__ void plane_sums_kernel(const float* __restrict__ x, int64_t n, double2* __restrict__ part) {
+__global__ void plane_sums_kernel(const float* __restrict__ x, int64_t n, double2* __restrict__ sums) {
     const int64_t plane = blockIdx.x;
-    const int64_t per = (n + kSplits - 1) / kSplits;
+    const int64_t per = (n + gridDim.y - 1) / gridDim.y;
     const int64_t lo = per * blockIdx.y, hi = min(n, lo + per);
     const float* p = x + plane * n;
     double s = 0.0, q = 0.0;
@@ -50,30 +53,50 @@ __global__ void plane_sums_kernel(const float* __restrict__ x, int64_t n, double
             s += __shfl_xor_sync(0xffffffffu, s, o);
             q += __shfl_xor_sync(0xffffffffu, q, o);
         }
-        if (lane == 0) part[plane * kSplits + blockIdx.y] = make_double2(s, q);
+        if (lane == 0) {
+            atomicAdd(&sums[plane].x, s);
+            atomicAdd(&sums[plane].y, q);
+        }
     }
 }
 
-// One warp per plane: add the partial sums, then scale = γ/√(var + eps), shift = β − mean·scale.
-__global__ void plane_coef_kernel(const double2* __restrict__ part, int64_t planes, int64_t n, int channels,
-                                  const float* __restrict__ gamma, const float* __restrict__ beta, float eps,
-                                  float2* __restrict__ coef) {
-    const int64_t plane = blockIdx.x * (int64_t)(blockDim.x / 32) + threadIdx.x / 32;
-    const int lane = threadIdx.x % 32;
-    if (plane >= planes) return;
-    const double2 v = part[plane * kSplits + lane];  // kSplits == 32: one partial per lane
-    double s = v.x, q = v.y;
-    for (int o = 16; o > 0; o >>= 1) {
-        s += __shfl_xor_sync(0xffffffffu, s, o);
-        q += __shfl_xor_sync(0xffffffffu, q, o);
-    }
-    if (lane == 0) {
-        const double mean = s / (double)n;
-        const double var = fmax(q / (double)n - mean * mean, 0.0);
-        const int c = (int)(plane % channels);
-        const double scale = (double)gamma[c] / sqrt(var + (double)eps);
-        coef[plane] = make_float2((float)scale, (float)((double)beta[c] - mean * scale));
-    }
+// (scale, shift) of the instance norm of one plane: γ/√(var + eps) and β − mean·scale.
+__device__ __forceinline__ float2 norm_coef(double2 sum, int64_t n, float gamma, float beta, float eps) {
+    const double mean = sum.x / (double)n;
+    const double var = fmax(sum.y / (double)n - mean * mean, 0.0);
+    const double scale = (double)gamma / sqrt(var + (double)eps);
+    return make_float2((float)scale, (float)((double)beta - mean * scale));
+}
+
+
+// GELU of a value that is stored in a 16-bit type (the exact erf form, x·Φ(x) with Φ from
+// Abramowitz–Stegun 7.1.26 on the MUFU pipe, |ΔΦ| ≤ 1.5e-7: far below the storage rounding)
+// or in f32 (erff).
+template <typename OutT>
+__device__ __forceinline__ float gelu_out(float x) {
+    if constexpr (std::is_same<OutT, float>::value) return gelu_erf(x);
+    else return gelu_fast(x);
+}
+
+// Norm coefficients for a 16-bit consumer: statistics in f64, the reciprocal square root in
+// f32 (relative error ~1e-7, far below the 16-bit storage).
+__device__ __forceinline__ float2 norm_coef_fast(double2 sum, int64_t n, float gamma, float beta, float eps) {
+    const double mean = sum.x / (double)n;
+    const double var = fmax(sum.y / (double)n - mean * mean, 0.0);
+    const float scale = gamma * rsqrtf((float)var + eps);
+    return make_float2(scale, beta - (float)mean * scale);
+}
+
+// Coefficients of channel c of the concatenation (a, b) for image `img`; (1, 0) without norm.
+template <typename OutT>
+__device__ __forceinline__ float2 source_coef(const PackArgs& a, int img, int c, int64_t n) {
+    const bool first = c < a.a.channels;
+    const PackSource& src = first ? a.a : a.b;
+    const int cs = first ? c : c - a.a.channels;
+    if (!src.sums) return make_float2(1.f, 0.f);
+    const double2 sum = src.sums[(int64_t)img * src.channels + cs];
+    return std::is_same<OutT, float>::value ? norm_coef(sum, n, src.gamma[cs], src.beta[cs], a.eps)
+                                            : norm_coef_fast(sum, n, src.gamma[cs], src.beta[cs], a.eps);
 }
 
 template <typename T> struct Pack8;
@@ -110,26 +133,25 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackArgs a, int nchunks
     constexpr int NCOLS = (kPackCols - 1) * S + K;
     constexpr int TAPS = K * K;
     __shared__ float tile[kPackChans * K * NCOLS];
+    __shared__ float2 coef[kPackChans];
     const int ctot = a.a.channels + a.b.channels;
     const int chunk = blockIdx.z % nchunks, b = blockIdx.z / nchunks;
     const int ho = blockIdx.y, wo0 = blockIdx.x * kPackCols;
     const int c0 = chunk * kPackChans, cc = min(kPackChans, ctot - c0);
     const int hi0 = ho * S - a.ph, wi0 = wo0 * S - a.pw;
     const int64_t plane_n = (int64_t)a.h * a.w;
+    if (threadIdx.x < cc) coef[threadIdx.x] = source_coef<OutT>(a, b, c0 + threadIdx.x, plane_n);
+    __syncthreads();
     for (int i = threadIdx.x; i < cc * K * NCOLS; i += blockDim.x) {
-        const int col = i % NCOLS, r = (i / NCOLS) % K, c = c0 + i / (NCOLS * K);
+        const int col = i % NCOLS, r = (i / NCOLS) % K, cl = i / (NCOLS * K), c = c0 + cl;
         const int hi = hi0 + r, wi = wi0 + col;
         float v = 0.f;
         if (hi >= 0 && hi < a.h && wi >= 0 && wi < a.w) {
             const bool first = c < a.a.channels;
             const PackSource& src = first ? a.a : a.b;
             const int64_t plane = (int64_t)b * src.channels + (first ? c : c - a.a.channels);
-            v = src.x[plane * plane_n + (int64_t)hi * a.w + wi];
-            if (src.coef) {
-                const float2 k = src.coef[plane];
-                v = fmaf(v, k.x, k.y);
-            }
-            if (a.gelu) v = gelu_erf(v);
+            v = fmaf(src.x[plane * plane_n + (int64_t)hi * a.w + wi], coef[cl].x, coef[cl].y);
+            if (a.gelu) v = gelu_out<OutT>(v);
         }
         tile[i] = v;
     }
@@ -155,76 +177,98 @@ __global__ void __launch_bounds__(256) pack_kernel(const PackArgs a, int nchunks
     }
 }
 
-// 32 positions × 64 channels per CTA through shared memory: coalesced reads along the planes,
-// 128-byte writes along the channels.
+// 128 positions × 64 channels per CTA through shared memory: every thread issues its 32
+// coalesced loads (8 channel rows × 4 runs of 32 positions) before any use, then each warp
+// writes whole 128-byte channel runs of 16 positions. Row stride 129 keeps both phases free
+// of shared-memory bank conflicts (2-way on the channel pairs).
+constexpr int kPreactPos = 128;
 template <typename OutT>
-__global__ void __launch_bounds__(256) preact_nhwc_kernel(const PackSource a, const PackSource b, int64_t pos,
-                                                          bool gelu, OutT* __restrict__ out) {
-    __shared__ float t[64][33];
-    const int ctot = a.channels + b.channels;
-    const int64_t p0 = (int64_t)blockIdx.x * 32;
+__global__ void __launch_bounds__(256) preact_nhwc_kernel(const PackArgs a, int64_t pos, OutT* __restrict__ out) {
+    __shared__ float t[64][kPreactPos + 1];
+    __shared__ float2 coef[64];
+    const int ctot = a.a.channels + a.b.channels;
+    const int64_t p0 = (int64_t)blockIdx.x * kPreactPos;
     const int c0 = blockIdx.y * 64, img = blockIdx.z;
     const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;
-    for (int r = ty; r < 64; r += 8) {
-        const int c = c0 + r;
-        const int64_t q = p0 + tx;
-        float v = 0.f;
-        if (q < pos) {
-            const bool first = c < a.channels;
-            const PackSource& src = first ? a : b;
-            const int64_t plane = (int64_t)img * src.channels + (first ? c : c - a.channels);
-            v = src.x[plane * pos + q];
-            if (src.coef) {
-                const float2 k = src.coef[plane];
-                v = fmaf(v, k.x, k.y);
-            }
-            if (gelu) v = gelu_erf(v);
+    if (threadIdx.x < 64) {
+        const int c = c0 + threadIdx.x;
+        const bool first = c < a.a.channels;
+        const PackSource& src = first ? a.a : a.b;
+        const int cs = first ? c : c - a.a.channels;
+        coef[threadIdx.x] = src.sums ? norm_coef_fast(src.sums[(int64_t)img * src.channels + cs], pos, src.gamma[cs],
+                                                      src.beta[cs], a.eps)
+                                     : make_float2(1.f, 0.f);
+    }
+    float v[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = ty + 8 * i, c = c0 + r;
+        const bool first = c < a.a.channels;
+        const PackSource& src = first ? a.a : a.b;
+        const float* plane = src.x + ((int64_t)img * src.channels + (first ? c : c - a.a.channels)) * pos;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int64_t q = p0 + 32 * j + tx;
+            v[i][j] = q < pos ? plane[q] : 0.f;
         }
-        t[r][tx] = v;
+    }
+    __syncthreads();  // coef
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int r = ty + 8 * i;
+        const float2 k = coef[r];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float x = fmaf(v[i][j], k.x, k.y);
+            if (a.gelu) x = gelu_out<OutT>(x);
+            t[r][32 * j + tx] = x;
+        }
     }
     __syncthreads();
-    for (int r = ty; r < 32; r += 8) {
-        const int64_t q = p0 + r;
-        if (q >= pos) break;
-        OutT* row = out + ((int64_t)img * pos + q) * ctot + c0;
-        const float v0 = t[2 * tx][r], v1 = t[2 * tx + 1][r];
-        if constexpr (sizeof(OutT) == 2) {
-            if constexpr (std::is_same<OutT, __half>::value)
-                reinterpret_cast<__half2*>(row)[tx] = __floats2half2_rn(v0, v1);
-            else
-                reinterpret_cast<__nv_bfloat162*>(row)[tx] = __floats2bfloat162_rn(v0, v1);
-        }
+    for (int q = ty; q < kPreactPos; q += 8) {
+        if (p0 + q >= pos) break;
+        OutT* row = out + ((int64_t)img * pos + p0 + q) * ctot + c0;
+        const float v0 = t[2 * tx][q], v1 = t[2 * tx + 1][q];
+        if constexpr (std::is_same<OutT, __half>::value)
+            reinterpret_cast<__half2*>(row)[tx] = __floats2half2_rn(v0, v1);
+        else
+            reinterpret_cast<__nv_bfloat162*>(row)[tx] = __floats2bfloat162_rn(v0, v1);
     }
 }
 
-// Planes whose length is not a multiple of 8 (small bottlenecks): one element per thread.
-__global__ void norm_act_scalar_kernel(const float* __restrict__ x, int64_t total, int64_t n,
-                                       const float2* __restrict__ coef, bool gelu, void* out, int out_type) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const float2 k = coef ? coef[i / n] : make_float2(1.f, 0.f);
-        float v = fmaf(x[i], k.x, k.y);
-        if (gelu) v = gelu_erf(v);
-        store_elt(out, i, v, out_type);
-    }
-}
-
+// grid (segments, planes): one plane's coefficients per CTA, 8 elements per thread when the
+// plane length allows 16-byte vectors, else one.
 template <typename OutT>
-__global__ void norm_act_kernel(const float* __restrict__ x, int64_t total8, int64_t n,
-                                const float2* __restrict__ coef, bool gelu, OutT* __restrict__ out) {
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total8;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t e = i * 8;
-        const float4 a = reinterpret_cast<const float4*>(x + e)[0];
-        const float4 b = reinterpret_cast<const float4*>(x + e)[1];
-        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-        const float2 k = coef ? coef[e / n] : make_float2(1.f, 0.f);  // n % 8 == 0: one plane per vector
+__global__ void __launch_bounds__(256) norm_act_kernel(const float* __restrict__ x, int64_t n, int channels,
+                                                       const double2* __restrict__ sums,
+                                                       const float* __restrict__ gamma,
+                                                       const float* __restrict__ beta, float eps, bool gelu,
+                                                       bool vec, OutT* __restrict__ out) {
+    const int64_t plane = blockIdx.y;
+    const int c = (int)(plane % channels);
+    const float2 k = !sums ? make_float2(1.f, 0.f)
+                     : std::is_same<OutT, float>::value ? norm_coef(sums[plane], n, gamma[c], beta[c], eps)
+                                                        : norm_coef_fast(sums[plane], n, gamma[c], beta[c], eps);
+    const float* xp = x + plane * n;
+    OutT* op = out + plane * n;
+    if (vec) {
+        for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n / 8; i += (int64_t)gridDim.x * blockDim.x) {
+            const float4 a = reinterpret_cast<const float4*>(xp + i * 8)[0];
+            const float4 b = reinterpret_cast<const float4*>(xp + i * 8)[1];
+            float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            v[u] = fmaf(v[u], k.x, k.y);
-            if (gelu) v[u] = gelu_erf(v[u]);
+            for (int u = 0; u < 8; ++u) {
+                v[u] = fmaf(v[u], k.x, k.y);
+                if (gelu) v[u] = gelu_out<OutT>(v[u]);
+            }
+            Pack8<OutT>::store(op + i * 8, v);
         }
-        Pack8<OutT>::store(out + e, v);
+    } else {
+        for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+            float v = fmaf(xp[i], k.x, k.y);
+            if (gelu) v = gelu_out<OutT>(v);
+            store_f(op + i, v);
+        }
     }
 }
 
@@ -248,36 +292,30 @@ __global__ void transpose_kernel(const float* __restrict__ x, const float* __res
     }
 }
 
-__global__ void shuffle2x2_kernel(const float* __restrict__ y, int channels, int h, int w,
-                                  int64_t total, float* __restrict__ out, int c_total, int c_off) {
-    const int ow = 2 * w, oh = 2 * h;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int ox = (int)(i % ow);
-        const int oy = (int)((i / ow) % oh);
-        const int c = (int)((i / ((int64_t)ow * oh)) % channels);
-        const int64_t b = i / ((int64_t)ow * oh * channels);
-        const int row = (c * 2 + (oy & 1)) * 2 + (ox & 1);
-        const float v = y[(b * channels * 4 + row) * (int64_t)h * w + (int64_t)(oy >> 1) * w + (ox >> 1)];
-        out[((b * c_total + c_off + c) * oh + oy) * (int64_t)ow + ox] = v;
-    }
-}
-
-int grid_for(int64_t total) {
-    return (int)std::min<int64_t>(ceil_div(total, 256), 148 * 16);
+// grid (⌈w / 256⌉, 2·h, batch · channels): thread x writes the pair of output columns
+// (2x, 2x + 1) of output row oy, which come from the dx = 0 and dx = 1 GEMM rows at input
+// position (oy / 2, x).
+__global__ void shuffle2x2_kernel(const float* __restrict__ y, int channels, int h, int w, float* __restrict__ out,
+                                  int c_total, int c_off) {
+    const int x = blockIdx.x * blockDim.x + threadIdx.x;
+    if (x >= w) return;
+    const int oy = blockIdx.y;
+    const int64_t bc = blockIdx.z;
+    const int64_t b = bc / channels, c = bc % channels;
+    const int64_t plane = (int64_t)h * w;
+    const float* src = y + ((b * channels + c) * 4 + (oy & 1) * 2) * plane + (int64_t)(oy >> 1) * w + x;
+    const float2 v = make_float2(src[0], src[plane]);
+    reinterpret_cast<float2*>(out + ((b * c_total + c_off + c) * 2 * h + oy) * (int64_t)(2 * w))[x] = v;
 }
 
 }  // namespace
 
-int mdx_norm_coef(const float* x, int64_t planes, int64_t n, int channels, const float* gamma,
-                  const float* beta, float eps, double2* scratch, float2* coef, cudaStream_t s) {
-    if (planes <= 0 || n <= 0 || channels <= 0) return fail(ANCHA_E_INVALID, "mdx_norm_coef: empty");
-    if (planes > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "mdx_norm_coef: too many planes");
-    plane_sums_kernel<<<dim3((unsigned)planes, kSplits), 256, 0, s>>>(x, n, scratch);
-    ANCHA_TRY(check_launch("mdx_norm_coef"));
-    plane_coef_kernel<<<(unsigned)ceil_div(planes, 8), 256, 0, s>>>(scratch, planes, n, channels, gamma, beta, eps,
-                                                                      coef);
-    return check_launch("mdx_norm_coef");
+int mdx_plane_sums(const float* x, int64_t planes, int64_t n, double2* sums, cudaStream_t s) {
+    if (planes <= 0 || n <= 0) return fail(ANCHA_E_INVALID, "mdx_plane_sums: empty");
+    if (planes > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "mdx_plane_sums: too many planes");
+    const int splits = (int)std::min<int64_t>(kSplits, ceil_div(n, 4096));
+    plane_sums_kernel<<<dim3((unsigned)planes, splits), 256, 0, s>>>(x, n, sums);
+    return check_launch("mdx_plane_sums");
 }
 
 namespace {
@@ -306,37 +344,40 @@ int mdx_pack(const PackArgs& a, cudaStream_t s) {
     return fail(ANCHA_E_UNSUPPORTED, "mdx_pack: geometry");
 }
 
-int mdx_preact_nhwc(const PackSource& a, const PackSource& b, int batch, int64_t pos, bool gelu, void* out,
-                    int out_type, cudaStream_t s) {
+int mdx_preact_nhwc(const PackSource& a, const PackSource& b, int batch, int64_t pos, bool gelu, float eps,
+                    void* out, int out_type, cudaStream_t s) {
     const int ctot = a.channels + b.channels;
     if (batch <= 0 || pos <= 0 || ctot <= 0 || ctot % 64 || (out_type != ELT_F16 && out_type != ELT_BF16))
         return fail(ANCHA_E_INVALID, "mdx_preact_nhwc: shape");
-    if (batch > 65535 || ctot / 64 > 65535 || ceil_div(pos, 32) > 0x7fffffff)
+    if (batch > 65535 || ctot / 64 > 65535 || ceil_div(pos, kPreactPos) > 0x7fffffff)
         return fail(ANCHA_E_UNSUPPORTED, "mdx_preact_nhwc: grid too large");
-    const dim3 grid((unsigned)ceil_div(pos, 32), (unsigned)(ctot / 64), (unsigned)batch);
+    PackArgs p{};
+    p.a = a; p.b = b; p.gelu = gelu; p.eps = eps;
+    const dim3 grid((unsigned)ceil_div(pos, kPreactPos), (unsigned)(ctot / 64), (unsigned)batch);
     if (out_type == ELT_F16)
-        preact_nhwc_kernel<__half><<<grid, 256, 0, s>>>(a, b, pos, gelu, reinterpret_cast<__half*>(out));
+        preact_nhwc_kernel<__half><<<grid, 256, 0, s>>>(p, pos, reinterpret_cast<__half*>(out));
     else
-        preact_nhwc_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(a, b, pos, gelu, reinterpret_cast<__nv_bfloat16*>(out));
+        preact_nhwc_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(p, pos, reinterpret_cast<__nv_bfloat16*>(out));
     return check_launch("mdx_preact_nhwc");
 }
 
-int mdx_norm_act(const float* x, int64_t planes, int64_t n, const float2* coef, bool gelu, void* out, int out_type,
-                 cudaStream_t s) {
-    const int64_t total = planes * n;
-    if (total <= 0) return ANCHA_OK;
-    if (n % 8 || reinterpret_cast<uintptr_t>(x) % 32 || reinterpret_cast<uintptr_t>(out) % 32) {
-        norm_act_scalar_kernel<<<grid_for(total), 256, 0, s>>>(x, total, n, coef, gelu, out, out_type);
-        return check_launch("mdx_norm_act");
-    }
-    const int64_t total8 = total / 8;
-    const int g = grid_for(total8);
+int mdx_norm_act(const float* x, int64_t planes, int64_t n, int channels, const double2* sums, const float* gamma,
+                 const float* beta, float eps, bool gelu, void* out, int out_type, cudaStream_t s) {
+    if (planes <= 0 || n <= 0) return ANCHA_OK;
+    if (planes > 65535) return fail(ANCHA_E_UNSUPPORTED, "mdx_norm_act: too many planes");
+    const bool vec = n % 8 == 0 && reinterpret_cast<uintptr_t>(x) % 32 == 0 && reinterpret_cast<uintptr_t>(out) % 32 == 0;
+    const int64_t per_plane = vec ? n / 8 : n;
+    const int segs = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(per_plane, 256), ceil_div(148 * 8, planes)));
+    const dim3 grid((unsigned)segs, (unsigned)planes);
     if (out_type == ELT_F16)
-        norm_act_kernel<__half><<<g, 256, 0, s>>>(x, total8, n, coef, gelu, reinterpret_cast<__half*>(out));
+        norm_act_kernel<__half><<<grid, 256, 0, s>>>(x, n, channels, sums, gamma, beta, eps, gelu, vec,
+                                                     reinterpret_cast<__half*>(out));
     else if (out_type == ELT_BF16)
-        norm_act_kernel<__nv_bfloat16><<<g, 256, 0, s>>>(x, total8, n, coef, gelu, reinterpret_cast<__nv_bfloat16*>(out));
+        norm_act_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(x, n, channels, sums, gamma, beta, eps, gelu, vec,
+                                                            reinterpret_cast<__nv_bfloat16*>(out));
     else
-        norm_act_kernel<float><<<g, 256, 0, s>>>(x, total8, n, coef, gelu, reinterpret_cast<float*>(out));
+        norm_act_kernel<float><<<grid, 256, 0, s>>>(x, n, channels, sums, gamma, beta, eps, gelu, vec,
+                                                    reinterpret_cast<float*>(out));
     return check_launch("mdx_norm_act");
 }
 
@@ -351,9 +392,11 @@ int mdx_transpose(const float* x, const float* mul, int64_t planes, int rows, in
 
 int mdx_shuffle2x2(const float* y, int batch, int channels, int h, int w, float* out, int c_total,
                    int c_off, cudaStream_t s) {
-    const int64_t total = (int64_t)batch * channels * 4 * h * w;
-    if (total <= 0) return ANCHA_OK;
-    shuffle2x2_kernel<<<grid_for(total), 256, 0, s>>>(y, channels, h, w, total, out, c_total, c_off);
+    if (batch <= 0 || channels <= 0 || h <= 0 || w <= 0) return ANCHA_OK;
+    if ((int64_t)batch * channels > 65535 || 2 * (int64_t)h > 65535)
+        return fail(ANCHA_E_UNSUPPORTED, "mdx_shuffle2x2: grid too large");
+    const dim3 grid((unsigned)ceil_div(w, 256), (unsigned)(2 * h), (unsigned)(batch * channels));
+    shuffle2x2_kernel<<<grid, 256, 0, s>>>(y, channels, h, w, out, c_total, c_off);
     return check_launch("mdx_shuffle2x2");
 }
 

@@ -1,4 +1,4 @@
-// Device kernels of the MDX23C (TFC-TDF v3) network: per-plane instance-norm coefficients,
+// Device kernels of the MDX23C (TFC-TDF v3) network: per-plane instance-norm statistics,
 // the fused norm → GELU → patch gather that feeds every convolution's GEMM, the row-wise
 // norm → GELU that feeds the TDF GEMMs, plane transposes and the 2 × 2 transpose-convolution
 // scatter. Activations are NCHW f32 planes; GEMM operands are f32, f16 or bf16.
@@ -7,19 +7,20 @@
 
 namespace ancha {
 
-// Instance-norm coefficients of `planes` contiguous planes of `n` floats: with the plane's
-// mean and biased variance (f64 sums), coef[p] = (γ[c]/√(var + eps), β[c] − mean·γ[c]/√(var + eps))
-// for channel c = p % channels, so normalising is one FMA. `scratch` holds planes · 32
-// doubles2 of partial sums.
-int mdx_norm_coef(const float* x, int64_t planes, int64_t n, int channels, const float* gamma,
-                  const float* beta, float eps, double2* scratch, float2* coef, cudaStream_t s);
+// Adds Σ x and Σ x² (f64) of each of `planes` contiguous planes of `n` floats into
+// sums[plane] (which the caller zeroes): the statistics of a tensor that no GEMM epilogue
+// produced (the GEMMs accumulate theirs, GemmEpilogue::stats).
+int mdx_plane_sums(const float* x, int64_t planes, int64_t n, double2* sums, cudaStream_t s);
 
-// One NCHW source of a patch gather: `channels` planes of [h][w] per batch item and, when
-// `coef` is set, their instance norm as per-plane (scale, shift) from mdx_norm_coef.
+// One NCHW source of a gather: `channels` planes of [h][w] per batch item and, when `sums` is
+// set, their instance norm γ[c]·(x − mean)/√(var + eps) + β[c] from the planes' (Σ x, Σ x²)
+// (biased variance, mdx23c.rs:200-213); gamma / beta start at this source's first channel.
 struct PackSource {
     const float* x;
     int channels;
-    const float2* coef;  // [batch · channels] or null (no norm)
+    const double2* sums;  // [batch · channels] or null (no norm)
+    const float* gamma;
+    const float* beta;
 };
 
 // Patch matrix of a bias-free convolution: P[b][ho·wo_n + wo][k], k = (c·kh + ky)·kw + kx
@@ -32,6 +33,7 @@ struct PackArgs {
     int batch, h, w, ho_n, wo_n;
     int kh, kw, sh, sw, ph, pw;
     bool gelu;
+    float eps;
     int64_t kp;
     void* out;
     int out_type;
@@ -41,13 +43,13 @@ int mdx_pack(const PackArgs& a, cudaStream_t s);
 // Channels-last copy for the implicit-GEMM convolution: out[b][pos][c] (f16 / bf16) =
 // act(norm(x)) over the channel concatenation of `a` and `b` (NCHW planes of `pos` values);
 // a.channels + b.channels must be a multiple of 64.
-int mdx_preact_nhwc(const PackSource& a, const PackSource& b, int batch, int64_t pos, bool gelu, void* out,
-                    int out_type, cudaStream_t s);
+int mdx_preact_nhwc(const PackSource& a, const PackSource& b, int batch, int64_t pos, bool gelu, float eps,
+                    void* out, int out_type, cudaStream_t s);
 
-// out[i] = act(x[i]·coef[p].x + coef[p].y) over `planes` contiguous planes of `n` floats
-// (p = i / n), written as `out_type`; the TDF GEMM input.
-int mdx_norm_act(const float* x, int64_t planes, int64_t n, const float2* coef, bool gelu, void* out,
-                 int out_type, cudaStream_t s);
+// out[i] = act(norm(x[i])) over `planes` contiguous planes of `n` floats (plane p = i / n,
+// channel p % channels, statistics sums[p]), written as `out_type`; the TDF GEMM input.
+int mdx_norm_act(const float* x, int64_t planes, int64_t n, int channels, const double2* sums, const float* gamma,
+                 const float* beta, float eps, bool gelu, void* out, int out_type, cudaStream_t s);
 
 // out[p][c][r] = x[p][r][c] · (mul ? mul[p][c][r] : 1) for `planes` planes of rows × cols.
 int mdx_transpose(const float* x, const float* mul, int64_t planes, int rows, int cols, float* out,

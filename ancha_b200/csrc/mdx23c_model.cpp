@@ -254,8 +254,8 @@ int Mdx23c::ensure_workspace(int batch, int frames) {
         const int64_t cin = l < c.scales ? 2 * cl : cl;  // decoder blocks read cat(up, skip)
         patch = std::max(patch, b * pos(l) * round8(9 * std::max(cin, cl)));
         if (l < c.scales) {
-            patch = std::max(patch, b * pos(l + 1) * round8(4 * cl));                    // down
-            patch = std::max(patch, b * pos(l + 1) * round8(cl + c.growth));              // up
+            patch = std::max(patch, b * pos(l + 1) * round8(4 * cl));        // down
+            patch = std::max(patch, b * pos(l + 1) * round8(cl + c.growth));  // up
         }
     }
     const int64_t input = 4 * c.subbands;
@@ -267,11 +267,15 @@ int Mdx23c::ensure_workspace(int batch, int frames) {
     cur_.alloc((size_t)act * fb);
     patch_.alloc((size_t)patch * es);
     rows_.alloc((size_t)rows * es);
-    sums_.alloc((size_t)b * 2048 * 32 * sizeof(double2));
-    coef_a_.alloc((size_t)b * 2048 * sizeof(float2));
-    coef_b_.alloc((size_t)b * 2048 * sizeof(float2));
+    // One statistics slot per normalised tensor of a forward: block input, h, y1, s and output
+    // per block, the level inputs, the up-convolution outputs.
+    const int blocks = (2 * c.scales + 1) * c.blocks_per_scale;
+    stat_slots_ = 4 * blocks + 2 * c.scales + 4;
+    stat_slot_len_ = b * 2048;
+    stats_.alloc((size_t)stat_slots_ * stat_slot_len_ * sizeof(double2));
     skips_.clear();
     skips_.resize(c.scales);
+    skip_stats_.assign(c.scales, nullptr);
     for (int l = 0; l < c.scales; ++l)
         skips_[l].alloc((size_t)(b * (c.channels + (int64_t)l * c.growth) * pos(l)) * fb);
     ws_batch_ = batch;
@@ -279,8 +283,13 @@ int Mdx23c::ensure_workspace(int batch, int frames) {
     return ANCHA_OK;
 }
 
+double2* Mdx23c::take_stats() {
+    if (next_slot_ >= stat_slots_) return nullptr;
+    return stats_.as<double2>() + (size_t)(next_slot_++) * stat_slot_len_;
+}
+
 int Mdx23c::gemm(const void* a, int64_t lda, const void* b, int64_t ldb, int m, int n, int k, float* out,
-                 int64_t ldo, const float* residual, cudaStream_t s) {
+                 int64_t ldo, const float* residual, double2* stats, int stats_div, cudaStream_t s) {
     GemmGroup g{};
     g.a = a; g.b = b; g.bias = nullptr; g.residual = residual; g.out = out;
     g.m = m; g.n = n; g.k = k;
@@ -291,33 +300,46 @@ int Mdx23c::gemm(const void* a, int64_t lda, const void* b, int64_t ldb, int m, 
     e.rope_tokens = 1;
     e.rope_div = 1;
     e.rope_hd = 64;
+    e.stats = stats;
+    e.stats_div = stats_div;
     if (elt_ != ELT_F32) {
         const int st = gemm_tc(g, elt_, e, s);
         if (st != ANCHA_E_UNSUPPORTED) return st;
     }
-    return gemm_ffma(g, nullptr, 1, m, n, elt_, elt_, 1, e, s);
+    e.stats = nullptr;
+    ANCHA_TRY(gemm_ffma(g, nullptr, 1, m, n, elt_, elt_, 1, e, s));
+    // The FFMA kernel has no statistics epilogue: planes of stats_div rows are contiguous.
+    if (stats) {
+        if (ldo != n || m % stats_div) return fail(ANCHA_E_INVALID, "mdx23c: statistics of a strided output");
+        return mdx_plane_sums(out, m / stats_div, (int64_t)stats_div * n, stats, s);
+    }
+    return ANCHA_OK;
 }
 
 int Mdx23c::conv(const Conv& w, const PackSource& a, const PackSource& b, int batch, int h, int wd, int stride,
-                 int pad, bool gelu, float* out, const float* residual, cudaStream_t s) {
+                 int pad, bool gelu, float* out, const float* residual, double2* stats, int stats_div,
+                 cudaStream_t s) {
     if (a.channels + b.channels != w.k / (w.kh * w.kw)) return fail(ANCHA_E_INVALID, "mdx23c: conv channels");
     const int ho = (h + 2 * pad - w.kh) / stride + 1, wo = (wd + 2 * pad - w.kw) / stride + 1;
     const int64_t npos = (int64_t)ho * wo;
     const size_t es = elt_size(elt_);
     const int cin = a.channels + b.channels;
+    // Output statistics per image: planes co / stats_div of that image.
+    auto image_stats = [&](int i) { return stats ? stats + (size_t)i * (w.co / stats_div) : nullptr; };
     const bool implicit = elt_ != ELT_F32 && stride == 1 && cin % 64 == 0 && (wd % 256 == 0 || 256 % wd == 0) &&
                           ((w.kh == 1 && pad == 0) || (w.kh == 3 && pad == 1 && w.tap_major));
     if (implicit) {
         // Channels-last act(norm(x)) once, then the GEMM reads each tap's shifted window
         // through TMA (zero fill at the borders is the padding).
         if ((size_t)(batch * npos * cin) * es > patch_.bytes) return fail(ANCHA_E_INVALID, "mdx23c: patch workspace");
-        ANCHA_TRY(mdx_preact_nhwc(a, b, batch, npos, gelu, patch_.p, elt_, s));
+        ANCHA_TRY(mdx_preact_nhwc(a, b, batch, npos, gelu, kNormEps, patch_.p, elt_, s));
         GemmEpilogue e{};
         e.act = ANCHA_ACT_NONE;
         e.out_type = ELT_F32;
         e.rope_tokens = 1;
         e.rope_div = 1;
         e.rope_hd = 64;
+        e.stats_div = stats_div;
         for (int i = 0; i < batch; ++i) {
             ConvGemm q{};
             q.weight = w.w.p; q.ldw = w.kp; q.co = w.co;
@@ -326,6 +348,7 @@ int Mdx23c::conv(const Conv& w, const PackSource& a, const PackSource& b, int ba
             q.residual = residual ? residual + (size_t)i * w.co * npos : nullptr;
             q.out = out + (size_t)i * w.co * npos;
             q.ldo = npos;
+            e.stats = image_stats(i);
             ANCHA_TRY(gemm_tc_conv(q, elt_, e, s));
         }
         return ANCHA_OK;
@@ -336,54 +359,50 @@ int Mdx23c::conv(const Conv& w, const PackSource& a, const PackSource& b, int ba
     p.a = a; p.b = b;
     p.batch = batch; p.h = h; p.w = wd; p.ho_n = ho; p.wo_n = wo;
     p.kh = w.kh; p.kw = w.kw; p.sh = p.sw = stride; p.ph = p.pw = pad;
-    p.gelu = gelu; p.kp = w.kp; p.out = patch_.p; p.out_type = elt_;
+    p.gelu = gelu; p.eps = kNormEps; p.kp = w.kp; p.out = patch_.p; p.out_type = elt_;
     ANCHA_TRY(mdx_pack(p, s));
     for (int i = 0; i < batch; ++i) {
         const uint8_t* pb = patch_.as<uint8_t>() + (size_t)(i * npos * w.kp) * es;
         ANCHA_TRY(gemm(w.w.p, w.kp, pb, w.kp, w.co, (int)npos, w.kp, out + (size_t)i * w.co * npos, npos,
-                       residual ? residual + (size_t)i * w.co * npos : nullptr, s));
+                       residual ? residual + (size_t)i * w.co * npos : nullptr, image_stats(i), stats_div, s));
     }
     return ANCHA_OK;
 }
 
-int Mdx23c::block(const Block& bk, const PackSource& a, const PackSource& b, int batch, int t, int f, float* out,
+int Mdx23c::block(const Block& bk, const Act& a, const Act& b, int batch, int t, int f, const Act& out,
                   cudaStream_t s) {
     // Block::forward (mdx23c.rs:264-274).
     const int64_t pos = (int64_t)t * f;
     const int co = bk.co;
-    const PackSource none{nullptr, 0, nullptr};
-    const PackSource ar{a.x, a.channels, nullptr}, br{b.x, b.channels, nullptr};
-    ANCHA_TRY(conv(bk.sc, ar, b.channels ? br : none, batch, t, f, 1, 0, false, skip_sc_.as<float>(), nullptr, s));
-    // x = tfc1(x): norm over the channels of the concatenation, per source.
-    float2* ka = coef_a_.as<float2>();
-    float2* kb = coef_b_.as<float2>();
+    const PackSource none{nullptr, 0, nullptr, nullptr, nullptr};
+    const PackSource ar{a.x, a.channels, nullptr, nullptr, nullptr}, br{b.x, b.channels, nullptr, nullptr, nullptr};
+    ANCHA_TRY(conv(bk.sc, ar, b.channels ? br : none, batch, t, f, 1, 0, false, skip_sc_.as<float>(), nullptr,
+                   nullptr, 1, s));
+    // x = tfc1(x): the norm over the channels of the concatenation, per source.
     const float* g1 = bk.n1.gamma.as<float>();
     const float* b1 = bk.n1.beta.as<float>();
-    ANCHA_TRY(norm_coef(a.x, batch, a.channels, pos, g1, b1, ka, s));
-    if (b.channels) ANCHA_TRY(norm_coef(b.x, batch, b.channels, pos, g1 + a.channels, b1 + a.channels, kb, s));
-    const PackSource an{a.x, a.channels, ka}, bn{b.x, b.channels, kb};
+    const PackSource an{a.x, a.channels, a.stats, g1, b1};
+    const PackSource bn{b.x, b.channels, b.stats, g1 + a.channels, b1 + a.channels};
+    double2* sh = take_stats();
+    double2* sy = take_stats();
+    double2* ss = take_stats();
+    if (!sh || !sy || !ss) return fail(ANCHA_E_INVALID, "mdx23c: statistics workspace");
     float* h = h_.as<float>();
-    ANCHA_TRY(conv(bk.c1, an, b.channels ? bn : none, batch, t, f, 1, 1, true, h, nullptr, s));
-    // y = tdf2(gelu(norm(tdf1(gelu(norm(x)))))); s = x + y.
+    ANCHA_TRY(conv(bk.c1, an, b.channels ? bn : none, batch, t, f, 1, 1, true, h, nullptr, sh, 1, s));
+    // y = tdf2(gelu(norm(tdf1(gelu(norm(x)))))); s = x + y. The TDF rows are (batch, channel,
+    // time), so a plane is `t` consecutive rows.
     const int64_t rows = (int64_t)batch * co * t;
-    ANCHA_TRY(norm_coef(h, batch, co, pos, bk.t0.gamma.as<float>(), bk.t0.beta.as<float>(), ka, s));
-    ANCHA_TRY(mdx_norm_act(h, (int64_t)batch * co, pos, ka, true, rows_.p, elt_, s));
+    ANCHA_TRY(mdx_norm_act(h, (int64_t)batch * co, pos, co, sh, bk.t0.gamma.as<float>(), bk.t0.beta.as<float>(),
+                           kNormEps, true, rows_.p, elt_, s));
     float* y1 = y1_.as<float>();
-    ANCHA_TRY(gemm(rows_.p, f, bk.tdf1.p, f, (int)rows, bk.fb, f, y1, bk.fb, nullptr, s));
-    ANCHA_TRY(norm_coef(y1, batch, co, (int64_t)t * bk.fb, bk.t3.gamma.as<float>(), bk.t3.beta.as<float>(), ka, s));
-    ANCHA_TRY(mdx_norm_act(y1, (int64_t)batch * co, (int64_t)t * bk.fb, ka, true, rows_.p, elt_, s));
+    ANCHA_TRY(gemm(rows_.p, f, bk.tdf1.p, f, (int)rows, bk.fb, f, y1, bk.fb, nullptr, sy, t, s));
+    ANCHA_TRY(mdx_norm_act(y1, (int64_t)batch * co, (int64_t)t * bk.fb, co, sy, bk.t3.gamma.as<float>(),
+                           bk.t3.beta.as<float>(), kNormEps, true, rows_.p, elt_, s));
     float* sum = s_.as<float>();
-    ANCHA_TRY(gemm(rows_.p, bk.fb, bk.tdf2.p, bk.fb, (int)rows, f, bk.fb, sum, f, h, s));
+    ANCHA_TRY(gemm(rows_.p, bk.fb, bk.tdf2.p, bk.fb, (int)rows, f, bk.fb, sum, f, h, ss, t, s));
     // out = tfc2(s) + shortcut(x).
-    ANCHA_TRY(norm_coef(sum, batch, co, pos, bk.n2.gamma.as<float>(), bk.n2.beta.as<float>(), ka, s));
-    const PackSource sn{sum, co, ka};
-    return conv(bk.c2, sn, none, batch, t, f, 1, 1, true, out, skip_sc_.as<float>(), s);
-}
-
-int Mdx23c::norm_coef(const float* x, int batch, int channels, int64_t n, const float* gamma, const float* beta,
-                      float2* coef, cudaStream_t s) {
-    return mdx_norm_coef(x, (int64_t)batch * channels, n, channels, gamma, beta, kNormEps, sums_.as<double2>(), coef,
-                         s);
+    const PackSource sn{sum, co, ss, bk.n2.gamma.as<float>(), bk.n2.beta.as<float>()};
+    return conv(bk.c2, sn, none, batch, t, f, 1, 1, true, out.x, skip_sc_.as<float>(), out.stats, 1, s);
 }
 
 int Mdx23c::forward(const float* spectrum, int batch, int frames, float* out, const volatile int* cancel,
@@ -396,63 +415,70 @@ int Mdx23c::forward(const float* spectrum, int batch, int frames, float* out, co
     if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
     ANCHA_CUDA(cudaSetDevice(device));
     ANCHA_TRY(ensure_workspace(batch, frames));
+    ANCHA_CUDA(cudaMemsetAsync(stats_.p, 0, stats_.bytes, s));
+    next_slot_ = 0;
     const int input = 4 * c.subbands, f0 = c.bins / c.subbands, ch = c.channels;
-    const PackSource none{nullptr, 0, nullptr};
+    const PackSource none{nullptr, 0, nullptr, nullptr, nullptr};
     // mix = spectrum viewed as [batch][4·subbands][bins / subbands][frames] (mdx23c.rs:435).
-    const PackSource mix{spectrum, input, nullptr};
+    const PackSource mix{spectrum, input, nullptr, nullptr, nullptr};
     float* first = first_f_.as<float>();
-    ANCHA_TRY(conv(first_, mix, none, batch, f0, frames, 1, 0, false, first, nullptr, s));
+    ANCHA_TRY(conv(first_, mix, none, batch, f0, frames, 1, 0, false, first, nullptr, nullptr, 1, s));
     ANCHA_TRY(mdx_transpose(first, nullptr, (int64_t)batch * ch, f0, frames, x0_.as<float>(), s));
-    auto run_blocks = [&](const std::vector<Block>& blocks, PackSource a, PackSource b, int t, int f,
-                          float* dst) -> int {
+    Act x{x0_.as<float>(), ch, take_stats()};
+    ANCHA_TRY(mdx_plane_sums(x.x, (int64_t)batch * ch, (int64_t)frames * f0, x.stats, s));
+    const Act none_act{nullptr, 0, nullptr};
+    auto run_blocks = [&](const std::vector<Block>& blocks, Act a, Act b, int t, int f, const Act& dst) -> int {
         for (size_t i = 0; i < blocks.size(); ++i) {
             if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
-            float* o = i + 1 == blocks.size() ? dst : (i % 2 ? blk_b_.as<float>() : blk_a_.as<float>());
+            Act o = i + 1 == blocks.size()
+                        ? dst
+                        : Act{i % 2 ? blk_b_.as<float>() : blk_a_.as<float>(), blocks[i].co, take_stats()};
+            if (!o.stats) return fail(ANCHA_E_INVALID, "mdx23c: statistics workspace");
             ANCHA_TRY(block(blocks[i], a, b, batch, t, f, o, s));
-            a = PackSource{o, blocks[i].co, nullptr};
-            b = none;
+            a = o;
+            b = none_act;
         }
         return ANCHA_OK;
     };
     // Encoder (mdx23c.rs:440-444): blocks, keep the skip, then norm → GELU → 2 × 2 / 2 conv.
-    PackSource x{x0_.as<float>(), ch, nullptr};
     int t = frames, f = f0, cl = ch;
     for (int l = 0; l < c.scales; ++l) {
-        float* skip = skips_[l].as<float>();
-        ANCHA_TRY(run_blocks(down_[l].blocks, x, none, t, f, skip));
-        float2* ka = coef_a_.as<float2>();
-        ANCHA_TRY(norm_coef(skip, batch, cl, (int64_t)t * f, down_[l].norm.gamma.as<float>(),
-                            down_[l].norm.beta.as<float>(), ka, s));
-        const PackSource sn{skip, cl, ka};
-        ANCHA_TRY(conv(down_[l].conv, sn, none, batch, t, f, 2, 0, true, in_.as<float>(), nullptr, s));
+        const Act skip{skips_[l].as<float>(), cl, take_stats()};
+        skip_stats_[l] = skip.stats;
+        ANCHA_TRY(run_blocks(down_[l].blocks, x, none_act, t, f, skip));
+        const PackSource sn{skip.x, cl, skip.stats, down_[l].norm.gamma.as<float>(), down_[l].norm.beta.as<float>()};
+        x = Act{in_.as<float>(), cl + c.growth, take_stats()};
+        if (!x.stats) return fail(ANCHA_E_INVALID, "mdx23c: statistics workspace");
+        ANCHA_TRY(conv(down_[l].conv, sn, none, batch, t, f, 2, 0, true, in_.as<float>(), nullptr, x.stats, 1, s));
         t /= 2; f /= 2; cl += c.growth;
-        x = PackSource{in_.as<float>(), cl, nullptr};
     }
-    ANCHA_TRY(run_blocks(bottom_, x, none, t, f, cur_.as<float>()));
-    // Decoder (Up::forward, mdx23c.rs:330-355): norm → GELU → ConvTranspose2d(2, 2) as a
-    // GEMM over the input positions plus a scatter, then blocks over cat(up, skip).
+    Act cur{cur_.as<float>(), cl, take_stats()};
+    ANCHA_TRY(run_blocks(bottom_, x, none_act, t, f, cur));
+    // Decoder (Up::forward, mdx23c.rs:330-355): norm → GELU → ConvTranspose2d(2, 2) as a GEMM
+    // over the input positions (rows (co, dy, dx): a plane's statistics are 4 rows) plus a
+    // scatter, then blocks over cat(up, skip).
     for (int i = 0; i < c.scales; ++i) {
         const Up& u = up_[i];
-        float2* ka = coef_a_.as<float2>();
-        ANCHA_TRY(norm_coef(cur_.as<float>(), batch, cl, (int64_t)t * f, u.norm.gamma.as<float>(),
-                            u.norm.beta.as<float>(), ka, s));
-        const PackSource un{cur_.as<float>(), cl, ka};
-        ANCHA_TRY(conv(u.conv, un, none, batch, t, f, 1, 0, true, up_raw_.as<float>(), nullptr, s));
+        const PackSource un{cur.x, cl, cur.stats, u.norm.gamma.as<float>(), u.norm.beta.as<float>()};
+        const Act up{up_out_.as<float>(), u.co, take_stats()};
+        if (!up.stats) return fail(ANCHA_E_INVALID, "mdx23c: statistics workspace");
+        ANCHA_TRY(conv(u.conv, un, none, batch, t, f, 1, 0, true, up_raw_.as<float>(), nullptr, up.stats, 4, s));
         ANCHA_TRY(mdx_shuffle2x2(up_raw_.as<float>(), batch, u.co, t, f, up_out_.as<float>(), u.co, 0, s));
         t *= 2; f *= 2; cl = u.co;
         const int l = c.scales - 1 - i;
-        const PackSource up{up_out_.as<float>(), u.co, nullptr};
-        const PackSource sk{skips_[l].as<float>(), u.co, nullptr};
-        ANCHA_TRY(run_blocks(u.blocks, up, sk, t, f, cur_.as<float>()));
+        const Act sk{skips_[l].as<float>(), u.co, skip_stats_[l]};
+        cur = Act{cur_.as<float>(), u.co, take_stats()};
+        if (!cur.stats) return fail(ANCHA_E_INVALID, "mdx23c: statistics workspace");
+        ANCHA_TRY(run_blocks(u.blocks, up, sk, t, f, cur));
     }
     if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
     // x.swap_dims(2, 3) · first, then final_conv = 1×1 → GELU → 1×1 over cat(mix, x)
     // (mdx23c.rs:475-480).
-    ANCHA_TRY(mdx_transpose(cur_.as<float>(), first, (int64_t)batch * ch, frames, f0, z_.as<float>(), s));
-    const PackSource z{z_.as<float>(), ch, nullptr};
-    ANCHA_TRY(conv(final_first_, mix, z, batch, f0, frames, 1, 0, false, ff_.as<float>(), nullptr, s));
-    const PackSource ffs{ff_.as<float>(), ch, nullptr};
-    return conv(final_last_, ffs, none, batch, f0, frames, 1, 0, true, out, nullptr, s);
+    ANCHA_TRY(mdx_transpose(cur.x, first, (int64_t)batch * ch, frames, f0, z_.as<float>(), s));
+    const PackSource z{z_.as<float>(), ch, nullptr, nullptr, nullptr};
+    ANCHA_TRY(conv(final_first_, mix, z, batch, f0, frames, 1, 0, false, ff_.as<float>(), nullptr, nullptr, 1, s));
+    const PackSource ffs{ff_.as<float>(), ch, nullptr, nullptr, nullptr};
+    return conv(final_last_, ffs, none, batch, f0, frames, 1, 0, true, out, nullptr, nullptr, 1, s);
 }
 
 }  // namespace ancha

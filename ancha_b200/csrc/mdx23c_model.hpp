@@ -58,19 +58,19 @@ public:
     struct Up { Norm norm; Conv conv; std::vector<Block> blocks; int co = 0; };  // conv rows (co, dy, dx)
 
 private:
+    // An NCHW activation and the (Σ x, Σ x²) of its planes (null when it is never normalised).
+    struct Act { float* x; int channels; double2* stats; };
     // Bias-free convolution of the channel concatenation (a, b) of NCHW [batch][·][h][wd]
-    // planes: patch gather (with the sources' norms and GELU) then one GEMM per batch item,
-    // out[b][co][ho][wo] (+ residual of the same shape).
+    // planes: a gather (with the sources' norms and GELU) then one GEMM per batch item,
+    // out[b][co][ho][wo] (+ residual of the same shape); `stats` (if set) receives the output's
+    // plane statistics, a plane being `stats_div` consecutive output rows.
     int conv(const Conv& w, const PackSource& a, const PackSource& b, int batch, int h, int wd, int stride,
-             int pad, bool gelu, float* out, const float* residual, cudaStream_t s);
+             int pad, bool gelu, float* out, const float* residual, double2* stats, int stats_div, cudaStream_t s);
     int gemm(const void* a, int64_t lda, const void* b, int64_t ldb, int m, int n, int k, float* out,
-             int64_t ldo, const float* residual, cudaStream_t s);
-    int block(const Block& bk, const PackSource& a, const PackSource& b, int batch, int t, int f, float* out,
-              cudaStream_t s);
-    // Instance-norm (scale, shift) per plane of batch · channels planes of n values.
-    int norm_coef(const float* x, int batch, int channels, int64_t n, const float* gamma, const float* beta,
-                  float2* coef, cudaStream_t s);
+             int64_t ldo, const float* residual, double2* stats, int stats_div, cudaStream_t s);
+    int block(const Block& bk, const Act& a, const Act& b, int batch, int t, int f, const Act& out, cudaStream_t s);
     int ensure_workspace(int batch, int frames);
+    double2* take_stats();  // the next zeroed statistics slot of this forward (null when exhausted)
 
     int elt_ = 0;
     Conv first_, final_first_, final_last_;
@@ -80,8 +80,11 @@ private:
     // Workspace for one (batch, frames) shape.
     int ws_batch_ = 0, ws_frames_ = 0;
     DevBuf first_f_, x0_, skip_sc_, h_, y1_, s_, blk_a_, blk_b_, up_raw_, up_out_, z_, ff_, in_, cur_, patch_,
-        rows_, sums_, coef_a_, coef_b_;
+        rows_, stats_;
     std::vector<DevBuf> skips_;
+    std::vector<double2*> skip_stats_;
+    int stat_slots_ = 0, next_slot_ = 0;
+    int64_t stat_slot_len_ = 0;
 };
 
 }  // namespace ancha
