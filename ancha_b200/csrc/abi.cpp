@@ -263,6 +263,12 @@ int ancha_mdx23c_forward(ancha_mdx23c* model, const float* spectrum, int batch, 
     }
 }
 
+int ancha_mdx23c_separate_pcm(ancha_mdx23c* model, const float* planes, int64_t samples, int overlap, int batch,
+                              const volatile int* cancel, float* stems_out, double* seconds_out) {
+    if (!model || !planes || !stems_out) return fail(ANCHA_E_INVALID, "mdx23c_separate_pcm: null argument");
+    return model->impl->separate_pcm(planes, samples, overlap, batch, cancel, stems_out, seconds_out);
+}
+
 void ancha_mdx23c_free(ancha_mdx23c* model) { delete model; }
 
 void ancha_free_string(char* s) { std::free(s); }

@@ -60,4 +60,43 @@ int mdx_transpose(const float* x, const float* mul, int64_t planes, int rows, in
 int mdx_shuffle2x2(const float* y, int batch, int channels, int h, int w, float* out, int c_total,
                    int c_off, cudaStream_t s);
 
+// ---- Spectral runtime of the MDX23C task (src/mdx23c_runtime.rs, src/spectral.rs) ----------
+
+// Per-device tables for an n_fft-point transform (n_fft a power of two, 32..8192): the
+// periodic Hann window in the reference's f32 form and exp(−2πik/8192), k ≤ 4096, from which
+// every smaller power-of-two twiddle is a strided read.
+struct MdxDsp {
+    int n_fft = 0;
+    float* window = nullptr;   // [n_fft]
+    float2* twiddle = nullptr; // [4097]
+};
+int mdx_dsp_tables(int n_fft, float* window, float2* twiddle, cudaStream_t s);
+
+// UVR chunk windows of the zero-bordered track (mdx23c_runtime.rs:116-132):
+// out[c][ch][i] = planes[ch][starts[c] + i − border] inside the track, else 0 (at most 4
+// chunks per call, starts on the host).
+int mdx_gather(const float* planes, int64_t samples, const int64_t* starts, int chunks, int chunk, int64_t border,
+               float* out, cudaStream_t s);
+
+// Centred periodic-Hann STFT (reflect padding inside each chunk, dsp.rs:52-79) packed as
+// spectral::pack does (spectral.rs:5-36): audio[c][2][samples] → out[c][4][bins][frames]
+// (L.re, L.im, R.re, R.im), frames = samples / hop + 1.
+int mdx_stft(const MdxDsp& d, const float* audio, int chunks, int samples, int hop, int bins, float* out,
+             cudaStream_t s);
+
+// Inverse of each stem's packed spectrum (spectral::unpack + Stft::inverse, spectral.rs:38-76,
+// dsp.rs:82-133; bins past `bins` are zero, Im of DC / Nyquist dropped, 1/n scale,
+// window-square normalised overlap-add): spec[c][stems·4][bins][frames] →
+// waves[c][stem][2][samples]. `scratch` holds chunks·stems·2·frames·n_fft floats; bit 2 of
+// *flag is set where a sample is uncovered.
+int mdx_istft(const MdxDsp& d, const float* spec, int chunks, int stems, int bins, int frames, int hop, int samples,
+              float* scratch, float* waves, int* flag, cudaStream_t s);
+
+// Rectangular overlap-add of chunk outputs, in chunk order (mdx23c_runtime.rs:214-223):
+// sums[p][j − border] += waves[c][p][j − starts[c]] for j in
+// [max(start, border), min(start + chunk, border + samples)), p over stems·2 planes; at most
+// 4 chunks per call (starts on the host, ascending). Bit 0 of *flag marks a non-finite value.
+int mdx_overlap_add(const float* waves, const int64_t* starts, int chunks, int planes, int chunk, int64_t border,
+                    int64_t samples, float* sums, int* flag, cudaStream_t s);
+
 }  // namespace ancha

@@ -12,6 +12,7 @@
 #include "mdx23c_model.hpp"
 
 #include <algorithm>
+#include <chrono>
 #include <cstring>
 #include <set>
 #include <stdexcept>
@@ -231,6 +232,12 @@ std::unique_ptr<Mdx23c> Mdx23c::load(const std::string& package, int device, int
         conv(m->final_first_, "final_conv.0.weight", ch, ch + input, 1);
         conv(m->final_last_, "final_conv.2.weight", (int)c.stems.size() * input, ch, 1);
         m->tensor_count = w.finish();
+        m->dsp_window_.alloc((size_t)c.n_fft * sizeof(float));
+        m->dsp_twiddle_.alloc((size_t)4097 * sizeof(float2));
+        if (mdx_dsp_tables(c.n_fft, m->dsp_window_.as<float>(), m->dsp_twiddle_.as<float2>(), 0) != ANCHA_OK)
+            bad(std::string("MDX23C DSP tables: ") + ancha_last_error());
+        const cudaError_t te = cudaDeviceSynchronize();
+        if (te != cudaSuccess) bad(std::string("MDX23C DSP tables: ") + cudaGetErrorString(te));
     } catch (...) {
         hasher.join();
         throw;
@@ -479,6 +486,88 @@ int Mdx23c::forward(const float* spectrum, int batch, int frames, float* out, co
     ANCHA_TRY(conv(final_first_, mix, z, batch, f0, frames, 1, 0, false, ff_.as<float>(), nullptr, nullptr, 1, s));
     const PackSource ffs{ff_.as<float>(), ch, nullptr, nullptr, nullptr};
     return conv(final_last_, ffs, none, batch, f0, frames, 1, 0, true, out, nullptr, nullptr, 1, s);
+}
+
+int Mdx23c::separate_pcm(const float* planes, int64_t samples, int overlap, int batch, const volatile int* cancel,
+                         float* stems, double* seconds) {
+    const auto t_start = std::chrono::steady_clock::now();
+    const Mdx23cConfig& c = manifest.config;
+    if (!planes || !stems || samples <= 0) return fail(ANCHA_E_INVALID, "mdx23c_separate: empty input");
+    const int ov = overlap > 0 ? overlap : c.overlap;
+    const int64_t chunk = c.chunk_samples();
+    // OverlapPlan::new (mdx23c_runtime.rs:84-115).
+    if (ov < 1 || ov > 16 || ov > chunk) return fail(ANCHA_E_INVALID, "invalid MDX23C overlap plan");
+    const int64_t step = chunk / ov;
+    const int64_t left = samples % step, right = chunk % step;
+    const int64_t remainder = left >= right ? left - right : step - (right - left);
+    const int64_t pad = step - remainder, border = chunk - step;
+    const int64_t padded = samples + pad + 2 * border;
+    if (padded < chunk) return fail(ANCHA_E_INVALID, "insufficient MDX23C padding");
+    const int64_t n_chunks = (padded - chunk) / step + 1;
+    std::vector<int64_t> starts;
+    for (int64_t i = 0; i < n_chunks; ++i) {
+        const int64_t s0 = i * step;
+        if (s0 < border + samples && s0 + chunk > border) starts.push_back(s0);  // OverlapPlan::intersects
+    }
+    const int b = batch > 0 ? std::min(batch, 4) : 4;
+    if (batch < 0) return fail(ANCHA_E_INVALID, "mdx23c_separate: batch");
+    const int stems_n = (int)c.stems.size(), frames = c.frames, bins = c.bins;
+    if (chunk / c.hop + 1 != frames) return fail(ANCHA_E_INVALID, "MDX23C STFT frame count mismatch");
+    ANCHA_CUDA(cudaSetDevice(device));
+    try {
+        cudaStream_t s = nullptr;
+        ANCHA_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        DevBuf track, audio, spec, yout, scratch, waves, sums, flag;
+        // Declared after the buffers, so destroyed before them: no buffer is freed while work
+        // queued on the stream (an early error return) may still use it.
+        struct StreamGuard {
+            cudaStream_t s;
+            ~StreamGuard() {
+                cudaStreamSynchronize(s);
+                cudaStreamDestroy(s);
+            }
+        } guard{s};
+        track.alloc((size_t)2 * samples * sizeof(float));
+        audio.alloc((size_t)b * 2 * chunk * sizeof(float));
+        spec.alloc((size_t)b * 4 * bins * frames * sizeof(float));
+        yout.alloc((size_t)b * stems_n * 4 * bins * frames * sizeof(float));
+        scratch.alloc((size_t)b * stems_n * 2 * frames * c.n_fft * sizeof(float));
+        waves.alloc((size_t)b * stems_n * 2 * chunk * sizeof(float));
+        sums.alloc((size_t)stems_n * 2 * samples * sizeof(float));
+        flag.alloc(sizeof(int));
+        ANCHA_CUDA(cudaMemcpyAsync(track.p, planes, (size_t)2 * samples * sizeof(float), cudaMemcpyHostToDevice, s));
+        ANCHA_CUDA(cudaMemsetAsync(sums.p, 0, sums.bytes, s));
+        ANCHA_CUDA(cudaMemsetAsync(flag.p, 0, sizeof(int), s));
+        MdxDsp d;
+        d.n_fft = c.n_fft;
+        d.window = dsp_window_.as<float>();
+        d.twiddle = dsp_twiddle_.as<float2>();
+        for (size_t i = 0; i < starts.size(); i += b) {
+            if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
+            const int n = (int)std::min<size_t>(b, starts.size() - i);
+            const int64_t* st = starts.data() + i;
+            ANCHA_TRY(mdx_gather(track.as<float>(), samples, st, n, (int)chunk, border, audio.as<float>(), s));
+            ANCHA_TRY(mdx_stft(d, audio.as<float>(), n, (int)chunk, c.hop, bins, spec.as<float>(), s));
+            ANCHA_TRY(forward(spec.as<float>(), n, frames, yout.as<float>(), cancel, s));
+            ANCHA_TRY(mdx_istft(d, yout.as<float>(), n, stems_n, bins, frames, c.hop, (int)chunk, scratch.as<float>(),
+                                waves.as<float>(), flag.as<int>(), s));
+            ANCHA_TRY(mdx_overlap_add(waves.as<float>(), st, n, stems_n * 2, (int)chunk, border, samples,
+                                      sums.as<float>(), flag.as<int>(), s));
+        }
+        ANCHA_CUDA(cudaMemcpyAsync(stems, sums.p, sums.bytes, cudaMemcpyDeviceToHost, s));
+        int status = 0;
+        ANCHA_CUDA(cudaMemcpyAsync(&status, flag.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+        ANCHA_CUDA(cudaStreamSynchronize(s));
+        if (status & 1) return fail(ANCHA_E_NONFINITE, "non-finite MDX23C output");
+        if (status & 2) return fail(ANCHA_E_INVALID, "iSTFT has an uncovered sample");
+        const float inv = 1.f / (float)ov;
+        for (size_t i = 0; i < (size_t)stems_n * 2 * samples; ++i) stems[i] *= inv;
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_CUDA, e.what());
+    }
+    if (seconds)
+        *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t_start).count();
+    return ANCHA_OK;
 }
 
 }  // namespace ancha

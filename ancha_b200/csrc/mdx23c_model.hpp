@@ -39,6 +39,12 @@ public:
     // (mdx23c.rs:420-481). Checks *cancel (host, may be null) before every block.
     int forward(const float* spectrum, int batch, int frames, float* out, const volatile int* cancel,
                 cudaStream_t s);
+    // mdx23c_runtime::separate without file I/O (mdx23c_runtime.rs:135-248): host planes
+    // [2][samples] → host stems [stems][2][samples]; chunks that lie entirely in the zero
+    // borders are skipped as the reference does by default. overlap 0 = the manifest's;
+    // batch = chunks per forward (1..4, 0 = 4). *seconds (may be null) = wall time.
+    int separate_pcm(const float* planes, int64_t samples, int overlap, int batch, const volatile int* cancel,
+                     float* stems, double* seconds);
 
     Mdx23cManifest manifest;
     int device = 0, precision = 0;
@@ -73,6 +79,7 @@ private:
     double2* take_stats();  // the next zeroed statistics slot of this forward (null when exhausted)
 
     int elt_ = 0;
+    DevBuf dsp_window_, dsp_twiddle_;  // MdxDsp tables for the manifest's n_fft
     Conv first_, final_first_, final_last_;
     std::vector<Down> down_;
     std::vector<Block> bottom_;

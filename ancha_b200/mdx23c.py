@@ -47,6 +47,21 @@ class Mdx23c:
                                              None if cancel is None else C.byref(cancel), stream))
         return out
 
+    def separate_pcm(self, planes, overlap: int = 0, batch: int = 0, cancel: Optional[C.c_int] = None):
+        """``mdx23c_runtime::separate`` on host PCM: ``[2, samples]`` f32 → ``([stems, 2, samples],
+        seconds)``; chunking, STFT, network, iSTFT and overlap-add all run on this model's GPU."""
+        import numpy as np
+        x = np.ascontiguousarray(planes, dtype=np.float32)
+        if x.ndim != 2 or x.shape[0] != 2:
+            raise N.AnchaError(N.E_INVALID, "planes must be [2, samples]")
+        out = np.empty((self.stems, 2, x.shape[1]), dtype=np.float32)
+        secs = C.c_double()
+        fp = C.POINTER(C.c_float)
+        N.check(N.lib().ancha_mdx23c_separate_pcm(self._h, x.ctypes.data_as(fp), x.shape[1], overlap, batch,
+                                                  None if cancel is None else C.byref(cancel),
+                                                  out.ctypes.data_as(fp), C.byref(secs)))
+        return out, secs.value
+
     def close(self) -> None:
         if self._h:
             N.lib().ancha_mdx23c_free(self._h)

@@ -215,6 +215,16 @@ ANCHA_API int ancha_mdx23c_info(const ancha_mdx23c* model, int* bins, int* frame
 ANCHA_API int ancha_mdx23c_forward(ancha_mdx23c* model, const float* spectrum, int batch, int frames,
                          float* out, const volatile int* cancel, void* stream);
 
+/* mdx23c_runtime::separate without file I/O (src/mdx23c_runtime.rs:135-248) on the model's
+ * GPU: host planes[2][samples] (f32, 44.1 kHz) → host stems_out[stems][2][samples]. UVR chunks
+ * (zero borders, step = chunk / overlap), centred n_fft STFT packed as spectral::pack, the
+ * network, each stem's inverse STFT, rectangular overlap-add divided by `overlap`, all on the
+ * device; chunks entirely inside the zero borders are skipped (the reference's default).
+ * overlap 0 = the manifest's; batch = chunks per forward (1..4, 0 = 4). *seconds_out (may be
+ * NULL) = wall time. ANCHA_E_NONFINITE for a non-finite model output. */
+ANCHA_API int ancha_mdx23c_separate_pcm(ancha_mdx23c* model, const float* planes, int64_t samples, int overlap,
+                              int batch, const volatile int* cancel, float* stems_out, double* seconds_out);
+
 ANCHA_API void ancha_mdx23c_free(ancha_mdx23c* model);
 
 /* ------------------------------------------------------------------------------------ *

@@ -187,3 +187,42 @@ def test_corrupt_checksum_is_rejected(torch_cuda, golden, tmp_path):
     with pytest.raises(N.AnchaError) as e:
         Mdx23c(d, 0, "f32")
     assert "checksum" in str(e.value)
+
+
+def test_separate_pcm_tiny_matches_oracle(torch_cuda, golden):
+    """The whole task on the device (UVR chunks, STFT 64 / hop 8, network, iSTFT, overlap-add)
+    against the oracle's restatement of mdx23c_runtime::separate."""
+    g, w, d = golden
+    x = (np.random.default_rng(1).standard_normal((2, 300)) * 0.1).astype(np.float32)
+    ref = M.separate(g["config"], w, x)
+    for batch in (1, 3):
+        y, secs = Mdx23c(d, 0, "f32").separate_pcm(x, batch=batch)
+        assert y.shape == ref.shape and secs > 0
+        err = np.abs(y - ref).max() / np.abs(ref).max()
+        print(f"separate tiny batch {batch}: max |d| / max |ref| {err:.2e}")
+        assert err < 1e-5
+
+
+@pytest.mark.parametrize("precision", ["f32", "f16"])
+def test_separate_pcm_mid_matches_oracle(torch_cuda, mid, precision):
+    c, w, d = mid  # n_fft 512, hop 128, 3968-sample chunks, overlap 4
+    x = (np.random.default_rng(2).standard_normal((2, 6000)) * 0.1).astype(np.float32)
+    ref = M.separate(c, w, x)
+    y, _ = Mdx23c(d, 0, precision).separate_pcm(x)
+    s = snr_db(ref, y)
+    print(f"separate mid {precision}: {s:.1f} dB")
+    if precision == "f32":
+        assert np.abs(y - ref).max() / np.abs(ref).max() < 1e-5
+    else:
+        assert s >= SNR_FLOOR[precision]
+
+
+def test_separate_pcm_cancel_and_shape_errors(torch_cuda, golden):
+    _, _, d = golden
+    m = Mdx23c(d, 0, "f32")
+    x = np.zeros((2, 300), np.float32)
+    with pytest.raises(N.AnchaError) as e:
+        m.separate_pcm(x, cancel=C.c_int(1))
+    assert e.value.status == N.E_CANCELLED
+    with pytest.raises(N.AnchaError):
+        m.separate_pcm(np.zeros((1, 300), np.float32))

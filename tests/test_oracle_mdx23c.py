@@ -112,3 +112,25 @@ def test_uvr_overlap_plan_reconstructs_boundaries():
                 lo, hi = max(s, p.border), min(s + p.chunk, p.border + n)
                 y[lo - p.border:hi - p.border] += wave[0, lo - s:hi - s]
             assert np.abs(y / overlap - x[0]).max() < 1e-6
+
+
+def test_spectral_packing_retains_dc_and_stereo_complex_order():
+    # mdx23c_runtime_contracts.rs:49-64: constant planes 0.25 / -0.125, n_fft 64, hop 8.
+    from oracle.dsp import Stft
+    st = Stft(64, 8)
+    planes = np.stack([np.full(56, 0.25), np.full(56, -0.125)])
+    p = M.pack(st, planes, 32)
+    assert p.shape == (4, 32, 8)
+    assert abs(p.ravel()[0] - 8.0) < 1e-6
+    assert abs(p.ravel()[2 * 32 * 8] + 4.0) < 1e-6
+    assert np.abs(M.unpack(st, p, 56) - planes).max() < 1e-6
+
+
+def test_separate_length_and_chunk_skipping(golden):
+    c = golden["config"]
+    w = M.fixture_weights([(x["name"], x["shape"]) for x in golden["weights"]])
+    x = np.random.default_rng(0).standard_normal((2, 300)) * 0.1
+    y = M.separate(c, w, x)
+    assert y.shape == (2, 2, 300) and np.isfinite(y).all()
+    # Chunks entirely inside the zero borders contribute nothing: skipping them is exact.
+    assert np.array_equal(y, M.separate(c, w, x, optimized=False))
