@@ -69,9 +69,8 @@ __device__ __forceinline__ float2 norm_coef(double2 sum, int64_t n, float gamma,
 }
 
 
-// GELU of a value that is stored in a 16-bit type (the exact erf form, x·Φ(x) with Φ from
-// Abramowitz–Stegun 7.1.26 on the MUFU pipe, |ΔΦ| ≤ 1.5e-7: far below the storage rounding)
-// or in f32 (erff).
+// GELU of a value that is stored in a 16-bit type (gelu_fast of tc.cuh: one MUFU ex2,
+// |Δ| ≤ 7e-7, far below the storage rounding) or in f32 (the exact erf form).
 template <typename OutT>
 __device__ __forceinline__ float gelu_out(float x) {
     if constexpr (std::is_same<OutT, float>::value) return gelu_erf(x);

@@ -280,23 +280,23 @@ __device__ __forceinline__ float rcp_approx(float x) {
 // rcp instructions plus a few FMAs instead of the libm-accurate erff / tanhf, whose
 // instruction count made the GEMM epilogues issue-bound.
 //
-// erf: Abramowitz & Stegun, Handbook of Mathematical Functions, formula 7.1.26 (Hastings'
-// approximation): erf(z) = 1 − (a1·t + a2·t² + a3·t³ + a4·t⁴ + a5·t⁵)·e^(−z²),
-// t = 1 / (1 + p·z) for z ≥ 0, |error| ≤ 1.5e-7.
-//
-// GELU(x) = x·Φ(x). With 7.1.26 at z = |x|/√2: 1 − Φ(|x|) = ½·erfc(z) = h,
-// h = ½·poly(t)·e^(−x²/2), t = 1 / (1 + p·z); Φ(x) = 1 − h for x ≥ 0 and h for x < 0.
+// GELU(x) = x·Φ(x) = max(x, 0) − |x|·Φ(−|x|), with Φ(−u) = 2^R(u) for u = min(|x|, 5.5) and R
+// a degree-7 polynomial in v = u·2/5.5 − 1: a Chebyshev least-squares fit of log2 Φ(−u) on
+// [0, 5.5] made for this kernel (Φ(−5.5) = 1.9e-8, so the clamp costs < 2.5e-7 at |x| ≤ 12).
+// One MUFU op per element (ex2) and 11 other instructions; emulated in f32 over [−12, 12] the
+// error is ≤ 7e-7 absolute and ≤ 5e-6 relative where |GELU| > 1e-3, far below the 16-bit
+// output rounding.
 __device__ __forceinline__ float gelu_fast(float x) {
-    constexpr float kP = 0.3275911f * 0.70710678118654752f;
-    const float t = rcp_approx(fmaf(kP, fabsf(x), 1.0f));
-    float q = fmaf(0.5f * 1.061405429f, t, 0.5f * -1.453152027f);
-    q = fmaf(q, t, 0.5f * 1.421413741f);
-    q = fmaf(q, t, 0.5f * -0.284496736f);
-    q = fmaf(q, t, 0.5f * 0.254829592f);
-    q *= t;
-    const float h = q * ex2_approx(x * x * (-0.5f * 1.4426950408889634f));
-    const float xh = x * h;
-    return x >= 0.f ? x - xh : xh;
+    const float v = fmaf(fminf(fabsf(x), 5.5f), 2.0f / 5.5f, -1.0f);
+    float r = -0.0022850772365927696f;
+    r = fmaf(r, v, 0.011377031914889812f);
+    r = fmaf(r, v, -0.03212796524167061f);
+    r = fmaf(r, v, 0.07807064056396484f);
+    r = fmaf(r, v, -0.1830366849899292f);
+    r = fmaf(r, v, -5.023968696594238f);
+    r = fmaf(r, v, -12.107662200927734f);
+    r = fmaf(r, v, -8.390584945678711f);
+    return fmaf(-fabsf(x), ex2_approx(r), fmaxf(x, 0.f));
 }
 // tanh(x) = sign(x)·(1 − 2 / (e^(2|x|) + 1)); absolute error ~1e-7.
 __device__ __forceinline__ float tanh_fast(float x) {
