@@ -8,9 +8,10 @@ import pytest
 from ancha_b200.config import ConfigError, Manifest, ModelConfig, mel_band_table
 from ancha_b200 import synthetic
 
-REFERENCE_MEL = "/root/reference/configs/mel-karaoke.json"
-# SHA-256 of json.dumps(bands) for the 60-band Slaney table (checked against the reference's
-# configs/mel-karaoke.json where that file is available).
+# The reference project's checkout, when the environment names one (ANCHA_REFERENCE_ROOT).
+REFERENCE_MEL = os.path.join(os.environ.get("ANCHA_REFERENCE_ROOT", "/nonexistent"), "configs", "mel-karaoke.json")
+# SHA-256 of json.dumps(bands) for the 60-band Slaney table (equal to the bands of the
+# reference's configs/mel-karaoke.json; compared with the file itself where it is available).
 MEL_SHA = "9a633e38e5ac65de299c8e854842a837f9778a5053e4797fc6e14be0bec02f86"
 
 
