@@ -90,6 +90,7 @@ struct PipelineBuffers {
     int64_t chunk = 0;
     DevBuf audio, packed, masks, scratch, y, flag, acc;
     DevBuf pcm, span;  // host-PCM separations: the uploaded track and the span accumulators
+    DevBuf stems;      // single-device host-PCM separations: the finished stems before the copy
 };
 
 class Model {

@@ -179,6 +179,56 @@ struct PcmResult {
     size_t chunks = 0;
 };
 
+// One device, the whole track: overlap-add, division and crop stay on the device and the
+// stems are copied once into the caller's buffer (no host-side span merge).
+PcmResult separate_single(Model& model, const float* planes, const TrackPlan& plan, int batch,
+                          const volatile int* cancel, float* stems_out) {
+    PcmResult r;
+    r.chunks = plan.starts.size();
+    const int64_t samples = plan.samples;
+    const int planes_n = (int)model.manifest.config.stems.size() * 2;
+    if (cudaSetDevice(model.device) != cudaSuccess) { r.status = fail(ANCHA_E_CUDA, "cudaSetDevice"); return r; }
+    cudaStream_t s;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) {
+        r.status = fail(ANCHA_E_CUDA, "cudaStreamCreate");
+        return r;
+    }
+    int st = ANCHA_OK;
+    try {
+        PipelineBuffers& pb = model.pipe;
+        const size_t acc = (size_t)(planes_n + 1) * plan.length;
+        if (pb.pcm.bytes < (size_t)(2 * samples * 4)) pb.pcm.alloc(2 * samples * 4);
+        if (pb.span.bytes < acc * 4) pb.span.alloc(acc * 4);
+        if (pb.stems.bytes < (size_t)planes_n * samples * 4) pb.stems.alloc((size_t)planes_n * samples * 4);
+        float* d_planes = pb.pcm.as<float>();
+        float* d_sums = pb.span.as<float>();
+        float* d_weights = d_sums + (size_t)planes_n * plan.length;
+        st = cudaMemcpyAsync(d_planes, planes, 2 * samples * 4, cudaMemcpyHostToDevice, s) == cudaSuccess
+                 ? ANCHA_OK : fail(ANCHA_E_CUDA, "upload PCM");
+        if (!st) st = cudaMemsetAsync(d_sums, 0, acc * 4, s) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "memset");
+        if (!st) st = run_chunks(model, d_planes, plan, 0, plan.starts.size(), batch, 0, plan.length, d_sums,
+                                 d_weights, cancel, s, &r.model_seconds);
+        if (!st) st = ola_finish(d_sums, d_weights, planes_n, plan.length, plan.border, samples, nullptr,
+                                 pb.stems.as<float>(), nullptr, pb.flag.as<int>() + 1, s);
+        if (!st) st = cudaMemcpyAsync(stems_out, pb.stems.p, (size_t)planes_n * samples * 4, cudaMemcpyDeviceToHost,
+                                      s) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "download stems");
+        int flags[2] = {0, 0};
+        if (!st) st = cudaMemcpyAsync(flags, pb.flag.p, 8, cudaMemcpyDeviceToHost, s) == cudaSuccess
+                          ? ANCHA_OK : fail(ANCHA_E_CUDA, "read status");
+        int mflag = 0;
+        if (!st) st = model.read_flag(s, &mflag);  // synchronises the stream
+        if (!st && (mflag || (flags[1] & 1))) st = fail(ANCHA_E_NONFINITE, "non-finite chunk output");
+        if (!st && (flags[0] || (flags[1] & 4))) st = fail(ANCHA_E_INVALID, "uncovered overlap-add sample");
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (!st && e != cudaSuccess) st = cuda_fail(e, "separate");
+    } catch (const std::exception& ex) {
+        st = fail(ANCHA_E_CUDA, ex.what());
+    }
+    cudaStreamDestroy(s);
+    r.status = st;
+    return r;
+}
+
 // Stems [stems][2][samples] of host planes [2][samples] on the given models (one per GPU).
 PcmResult separate_pcm(Model* const* models, int n, const float* planes, int64_t samples,
                        int64_t chunk, int overlap, int batch, const volatile int* cancel,
@@ -203,6 +253,7 @@ PcmResult separate_pcm(Model* const* models, int n, const float* planes, int64_t
     r.chunks = plan.starts.size();
     if (batch <= 0) batch = default_batch((plan.starts.size() + n - 1) / n);
     batch = std::min(batch, kMaxChunksPerCall);
+    if (n == 1) return separate_single(*models[0], planes, plan, batch, cancel, stems_out);
     const int stems = (int)c.stems.size();
     const int planes_n = stems * 2;
     // Contiguous ranges of chunk starts, ceil(chunks / n) per device.
