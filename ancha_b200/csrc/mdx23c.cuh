@@ -99,4 +99,7 @@ int mdx_istft(const MdxDsp& d, const float* spec, int chunks, int stems, int bin
 int mdx_overlap_add(const float* waves, const int64_t* starts, int chunks, int planes, int chunk, int64_t border,
                     int64_t samples, float* sums, int* flag, cudaStream_t s);
 
+// x[i] *= k for i < n (the overlap-add's division by the overlap count).
+int mdx_scale(float* x, int64_t n, float k, cudaStream_t s);
+
 }  // namespace ancha

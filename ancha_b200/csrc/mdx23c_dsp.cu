@@ -187,6 +187,11 @@ __global__ void overlap_add_kernel(const float* __restrict__ waves, Starts4 star
     sums[(int64_t)p * samples + j - border] = acc;
 }
 
+__global__ void scale_kernel(float* __restrict__ x, int64_t n, float k) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+        x[i] *= k;
+}
+
 int log2_exact(int n) {
     int l = 0;
     while ((1 << l) < n) ++l;
@@ -259,6 +264,12 @@ int mdx_overlap_add(const float* waves, const int64_t* starts, int chunks, int p
     overlap_add_kernel<<<dim3((unsigned)ceil_div(hi - lo, 256), planes), 256, 0, s>>>(
         waves, st, chunks, planes, chunk, border, samples, lo, hi, sums, flag);
     return check_launch("mdx_overlap_add");
+}
+
+int mdx_scale(float* x, int64_t n, float k, cudaStream_t s) {
+    if (n <= 0) return ANCHA_OK;
+    scale_kernel<<<(unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 16), 256, 0, s>>>(x, n, k);
+    return check_launch("mdx_scale");
 }
 
 }  // namespace ancha

@@ -248,7 +248,8 @@ std::unique_ptr<Mdx23c> Mdx23c::load(const std::string& package, int device, int
 }
 
 int Mdx23c::ensure_workspace(int batch, int frames) {
-    if (batch == ws_batch_ && frames == ws_frames_) return ANCHA_OK;
+    // Buffers sized for a larger batch serve a smaller one (the last call of a separation).
+    if (frames == ws_frames_ && batch <= ws_batch_) return ANCHA_OK;
     const Mdx23cConfig& c = manifest.config;
     const int64_t b = batch, f0 = c.bins / c.subbands, t0 = frames;
     const size_t es = elt_size(elt_);
@@ -554,14 +555,13 @@ int Mdx23c::separate_pcm(const float* planes, int64_t samples, int overlap, int 
             ANCHA_TRY(mdx_overlap_add(waves.as<float>(), st, n, stems_n * 2, (int)chunk, border, samples,
                                       sums.as<float>(), flag.as<int>(), s));
         }
+        ANCHA_TRY(mdx_scale(sums.as<float>(), (int64_t)stems_n * 2 * samples, 1.f / (float)ov, s));
         ANCHA_CUDA(cudaMemcpyAsync(stems, sums.p, sums.bytes, cudaMemcpyDeviceToHost, s));
         int status = 0;
         ANCHA_CUDA(cudaMemcpyAsync(&status, flag.p, sizeof(int), cudaMemcpyDeviceToHost, s));
         ANCHA_CUDA(cudaStreamSynchronize(s));
         if (status & 1) return fail(ANCHA_E_NONFINITE, "non-finite MDX23C output");
         if (status & 2) return fail(ANCHA_E_INVALID, "iSTFT has an uncovered sample");
-        const float inv = 1.f / (float)ov;
-        for (size_t i = 0; i < (size_t)stems_n * 2 * samples; ++i) stems[i] *= inv;
     } catch (const std::exception& e) {
         return fail(ANCHA_E_CUDA, e.what());
     }
