@@ -269,6 +269,21 @@ int ancha_mdx23c_separate_pcm(ancha_mdx23c* model, const float* planes, int64_t 
     return model->impl->separate_pcm(planes, samples, overlap, batch, cancel, stems_out, seconds_out);
 }
 
+int ancha_mdx23c_plan(int64_t samples, int64_t chunk_samples, int overlap, int64_t* step, int64_t* border,
+                      int64_t* pad, int64_t* padded, int64_t* chunks) {
+    try {
+        const Mdx23cPlan p = Mdx23cPlan::make(samples, chunk_samples, overlap);
+        if (step) *step = p.step;
+        if (border) *border = p.border;
+        if (pad) *pad = p.pad;
+        if (padded) *padded = p.padded;
+        if (chunks) *chunks = p.chunks;
+        return ANCHA_OK;
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
+    }
+}
+
 void ancha_mdx23c_free(ancha_mdx23c* model) { delete model; }
 
 void ancha_free_string(char* s) { std::free(s); }

@@ -13,6 +13,7 @@
 
 #include <algorithm>
 #include <chrono>
+#include <climits>
 #include <cstring>
 #include <set>
 #include <stdexcept>
@@ -69,6 +70,24 @@ int64_t round8(int64_t k) { return (k + 7) / 8 * 8; }
 constexpr float kNormEps = 1e-5f;  // Preact's InstanceNorm epsilon (mdx23c.rs:204)
 
 }  // namespace
+
+Mdx23cPlan Mdx23cPlan::make(int64_t length, int64_t chunk, int overlap) {
+    ensure(length > 0 && chunk > 0 && overlap >= 1 && overlap <= 16 && overlap <= chunk,
+           "invalid MDX23C overlap plan");
+    Mdx23cPlan p;
+    p.length = length;
+    p.chunk = chunk;
+    p.step = chunk / overlap;
+    const int64_t left = length % p.step, right = chunk % p.step;
+    const int64_t remainder = left >= right ? left - right : p.step - (right - left);
+    p.pad = p.step - remainder;
+    p.border = chunk - p.step;
+    if (length > INT64_MAX - p.pad - 2 * p.border) bad("MDX23C padded length overflow");
+    p.padded = length + p.pad + 2 * p.border;
+    ensure(p.padded >= chunk, "insufficient MDX23C padding");
+    p.chunks = (p.padded - chunk) / p.step + 1;
+    return p;
+}
 
 void Mdx23cConfig::validate() const {
     // mdx23c.rs:76-122.
@@ -496,20 +515,16 @@ int Mdx23c::separate_pcm(const float* planes, int64_t samples, int overlap, int 
     if (!planes || !stems || samples <= 0) return fail(ANCHA_E_INVALID, "mdx23c_separate: empty input");
     const int ov = overlap > 0 ? overlap : c.overlap;
     const int64_t chunk = c.chunk_samples();
-    // OverlapPlan::new (mdx23c_runtime.rs:84-115).
-    if (ov < 1 || ov > 16 || ov > chunk) return fail(ANCHA_E_INVALID, "invalid MDX23C overlap plan");
-    const int64_t step = chunk / ov;
-    const int64_t left = samples % step, right = chunk % step;
-    const int64_t remainder = left >= right ? left - right : step - (right - left);
-    const int64_t pad = step - remainder, border = chunk - step;
-    const int64_t padded = samples + pad + 2 * border;
-    if (padded < chunk) return fail(ANCHA_E_INVALID, "insufficient MDX23C padding");
-    const int64_t n_chunks = (padded - chunk) / step + 1;
-    std::vector<int64_t> starts;
-    for (int64_t i = 0; i < n_chunks; ++i) {
-        const int64_t s0 = i * step;
-        if (s0 < border + samples && s0 + chunk > border) starts.push_back(s0);  // OverlapPlan::intersects
+    Mdx23cPlan plan;
+    try {
+        plan = Mdx23cPlan::make(samples, chunk, ov);
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
     }
+    const int64_t border = plan.border;
+    std::vector<int64_t> starts;
+    for (int64_t i = 0; i < plan.chunks; ++i)
+        if (plan.intersects(i * plan.step)) starts.push_back(i * plan.step);
     const int b = batch > 0 ? std::min(batch, 4) : 4;
     if (batch < 0) return fail(ANCHA_E_INVALID, "mdx23c_separate: batch");
     const int stems_n = (int)c.stems.size(), frames = c.frames, bins = c.bins;

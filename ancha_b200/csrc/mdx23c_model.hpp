@@ -23,6 +23,15 @@ struct Mdx23cConfig {
     static Mdx23cConfig from_json(const Json& j);  // strict keys (deny_unknown_fields)
 };
 
+// OverlapPlan::new of mdx23c_runtime.rs:84-115 (UVR padding, Python modulo semantics):
+// step = chunk / overlap, border = chunk − step, pad, padded length and chunk count; throws
+// std::runtime_error on invalid arguments. `intersects` is OverlapPlan::intersects.
+struct Mdx23cPlan {
+    int64_t length = 0, chunk = 0, step = 0, border = 0, pad = 0, padded = 0, chunks = 0;
+    static Mdx23cPlan make(int64_t length, int64_t chunk, int overlap);
+    bool intersects(int64_t start) const { return start < border + length && start + chunk > border; }
+};
+
 struct Mdx23cManifest {
     int schema_version = 0;
     std::string model_id, weights_sha256, checkpoint_sha256, source_url, forward_revision,

@@ -74,6 +74,20 @@ class Mdx23c:
             pass
 
 
+class OverlapPlan:
+    """``OverlapPlan::new`` (src/mdx23c_runtime.rs:84-115) through ``ancha_mdx23c_plan``:
+    ``step``, ``border``, ``pad``, ``padded`` and ``chunks`` of a ``samples``-long track."""
+
+    def __init__(self, samples: int, chunk_samples: int, overlap: int):
+        vals = [C.c_int64() for _ in range(5)]
+        N.check(N.lib().ancha_mdx23c_plan(samples, chunk_samples, overlap, *[C.byref(v) for v in vals]))
+        self.samples, self.chunk = samples, chunk_samples
+        self.step, self.border, self.pad, self.padded, self.chunks = (v.value for v in vals)
+
+    def intersects(self, start: int) -> bool:
+        return start < self.border + self.samples and start + self.chunk > self.border
+
+
 def write_package(directory: str, config: dict, tensors: dict, model_id: str = "synthetic-mdx23c") -> dict:
     """Write ``model.safetensors`` (F32) and a schema-1 ``manifest.json``; returns the manifest."""
     os.makedirs(directory, exist_ok=True)

@@ -225,6 +225,13 @@ ANCHA_API int ancha_mdx23c_forward(ancha_mdx23c* model, const float* spectrum, i
 ANCHA_API int ancha_mdx23c_separate_pcm(ancha_mdx23c* model, const float* planes, int64_t samples, int overlap,
                               int batch, const volatile int* cancel, float* stems_out, double* seconds_out);
 
+/* The UVR chunk plan of a `samples`-long track (OverlapPlan::new, mdx23c_runtime.rs:84-115):
+ * step = chunk / overlap, border = chunk − step, right pad, padded length and chunk count
+ * (chunk i starts at i·step of the zero-bordered track). Any output pointer may be NULL.
+ * Host-only. */
+ANCHA_API int ancha_mdx23c_plan(int64_t samples, int64_t chunk_samples, int overlap, int64_t* step, int64_t* border,
+                      int64_t* pad, int64_t* padded, int64_t* chunks);
+
 ANCHA_API void ancha_mdx23c_free(ancha_mdx23c* model);
 
 /* ------------------------------------------------------------------------------------ *

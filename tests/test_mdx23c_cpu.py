@@ -69,3 +69,19 @@ def test_missing_package_is_an_io_error(tmp_path):
 
 def test_forward_rejects_null_handle():
     assert N.lib().ancha_mdx23c_forward(None, None, 1, 8, None, None, None) == N.E_INVALID
+
+
+def test_overlap_plan_matches_reference_and_oracle():
+    # mdx23c_runtime_contracts.rs:16-24 and the oracle's restatement, through the C ABI.
+    from ancha_b200.mdx23c import OverlapPlan
+    p = OverlapPlan(132300, 261120, 8)
+    assert (p.step, p.border, p.pad, p.chunks) == (32640, 228480, 30900, 12)
+    for n in [1, 32, 127, 128, 129, 256, 333, 44100 * 37]:
+        for chunk, overlap in [(128, 1), (128, 2), (128, 8), (261120, 8), (1792, 4)]:
+            a, b = OverlapPlan(n, chunk, overlap), M.OverlapPlan(n, chunk, overlap)
+            assert (a.step, a.border, a.pad, a.padded, a.chunks) == (b.step, b.border, b.pad, b.padded, b.chunks)
+            assert [a.intersects(i * a.step) for i in range(a.chunks)] == \
+                   [b.intersects(i * b.step) for i in range(b.chunks)]
+    for bad in [(0, 128, 8), (10, 128, 0), (10, 128, 17), (10, 4, 8)]:
+        with pytest.raises(N.AnchaError):
+            OverlapPlan(*bad)
