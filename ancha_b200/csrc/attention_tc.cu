@@ -31,6 +31,7 @@ struct AttnTcParams {
     void* out;
     int64_t ld, out_ld, group_inner_stride, group_outer_stride, token_stride;
     uint32_t idesc_s, idesc_o;
+    uint32_t idesc_s_half;  // S with N = 64 keys: a last key block with at most 64 valid keys
     int* err;
 };
 
@@ -377,9 +378,12 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, abort, p.err)) return false;
                 tc_fence_after();
                 const uint64_t k_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_K + (j % PP_KV_STAGES) * QKV_BYTES));
+                // A key block with at most 64 valid keys (the last one) computes only S[:, 0:64];
+                // the softmax then reads only those columns.
+                const uint32_t idesc = p.tokens - j * TILE <= TILE / 2 ? p.idesc_s_half : p.idesc_s;
 #pragma unroll
                 for (int kk = 0; kk < HD / 16; ++kk)  // K step of 16 = 32 bytes = 2 descriptor units
-                    umma_f16(tmem, q_desc + 2 * kk, k_desc + 2 * kk, p.idesc_s, kk != 0);
+                    umma_f16(tmem, q_desc + 2 * kk, k_desc + 2 * kk, idesc, kk != 0);
                 umma_commit(s_full);
                 return true;
             };
@@ -387,8 +391,9 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 if (!mbar_wait(p_ready, k & 1, abort, p.err)) return false;
                 tc_fence_after();
                 const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_V + (k % PP_KV_STAGES) * QKV_BYTES));
-#pragma unroll
-                for (int kk = 0; kk < TILE / 16; ++kk)  // 16 keys = 16 rows of 128 bytes = 128 units
+                // Steps of 16 keys up to the last valid key: P is 0 beyond it.
+                const int steps = min(TILE / 16, (p.tokens - k * TILE + 15) / 16);
+                for (int kk = 0; kk < steps; ++kk)  // 16 keys = 16 rows of 128 bytes = 128 units
                     umma_f16_ts(tmem + PP_O_COL, tmem + PP_P_COL + kk * 8, v_desc + 128 * kk, p.idesc_o,
                                 (k > 0 || kk > 0) ? 1u : 0u);
                 umma_commit(pv_done);
@@ -424,6 +429,9 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             tc_fence_before();
             mbar_arrive(s_free);  // the tensor cores may compute S(kb + 1) now
             const int nvalid = min(TILE, p.tokens - kb * TILE);  // valid keys in this block
+            // With at most 64 valid keys S holds keys 0..63 only (N = 64); the masking below
+            // covers the stale columns 64..127 as well.
+            const bool half = nvalid <= TILE / 2;
             if (nvalid < TILE) {
 #pragma unroll
                 for (int c = 0; c < TILE; ++c)
@@ -477,7 +485,7 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 }
             }
             tmem_st32(p_addr, pk[0]);
-            tmem_st32(p_addr + 32, pk[1]);
+            if (!half) tmem_st32(p_addr + 32, pk[1]);  // P·V of a half block reads keys 0..63 only
             l += sum0 + sum1;
             tmem_wait_st();
             tc_fence_before();
@@ -585,6 +593,7 @@ int attention_tc(const AttnArgs& a, cudaStream_t stream) {
     p.token_stride = a.token_stride;
     p.idesc_s = umma_idesc_f16(a.elt == ELT_BF16, TILE, TILE, 0);
     p.idesc_o = umma_idesc_f16(a.elt == ELT_BF16, TILE, HD, 1);
+    p.idesc_s_half = umma_idesc_f16(a.elt == ELT_BF16, TILE, TILE / 2, 0);
     p.err = device_error_word();
     // Tensor map {columns, tokens, inner groups, outer groups}; unused strides still have to
     // be 16-byte multiples, so a one-long dimension reuses the row stride.

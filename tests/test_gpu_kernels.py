@@ -316,16 +316,18 @@ def attention_abi(buf, desc_kw, separate_kv=False, out_dtype=None):
 
 
 @pytest.mark.parametrize("dt,min_db", [(torch.float16, 60.0), (torch.bfloat16, 45.0)])
-@pytest.mark.parametrize("axis", ["time", "band", "band2", "short", "t129", "t300"])
+@pytest.mark.parametrize("axis", ["time", "band", "band2", "short", "t129", "t200", "t300"])
 @pytest.mark.parametrize("gated", [False, True])
 def test_tensor_core_attention_matches_ffma(dt, min_db, axis, gated):
     """The tcgen05 attention against the FFMA attention on the same 16-bit operands, in the
     model's layouts: time axis (60 bands × 801 frames, tokens contiguous), band axis (801
     frames × 60 bands, tokens 801 rows apart, two problems per tile; and two chunks of 51
-    frames × 33 bands, so the last tile of each chunk holds one problem), a short ragged case."""
+    frames × 33 bands, so the last tile of each chunk holds one problem), a short ragged case,
+    and time axes whose last key block holds 1, 33, 44 (at most 64: S computed for 64 keys) or
+    72 valid keys."""
     chunks, bands, frames, heads = {"time": (1, 60, 801, 8), "band": (1, 60, 801, 8), "band2": (2, 33, 51, 3),
                                      "short": (2, 3, 37, 2), "t129": (1, 4, 129, 2),
-                                     "t300": (2, 3, 300, 2)}[axis]
+                                     "t200": (1, 3, 200, 2), "t300": (2, 3, 300, 2)}[axis]
     ld = (3 * heads * 64 + heads + 7) // 8 * 8   # 16-byte rows, as the model's packed projection
     rows = chunks * bands * frames
     g = torch.Generator(device="cuda").manual_seed(5)
