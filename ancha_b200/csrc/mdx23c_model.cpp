@@ -251,12 +251,16 @@ std::unique_ptr<Mdx23c> Mdx23c::load(const std::string& package, int device, int
         conv(m->final_first_, "final_conv.0.weight", ch, ch + input, 1);
         conv(m->final_last_, "final_conv.2.weight", (int)c.stems.size() * input, ch, 1);
         m->tensor_count = w.finish();
-        m->dsp_window_.alloc((size_t)c.n_fft * sizeof(float));
-        m->dsp_twiddle_.alloc((size_t)4097 * sizeof(float2));
-        if (mdx_dsp_tables(c.n_fft, m->dsp_window_.as<float>(), m->dsp_twiddle_.as<float2>(), 0) != ANCHA_OK)
-            bad(std::string("MDX23C DSP tables: ") + ancha_last_error());
-        const cudaError_t te = cudaDeviceSynchronize();
-        if (te != cudaSuccess) bad(std::string("MDX23C DSP tables: ") + cudaGetErrorString(te));
+        // STFT tables for separate_pcm (power-of-two n_fft only; the network itself takes any
+        // valid config).
+        if ((c.n_fft & (c.n_fft - 1)) == 0) {
+            m->dsp_window_.alloc((size_t)c.n_fft * sizeof(float));
+            m->dsp_twiddle_.alloc((size_t)4097 * sizeof(float2));
+            if (mdx_dsp_tables(c.n_fft, m->dsp_window_.as<float>(), m->dsp_twiddle_.as<float2>(), 0) != ANCHA_OK)
+                bad(std::string("MDX23C DSP tables: ") + ancha_last_error());
+            const cudaError_t te = cudaDeviceSynchronize();
+            if (te != cudaSuccess) bad(std::string("MDX23C DSP tables: ") + cudaGetErrorString(te));
+        }
     } catch (...) {
         hasher.join();
         throw;
@@ -529,13 +533,15 @@ int Mdx23c::separate_pcm(const float* planes, int64_t samples, int overlap, int 
     if (batch < 0) return fail(ANCHA_E_INVALID, "mdx23c_separate: batch");
     const int stems_n = (int)c.stems.size(), frames = c.frames, bins = c.bins;
     if (chunk / c.hop + 1 != frames) return fail(ANCHA_E_INVALID, "MDX23C STFT frame count mismatch");
+    if (!dsp_window_.p) return fail(ANCHA_E_UNSUPPORTED, "MDX23C separation: n_fft must be a power of two");
     ANCHA_CUDA(cudaSetDevice(device));
     try {
+        DevBuf track, audio, spec, yout, scratch, waves, sums, flag;
         cudaStream_t s = nullptr;
         ANCHA_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
-        DevBuf track, audio, spec, yout, scratch, waves, sums, flag;
         // Declared after the buffers, so destroyed before them: no buffer is freed while work
-        // queued on the stream (an early error return) may still use it.
+        // queued on the stream (an early error return) may still use it, and the stream is
+        // released on every path, an allocation failure included.
         struct StreamGuard {
             cudaStream_t s;
             ~StreamGuard() {
