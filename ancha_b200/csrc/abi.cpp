@@ -10,6 +10,7 @@
 #include "dsp.cuh"
 #include "gemm.cuh"
 #include "mdx23c_model.hpp"
+#include "onnx.hpp"
 #include "model.hpp"
 
 namespace ancha {
@@ -285,6 +286,22 @@ int ancha_mdx23c_plan(int64_t samples, int64_t chunk_samples, int overlap, int64
 }
 
 void ancha_mdx23c_free(ancha_mdx23c* model) { delete model; }
+
+int ancha_mdx_graph_inspect(const void* onnx, size_t bytes, int optimized, int* nodes, int* instructions,
+                            int* folded_bn, int* constants) {
+    if (!onnx || bytes == 0) return fail(ANCHA_E_INVALID, "mdx_graph_inspect: empty model");
+    try {
+        const OnnxModel m = parse_onnx(static_cast<const uint8_t*>(onnx), bytes);
+        const MdxGraph g = MdxGraph::build(m, optimized != 0);
+        if (nodes) *nodes = g.nodes;
+        if (instructions) *instructions = (int)g.instructions.size();
+        if (folded_bn) *folded_bn = g.folded_bn;
+        if (constants) *constants = (int)g.constants.size();
+        return ANCHA_OK;
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
+    }
+}
 
 void ancha_free_string(char* s) { std::free(s); }
 

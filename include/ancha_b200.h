@@ -235,6 +235,21 @@ ANCHA_API int ancha_mdx23c_plan(int64_t samples, int64_t chunk_samples, int over
 ANCHA_API void ancha_mdx23c_free(ancha_mdx23c* model);
 
 /* ------------------------------------------------------------------------------------ *
+ * Classic MDX ONNX graphs (crates/ancha-models/src/mdx.rs)                             *
+ * ------------------------------------------------------------------------------------ */
+
+/* Read an ONNX model (`bytes` bytes at `onnx`, host memory) and build the classic MDX
+ * executable graph as Graph::from_bytes does (mdx.rs:161-472): opset 13, one input and one
+ * output, FLOAT initializers of at most four dims, the op set Conv / ConvTranspose / Relu /
+ * Transpose / MatMul / Add / Mul / BatchNormalization with their attribute allow-list, and
+ * with `optimized` the folding of a BatchNormalization into the ConvTranspose that is its
+ * only producer. Reports the graph's node count, scheduled instructions, folded
+ * BatchNormalizations and constants (any pointer may be NULL). Host-only, no device work;
+ * ANCHA_E_INVALID with the reference's message for a graph it would reject. */
+ANCHA_API int ancha_mdx_graph_inspect(const void* onnx, size_t bytes, int optimized, int* nodes, int* instructions,
+                            int* folded_bn, int* constants);
+
+/* ------------------------------------------------------------------------------------ *
  * Task API (replaces backend::separate / runtime::separate, src/backend.rs:145-199)    *
  * ------------------------------------------------------------------------------------ */
 
