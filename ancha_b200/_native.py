@@ -28,7 +28,8 @@ EXPORTS = ("ancha_last_error", "ancha_version", "ancha_available", "ancha_attent
            "ancha_linear_fwd", "ancha_stft_fwd", "ancha_istft_masked", "ancha_istft_masked_static", "ancha_ola_add",
            "ancha_model_load", "ancha_model_info", "ancha_model_forward", "ancha_model_free",
            "ancha_mdx23c_load", "ancha_mdx23c_info", "ancha_mdx23c_forward", "ancha_mdx23c_separate_pcm",
-           "ancha_mdx23c_plan", "ancha_mdx23c_free", "ancha_mdx_graph_inspect",
+           "ancha_mdx23c_plan", "ancha_mdx23c_free", "ancha_mdx_graph_inspect", "ancha_mdx_load",
+           "ancha_mdx_output_shape", "ancha_mdx_forward", "ancha_mdx_free",
            "ancha_separate", "ancha_separate_pcm", "ancha_separate_device",
            "ancha_separate_status", "ancha_chunk_plan", "ancha_chunk_span", "ancha_separate_span",
            "ancha_free_string")
@@ -106,6 +107,10 @@ def lib() -> C.CDLL:
             "ancha_mdx23c_plan": (i32, [i64, i64, i32] + [C.POINTER(i64)] * 5),
             "ancha_mdx23c_free": (None, [vp]),
             "ancha_mdx_graph_inspect": (i32, [vp, C.c_size_t, i32] + [C.POINTER(i32)] * 4),
+            "ancha_mdx_load": (i32, [vp, C.c_size_t, i32, i32, C.POINTER(vp)]),
+            "ancha_mdx_output_shape": (i32, [vp, C.POINTER(i64), C.POINTER(i64)]),
+            "ancha_mdx_forward": (i32, [vp, vp, C.POINTER(i64), vp, C.POINTER(i32), vp]),
+            "ancha_mdx_free": (None, [vp]),
             "ancha_separate": (i32, [C.POINTER(SeparateOpts), i32, C.POINTER(i32), PROGRESS,
                                      vp, C.POINTER(i32), C.POINTER(C.c_void_p)]),
             "ancha_separate_pcm": (i32, [C.POINTER(vp), i32, fp, i64, i64, i32, i32,

@@ -10,6 +10,7 @@
 #include "dsp.cuh"
 #include "gemm.cuh"
 #include "mdx23c_model.hpp"
+#include "mdx_exec.hpp"
 #include "onnx.hpp"
 #include "model.hpp"
 
@@ -304,5 +305,38 @@ int ancha_mdx_graph_inspect(const void* onnx, size_t bytes, int optimized, int* 
 }
 
 void ancha_free_string(char* s) { std::free(s); }
+
+int ancha_mdx_load(const void* onnx, size_t bytes, int optimized, int device, ancha_mdx** out) {
+    if (!onnx || bytes == 0 || !out) return fail(ANCHA_E_INVALID, "mdx_load: null argument");
+    *out = nullptr;
+    try {
+        auto m = MdxModel::load(static_cast<const uint8_t*>(onnx), bytes, optimized != 0, device);
+        *out = new ancha_mdx{std::move(m)};
+        return ANCHA_OK;
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
+    }
+}
+
+int ancha_mdx_output_shape(const ancha_mdx* graph, const int64_t input_shape[4], int64_t output_shape[4]) {
+    if (!graph || !input_shape || !output_shape) return fail(ANCHA_E_INVALID, "mdx_output_shape: null argument");
+    Shape4 in{input_shape[0], input_shape[1], input_shape[2], input_shape[3]}, out{};
+    ANCHA_TRY(graph->impl->output_shape(in, out));
+    for (int d = 0; d < 4; ++d) output_shape[d] = out[d];
+    return ANCHA_OK;
+}
+
+int ancha_mdx_forward(ancha_mdx* graph, const float* x, const int64_t input_shape[4], float* out,
+                      const volatile int* cancel, void* stream) {
+    if (!graph || !x || !input_shape || !out) return fail(ANCHA_E_INVALID, "mdx_forward: null argument");
+    Shape4 in{input_shape[0], input_shape[1], input_shape[2], input_shape[3]};
+    try {
+        return graph->impl->forward(x, in, out, cancel, as_stream(stream));
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_CUDA, e.what());
+    }
+}
+
+void ancha_mdx_free(ancha_mdx* graph) { delete graph; }
 
 }  // extern "C"

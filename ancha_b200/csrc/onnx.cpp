@@ -404,13 +404,8 @@ MdxGraph MdxGraph::build(const OnnxModel& m, bool optimized) {
             ins.eps = float_attr(n, "epsilon", 1e-5f);
             if (!std::isfinite(ins.eps) || !(ins.eps > 0.f)) bad("invalid BN epsilon");
             ins.op = MdxOp::Bn;
-            std::vector<float> scale, shift;
-            stats(n, scale, shift, ins.eps);
-            if (optimized) {
-                ins.affine = true;
-                ins.scale = std::move(scale);
-                ins.shift = std::move(shift);
-            }
+            stats(n, ins.scale, ins.shift, ins.eps);
+            ins.affine = optimized;
         } else {
             bad("unsupported ONNX operation " + n.op_type + " at " + n.name);
         }

@@ -57,8 +57,9 @@ struct MdxInstruction {
     int groups = 1;
     int perm[4] = {3, 2, 1, 0};
     float eps = 1e-5f;
-    bool affine = false;             // BatchNormalization as x·scale + shift (optimized)
-    std::vector<float> scale, shift; // [channels]
+    bool affine = false;             // the reference folds BatchNormalization to x·scale + shift
+                                     // (optimized); the device always runs that form
+    std::vector<float> scale, shift; // [channels] γ/√(var + ε), β − mean·scale
 };
 
 struct MdxConstant {

@@ -2,10 +2,13 @@
 
 :func:`inspect` reads an ONNX model and builds the classic MDX executable graph exactly as
 ``Graph::from_bytes`` does (validation, BatchNormalization folding, schedule), on the host.
+:class:`Graph` is that graph resident on one GPU; ``forward`` is ``Graph::forward`` on CUDA
+f32 NCHW tensors.
 """
 from __future__ import annotations
 
 import ctypes as C
+from typing import Optional
 
 from . import _native as N
 
@@ -17,3 +20,44 @@ def inspect(onnx: bytes, optimized: bool = True) -> dict:
     buf = C.create_string_buffer(onnx, len(onnx))
     N.check(N.lib().ancha_mdx_graph_inspect(buf, len(onnx), int(optimized), *[C.byref(v) for v in vals]))
     return dict(zip(("nodes", "instructions", "folded_bn", "constants"), (v.value for v in vals)))
+
+
+class Graph:
+    """A classic MDX ONNX graph on one GPU (not re-entrant)."""
+
+    def __init__(self, onnx: bytes, device: int = 0, optimized: bool = True):
+        handle = C.c_void_p()
+        buf = C.create_string_buffer(onnx, len(onnx))
+        N.check(N.lib().ancha_mdx_load(buf, len(onnx), int(optimized), device, C.byref(handle)))
+        self._h = handle
+        self.device = device
+
+    def output_shape(self, shape) -> tuple:
+        i = (C.c_int64 * 4)(*shape)
+        o = (C.c_int64 * 4)()
+        N.check(N.lib().ancha_mdx_output_shape(self._h, i, o))
+        return tuple(o)
+
+    def forward(self, x, cancel: Optional[C.c_int] = None):
+        """Output of the graph for a CUDA f32 NCHW tensor."""
+        import torch
+        x = x.contiguous().float()
+        if x.dim() != 4:
+            raise N.AnchaError(N.E_INVALID, "input must be NCHW")
+        shape = tuple(x.shape)
+        out = torch.empty(self.output_shape(shape), dtype=torch.float32, device=x.device)
+        stream = C.c_void_p(torch.cuda.current_stream(x.device).cuda_stream)
+        N.check(N.lib().ancha_mdx_forward(self._h, x.data_ptr(), (C.c_int64 * 4)(*shape), out.data_ptr(),
+                                          None if cancel is None else C.byref(cancel), stream))
+        return out
+
+    def close(self) -> None:
+        if self._h:
+            N.lib().ancha_mdx_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -249,6 +249,27 @@ ANCHA_API void ancha_mdx23c_free(ancha_mdx23c* model);
 ANCHA_API int ancha_mdx_graph_inspect(const void* onnx, size_t bytes, int optimized, int* nodes, int* instructions,
                             int* folded_bn, int* constants);
 
+typedef struct ancha_mdx ancha_mdx;
+
+/* Build the graph as ancha_mdx_graph_inspect does and upload its constants to `device`
+ * (Graph::from_bytes, mdx.rs:161-472). */
+ANCHA_API int ancha_mdx_load(const void* onnx, size_t bytes, int optimized, int device, ancha_mdx** out);
+
+/* Output shape of the graph for an NCHW input shape (host-only shape inference);
+ * ANCHA_E_INVALID when an operation's shapes disagree. */
+ANCHA_API int ancha_mdx_output_shape(const ancha_mdx* graph, const int64_t input_shape[4], int64_t output_shape[4]);
+
+/* Graph::forward (mdx.rs:474-568) on the device: x (device f32, NCHW `input_shape`) → out
+ * (device f32 of ancha_mdx_output_shape). Conv / ConvTranspose with any stride, padding,
+ * dilation, groups and output padding, Relu, Transpose, MatMul and Add / Mul with NCHW
+ * broadcasting, BatchNormalization as its per-channel affine form. Checks *cancel (host
+ * memory, may be NULL) before every operation. Intermediate values use stream-ordered
+ * allocations freed after their last consumer. Not re-entrant per handle. */
+ANCHA_API int ancha_mdx_forward(ancha_mdx* graph, const float* x, const int64_t input_shape[4], float* out,
+                      const volatile int* cancel, void* stream);
+
+ANCHA_API void ancha_mdx_free(ancha_mdx* graph);
+
 /* ------------------------------------------------------------------------------------ *
  * Task API (replaces backend::separate / runtime::separate, src/backend.rs:145-199)    *
  * ------------------------------------------------------------------------------------ */
