@@ -10,6 +10,8 @@ with numpy broadcasting over NCHW tensors, BatchNormalization as (x âˆ’ mean)/âˆ
 or its folded affine form. Arithmetic is float64.
 
 The protobuf reader below is this oracle's own, independent of the library's C++ reader.
+``pack`` / ``unpack`` / ``separate`` restate the task of ``src/mdx_runtime.rs:79-248`` (three
+zeroed low bins, UVR trim and pad, Hann-weighted chunk overlap-add, compensation, denoise).
 """
 from __future__ import annotations
 
@@ -401,3 +403,87 @@ def conv_transpose2d(x, w, stride, padding, padding_out, dilation, groups):
                 full[:, g * cog:(g + 1) * cog, ky * dh:ky * dh + sh * (h - 1) + 1:sh,
                      kx * dw:kx * dw + sw * (wd - 1) + 1:sw] += contrib
     return full[:, :, ph:ph + oh, pw:pw + ow]
+
+
+# ---- Task: src/mdx_runtime.rs -----------------------------------------------------------------
+
+def pack(stft, planes: np.ndarray, bins: int, zero_low_bins: int = 3) -> np.ndarray:
+    """``mdx_runtime::pack`` = ``spectral::pack`` with the lowest three bins zeroed
+    (src/mdx_runtime.rs:79-83, src/spectral.rs:5-36): ``[2, n]`` â†’ ``[4, bins, frames]``."""
+    frames = planes.shape[1] // stft.hop + 1
+    out = np.empty((4, bins, frames))
+    for ch in range(2):
+        spec = stft.forward(planes[ch])[:, :bins].copy()
+        spec[:, :zero_low_bins] = 0.0
+        out[2 * ch] = spec.real.T
+        out[2 * ch + 1] = spec.imag.T
+    return out
+
+
+def unpack(stft, packed: np.ndarray, length: int) -> np.ndarray:
+    """``spectral::unpack`` (src/spectral.rs:38-76): bins past ``bins`` are zero."""
+    _, bins, frames = packed.shape
+    out = []
+    for ch in range(2):
+        spec = np.zeros((frames, stft.n_fft // 2 + 1), dtype=np.complex128)
+        spec[:, :bins] = packed[2 * ch].T + 1j * packed[2 * ch + 1].T
+        out.append(stft.inverse(spec, length, False))
+    return np.stack(out)
+
+
+def separate(graph: Graph, n_fft: int, bins: int, frames: int, compensate: float, planes: np.ndarray,
+             hop: int = 1024, overlap=None, denoise: bool = False, optimized: bool = True,
+             batch: int = 1) -> tuple:
+    """``separate_mdx`` without file I/O (src/mdx_runtime.rs:84-248): UVR trim / pad, chunks
+    every ``gen_size`` samples (or (1 âˆ’ overlap)Â·chunk), Hann-weighted overlap-add divided by
+    the summed weights (rectangular for overlap 0), times ``compensate``; optional denoise
+    (f(x) âˆ’ f(âˆ’x))/2. Returns (predicted, residual), each ``[2, n]``."""
+    from .dsp import Stft
+    if not 1 <= batch <= 4:
+        raise GraphError("MDX batch size must be between 1 and 4")
+    if overlap is not None and not (np.isfinite(overlap) and 0.0 <= overlap <= 0.95):
+        raise GraphError("MDX overlap must be between 0 and 0.95")
+    n = planes.shape[1]
+    chunk = hop * (frames - 1)
+    trim = n_fft // 2
+    gen_size = chunk - n_fft
+    pad = gen_size + trim - n % gen_size
+    mixture_len = trim + n + pad
+    step = gen_size if overlap is None else int((1.0 - overlap) * chunk)
+    if step <= 0:
+        raise GraphError("zero MDX step")
+    starts = [s for s in range(0, mixture_len, step) if not optimized or s < trim + n]
+    stft = Stft(n_fft, hop)
+    result = np.zeros((2, n))
+    divisor = np.zeros(n)
+    for b0 in range(0, len(starts), batch):
+        group = starts[b0:b0 + batch]
+        packed = []
+        for s in group:
+            actual = min(chunk, mixture_len - s)
+            window = np.zeros((2, chunk))
+            for i in range(actual):
+                pos = s + i
+                if trim <= pos < trim + n:
+                    window[:, i] = planes[:, pos - trim]
+            p = pack(stft, window, bins)
+            if p.shape[2] != frames:
+                raise GraphError("MDX frame mismatch")
+            packed.append(p)
+        x = np.stack(packed)
+        y = (graph.forward(x) - graph.forward(-x)) * 0.5 if denoise else graph.forward(x)
+        if y.shape != x.shape:
+            raise GraphError("MDX output shape mismatch")
+        for k, s in enumerate(group):
+            audio = unpack(stft, y[k], chunk)
+            actual = min(chunk, mixture_len - s)
+            first, end = max(s, trim), min(s + actual, trim + n)
+            for pos in range(first, end):
+                local = pos - s
+                w = 1.0 if overlap == 0.0 else float(np.float32(0.5 - 0.5 * np.cos(2 * np.pi * local / (actual - 1))))
+                divisor[pos - trim] += w
+                result[:, pos - trim] += audio[:, local] * w
+    if np.any(divisor <= 0):
+        raise GraphError("MDX OLA uncovered sample; overlap setting is invalid")
+    predicted = result / divisor * compensate
+    return predicted, planes - predicted

@@ -146,3 +146,43 @@ def test_library_graph_builder_rejections():
         if g != b"\x0a\xff":
             with pytest.raises(M.GraphError):
                 M.Graph(g, True)
+
+
+def test_mdx_packing_zeroes_low_bins_and_pads_frequency():
+    # mdx_dsp_contracts.rs:6-41: for n_fft 5120 and 6144, pack then unpack equals the inverse
+    # STFT of the spectrum with bins < 3 and bins >= 2048 zeroed.
+    from oracle.dsp import Stft
+    n = 10240
+    planes = np.stack([np.sin(np.arange(n) * (0.015 + c * 0.09)) * 0.1 for c in range(2)])
+    for fft in (5120, 6144):
+        st = Stft(fft, 1024)
+        packed = M.pack(st, planes, 2048)
+        assert packed.shape == (4, 2048, n // 1024 + 1)
+        actual = M.unpack(st, packed, n)
+        for c in range(2):
+            z = st.forward(planes[c]).copy()
+            z[:, :3] = 0
+            z[:, 2048:] = 0
+            assert np.abs(actual[c] - st.inverse(z, n, False)).max() < 1e-7
+
+
+def test_mdx_separate_identity_graph_reconstructs_and_rejects_bad_options():
+    # An identity graph (a 1×1 Conv with the identity as weight) turns separate into STFT →
+    # iSTFT → weighted overlap-add: tones well above the three zeroed bins come back up to the
+    # chunk-edge effects of those bins, and predicted + residual is the input exactly.
+    g = M.Graph(model([Node("Conv", ["x", "w"], "out")], {"w": np.eye(4).reshape(4, 4, 1, 1)}), True)
+    n = 5000
+    x = np.stack([np.sin(np.arange(n) * 0.3), np.cos(np.arange(n) * 0.21)]) * 0.2
+    for overlap in (None, 0.0, 0.5):
+        pred, res = M.separate(g, n_fft=512, bins=256, frames=16, compensate=1.0, planes=x, hop=128,
+                               overlap=overlap)
+        assert np.abs(pred + res - x).max() < 1e-12
+        assert np.abs(pred - x).max() < 0.03
+        if overlap != 0.0:  # Hann-weighted chunks blend the edges away from the track ends
+            assert np.abs(pred - x)[:, 200:-200].max() < 1e-3
+    pred2, _ = M.separate(g, 512, 256, 16, 1.035, x, hop=128, denoise=True)
+    pred1, _ = M.separate(g, 512, 256, 16, 1.0, x, hop=128)
+    assert np.abs(pred2 - 1.035 * pred1).max() < 1e-10  # the identity graph is odd: denoise keeps it
+    for bad in (dict(overlap=0.99), dict(batch=0), dict(batch=5)):
+        with pytest.raises(M.GraphError):
+            M.separate(g, 512, 256, 16, 1.0, x, hop=128, **bad)
