@@ -337,6 +337,16 @@ int ancha_mdx_forward(ancha_mdx* graph, const float* x, const int64_t input_shap
     }
 }
 
+int ancha_mdx_separate_pcm(ancha_mdx* graph, const ancha_mdx_task* task, const float* planes, int64_t samples,
+                           const volatile int* cancel, float* predicted, float* residual, double* seconds_out) {
+    if (!graph || !task || !planes || !predicted || !residual) return fail(ANCHA_E_INVALID, "mdx_separate_pcm: null argument");
+    MdxTaskOpts o;
+    o.n_fft = task->n_fft; o.hop = task->hop; o.bins = task->bins; o.frames = task->frames;
+    o.compensate = (float)task->compensate; o.overlap = task->overlap; o.denoise = task->denoise != 0;
+    o.batch = task->batch;
+    return graph->impl->separate_pcm(o, planes, samples, cancel, predicted, residual, seconds_out);
+}
+
 void ancha_mdx_free(ancha_mdx* graph) { delete graph; }
 
 }  // extern "C"

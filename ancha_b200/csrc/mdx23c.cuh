@@ -92,6 +92,12 @@ int mdx_stft(const MdxDsp& d, const float* audio, int chunks, int samples, int h
 int mdx_istft(const MdxDsp& d, const float* spec, int chunks, int stems, int bins, int frames, int hop, int samples,
               float* scratch, float* waves, int* flag, cudaStream_t s);
 
+// Window-square normalised overlap-add of windowed time frames scratch[plane][frame][n_fft]
+// (any n_fft; `window` its periodic Hann) into out[plane][samples] (dsp.rs:82-133); bit 2 of
+// *flag marks an uncovered sample.
+int mdx_istft_overlap(const float* scratch, int64_t planes, int frames, int hop, int samples, int n_fft,
+                      const float* window, float* out, int* flag, cudaStream_t s);
+
 // Rectangular overlap-add of chunk outputs, in chunk order (mdx23c_runtime.rs:214-223):
 // sums[p][j − border] += waves[c][p][j − starts[c]] for j in
 // [max(start, border), min(start + chunk, border + samples)), p over stems·2 planes; at most

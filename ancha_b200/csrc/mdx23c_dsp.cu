@@ -252,6 +252,14 @@ int mdx_istft(const MdxDsp& d, const float* spec, int chunks, int stems, int bin
     return check_launch("mdx_istft_overlap");
 }
 
+int mdx_istft_overlap(const float* scratch, int64_t planes, int frames, int hop, int samples, int n_fft,
+                      const float* window, float* out, int* flag, cudaStream_t s) {
+    if (planes <= 0) return ANCHA_OK;
+    istft_overlap_kernel<<<(unsigned)ceil_div(planes * samples, 256), 256, 0, s>>>(scratch, planes, frames, hop, samples,
+                                                                                n_fft, window, out, flag);
+    return check_launch("mdx_istft_overlap");
+}
+
 int mdx_overlap_add(const float* waves, const int64_t* starts, int chunks, int planes, int chunk, int64_t border,
                     int64_t samples, float* sums, int* flag, cudaStream_t s) {
     if (chunks <= 0) return ANCHA_OK;

@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "mdx23c.cuh"
 #include "model.hpp"
 #include "onnx.hpp"
 
@@ -41,6 +42,48 @@ int mdx_ewise(const float* a, const float* b, float* out, const MdxEwise& e, cud
 int mdx_permute(const float* x, float* out, const MdxPermute& p, cudaStream_t s);
 int mdx_matmul(const float* a, const float* b, float* out, const MdxMatmul& m, cudaStream_t s);
 
+// ---- The classic MDX task (src/mdx_runtime.rs) -------------------------------------------------
+
+// Up to four chunks of one batch: start in the trimmed / padded mixture and valid length.
+struct MdxChunks4 {
+    int64_t start[4];
+    int64_t actual[4];
+};
+// True when the task's STFT can run n_fft points: n_fft/2 = 2^k, 3·2^k or 5·2^k, n_fft ≤ 8192.
+bool mdx_task_fft_supported(int n_fft);
+// Periodic Hann window [n_fft] (f32 form of dsp.rs:40-42) and exp(−2πij/n_fft), j ≤ n_fft/2.
+int mdx_task_tables(int n_fft, float* window, float2* twiddle, cudaStream_t s);
+// Centred STFT of audio[c][2][samples] packed as [c][4][bins][frames] with bins < zero_low
+// zeroed (mdx_runtime.rs:79-83).
+int mdx_task_stft(const float* audio, int chunks, int samples, int hop, int n_fft, int bins, int zero_low,
+                  const float* window, const float2* twiddle, float* packed, cudaStream_t s);
+// Inverse of spec[c][4][bins][frames] (spectral::unpack + Stft::inverse) into waves[c][2][samples];
+// scratch holds chunks·2·frames·n_fft floats.
+int mdx_task_istft(const float* spec, int chunks, int bins, int frames, int hop, int samples, int n_fft,
+                   const float* window, const float2* twiddle, float* scratch, float* waves, int* flag, cudaStream_t s);
+// Chunk windows of the mixture: out[c][ch][i] = planes[ch][start + i − trim] for i < actual inside
+// the track, else 0 (mdx_runtime.rs:152-169).
+int mdx_task_gather(const float* planes, int64_t samples, const MdxChunks4& ch, int chunks, int chunk, int64_t trim,
+                    float* out, cudaStream_t s);
+// Hann-weighted (or rectangular) overlap-add of waves[c][2][chunk] into result[2][samples] and
+// divisor[samples], chunks in order (mdx_runtime.rs:205-224).
+int mdx_task_ola(const float* waves, const MdxChunks4& ch, int chunks, int chunk, int64_t trim, int64_t samples,
+                 bool rectangular, float* result, float* divisor, cudaStream_t s);
+// predicted = result / divisor · compensate, residual = input − predicted (mdx_runtime.rs:227-237).
+int mdx_task_finish(const float* result, const float* divisor, const float* input, int64_t samples, float compensate,
+                    float* predicted, float* residual, int* flag, cudaStream_t s);
+int mdx_negate(const float* a, int64_t n, float* out, cudaStream_t s);
+int mdx_half_difference(const float* a, const float* b, int64_t n, float* out, cudaStream_t s);
+
+// Options of the task (the MdxConfig fields of a registered checkpoint, given explicitly here).
+struct MdxTaskOpts {
+    int n_fft = 6144, hop = 1024, bins = 3072, frames = 256;
+    float compensate = 1.f;
+    double overlap = -1.0;  // < 0: chunks every chunk − n_fft samples (the reference's default)
+    bool denoise = false;
+    int batch = 1;          // chunks per graph call, 1..4
+};
+
 using Shape4 = std::array<int64_t, 4>;
 
 class MdxModel {
@@ -52,6 +95,10 @@ public:
     // x: device [in] f32 → out: device, of output_shape(in). Checks *cancel (host, may be
     // null) before every instruction (mdx.rs:484).
     int forward(const float* x, const Shape4& in, float* out, const volatile int* cancel, cudaStream_t s);
+    // separate_mdx without file I/O (src/mdx_runtime.rs:84-248): host planes[2][samples] →
+    // host predicted[2][samples] and residual[2][samples]; *seconds (may be null) = wall time.
+    int separate_pcm(const MdxTaskOpts& o, const float* planes, int64_t samples, const volatile int* cancel,
+                     float* predicted, float* residual, double* seconds);
 
     MdxGraph graph;
     int device = 0;

@@ -1,6 +1,7 @@
 // Classic MDX graph executor, host side (mdx_exec.hpp): shape inference, constant upload and
 // the schedule of Graph::forward (crates/ancha-models/src/mdx.rs:474-568).
 #include <algorithm>
+#include <chrono>
 #include <stdexcept>
 #include <string>
 
@@ -242,6 +243,109 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
     }
     release_all();
     return st;
+}
+
+int MdxModel::separate_pcm(const MdxTaskOpts& o, const float* planes, int64_t samples, const volatile int* cancel,
+                           float* predicted, float* residual, double* seconds) {
+    const auto t0 = std::chrono::steady_clock::now();
+    // separate_mdx (src/mdx_runtime.rs:84-248): option checks, UVR trim / pad, chunk starts.
+    if (!planes || !predicted || !residual || samples <= 0) return fail(ANCHA_E_INVALID, "mdx_separate: empty input");
+    if (o.batch < 1 || o.batch > 4) return fail(ANCHA_E_INVALID, "MDX batch size must be between 1 and 4");
+    if (o.overlap >= 0.0 && !(o.overlap <= 0.95)) return fail(ANCHA_E_INVALID, "MDX overlap must be between 0 and 0.95");
+    if (o.hop <= 0 || o.frames < 2 || o.bins <= 0 || o.bins > o.n_fft / 2 + 1)
+        return fail(ANCHA_E_INVALID, "invalid MDX STFT configuration");
+    if (!mdx_task_fft_supported(o.n_fft)) return fail(ANCHA_E_UNSUPPORTED, "classic MDX STFT size not supported");
+    const int64_t chunk = (int64_t)o.hop * (o.frames - 1);
+    const int64_t trim = o.n_fft / 2, gen = chunk - o.n_fft;
+    if (gen <= 0 || chunk <= trim) return fail(ANCHA_E_INVALID, "MDX chunk shorter than its FFT");
+    const int64_t pad = gen + trim - samples % gen;
+    const int64_t mixture = trim + samples + pad;
+    const int64_t step = o.overlap < 0.0 ? gen : (int64_t)((1.0 - o.overlap) * (double)chunk);
+    if (step <= 0) return fail(ANCHA_E_INVALID, "zero MDX step");
+    std::vector<int64_t> starts;
+    for (int64_t s0 = 0; s0 < mixture; s0 += step)
+        if (s0 < trim + samples) starts.push_back(s0);  // chunks past the track are skipped (optimized)
+    ANCHA_CUDA(cudaSetDevice(device));
+    const int b = o.batch, bins = o.bins, frames = o.frames, n = o.n_fft;
+    const Shape4 in{b, 4, bins, frames};
+    Shape4 out_shape{};
+    ANCHA_TRY(output_shape(in, out_shape));
+    if (out_shape != in) return fail(ANCHA_E_INVALID, "MDX output shape mismatch");
+    try {
+        DevBuf track, audio, spec, neg, y, y2, scratch, waves, result, divisor, pred, res, win, tw, flag;
+        cudaStream_t s = nullptr;
+        ANCHA_CUDA(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+        struct StreamGuard {  // destroyed before the buffers (declared after them)
+            cudaStream_t s;
+            ~StreamGuard() {
+                cudaStreamSynchronize(s);
+                cudaStreamDestroy(s);
+            }
+        } guard{s};
+        const size_t spec_n = (size_t)b * 4 * bins * frames;
+        track.alloc((size_t)2 * samples * 4);
+        audio.alloc((size_t)b * 2 * chunk * 4);
+        spec.alloc(spec_n * 4);
+        y.alloc(spec_n * 4);
+        if (o.denoise) {
+            neg.alloc(spec_n * 4);
+            y2.alloc(spec_n * 4);
+        }
+        scratch.alloc((size_t)b * 2 * frames * n * 4);
+        waves.alloc((size_t)b * 2 * chunk * 4);
+        result.alloc((size_t)2 * samples * 4);
+        divisor.alloc((size_t)samples * 4);
+        pred.alloc((size_t)2 * samples * 4);
+        res.alloc((size_t)2 * samples * 4);
+        win.alloc((size_t)n * 4);
+        tw.alloc((size_t)(n / 2 + 1) * sizeof(float2));
+        flag.alloc(sizeof(int));
+        ANCHA_CUDA(cudaMemcpyAsync(track.p, planes, (size_t)2 * samples * 4, cudaMemcpyHostToDevice, s));
+        ANCHA_CUDA(cudaMemsetAsync(result.p, 0, result.bytes, s));
+        ANCHA_CUDA(cudaMemsetAsync(divisor.p, 0, divisor.bytes, s));
+        ANCHA_CUDA(cudaMemsetAsync(flag.p, 0, sizeof(int), s));
+        ANCHA_TRY(mdx_task_tables(n, win.as<float>(), tw.as<float2>(), s));
+        for (size_t i = 0; i < starts.size(); i += b) {
+            if (cancel && *cancel) return fail(ANCHA_E_CANCELLED, "task cancelled");
+            const int cnt = (int)std::min<size_t>(b, starts.size() - i);
+            MdxChunks4 ch{};
+            for (int c = 0; c < cnt; ++c) {
+                ch.start[c] = starts[i + c];
+                ch.actual[c] = std::min<int64_t>(chunk, mixture - starts[i + c]);
+            }
+            ANCHA_TRY(mdx_task_gather(track.as<float>(), samples, ch, cnt, (int)chunk, trim, audio.as<float>(), s));
+            if (cnt < b) ANCHA_CUDA(cudaMemsetAsync(spec.as<float>() + (size_t)cnt * 4 * bins * frames, 0,
+                                                    (size_t)(b - cnt) * 4 * bins * frames * 4, s));
+            ANCHA_TRY(mdx_task_stft(audio.as<float>(), cnt, (int)chunk, o.hop, n, bins, 3, win.as<float>(),
+                                    tw.as<float2>(), spec.as<float>(), s));
+            // The graph runs on the batch it was shaped for; unused slots hold zeros.
+            if (o.denoise) {
+                ANCHA_TRY(mdx_negate(spec.as<float>(), (int64_t)spec_n, neg.as<float>(), s));
+                ANCHA_TRY(forward(neg.as<float>(), in, y2.as<float>(), cancel, s));
+                ANCHA_TRY(forward(spec.as<float>(), in, y.as<float>(), cancel, s));
+                ANCHA_TRY(mdx_half_difference(y.as<float>(), y2.as<float>(), (int64_t)spec_n, y.as<float>(), s));
+            } else {
+                ANCHA_TRY(forward(spec.as<float>(), in, y.as<float>(), cancel, s));
+            }
+            ANCHA_TRY(mdx_task_istft(y.as<float>(), cnt, bins, frames, o.hop, (int)chunk, n, win.as<float>(),
+                                     tw.as<float2>(), scratch.as<float>(), waves.as<float>(), flag.as<int>(), s));
+            ANCHA_TRY(mdx_task_ola(waves.as<float>(), ch, cnt, (int)chunk, trim, samples, o.overlap == 0.0,
+                                   result.as<float>(), divisor.as<float>(), s));
+        }
+        ANCHA_TRY(mdx_task_finish(result.as<float>(), divisor.as<float>(), track.as<float>(), samples, o.compensate,
+                                  pred.as<float>(), res.as<float>(), flag.as<int>(), s));
+        ANCHA_CUDA(cudaMemcpyAsync(predicted, pred.p, pred.bytes, cudaMemcpyDeviceToHost, s));
+        ANCHA_CUDA(cudaMemcpyAsync(residual, res.p, res.bytes, cudaMemcpyDeviceToHost, s));
+        int status = 0;
+        ANCHA_CUDA(cudaMemcpyAsync(&status, flag.p, sizeof(int), cudaMemcpyDeviceToHost, s));
+        ANCHA_CUDA(cudaStreamSynchronize(s));
+        if (status & 1) return fail(ANCHA_E_NONFINITE, "non-finite MDX output");
+        if (status & 2) return fail(ANCHA_E_INVALID, "MDX OLA uncovered sample; overlap setting is invalid");
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_CUDA, e.what());
+    }
+    if (seconds) *seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    return ANCHA_OK;
 }
 
 }  // namespace ancha

@@ -51,6 +51,24 @@ class Graph:
                                           None if cancel is None else C.byref(cancel), stream))
         return out
 
+    def separate_pcm(self, planes, n_fft: int = 6144, hop: int = 1024, bins: int = 3072, frames: int = 256,
+                     compensate: float = 1.0, overlap: Optional[float] = None, denoise: bool = False,
+                     batch: int = 1, cancel: Optional[C.c_int] = None):
+        """``separate_mdx`` on host PCM ``[2, samples]`` → ``(predicted, residual, seconds)``."""
+        import numpy as np
+        x = np.ascontiguousarray(planes, dtype=np.float32)
+        if x.ndim != 2 or x.shape[0] != 2:
+            raise N.AnchaError(N.E_INVALID, "planes must be [2, samples]")
+        task = N.MdxTask(n_fft, hop, bins, frames, compensate, -1.0 if overlap is None else overlap, int(denoise), batch)
+        pred = np.empty_like(x)
+        res = np.empty_like(x)
+        secs = C.c_double()
+        fp = C.POINTER(C.c_float)
+        N.check(N.lib().ancha_mdx_separate_pcm(self._h, C.byref(task), x.ctypes.data_as(fp), x.shape[1],
+                                               None if cancel is None else C.byref(cancel),
+                                               pred.ctypes.data_as(fp), res.ctypes.data_as(fp), C.byref(secs)))
+        return pred, res, secs.value
+
     def close(self) -> None:
         if self._h:
             N.lib().ancha_mdx_free(self._h)

@@ -268,6 +268,24 @@ ANCHA_API int ancha_mdx_output_shape(const ancha_mdx* graph, const int64_t input
 ANCHA_API int ancha_mdx_forward(ancha_mdx* graph, const float* x, const int64_t input_shape[4], float* out,
                       const volatile int* cancel, void* stream);
 
+/* Options of the classic MDX task: the MdxConfig fields of a registered checkpoint
+ * (mdx.rs:21-97), given explicitly, and the task options of MdxOptions (mdx_runtime.rs:22-34). */
+typedef struct {
+    int n_fft, hop, bins, frames;  /* n_fft/2 = 2^k, 3·2^k or 5·2^k, at most 8192 */
+    double compensate;
+    double overlap;                /* < 0: chunks every chunk − n_fft samples; else 0..0.95 */
+    int denoise;                   /* (f(x) − f(−x)) / 2 */
+    int batch;                     /* chunks per graph call, 1..4 */
+} ancha_mdx_task;
+
+/* separate_mdx without file I/O (src/mdx_runtime.rs:84-248) on the graph's GPU: host
+ * planes[2][samples] → host predicted[2][samples] and residual[2][samples] (= input −
+ * predicted). UVR trim / pad chunking, centred STFT packed [4][bins][frames] with the three
+ * lowest bins zeroed, the graph, the inverse STFT and the Hann-weighted overlap-add divided by
+ * the summed weights, times `compensate`, all on the device. *seconds_out may be NULL. */
+ANCHA_API int ancha_mdx_separate_pcm(ancha_mdx* graph, const ancha_mdx_task* task, const float* planes, int64_t samples,
+                           const volatile int* cancel, float* predicted, float* residual, double* seconds_out);
+
 ANCHA_API void ancha_mdx_free(ancha_mdx* graph);
 
 /* ------------------------------------------------------------------------------------ *

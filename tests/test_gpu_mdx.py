@@ -119,3 +119,44 @@ def test_shape_errors_and_cancellation(torch_cuda):
         g.forward(torch_cuda.zeros((1, 4, 64, 32), device="cuda"), cancel=C.c_int(1))
     assert e.value.status == N.E_CANCELLED
     assert g.output_shape((2, 4, 64, 32)) == (2, 4, 128, 64)
+
+
+def shape_preserving_graph(seed=1):
+    rng = np.random.default_rng(seed)
+    w = {"c1w": rng.standard_normal((8, 4, 3, 3)) / 6.0, "c1b": 0.1 * rng.standard_normal(8),
+         "g": 1.0 + 0.1 * rng.standard_normal(8), "b": 0.1 * rng.standard_normal(8),
+         "m": 0.1 * rng.standard_normal(8), "v": 0.5 + rng.random(8),
+         "c2w": rng.standard_normal((4, 8, 1, 1)) / 3.0}
+    n = [Node("Conv", ["x", "c1w", "c1b"], "c1", attrs=[Attr("pads", ints=[1, 1, 1, 1])]),
+         Node("BatchNormalization", ["c1", "g", "b", "m", "v"], "bn"), Node("Relu", ["bn"], "r"),
+         Node("Conv", ["r", "c2w"], "out")]
+    return model(n, w)
+
+
+@pytest.mark.parametrize("n_fft,hop,bins,opts", [
+    (512, 128, 256, dict(batch=1)),                      # n_fft / 2 = 2^8
+    (384, 96, 160, dict(batch=3, overlap=0.5)),         # 3 · 2^6: radix-3 combination
+    (320, 80, 128, dict(batch=2, overlap=0.0, denoise=True)),  # 5 · 2^5: radix-5, rectangular, denoise
+])
+def test_separate_task_matches_oracle(torch_cuda, n_fft, hop, bins, opts):
+    from ancha_b200.mdx import Graph
+    onnx = shape_preserving_graph()
+    x = (np.random.default_rng(7).standard_normal((2, 4000)) * 0.1).astype(np.float32)
+    ref_p, ref_r = M.separate(M.Graph(onnx, True), n_fft, bins, 16, 1.035, x.astype(np.float64), hop=hop, **opts)
+    p, r, secs = Graph(onnx).separate_pcm(x, n_fft=n_fft, hop=hop, bins=bins, frames=16, compensate=1.035, **opts)
+    err = np.abs(p - ref_p).max() / np.abs(ref_p).max()
+    print(f"classic MDX task n_fft {n_fft} {opts}: max |d| / max |ref| {err:.2e}, {secs * 1e3:.1f} ms")
+    assert err < 2e-5
+    assert np.abs(p + r - x).max() < 1e-6
+
+
+def test_separate_task_rejects_bad_options(torch_cuda):
+    from ancha_b200.mdx import Graph
+    g = Graph(shape_preserving_graph())
+    x = np.zeros((2, 4000), np.float32)
+    for bad in (dict(overlap=0.99), dict(batch=5), dict(n_fft=448)):  # 448 / 2 = 7 · 2^5
+        with pytest.raises(N.AnchaError):
+            g.separate_pcm(x, **dict(dict(n_fft=512, hop=128, bins=256, frames=16), **bad))
+    with pytest.raises(N.AnchaError) as e:
+        g.separate_pcm(x, n_fft=512, hop=128, bins=256, frames=16, cancel=C.c_int(1))
+    assert e.value.status == N.E_CANCELLED
