@@ -53,11 +53,15 @@ class Attr:
     ints: Optional[Sequence[int]] = None
     i: Optional[int] = None
     f: Optional[float] = None
+    packed: bool = True  # onnx.proto (proto2) writers emit INTS unpacked; both forms are valid
 
     def encode(self) -> bytes:
         out = _str(1, self.name)
         if self.ints is not None:
-            out += _int(20, ATTR_INTS) + _len(8, b"".join(_varint(v) for v in self.ints))  # packed
+            if self.packed:
+                out += _int(20, ATTR_INTS) + _len(8, b"".join(_varint(v) for v in self.ints))
+            else:
+                out += _int(20, ATTR_INTS) + b"".join(_int(8, v) for v in self.ints)
         elif self.i is not None:
             out += _int(20, ATTR_INT) + _int(3, self.i)
         elif self.f is not None:
@@ -85,11 +89,11 @@ class Node:
         return out
 
 
-def tensor(name: str, array) -> bytes:
-    """TensorProto of a FLOAT array (dims, data_type, name, raw_data)."""
+def tensor(name: str, array, float_data: bool = False) -> bytes:
+    """TensorProto of a FLOAT array: dims, data_type, name and raw_data (or packed float_data)."""
     a = np.ascontiguousarray(array, dtype="<f4")
     out = b"".join(_int(1, d) for d in a.shape) + _int(2, FLOAT) + _str(8, name)
-    return out + _len(9, a.tobytes())
+    return out + (_len(4, a.tobytes()) if float_data else _len(9, a.tobytes()))
 
 
 def value_info(name: str, shape: Optional[Sequence[int]] = None) -> bytes:
@@ -102,10 +106,11 @@ def value_info(name: str, shape: Optional[Sequence[int]] = None) -> bytes:
 
 
 def model(nodes: Sequence[Node], initializers: dict, inputs=("x",), outputs=("out",),
-          input_shape=None, output_shape=None, opset: int = 13, ir_version: int = 7) -> bytes:
+          input_shape=None, output_shape=None, opset: int = 13, ir_version: int = 7,
+          float_data: bool = False) -> bytes:
     """ModelProto bytes: one graph over `nodes` with FLOAT `initializers` (name → array)."""
     g = b"".join(_len(1, n.encode()) for n in nodes) + _str(2, "graph")
-    g += b"".join(_len(5, tensor(k, v)) for k, v in initializers.items())
+    g += b"".join(_len(5, tensor(k, v, float_data)) for k, v in initializers.items())
     g += b"".join(_len(11, value_info(n, input_shape)) for n in inputs)
     g += b"".join(_len(12, value_info(n, output_shape)) for n in outputs)
     opset_id = _str(1, "") + _int(2, opset)

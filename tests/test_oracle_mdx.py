@@ -186,3 +186,23 @@ def test_mdx_separate_identity_graph_reconstructs_and_rejects_bad_options():
     for bad in (dict(overlap=0.99), dict(batch=0), dict(batch=5)):
         with pytest.raises(M.GraphError):
             M.separate(g, 512, 256, 16, 1.0, x, hop=128, **bad)
+
+
+def test_reader_accepts_both_protobuf_encodings():
+    """onnx.proto is proto2: INTS attributes arrive unpacked from most writers, packed from some,
+    and initializers as raw_data or packed float_data. Every combination builds the same graph
+    and, in the oracle, computes the same values."""
+    x = np.random.default_rng(1).standard_normal((1, 2, 5, 4))
+    w = {"w": np.random.default_rng(2).standard_normal((3, 2, 3, 3)), "b": np.array([0.1, -0.2, 0.3])}
+    outs = []
+    for packed in (True, False):
+        for float_data in (False, True):
+            g = model([Node("Conv", ["x", "w", "b"], "c", attrs=[Attr("pads", ints=[1, 1, 1, 1], packed=packed),
+                                                               Attr("strides", ints=[1, 2], packed=packed)]),
+                       Node("Transpose", ["c"], "out", attrs=[Attr("perm", ints=[0, 1, 3, 2], packed=packed)])],
+                      w, float_data=float_data)
+            assert _lib_inspect(g) == {"nodes": 2, "instructions": 2, "folded_bn": 0, "constants": 2}
+            outs.append(M.Graph(g).forward(x))
+    for o in outs[1:]:
+        assert np.array_equal(o, outs[0])
+    assert outs[0].shape == (1, 3, 2, 5)
