@@ -14,9 +14,6 @@
 
 namespace ancha {
 
-struct MdxConvShape {
-    int n, ci, h, w, co, oh, ow, kh, kw, sh, sw, ph, pw, dh, dw, groups;
-};
 // Elementwise op (0 Relu, 1 Add, 2 Mul, 3 per-channel x·scale + shift) over a 4-D output;
 // sa / sb are the inputs' element strides, 0 on broadcast dims (for op 3, sb indexes scale /
 // shift by channel).
@@ -83,8 +80,6 @@ struct MdxTaskOpts {
     bool denoise = false;
     int batch = 1;          // chunks per graph call, 1..4
 };
-
-using Shape4 = std::array<int64_t, 4>;
 
 class MdxModel {
 public:

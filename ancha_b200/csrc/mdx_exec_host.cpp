@@ -1,5 +1,5 @@
-// Classic MDX graph executor, host side (mdx_exec.hpp): shape inference, constant upload and
-// the schedule of Graph::forward (crates/ancha-models/src/mdx.rs:474-568).
+// Classic MDX graph executor, host side (mdx_exec.hpp): constant upload and the schedule of
+// Graph::forward (crates/ancha-models/src/mdx.rs:474-568) over the shapes of MdxGraph::infer.
 #include <algorithm>
 #include <chrono>
 #include <stdexcept>
@@ -13,42 +13,6 @@ namespace {
 Shape4 strides_of(const Shape4& s) { return {s[1] * s[2] * s[3], s[2] * s[3], s[3], 1}; }
 
 int64_t numel(const Shape4& s) { return s[0] * s[1] * s[2] * s[3]; }
-
-std::string shape_text(const Shape4& s) {
-    return "[" + std::to_string(s[0]) + ", " + std::to_string(s[1]) + ", " + std::to_string(s[2]) + ", " +
-           std::to_string(s[3]) + "]";
-}
-
-// Conv / ConvTranspose geometry of instruction `ins` on input x and weight w; false when the
-// shapes disagree (Burn's conv2d / conv_transpose2d rules).
-bool conv_shape(const MdxInstruction& ins, const Shape4& x, const Shape4& w, MdxConvShape& c, std::string& err) {
-    const bool t = ins.op == MdxOp::ConvTranspose;
-    c.n = (int)x[0]; c.ci = (int)x[1]; c.h = (int)x[2]; c.w = (int)x[3];
-    c.kh = (int)w[2]; c.kw = (int)w[3];
-    c.sh = ins.stride[0]; c.sw = ins.stride[1]; c.ph = ins.padding[0]; c.pw = ins.padding[1];
-    c.dh = ins.dilation[0]; c.dw = ins.dilation[1]; c.groups = ins.groups;
-    if (t) {
-        if (w[0] != x[1] || x[1] % ins.groups) { err = "conv_transpose channel mismatch"; return false; }
-        c.co = (int)(w[1] * ins.groups);
-        c.oh = (c.h - 1) * c.sh - 2 * c.ph + c.dh * (c.kh - 1) + ins.padding_out[0] + 1;
-        c.ow = (c.w - 1) * c.sw - 2 * c.pw + c.dw * (c.kw - 1) + ins.padding_out[1] + 1;
-    } else {
-        if (w[1] * ins.groups != x[1] || w[0] % ins.groups) { err = "conv2d channel mismatch"; return false; }
-        c.co = (int)w[0];
-        c.oh = (c.h + 2 * c.ph - c.dh * (c.kh - 1) - 1) / c.sh + 1;
-        c.ow = (c.w + 2 * c.pw - c.dw * (c.kw - 1) - 1) / c.sw + 1;
-    }
-    if (c.oh <= 0 || c.ow <= 0) { err = "convolution output is empty"; return false; }
-    return true;
-}
-
-bool broadcast(const Shape4& a, const Shape4& b, Shape4& out) {
-    for (int d = 0; d < 4; ++d) {
-        if (a[d] != b[d] && a[d] != 1 && b[d] != 1) return false;
-        out[d] = std::max(a[d], b[d]);
-    }
-    return true;
-}
 
 template <typename T>
 void upload(DevBuf& d, const std::vector<T>& v) {
@@ -78,55 +42,8 @@ std::unique_ptr<MdxModel> MdxModel::load(const uint8_t* onnx, size_t bytes, bool
 }
 
 int MdxModel::infer(const Shape4& in, std::vector<Shape4>& shapes) const {
-    if (std::any_of(in.begin(), in.end(), [](int64_t v) { return v <= 0; }))
-        return fail(ANCHA_E_INVALID, "MDX graph input shape must be positive");
-    shapes.assign(graph.values, Shape4{0, 0, 0, 0});
-    for (size_t i = 0; i < graph.constants.size(); ++i)
-        for (int d = 0; d < 4; ++d) shapes[i][d] = graph.constants[i].shape[d];
-    shapes[graph.input] = in;
-    for (const MdxInstruction& ins : graph.instructions) {
-        const Shape4& a = shapes[ins.inputs[0]];
-        Shape4 out = a;
-        std::string err;
-        switch (ins.op) {
-            case MdxOp::Conv:
-            case MdxOp::ConvTranspose: {
-                MdxConvShape c;
-                if (!conv_shape(ins, a, shapes[ins.inputs[1]], c, err)) return fail(ANCHA_E_INVALID, err);
-                if (ins.inputs.size() == 3 && numel(shapes[ins.inputs[2]]) != c.co)
-                    return fail(ANCHA_E_INVALID, "convolution bias length mismatch");
-                out = {c.n, c.co, c.oh, c.ow};
-                break;
-            }
-            case MdxOp::Relu: break;
-            case MdxOp::Transpose:
-                for (int d = 0; d < 4; ++d) out[d] = a[ins.perm[d]];
-                break;
-            case MdxOp::MatMul: {
-                const Shape4& b = shapes[ins.inputs[1]];
-                if (a[3] != b[2]) return fail(ANCHA_E_INVALID, "MatMul inner dimensions " + shape_text(a) + " · " + shape_text(b));
-                for (int d = 0; d < 2; ++d) {
-                    if (a[d] != b[d] && a[d] != 1 && b[d] != 1)
-                        return fail(ANCHA_E_INVALID, "MatMul batch dimensions do not broadcast");
-                    out[d] = std::max(a[d], b[d]);
-                }
-                out[2] = a[2];
-                out[3] = b[3];
-                break;
-            }
-            case MdxOp::Add:
-            case MdxOp::Mul:
-                if (!broadcast(a, shapes[ins.inputs[1]], out))
-                    return fail(ANCHA_E_INVALID, "shapes " + shape_text(a) + " and " +
-                                                     shape_text(shapes[ins.inputs[1]]) + " do not broadcast");
-                break;
-            case MdxOp::Bn:
-                if (a[1] != (int64_t)ins.scale.size()) return fail(ANCHA_E_INVALID, "BatchNormalization channel mismatch");
-                break;
-        }
-        if (numel(out) <= 0 || numel(out) > (int64_t)1 << 34) return fail(ANCHA_E_INVALID, "MDX value size out of range");
-        shapes[ins.output] = out;
-    }
+    std::string err;
+    if (!graph.infer(in, shapes, err)) return fail(ANCHA_E_INVALID, err);
     return ANCHA_OK;
 }
 
@@ -172,7 +89,7 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
             case MdxOp::ConvTranspose: {
                 MdxConvShape c;
                 std::string err;
-                conv_shape(ins, a, shapes[ins.inputs[1]], c, err);
+                mdx_conv_shape(ins, a, shapes[ins.inputs[1]], c, err);  // checked by infer
                 st = mdx_conv2d(va, values[ins.inputs[1]], ins.inputs.size() == 3 ? values[ins.inputs[2]] : nullptr, y,
                                 c, ins.op == MdxOp::ConvTranspose, s);
                 break;

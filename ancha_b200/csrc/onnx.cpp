@@ -164,7 +164,7 @@ OnnxTensor parse_tensor(const uint8_t* d, size_t n) {
     if (raw) {
         if (raw_size % 4) bad("invalid raw tensor data");
         t.data.resize(raw_size / 4);
-        std::memcpy(t.data.data(), raw, raw_size);  // little-endian host, as ONNX stores it
+        if (raw_size) std::memcpy(t.data.data(), raw, raw_size);  // little-endian host, as ONNX stores it
     } else {
         t.data = std::move(floats);
     }
@@ -203,7 +203,127 @@ void pair(const std::vector<int64_t>& v, bool positive, int out[2]) {
     }
 }
 
+std::string shape_text(const Shape4& s) {
+    return "[" + std::to_string(s[0]) + ", " + std::to_string(s[1]) + ", " + std::to_string(s[2]) + ", " +
+           std::to_string(s[3]) + "]";
+}
+
 }  // namespace
+
+int64_t mdx_checked_elements(const int64_t* dims, size_t n) {
+    int64_t count = 1;
+    for (size_t i = 0; i < n; ++i) {
+        if (dims[i] < 1 || dims[i] > kMdxMaxDim || count > kMdxMaxElements / dims[i]) return -1;
+        count *= dims[i];
+    }
+    return count;
+}
+
+bool mdx_conv_shape(const MdxInstruction& ins, const Shape4& x, const Shape4& w, MdxConvShape& c, std::string& err) {
+    // Inputs are values within kMdxMaxDim and attributes within 2^20, so no product below
+    // exceeds 2^51.
+    const int64_t g = ins.groups, kh = w[2], kw = w[3];
+    int64_t co, oh, ow;
+    if (ins.op == MdxOp::ConvTranspose) {
+        if (w[0] != x[1] || x[1] % g) { err = "conv_transpose channel mismatch"; return false; }
+        co = w[1] * g;
+        oh = (x[2] - 1) * ins.stride[0] - 2 * (int64_t)ins.padding[0] + ins.dilation[0] * (kh - 1) + ins.padding_out[0] + 1;
+        ow = (x[3] - 1) * ins.stride[1] - 2 * (int64_t)ins.padding[1] + ins.dilation[1] * (kw - 1) + ins.padding_out[1] + 1;
+    } else {
+        if (w[1] * g != x[1] || w[0] % g) { err = "conv2d channel mismatch"; return false; }
+        co = w[0];
+        // Positions the kernel's first tap can take; negative when the dilated kernel is wider
+        // than the padded input (an empty output, not one truncated towards zero).
+        const int64_t span_h = x[2] + 2 * (int64_t)ins.padding[0] - ins.dilation[0] * (kh - 1) - 1;
+        const int64_t span_w = x[3] + 2 * (int64_t)ins.padding[1] - ins.dilation[1] * (kw - 1) - 1;
+        oh = span_h < 0 ? 0 : span_h / ins.stride[0] + 1;
+        ow = span_w < 0 ? 0 : span_w / ins.stride[1] + 1;
+    }
+    if (oh <= 0 || ow <= 0) { err = "convolution output is empty"; return false; }
+    if (co > kMdxMaxDim || oh > kMdxMaxDim || ow > kMdxMaxDim) { err = "convolution output too large"; return false; }
+    c.n = (int)x[0]; c.ci = (int)x[1]; c.h = (int)x[2]; c.w = (int)x[3];
+    c.co = (int)co; c.oh = (int)oh; c.ow = (int)ow; c.kh = (int)kh; c.kw = (int)kw;
+    c.sh = ins.stride[0]; c.sw = ins.stride[1]; c.ph = ins.padding[0]; c.pw = ins.padding[1];
+    c.dh = ins.dilation[0]; c.dw = ins.dilation[1]; c.groups = ins.groups;
+    return true;
+}
+
+bool MdxGraph::infer(const Shape4& in, std::vector<Shape4>& shapes, std::string& err) const {
+    if (std::any_of(in.begin(), in.end(), [](int64_t v) { return v <= 0; })) {
+        err = "MDX graph input shape must be positive";
+        return false;
+    }
+    if (mdx_checked_elements(in.data(), 4) < 0) {
+        err = "MDX graph input shape " + shape_text(in) + " too large";
+        return false;
+    }
+    shapes.assign(values, Shape4{0, 0, 0, 0});
+    for (size_t i = 0; i < constants.size(); ++i)
+        for (int d = 0; d < 4; ++d) shapes[i][d] = constants[i].shape[d];
+    shapes[input] = in;
+    for (const MdxInstruction& ins : instructions) {
+        const Shape4& a = shapes[ins.inputs[0]];
+        Shape4 out = a;
+        switch (ins.op) {
+            case MdxOp::Conv:
+            case MdxOp::ConvTranspose: {
+                MdxConvShape c;
+                if (!mdx_conv_shape(ins, a, shapes[ins.inputs[1]], c, err)) return false;
+                if (ins.inputs.size() == 3 && mdx_checked_elements(shapes[ins.inputs[2]].data(), 4) != c.co) {
+                    err = "convolution bias length mismatch";
+                    return false;
+                }
+                out = {c.n, c.co, c.oh, c.ow};
+                break;
+            }
+            case MdxOp::Relu: break;
+            case MdxOp::Transpose:
+                for (int d = 0; d < 4; ++d) out[d] = a[ins.perm[d]];
+                break;
+            case MdxOp::MatMul: {
+                const Shape4& b = shapes[ins.inputs[1]];
+                if (a[3] != b[2]) {
+                    err = "MatMul inner dimensions " + shape_text(a) + " · " + shape_text(b);
+                    return false;
+                }
+                for (int d = 0; d < 2; ++d) {
+                    if (a[d] != b[d] && a[d] != 1 && b[d] != 1) {
+                        err = "MatMul batch dimensions do not broadcast";
+                        return false;
+                    }
+                    out[d] = std::max(a[d], b[d]);
+                }
+                out[2] = a[2];
+                out[3] = b[3];
+                break;
+            }
+            case MdxOp::Add:
+            case MdxOp::Mul: {
+                const Shape4& b = shapes[ins.inputs[1]];
+                for (int d = 0; d < 4; ++d) {
+                    if (a[d] != b[d] && a[d] != 1 && b[d] != 1) {
+                        err = "shapes " + shape_text(a) + " and " + shape_text(b) + " do not broadcast";
+                        return false;
+                    }
+                    out[d] = std::max(a[d], b[d]);
+                }
+                break;
+            }
+            case MdxOp::Bn:
+                if (a[1] != (int64_t)ins.scale.size()) {
+                    err = "BatchNormalization channel mismatch";
+                    return false;
+                }
+                break;
+        }
+        if (mdx_checked_elements(out.data(), 4) < 0) {
+            err = "MDX value size out of range";
+            return false;
+        }
+        shapes[ins.output] = out;
+    }
+    return true;
+}
 
 const OnnxAttr* OnnxNode::attr(const std::string& key) const {
     for (const auto& a : attrs)
@@ -261,8 +381,8 @@ MdxGraph MdxGraph::build(const OnnxModel& m, bool optimized) {
         MdxConstant c;
         c.name = t.name;
         for (size_t i = 0; i < t.dims.size(); ++i) c.shape[4 - t.dims.size() + i] = t.dims[i];
-        const int64_t count = c.shape[0] * c.shape[1] * c.shape[2] * c.shape[3];
-        if ((int64_t)t.data.size() != count ||
+        const int64_t count = mdx_checked_elements(c.shape, 4);  // −1 when out of bounds
+        if (count < 0 || (int64_t)t.data.size() != count ||
             std::any_of(t.data.begin(), t.data.end(), [](float v) { return !std::isfinite(v); }))
             bad("invalid initializer " + t.name);
         c.data = t.data;

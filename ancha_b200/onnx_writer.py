@@ -107,10 +107,12 @@ def value_info(name: str, shape: Optional[Sequence[int]] = None) -> bytes:
 
 def model(nodes: Sequence[Node], initializers: dict, inputs=("x",), outputs=("out",),
           input_shape=None, output_shape=None, opset: int = 13, ir_version: int = 7,
-          float_data: bool = False) -> bytes:
-    """ModelProto bytes: one graph over `nodes` with FLOAT `initializers` (name → array)."""
+          float_data: bool = False, raw_tensors: Sequence[bytes] = ()) -> bytes:
+    """ModelProto bytes: one graph over `nodes` with FLOAT `initializers` (name → array) and
+    `raw_tensors`, TensorProto payloads encoded by the caller (for malformed-input tests)."""
     g = b"".join(_len(1, n.encode()) for n in nodes) + _str(2, "graph")
     g += b"".join(_len(5, tensor(k, v, float_data)) for k, v in initializers.items())
+    g += b"".join(_len(5, t) for t in raw_tensors)
     g += b"".join(_len(11, value_info(n, input_shape)) for n in inputs)
     g += b"".join(_len(12, value_info(n, output_shape)) for n in outputs)
     opset_id = _str(1, "") + _int(2, opset)

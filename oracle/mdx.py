@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import struct
 
+import math
 import numpy as np
 
 OPS = {"Conv", "ConvTranspose", "Relu", "Transpose", "MatMul", "Add", "Mul", "BatchNormalization"}
@@ -210,7 +211,7 @@ class Graph:
                 raise GraphError(f"unsupported initializer {t['name']}")
             data = np.frombuffer(t["raw"], "<f4") if t["raw"] is not None else np.array(t["floats"], "<f4")
             shape = [1] * (4 - len(dims)) + list(dims)
-            if data.size != int(np.prod(shape)) or not np.all(np.isfinite(data)):
+            if data.size != math.prod(shape) or not np.all(np.isfinite(data)):  # exact, no int64 wrap
                 raise GraphError(f"invalid initializer {t['name']}")
             if t["name"] in raw:
                 raise GraphError("duplicate initializer")

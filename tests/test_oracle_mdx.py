@@ -124,6 +124,13 @@ def test_library_graph_builder_matches_oracle(optimized):
     assert _lib_inspect(fold_graph(), optimized)["folded_bn"] == (1 if optimized else 0)
 
 
+def _tensor_bytes(name, dims, floats=0):
+    """A FLOAT TensorProto with arbitrary dims and `floats` zero values of raw data."""
+    from ancha_b200 import onnx_writer as W
+    out = b"".join(W._int(1, d) for d in dims) + W._int(2, W.FLOAT) + W._str(8, name)
+    return out + W._len(9, bytes(4 * min(floats, 16)))
+
+
 def test_library_graph_builder_rejections():
     from ancha_b200 import _native as N
     cases = [
@@ -138,6 +145,11 @@ def test_library_graph_builder_rejections():
          "unsupported attribute"),
         (model([Node("Transpose", ["x"], "out", attrs=[Attr("perm", ints=[0, 1, 1, 2])])], {}), "permutation"),
         (b"\x0a\xff", "truncated"),
+        # dims whose product wraps a 64-bit count to 0 = the length of its empty data
+        (model([Node("Relu", ["x"], "out")], {}, raw_tensors=[_tensor_bytes("wrap", [1 << 32, 1 << 32])]),
+         "invalid initializer"),
+        (model([Node("Relu", ["x"], "out")], {}, raw_tensors=[_tensor_bytes("big", [1 << 31], 1 << 31)]),
+         "invalid initializer"),  # one dim past 2^30, with no data behind it
     ]
     for g, msg in cases:
         with pytest.raises(N.AnchaError) as e:
