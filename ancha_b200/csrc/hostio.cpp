@@ -24,7 +24,9 @@ const Json& Json::at(const std::string& key) const {
     return *j;
 }
 int64_t Json::as_int() const {
-    if (kind != Number || std::floor(num) != num) throw std::runtime_error("expected an integer");
+    // Integers beyond 2^53 are not exact in a double (and beyond 2^63 have no int64 value).
+    if (kind != Number || std::floor(num) != num || std::fabs(num) > 9007199254740992.0)
+        throw std::runtime_error("expected an integer");
     return (int64_t)num;
 }
 double Json::as_double() const {
@@ -47,8 +49,10 @@ void Json::set(const std::string& key, Json v) {
 
 namespace {
 struct Parser {
+    static constexpr int kMaxDepth = 256;  // nesting of arrays / objects; bounds the recursion
     const std::string& s;
     size_t i = 0;
+    int depth = 0;
     void ws() { while (i < s.size() && (s[i] == ' ' || s[i] == '\n' || s[i] == '\r' || s[i] == '\t')) ++i; }
     [[noreturn]] void err(const char* what) {
         throw std::runtime_error(std::string("JSON: ") + what + " at offset " + std::to_string(i));
@@ -76,7 +80,14 @@ struct Parser {
                 case 't': out.push_back('\t'); break;
                 case 'u': {
                     if (i + 4 > s.size()) err("bad unicode escape");
-                    unsigned cp = std::stoul(s.substr(i, 4), nullptr, 16);
+                    unsigned cp = 0;
+                    for (int k = 0; k < 4; ++k) {
+                        const char h = s[i + k];
+                        const int v = h >= '0' && h <= '9' ? h - '0' : h >= 'a' && h <= 'f' ? h - 'a' + 10
+                                    : h >= 'A' && h <= 'F' ? h - 'A' + 10 : -1;
+                        if (v < 0) err("bad unicode escape");
+                        cp = cp << 4 | (unsigned)v;
+                    }
                     i += 4;
                     if (cp < 0x80) out.push_back((char)cp);
                     else if (cp < 0x800) { out.push_back((char)(0xC0 | (cp >> 6))); out.push_back((char)(0x80 | (cp & 0x3F))); }
@@ -91,6 +102,8 @@ struct Parser {
     Json value() {
         char c = peek();
         Json j;
+        if ((c == '{' || c == '[') && depth >= kMaxDepth) err("nesting too deep");
+        struct Level { int& d; explicit Level(int& d_) : d(d_) { ++d; } ~Level() { --d; } } level(depth);
         if (c == '{') {
             ++i; j.kind = Json::Object;
             if (peek() == '}') { ++i; return j; }
@@ -300,13 +313,18 @@ SafeTensors::SafeTensors(const std::string& bytes) : bytes_(bytes) {
         if (kv.first == "__metadata__") continue;
         Entry e;
         e.dtype = kv.second.at("dtype").as_string();
-        for (auto& d : kv.second.at("shape").arr) e.shape.push_back(d.as_int());
+        for (auto& d : kv.second.at("shape").arr) {
+            e.shape.push_back(d.as_int());
+            if (e.shape.back() < 0) throw std::runtime_error("safetensors: negative dimension: " + kv.first);
+        }
         auto& off = kv.second.at("data_offsets").arr;
         if (off.size() != 2) throw std::runtime_error("safetensors: bad offsets");
-        e.begin = (size_t)off[0].as_int();
-        e.end = (size_t)off[1].as_int();
-        if (e.end < e.begin || data_offset_ + e.end > bytes.size())
+        const int64_t begin = off[0].as_int(), end = off[1].as_int();
+        // Offsets are relative to the data section; compare without forming a sum that could wrap.
+        if (begin < 0 || end < begin || (uint64_t)end > bytes.size() - data_offset_)
             throw std::runtime_error("safetensors: tensor out of range: " + kv.first);
+        e.begin = (size_t)begin;
+        e.end = (size_t)end;
         index_[kv.first] = e;
     }
 }
@@ -322,8 +340,11 @@ std::vector<float> SafeTensors::take(const std::string& name, const std::vector<
         throw std::runtime_error(name + ": expected [" + want + "], got [" + got + "]");
     }
     if (e.dtype != "F32") throw std::runtime_error(name + ": schema 1 requires F32 weights, got " + e.dtype);
-    size_t count = 1;
-    for (auto d : shape) count *= (size_t)d;
+    size_t count = 1;  // bounded by the tensor's byte range, so count · 4 cannot wrap
+    for (auto d : shape) {
+        if (d < 0 || (d && count > (e.end - e.begin) / 4 / (size_t)d)) throw std::runtime_error(name + ": byte size mismatch");
+        count *= (size_t)d;
+    }
     if (e.end - e.begin != count * 4) throw std::runtime_error(name + ": byte size mismatch");
     std::vector<float> out(count);
     std::memcpy(out.data(), bytes_.data() + data_offset_ + e.begin, count * 4);
