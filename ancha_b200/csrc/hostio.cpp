@@ -1,6 +1,7 @@
 // Host-side file formats (see hostio.hpp).
 #include "hostio.hpp"
 
+#include <climits>
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -28,6 +29,11 @@ int64_t Json::as_int() const {
     if (kind != Number || std::floor(num) != num || std::fabs(num) > 9007199254740992.0)
         throw std::runtime_error("expected an integer");
     return (int64_t)num;
+}
+int Json::as_int32() const {
+    const int64_t v = as_int();
+    if (v < INT32_MIN || v > INT32_MAX) throw std::runtime_error("integer out of range");
+    return (int)v;
 }
 double Json::as_double() const {
     if (kind != Number) throw std::runtime_error("expected a number");

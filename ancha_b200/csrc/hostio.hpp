@@ -25,6 +25,7 @@ struct Json {
     const Json* find(const std::string& key) const;
     const Json& at(const std::string& key) const;  // throws if missing
     int64_t as_int() const;
+    int as_int32() const;  // throws outside the int range
     double as_double() const;
     bool as_bool() const;
     const std::string& as_string() const;

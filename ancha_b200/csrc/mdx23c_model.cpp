@@ -117,12 +117,12 @@ Mdx23cConfig Mdx23cConfig::from_json(const Json& j) {
                "MDX23C config");
     ensure(j.at("family").as_string() == "mdx23c", "not an MDX23C package");
     Mdx23cConfig c;
-    auto i = [&](const char* k) { return (int)j.at(k).as_int(); };
+    auto i = [&](const char* k) { return j.at(k).as_int32(); };
     c.sample_rate = i("sample_rate"); c.n_fft = i("n_fft"); c.hop = i("hop"); c.bins = i("bins");
     c.frames = i("frames"); c.overlap = i("overlap"); c.subbands = i("subbands"); c.channels = i("channels");
     c.growth = i("growth"); c.scales = i("scales"); c.blocks_per_scale = i("blocks_per_scale");
     c.bottleneck_factor = i("bottleneck_factor");
-    for (const Json& v : j.at("scale").arr) c.scale.push_back((int)v.as_int());
+    for (const Json& v : j.at("scale").arr) c.scale.push_back(v.as_int32());
     for (const Json& v : j.at("stems").arr) c.stems.push_back(v.as_string());
     return c;
 }
@@ -132,7 +132,7 @@ Mdx23cManifest Mdx23cManifest::from_json(const Json& j) {
                    "forward_revision", "weight_license", "config"},
                "manifest");
     Mdx23cManifest m;
-    m.schema_version = (int)j.at("schema_version").as_int();
+    m.schema_version = j.at("schema_version").as_int32();
     m.model_id = j.at("model_id").as_string();
     m.weights_sha256 = j.at("weights_sha256").as_string();
     m.checkpoint_sha256 = j.at("checkpoint_sha256").as_string();

@@ -97,23 +97,23 @@ ModelConfig ModelConfig::from_json(const Json& j) {
     check_keys(j, kConfigKeys, "config");
     ModelConfig c;
     c.family = j.at("family").as_string();
-    c.dim = (int)j.at("dim").as_int();
-    c.depth = (int)j.at("depth").as_int();
-    c.heads = (int)j.at("heads").as_int();
-    c.head_dim = (int)j.at("head_dim").as_int();
-    c.ff_mult = (int)j.at("ff_mult").as_int();
-    c.mask_depth = (int)j.at("mask_depth").as_int();
-    c.mask_expansion = (int)j.at("mask_expansion").as_int();
-    c.sample_rate = (int)j.at("sample_rate").as_int();
-    c.n_fft = (int)j.at("n_fft").as_int();
-    c.hop = (int)j.at("hop").as_int();
+    c.dim = j.at("dim").as_int32();
+    c.depth = j.at("depth").as_int32();
+    c.heads = j.at("heads").as_int32();
+    c.head_dim = j.at("head_dim").as_int32();
+    c.ff_mult = j.at("ff_mult").as_int32();
+    c.mask_depth = j.at("mask_depth").as_int32();
+    c.mask_expansion = j.at("mask_expansion").as_int32();
+    c.sample_rate = j.at("sample_rate").as_int32();
+    c.n_fft = j.at("n_fft").as_int32();
+    c.hop = j.at("hop").as_int32();
     c.chunk_samples = j.at("chunk_samples").as_int();
-    c.overlap = (int)j.at("overlap").as_int();
+    c.overlap = j.at("overlap").as_int32();
     c.zero_dc = j.at("zero_dc").as_bool();
     for (auto& s : j.at("stems").arr) c.stems.push_back(s.as_string());
     for (auto& b : j.at("bands").arr) {
         std::vector<int> band;
-        for (auto& f : b.arr) band.push_back((int)f.as_int());
+        for (auto& f : b.arr) band.push_back(f.as_int32());
         c.bands.push_back(band);
     }
     if (c.family != "bs-roformer" && c.family != "mel-band-roformer" && c.family != "hyperace-v2")
@@ -196,7 +196,7 @@ void ModelConfig::validate() const {
 Manifest Manifest::from_json(const Json& j) {
     check_keys(j, kManifestKeys, "manifest");
     Manifest m;
-    m.schema_version = (int)j.at("schema_version").as_int();
+    m.schema_version = j.at("schema_version").as_int32();
     m.model_id = j.at("model_id").as_string();
     m.weights_sha256 = j.at("weights_sha256").as_string();
     m.checkpoint_sha256 = j.at("checkpoint_sha256").as_string();

@@ -50,6 +50,8 @@ def _package(tmp_path, golden, change=None, extra_key=False):
     ({"bottleneck_factor": 0}, "network size"),
     ({"stems": ["instrumental", "vocals"]}, "vocals/instrumental"),
     ({"sample_rate": 48000}, "44100"),
+    ({"frames": 2**32 + 256}, "integer out of range"),  # not read as 256 after truncation
+    ({"n_fft": 1e300}, "expected an integer"),
 ])
 def test_invalid_config_rejected_before_device_work(tmp_path, golden, change, message):
     st, err = _load(_package(tmp_path, golden, change))
