@@ -40,6 +40,15 @@ inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s
 
 inline int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+// Longest track a separation entry point accepts, per channel: 2^36 samples (about 18 days at
+// 44.1 kHz), which keeps every byte count derived from it far from overflowing 64 bits.
+constexpr int64_t kMaxTrackSamples = int64_t(1) << 36;
+// The model schema's context limits (crates/ancha-models/src/config.rs:64): a chunk of at most
+// 60 s at 44.1 kHz and an overlap divisor of at most 16. They also hold for a chunk or overlap
+// given at call time, as the reference validates its config after command-line overrides.
+constexpr int64_t kMaxChunkSamples = 44100 * 60;
+constexpr int kMaxOverlap = 16;
+
 __device__ __forceinline__ float load_f(const float* p) { return *p; }
 __device__ __forceinline__ float load_f(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 __device__ __forceinline__ float load_f(const __half* p) { return __half2float(*p); }

@@ -517,6 +517,7 @@ int Mdx23c::separate_pcm(const float* planes, int64_t samples, int overlap, int 
     const auto t_start = std::chrono::steady_clock::now();
     const Mdx23cConfig& c = manifest.config;
     if (!planes || !stems || samples <= 0) return fail(ANCHA_E_INVALID, "mdx23c_separate: empty input");
+    if (samples > kMaxTrackSamples) return fail(ANCHA_E_INVALID, "mdx23c_separate: track longer than 2^36 samples");
     const int ov = overlap > 0 ? overlap : c.overlap;
     const int64_t chunk = c.chunk_samples();
     Mdx23cPlan plan;

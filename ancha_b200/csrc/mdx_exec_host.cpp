@@ -2,6 +2,7 @@
 // Graph::forward (crates/ancha-models/src/mdx.rs:474-568) over the shapes of MdxGraph::infer.
 #include <algorithm>
 #include <chrono>
+#include <cmath>
 #include <stdexcept>
 #include <string>
 
@@ -167,12 +168,15 @@ int MdxModel::separate_pcm(const MdxTaskOpts& o, const float* planes, int64_t sa
     const auto t0 = std::chrono::steady_clock::now();
     // separate_mdx (src/mdx_runtime.rs:84-248): option checks, UVR trim / pad, chunk starts.
     if (!planes || !predicted || !residual || samples <= 0) return fail(ANCHA_E_INVALID, "mdx_separate: empty input");
+    if (samples > kMaxTrackSamples) return fail(ANCHA_E_INVALID, "mdx_separate: track longer than 2^36 samples");
     if (o.batch < 1 || o.batch > 4) return fail(ANCHA_E_INVALID, "MDX batch size must be between 1 and 4");
-    if (o.overlap >= 0.0 && !(o.overlap <= 0.95)) return fail(ANCHA_E_INVALID, "MDX overlap must be between 0 and 0.95");
-    if (o.hop <= 0 || o.frames < 2 || o.bins <= 0 || o.bins > o.n_fft / 2 + 1)
+    if (std::isnan(o.overlap) || (o.overlap >= 0.0 && !(o.overlap <= 0.95)))
+        return fail(ANCHA_E_INVALID, "MDX overlap must be between 0 and 0.95");
+    if (o.hop <= 0 || o.hop > o.n_fft || o.frames < 2 || o.bins <= 0 || o.bins > o.n_fft / 2 + 1)
         return fail(ANCHA_E_INVALID, "invalid MDX STFT configuration");
     if (!mdx_task_fft_supported(o.n_fft)) return fail(ANCHA_E_UNSUPPORTED, "classic MDX STFT size not supported");
-    const int64_t chunk = (int64_t)o.hop * (o.frames - 1);
+    const int64_t chunk = (int64_t)o.hop * (o.frames - 1);  // < 2^62: no overflow
+    if (chunk > kMaxChunkSamples) return fail(ANCHA_E_INVALID, "MDX chunk longer than 60 s");
     const int64_t trim = o.n_fft / 2, gen = chunk - o.n_fft;
     if (gen <= 0 || chunk <= trim) return fail(ANCHA_E_INVALID, "MDX chunk shorter than its FFT");
     const int64_t pad = gen + trim - samples % gen;

@@ -40,6 +40,9 @@ struct TrackPlan {
 // runtime.rs:103-111 and chunk.rs:10-23.
 TrackPlan make_plan(int64_t samples, int64_t chunk, int overlap) {
     if (chunk <= 0 || overlap <= 0 || overlap > chunk) throw std::runtime_error("invalid chunk or overlap divisor");
+    if (chunk > kMaxChunkSamples || overlap > kMaxOverlap)
+        throw std::runtime_error("chunk longer than 60 s or overlap divisor above 16");
+    if (samples > kMaxTrackSamples) throw std::runtime_error("track longer than 2^36 samples");
     TrackPlan p;
     p.samples = samples;
     p.chunk = chunk;

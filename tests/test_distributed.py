@@ -41,7 +41,9 @@ def test_chunk_plan_matches_oracle(samples, chunk, overlap):
 
 
 def test_chunk_plan_rejects_invalid():
-    for args in [(0, 4096, 4), (1000, 0, 4), (1000, 4096, 0), (1000, 4, 8)]:
+    # the last three: a chunk past 60 s, an overlap divisor above 16 (config.rs:64), a track past 2^36 samples
+    for args in [(0, 4096, 4), (1000, 0, 4), (1000, 4096, 0), (1000, 4, 8), (1000, 44100 * 60 + 1, 1),
+                 (100000, 8192, 17), ((1 << 36) + 1, 8192, 4)]:
         with pytest.raises(N.AnchaError):
             ChunkPlan.of(*args)
     plan = ChunkPlan.of(44100, 8192, 4)

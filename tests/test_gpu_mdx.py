@@ -154,7 +154,9 @@ def test_separate_task_rejects_bad_options(torch_cuda):
     from ancha_b200.mdx import Graph
     g = Graph(shape_preserving_graph())
     x = np.zeros((2, 4000), np.float32)
-    for bad in (dict(overlap=0.99), dict(batch=5), dict(n_fft=448)):  # 448 / 2 = 7 · 2^5
+    for bad in (dict(overlap=0.99), dict(batch=5), dict(n_fft=448),  # 448 / 2 = 7 · 2^5
+                dict(overlap=float("nan")), dict(hop=1024),           # hop above n_fft
+                dict(frames=1 << 20)):                                 # a chunk past 60 s
         with pytest.raises(N.AnchaError):
             g.separate_pcm(x, **dict(dict(n_fft=512, hop=128, bins=256, frames=16), **bad))
     with pytest.raises(N.AnchaError) as e:
