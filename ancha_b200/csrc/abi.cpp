@@ -154,6 +154,9 @@ int ancha_istft_masked(const float* packed, const float* masks, int chunks, int 
         return fail(ANCHA_E_INVALID, "istft: invalid arguments");
     if (reinterpret_cast<uintptr_t>(packed) % 16 || reinterpret_cast<uintptr_t>(scratch) % 8)
         return fail(ANCHA_E_INVALID, "istft: packed must be 16-byte and scratch 8-byte aligned");
+    // Checked here as well as in istft_masked: the status word's address below derives from them.
+    if (hop > 1024 || samples <= 1024)
+        return fail(ANCHA_E_INVALID, "istft: require hop in 1..=1024 and samples > 1024");
     // The status word sits after the frame scratch; bit 2 = an uncovered sample.
     const int frames = samples / hop + 1;
     int* flag = reinterpret_cast<int*>(scratch + (int64_t)chunks * stems * 2 * frames * 2048);

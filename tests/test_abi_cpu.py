@@ -58,6 +58,11 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     assert lib.ancha_attention_fwd(C.byref(d), 1, 1, 1, None, 1, None) == N.E_UNSUPPORTED
     ld = N.LinearDesc(4, 128, 12, N.F32, N.F32, N.W_KN, 12, 128, 128, 0, N.ACT_NONE, 0, 1, 1)
     assert lib.ancha_linear_fwd(C.byref(ld), 1, 1, None, None, None, 1, None) != N.OK
+    # A negative length is rejected before the status word behind the scratch is addressed
+    # (without a GPU a device memset would answer with a CUDA error instead).
+    for samples, hop in ((-100000, 1), (1024, 512), (44100, 2048)):
+        assert lib.ancha_istft_masked(16, 16, 1, 1, samples, hop, 0, 16, 16, None) == N.E_INVALID
+        assert "require hop" in N.last_error()
     h = C.c_void_p()
     assert lib.ancha_model_load(b"/nonexistent-package", 0, 0, C.byref(h)) != N.OK
     assert not h.value
