@@ -18,6 +18,7 @@
 #include <thread>
 
 #include "attention.cuh"
+#include "dsp.cuh"
 #include "rowops.cuh"
 
 namespace ancha {
@@ -732,6 +733,10 @@ int Model::forward(const float* spectrum, int chunks, int frames, float* masks,
                    const volatile int* cancel, cudaStream_t s, bool check) {
     const ModelConfig& c = manifest.config;
     if (chunks <= 0 || frames <= 0) return fail(ANCHA_E_INVALID, "invalid model spectrum shape");
+    // The runtime's own calls: at most kMaxChunksPerCall chunks of at most 60 s, which keeps the
+    // row counts in int and every workspace byte count far below 2^63.
+    if (chunks > kMaxChunksPerCall || frames > kMaxChunkSamples / c.hop + 1)
+        return fail(ANCHA_E_INVALID, "model_forward: at most 128 chunks of at most 60 s per call");
     ANCHA_CUDA(cudaSetDevice(device));
     ANCHA_TRY(ensure_workspace(chunks, frames, s));
     cur_chunks_ = chunks;

@@ -217,3 +217,18 @@ def test_config3_bs_roformer_512_parity(bs512_package):
     assert results["f32"][1] <= 1e-4 and results["f32"][0] >= 80.0
     assert results["f16"][0] >= 50.0
     assert results["bf16"][0] >= 40.0
+
+
+def test_forward_rejects_oversized_calls(tmp_path):
+    """More chunks per call than the runtime ever batches (128), or more frames than a 60 s
+    chunk has, fail with ANCHA_E_INVALID before any device work."""
+    import ctypes as C
+    from ancha_b200 import _native as N
+    d = str(tmp_path / "pkg")
+    synthetic.tiny_package(d, "mel-band-roformer")
+    m = Roformer(d, 0, "f32")
+    buf = torch.zeros(16, device="cuda")
+    for chunks, frames in ((129, 8), (1, 10 ** 7)):
+        st = N.lib().ancha_model_forward(m._h, buf.data_ptr(), chunks, frames, buf.data_ptr(), None, None)
+        assert st == N.E_INVALID and "at most 128 chunks" in N.last_error()
+    m.close()
