@@ -432,6 +432,8 @@ void write_wav(const std::string& path, const Audio& audio) {
     const int64_t n = audio.samples();
     if (channels == 0 || n == 0) throw std::runtime_error("write_wav: empty audio");
     std::string s;
+    // RIFF sizes are 32-bit: refuse what does not fit, as the reference's WAV writer does.
+    if ((uint64_t)n * channels * 4 > 0xFFFFFFFFull - 36) throw std::runtime_error("write_wav: more than 4 GiB of samples");
     const uint32_t data_bytes = (uint32_t)(n * channels * 4);
     s.append("RIFF");
     put32(s, 36 + data_bytes);
