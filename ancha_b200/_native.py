@@ -29,7 +29,7 @@ EXPORTS = ("ancha_last_error", "ancha_version", "ancha_available", "ancha_attent
            "ancha_model_load", "ancha_model_info", "ancha_model_forward", "ancha_model_free",
            "ancha_mdx23c_load", "ancha_mdx23c_info", "ancha_mdx23c_forward", "ancha_mdx23c_separate_pcm",
            "ancha_mdx23c_plan", "ancha_mdx23c_free", "ancha_mdx_graph_inspect", "ancha_mdx_load",
-           "ancha_mdx_output_shape", "ancha_mdx_forward", "ancha_mdx_separate_pcm", "ancha_mdx_free",
+           "ancha_mdx_output_shape", "ancha_mdx_forward", "ancha_mdx_separate_pcm", "ancha_mdx_set_gemm", "ancha_mdx_free",
            "ancha_separate", "ancha_separate_pcm", "ancha_separate_device",
            "ancha_separate_status", "ancha_chunk_plan", "ancha_chunk_span", "ancha_separate_span",
            "ancha_free_string")
@@ -117,6 +117,7 @@ def lib() -> C.CDLL:
             "ancha_mdx_forward": (i32, [vp, vp, C.POINTER(i64), vp, C.POINTER(i32), vp]),
             "ancha_mdx_separate_pcm": (i32, [vp, C.POINTER(MdxTask), fp, i64, C.POINTER(i32), fp, fp,
                                              C.POINTER(C.c_double)]),
+            "ancha_mdx_set_gemm": (i32, [vp, i32]),
             "ancha_mdx_free": (None, [vp]),
             "ancha_separate": (i32, [C.POINTER(SeparateOpts), i32, C.POINTER(i32), PROGRESS,
                                      vp, C.POINTER(i32), C.POINTER(C.c_void_p)]),

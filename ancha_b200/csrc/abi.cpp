@@ -350,6 +350,11 @@ int ancha_mdx_separate_pcm(ancha_mdx* graph, const ancha_mdx_task* task, const f
     return graph->impl->separate_pcm(o, planes, samples, cancel, predicted, residual, seconds_out);
 }
 
+int ancha_mdx_set_gemm(ancha_mdx* graph, int precision) {
+    if (!graph) return fail(ANCHA_E_INVALID, "mdx_set_gemm: null graph");
+    return graph->impl->set_gemm(precision);
+}
+
 void ancha_mdx_free(ancha_mdx* graph) { delete graph; }
 
 }  // extern "C"

@@ -158,6 +158,21 @@ int mdx_permute(const float* x, float* out, const MdxPermute& p, cudaStream_t s)
     return check_launch("mdx_permute");
 }
 
+namespace {
+__global__ void channel_bias_kernel(float* __restrict__ y, const float* __restrict__ bias, int channels,
+                                    int64_t plane, int64_t total) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+        y[i] += bias[(i / plane) % channels];
+}
+}  // namespace
+
+int mdx_channel_bias(float* y, const float* bias, int64_t batch, int channels, int64_t plane, cudaStream_t s) {
+    const int64_t total = batch * channels * plane;
+    if (total <= 0) return ANCHA_OK;
+    channel_bias_kernel<<<blocks_for(total), kThreads, 0, s>>>(y, bias, channels, plane, total);
+    return check_launch("mdx_channel_bias");
+}
+
 int mdx_matmul(const float* a, const float* b, float* out, const MdxMatmul& m, cudaStream_t s) {
     const int64_t batches = m.batch[0] * m.batch[1];
     if (batches <= 0 || m.m <= 0 || m.n <= 0) return ANCHA_OK;

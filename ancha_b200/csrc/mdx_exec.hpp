@@ -38,6 +38,9 @@ int mdx_conv2d(const float* x, const float* w, const float* bias, float* out, co
 int mdx_ewise(const float* a, const float* b, float* out, const MdxEwise& e, cudaStream_t s);
 int mdx_permute(const float* x, float* out, const MdxPermute& p, cudaStream_t s);
 int mdx_matmul(const float* a, const float* b, float* out, const MdxMatmul& m, cudaStream_t s);
+// y[i][c][·] += bias[c] for `batch` images of `channels` planes of `plane` elements (the bias
+// of a convolution run as a GEMM, whose epilogue bias runs along the other axis).
+int mdx_channel_bias(float* y, const float* bias, int64_t batch, int channels, int64_t plane, cudaStream_t s);
 
 // ---- The classic MDX task (src/mdx_runtime.rs) -------------------------------------------------
 
@@ -95,11 +98,27 @@ public:
     int separate_pcm(const MdxTaskOpts& o, const float* planes, int64_t samples, const volatile int* cancel,
                      float* predicted, float* residual, double* seconds);
 
+    // Graph::forward's conv_gemm (mdx.rs:472-530, spatial.rs:21-67): ungrouped, undilated
+    // convolutions with constant weights in the patch-gather geometries (1×1, 3×3 with padding
+    // 1, 2×2 with stride 2) run as the weight matrix [co][ci·kh·kw] times a patch matrix, and a
+    // MatMul by a constant 2-D right operand runs as one GEMM. precision < 0: off, every op on
+    // its direct kernel (the default). ANCHA_PRECISION_F32: those GEMMs on the FFMA kernel.
+    // ANCHA_PRECISION_BF16 / _F16: the convolutions on the tcgen05 kernel with 16-bit weights
+    // and patches, fp32 accumulation and output; the MatMuls stay f32 FFMA. Uploads the
+    // converted weights; not re-entrant with forward on the same handle.
+    int set_gemm(int precision);
+
     MdxGraph graph;
     int device = 0;
 
 private:
     int infer(const Shape4& in, std::vector<Shape4>& shapes) const;
+    // Instruction k (an eligible Conv) on x as pack + GEMM + bias into y; ANCHA_E_UNSUPPORTED,
+    // with nothing enqueued, when the patch gather does not take the shape.
+    int conv_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c, cudaStream_t s);
+    int gemm_elt_ = -1;             // ELT_* of the convolution GEMMs, −1 = off
+    std::vector<DevBuf> gemm_w_;    // by instruction: [co][kp] weights in gemm_elt_
+    std::vector<int64_t> gemm_kp_;  // by instruction: ci·kh·kw rounded up to 8, 0 = direct kernel
     std::vector<DevBuf> constants_;          // by value id
     std::vector<DevBuf> bn_scale_, bn_shift_;  // by instruction (BatchNormalization only)
 };

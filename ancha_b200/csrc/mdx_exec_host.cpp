@@ -2,6 +2,7 @@
 // Graph::forward (crates/ancha-models/src/mdx.rs:474-568) over the shapes of MdxGraph::infer.
 #include <algorithm>
 #include <chrono>
+#include <climits>
 #include <cmath>
 #include <stdexcept>
 #include <string>
@@ -20,6 +21,40 @@ void upload(DevBuf& d, const std::vector<T>& v) {
     d.alloc(std::max<size_t>(v.size(), 1) * sizeof(T));
     if (!v.empty() && cudaMemcpy(d.p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice) != cudaSuccess)
         throw std::runtime_error("cudaMemcpy of an MDX constant");
+}
+
+void upload_elt(DevBuf& d, const std::vector<float>& v, int elt) {
+    if (elt == ELT_F32) return upload(d, v);
+    if (elt == ELT_BF16) {
+        std::vector<__nv_bfloat16> h(v.size());
+        for (size_t i = 0; i < v.size(); ++i) h[i] = __float2bfloat16_rn(v[i]);
+        return upload(d, h);
+    }
+    std::vector<__half> h(v.size());
+    for (size_t i = 0; i < v.size(); ++i) h[i] = __float2half_rn(v[i]);
+    upload(d, h);
+}
+
+// The patch-gather geometries (mdx_pack): 1×1 stride 1, 3×3 stride 1 padding 1, 2×2 stride 2,
+// of an ungrouped, undilated Conv whose kernel is kh × kw.
+bool gemm_geometry(const MdxInstruction& ins, int64_t kh, int64_t kw) {
+    if (ins.op != MdxOp::Conv || ins.groups != 1 || ins.dilation[0] != 1 || ins.dilation[1] != 1) return false;
+    if (kh != kw || ins.stride[0] != ins.stride[1] || ins.padding[0] != ins.padding[1]) return false;
+    const int s = ins.stride[0], p = ins.padding[0];
+    return (kh == 1 && s == 1 && p == 0) || (kh == 3 && s == 1 && p == 1) || (kh == 2 && s == 2 && p == 0);
+}
+
+// The patch matrix's GEMM takes oh·ow as an int column count.
+bool npos_fits(const MdxConvShape& c) { return (int64_t)c.oh * c.ow <= INT32_MAX; }
+
+GemmEpilogue plain_f32_epilogue() {
+    GemmEpilogue e{};
+    e.act = ANCHA_ACT_NONE;
+    e.out_type = ELT_F32;
+    e.rope_tokens = 1;
+    e.rope_div = 1;
+    e.rope_hd = 64;
+    return e;
 }
 
 }  // namespace
@@ -46,6 +81,76 @@ int MdxModel::infer(const Shape4& in, std::vector<Shape4>& shapes) const {
     std::string err;
     if (!graph.infer(in, shapes, err)) return fail(ANCHA_E_INVALID, err);
     return ANCHA_OK;
+}
+
+int MdxModel::set_gemm(int precision) {
+    if (precision < 0) {
+        gemm_elt_ = -1;
+        gemm_w_.clear();
+        gemm_kp_.clear();
+        return ANCHA_OK;
+    }
+    if (precision != ANCHA_PRECISION_F32 && precision != ANCHA_PRECISION_BF16 && precision != ANCHA_PRECISION_F16)
+        return fail(ANCHA_E_INVALID, "mdx_set_gemm: unknown precision");
+    const int elt = precision == ANCHA_PRECISION_BF16 ? ELT_BF16 : precision == ANCHA_PRECISION_F16 ? ELT_F16 : ELT_F32;
+    ANCHA_CUDA(cudaSetDevice(device));
+    const size_t n = graph.instructions.size();
+    std::vector<DevBuf> w(n);
+    std::vector<int64_t> kp(n, 0);
+    try {
+        for (size_t k = 0; k < n; ++k) {
+            const MdxInstruction& ins = graph.instructions[k];
+            if (ins.op != MdxOp::Conv || ins.inputs[1] >= (int)graph.constants.size()) continue;
+            const MdxConstant& wc = graph.constants[ins.inputs[1]];
+            if (!gemm_geometry(ins, wc.shape[2], wc.shape[3])) continue;
+            // [co][ci][kh][kw] flattened is the patch order (c, ky, kx); rows padded to kp.
+            const int64_t co = wc.shape[0], kk = wc.shape[1] * wc.shape[2] * wc.shape[3];
+            const int64_t p = (kk + 7) / 8 * 8;
+            std::vector<float> padded((size_t)(co * p), 0.f);
+            for (int64_t o = 0; o < co; ++o)
+                std::copy(wc.data.begin() + o * kk, wc.data.begin() + (o + 1) * kk, padded.begin() + o * p);
+            upload_elt(w[k], padded, elt);
+            kp[k] = p;
+        }
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_CUDA, e.what());
+    }
+    gemm_w_ = std::move(w);
+    gemm_kp_ = std::move(kp);
+    gemm_elt_ = elt;
+    return ANCHA_OK;
+}
+
+int MdxModel::conv_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c,
+                           cudaStream_t s) {
+    const int64_t kp = gemm_kp_[k], npos = (int64_t)c.oh * c.ow;
+    const size_t es = elt_size(gemm_elt_);
+    if ((int64_t)c.ci * c.kh * c.kw > kp) return fail(ANCHA_E_INVALID, "mdx conv_gemm: weight / input channels");
+    void* patches = nullptr;
+    if (cudaMallocAsync(&patches, (size_t)c.n * npos * kp * es, s) != cudaSuccess)
+        return fail(ANCHA_E_CUDA, "cudaMallocAsync of an MDX patch matrix");
+    PackArgs p{};
+    p.a = PackSource{x, c.ci, nullptr, nullptr, nullptr};  // no norm, no activation: plain im2col
+    p.b = PackSource{nullptr, 0, nullptr, nullptr, nullptr};
+    p.batch = c.n; p.h = c.h; p.w = c.w; p.ho_n = c.oh; p.wo_n = c.ow;
+    p.kh = c.kh; p.kw = c.kw; p.sh = c.sh; p.sw = c.sw; p.ph = c.ph; p.pw = c.pw;
+    p.gelu = false; p.eps = 0.f; p.kp = kp; p.out = patches; p.out_type = gemm_elt_;
+    int st = mdx_pack(p, s);
+    const GemmEpilogue e = plain_f32_epilogue();
+    for (int i = 0; i < c.n && st == ANCHA_OK; ++i) {
+        // Image i: y[i] [co][oh·ow] = W [co][kp] · P[i] [oh·ow][kp]ᵀ, NCHW as it stands.
+        GemmGroup g{};
+        g.a = gemm_w_[k].p; g.lda = kp;
+        g.b = static_cast<const uint8_t*>(patches) + (size_t)i * npos * kp * es; g.ldb = kp;
+        g.out = y + (size_t)i * c.co * npos; g.ldo = npos; g.ldr = npos;
+        g.m = c.co; g.n = (int)npos; g.k = (int)kp;
+        st = ANCHA_E_UNSUPPORTED;
+        if (gemm_elt_ != ELT_F32) st = gemm_tc(g, gemm_elt_, e, s);
+        if (st == ANCHA_E_UNSUPPORTED) st = gemm_ffma(g, nullptr, 1, g.m, g.n, gemm_elt_, gemm_elt_, 1, e, s);
+    }
+    cudaFreeAsync(patches, s);
+    if (st == ANCHA_OK && bias) st = mdx_channel_bias(y, bias, c.n, c.co, npos, s);
+    return st;
 }
 
 int MdxModel::output_shape(const Shape4& in, Shape4& out) const {
@@ -91,8 +196,11 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
                 MdxConvShape c;
                 std::string err;
                 mdx_conv_shape(ins, a, shapes[ins.inputs[1]], c, err);  // checked by infer
-                st = mdx_conv2d(va, values[ins.inputs[1]], ins.inputs.size() == 3 ? values[ins.inputs[2]] : nullptr, y,
-                                c, ins.op == MdxOp::ConvTranspose, s);
+                const float* bias = ins.inputs.size() == 3 ? values[ins.inputs[2]] : nullptr;
+                st = ANCHA_E_UNSUPPORTED;
+                if (gemm_elt_ >= 0 && gemm_kp_[k] && npos_fits(c)) st = conv_as_gemm(k, va, bias, y, c, s);
+                if (st == ANCHA_E_UNSUPPORTED)
+                    st = mdx_conv2d(va, values[ins.inputs[1]], bias, y, c, ins.op == MdxOp::ConvTranspose, s);
                 break;
             }
             case MdxOp::Relu:
@@ -132,6 +240,17 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
             }
             case MdxOp::MatMul: {
                 const Shape4& b = shapes[ins.inputs[1]];
+                const int64_t rows = a[0] * a[1] * a[2];
+                if (gemm_elt_ >= 0 && ins.inputs[1] < nconst && b[0] == 1 && b[1] == 1 && rows <= 65535LL * 128) {
+                    // [a0·a1·m, k] · [k, n] in one FFMA GEMM (right operand KN, as ONNX stores it).
+                    GemmGroup g{};
+                    g.a = va; g.lda = a[3];
+                    g.b = values[ins.inputs[1]]; g.ldb = b[3];
+                    g.out = y; g.ldo = b[3]; g.ldr = b[3];
+                    g.m = (int)rows; g.n = (int)b[3]; g.k = (int)a[3];
+                    st = gemm_ffma(g, nullptr, 1, g.m, g.n, ELT_F32, ELT_F32, 0, plain_f32_epilogue(), s);
+                    break;
+                }
                 MdxMatmul mm{};
                 mm.batch[0] = os[0];
                 mm.batch[1] = os[1];

@@ -25,12 +25,16 @@ def inspect(onnx: bytes, optimized: bool = True) -> dict:
 class Graph:
     """A classic MDX ONNX graph on one GPU (not re-entrant)."""
 
-    def __init__(self, onnx: bytes, device: int = 0, optimized: bool = True):
+    def __init__(self, onnx: bytes, device: int = 0, optimized: bool = True, gemm: Optional[str] = None):
+        """``gemm``: None runs every operation on its direct kernel; "f32", "bf16" or "f16" runs
+        eligible convolutions and constant-weight MatMuls as GEMMs (``ancha_mdx_set_gemm``)."""
         handle = C.c_void_p()
         buf = C.create_string_buffer(onnx, len(onnx))
         N.check(N.lib().ancha_mdx_load(buf, len(onnx), int(optimized), device, C.byref(handle)))
         self._h = handle
         self.device = device
+        if gemm is not None:
+            N.check(N.lib().ancha_mdx_set_gemm(self._h, N.PRECISIONS[gemm]))
 
     def output_shape(self, shape) -> tuple:
         i = (C.c_int64 * 4)(*shape)

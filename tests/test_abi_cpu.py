@@ -63,6 +63,7 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     for samples, hop in ((-100000, 1), (1024, 512), (44100, 2048)):
         assert lib.ancha_istft_masked(16, 16, 1, 1, samples, hop, 0, 16, 16, None) == N.E_INVALID
         assert "require hop" in N.last_error()
+    assert lib.ancha_mdx_set_gemm(None, N.PRECISION_F16) == N.E_INVALID
     h = C.c_void_p()
     assert lib.ancha_model_load(b"/nonexistent-package", 0, 0, C.byref(h)) != N.OK
     assert not h.value
