@@ -73,3 +73,18 @@ def test_separate_task_with_gemm_matches_oracle(torch_cuda, mode):
     print(f"classic MDX task conv_gemm {mode}: max |d| / max |ref| {err:.2e}")
     assert err < {"f32": 2e-5, "bf16": 3e-2}[mode]
     assert np.abs(p + r - x).max() < 1e-6
+
+
+@pytest.mark.parametrize("mode", [None, "f32", "bf16"])
+def test_mdx_net_graph_matches_oracle(torch_cuda, mode):
+    """BASELINE config 5's network family at full depth (five scales) on a small tile."""
+    from ancha_b200 import mdx_net as MN
+    from ancha_b200.mdx import Graph
+    c = MN.MdxNetConfig(dim_f=256, dim_t=64, growth=8, scales=5, layers=3, bottleneck=8)
+    onnx = MN.tfc_tdf_v1(c, seed=0)
+    x = np.random.default_rng(5).standard_normal((2, 4, c.dim_f, c.dim_t))
+    ref = M.Graph(onnx, True).forward(x)
+    y = run(torch_cuda, Graph(onnx, 0, True, gemm=mode), x)
+    err = np.abs(y - ref).max() / np.abs(ref).max()
+    print(f"TFC-TDF v1 conv_gemm {mode}: max |d| / max |ref| {err:.2e}")
+    assert err < {None: 1e-5, "f32": 1e-5, "bf16": 5e-2}[mode]
