@@ -8,6 +8,7 @@
 #include <string>
 
 #include "mdx_exec.hpp"
+#include "rowops.cuh"
 
 namespace ancha {
 namespace {
@@ -100,8 +101,21 @@ int MdxModel::set_gemm(int precision) {
     try {
         for (size_t k = 0; k < n; ++k) {
             const MdxInstruction& ins = graph.instructions[k];
-            if (ins.op != MdxOp::Conv || ins.inputs[1] >= (int)graph.constants.size()) continue;
+            if ((ins.op != MdxOp::Conv && ins.op != MdxOp::MatMul) || ins.inputs[1] >= (int)graph.constants.size())
+                continue;
             const MdxConstant& wc = graph.constants[ins.inputs[1]];
+            if (ins.op == MdxOp::MatMul) {
+                // A constant 2-D right operand [K][N] for the tensor cores: its transpose [N][K]
+                // (the NK operand) in the 16-bit type. f32 mode reads the constant as stored.
+                const int64_t kk = wc.shape[2], nn = wc.shape[3];
+                if (elt == ELT_F32 || wc.shape[0] != 1 || wc.shape[1] != 1 || kk % 8) continue;
+                std::vector<float> t((size_t)(kk * nn));
+                for (int64_t r = 0; r < kk; ++r)
+                    for (int64_t c = 0; c < nn; ++c) t[(size_t)(c * kk + r)] = wc.data[(size_t)(r * nn + c)];
+                upload_elt(w[k], t, elt);
+                kp[k] = kk;
+                continue;
+            }
             if (!gemm_geometry(ins, wc.shape[2], wc.shape[3])) continue;
             // [co][ci][kh][kw] flattened is the patch order (c, ky, kx); rows padded to kp.
             const int64_t co = wc.shape[0], kk = wc.shape[1] * wc.shape[2] * wc.shape[3];
@@ -150,6 +164,22 @@ int MdxModel::conv_as_gemm(size_t k, const float* x, const float* bias, float* y
     }
     cudaFreeAsync(patches, s);
     if (st == ANCHA_OK && bias) st = mdx_channel_bias(y, bias, c.n, c.co, npos, s);
+    return st;
+}
+
+int MdxModel::matmul_as_tc(size_t k, const float* a, int64_t rows, int kk, int nn, float* y, cudaStream_t s) {
+    if (gemm_kp_[k] != kk) return fail(ANCHA_E_UNSUPPORTED, "mdx conv_gemm: no tensor-core weight");
+    void* a16 = nullptr;
+    if (cudaMallocAsync(&a16, (size_t)rows * kk * 2, s) != cudaSuccess)
+        return fail(ANCHA_E_CUDA, "cudaMallocAsync of an MDX MatMul operand");
+    int st = cast_rows(a, kk, a16, gemm_elt_, kk, rows, kk, s);
+    GemmGroup g{};
+    g.a = a16; g.lda = kk;
+    g.b = gemm_w_[k].p; g.ldb = kk;
+    g.out = y; g.ldo = nn; g.ldr = nn;
+    g.m = (int)rows; g.n = nn; g.k = kk;
+    if (st == ANCHA_OK) st = gemm_tc(g, gemm_elt_, plain_f32_epilogue(), s);
+    cudaFreeAsync(a16, s);
     return st;
 }
 
@@ -243,12 +273,18 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
                 const int64_t rows = a[0] * a[1] * a[2];
                 if (gemm_elt_ >= 0 && ins.inputs[1] < nconst && b[0] == 1 && b[1] == 1 && rows <= 65535LL * 128) {
                     // [a0·a1·m, k] · [k, n] in one FFMA GEMM (right operand KN, as ONNX stores it).
-                    GemmGroup g{};
-                    g.a = va; g.lda = a[3];
-                    g.b = values[ins.inputs[1]]; g.ldb = b[3];
-                    g.out = y; g.ldo = b[3]; g.ldr = b[3];
-                    g.m = (int)rows; g.n = (int)b[3]; g.k = (int)a[3];
-                    st = gemm_ffma(g, nullptr, 1, g.m, g.n, ELT_F32, ELT_F32, 0, plain_f32_epilogue(), s);
+                    // 16-bit modes: A cast once, then the tensor cores; f32 (or a shape the
+                    // tensor-core kernel declines, with nothing written): the FFMA GEMM.
+                    st = ANCHA_E_UNSUPPORTED;
+                    if (gemm_elt_ != ELT_F32) st = matmul_as_tc(k, va, rows, (int)a[3], (int)b[3], y, s);
+                    if (st == ANCHA_E_UNSUPPORTED) {
+                        GemmGroup g{};
+                        g.a = va; g.lda = a[3];
+                        g.b = values[ins.inputs[1]]; g.ldb = b[3];
+                        g.out = y; g.ldo = b[3]; g.ldr = b[3];
+                        g.m = (int)rows; g.n = (int)b[3]; g.k = (int)a[3];
+                        st = gemm_ffma(g, nullptr, 1, g.m, g.n, ELT_F32, ELT_F32, 0, plain_f32_epilogue(), s);
+                    }
                     break;
                 }
                 MdxMatmul mm{};

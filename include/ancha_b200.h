@@ -292,9 +292,9 @@ ANCHA_API int ancha_mdx_separate_pcm(ancha_mdx* graph, const ancha_mdx_task* tas
  * [co][ci*kh*kw] times a patch matrix, and a MatMul by a constant 2-D right operand as one
  * GEMM, for every later ancha_mdx_forward / ancha_mdx_separate_pcm on this handle.
  * precision < 0: off (the default; every operation on its direct kernel).
- * ANCHA_PRECISION_F32: those GEMMs in fp32 on FFMA. ANCHA_PRECISION_BF16 / _F16: the
- * convolutions on the tensor cores with 16-bit weights and patches and fp32 accumulation and
- * output; MatMuls stay fp32. Other convolutions keep their direct kernels. Uploads converted
+ * ANCHA_PRECISION_F32: those GEMMs in fp32 on FFMA. ANCHA_PRECISION_BF16 / _F16: on the
+ * tensor cores with 16-bit weights and operands (patches; MatMul inputs cast once) and fp32
+ * accumulation and output. Other convolutions keep their direct kernels. Uploads converted
  * weights; not to be called while a forward on this handle is in flight. */
 ANCHA_API int ancha_mdx_set_gemm(ancha_mdx* graph, int precision);
 

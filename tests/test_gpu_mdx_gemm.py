@@ -1,7 +1,7 @@
 """Classic MDX graphs with conv_gemm (``ancha_mdx_set_gemm``; Graph::forward's option,
 crates/ancha-models/src/mdx.rs:472-530): eligible convolutions as patch gather + GEMM and
-constant-weight MatMuls as one GEMM, in f32 (FFMA) and with 16-bit tensor-core convolutions,
-against the numpy oracle and against the direct kernels.
+constant-weight MatMuls as one GEMM, in f32 (FFMA) and with 16-bit operands on the tensor
+cores, against the numpy oracle and against the direct kernels.
 
 These tests have not yet run on a GPU; they run when ANCHA_GPU_PENDING=1 is set.
 """
