@@ -25,6 +25,12 @@ independent, so ranks shard the work with no collective ("scaling": "weak").
 * ``config4``: BASELINE config 4, the MDX23C inst_voc_hq2 forward in bf16, 16 chunks per GPU
   (4 calls of batch 4) on spectra in HBM: ms, TFLOP/s against the measured bf16 peak, and
   model-only ×realtime (0.74 s of new audio per chunk at overlap 8).
+* ``config5`` (only with ``--config5``; its conv_gemm path has not yet run on a GPU): BASELINE
+  config 5, a synthetic classic MDX-Net (TFC-TDF v1) ONNX graph (``ancha_b200.mdx_net``; n_fft
+  6144, hop 1024, dim_f 3072, dim_t 256) through the classic MDX executor with conv_gemm, bf16
+  and fp32: model-only ms and TFLOP/s for 16 tiles per GPU (4 calls of batch 4), and end to
+  end 64 four-minute tracks sharded over the ranks through ``ancha_mdx_separate_pcm`` (bf16),
+  aggregate ×realtime from the slowest rank's summed separation time.
 * ``cpu_baseline``: the numpy oracle (f32, all host cores) on one native chunk (rank 0, N=1).
 * ``--impl reference`` times that CPU port per step instead (the reference itself is Rust and
   cannot be built offline).
@@ -61,9 +67,73 @@ def parse():
     p.add_argument("--package", default=os.environ.get("ANCHA_BENCH_PACKAGE", "/tmp/ancha_bench/mel-seed0"))
     p.add_argument("--no-config3", action="store_true")
     p.add_argument("--no-config4", action="store_true")
+    p.add_argument("--config5", action="store_true", help="also run BASELINE config 5 (classic MDX-Net)")
     p.add_argument("--pipeline-only", action="store_true",
                    help="run only the warm-up and timed pipeline steps (for launch-list captures)")
     return p.parse_args()
+
+
+def config5(local: int, world: int, rank: int, dist, steps: int = 2):
+    """BASELINE config 5 (see the module docstring); returns the JSON block on rank 0."""
+    import torch
+    from ancha_b200.mdx import Graph
+    from ancha_b200.mdx_net import MdxNetConfig, forward_flops, tfc_tdf_v1
+    c = MdxNetConfig()
+    onnx = tfc_tdf_v1(c, seed=0)
+    g = torch.Generator(device="cuda").manual_seed(6000 + rank)
+    x = torch.randn(16, 4, c.dim_f, c.dim_t, device="cuda", generator=g) * 0.1
+    out = torch.empty_like(x)
+
+    def max_over_ranks(v):
+        if dist:
+            t = torch.tensor([v], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            v = float(t.item())
+        return v
+
+    ms, e2e_s, tracks = {}, None, 64 // world
+    for mode in ("bf16", "f32"):
+        graph = Graph(onnx, local, True, gemm=mode)
+
+        def step():
+            for i in range(0, 16, 4):
+                out[i:i + 4] = graph.forward(x[i:i + 4])
+
+        step()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(steps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        ms[mode] = max_over_ranks(a.elapsed_time(b) / steps)
+        assert bool(torch.isfinite(out).all())
+        if mode == "bf16":
+            # End to end: this rank's share of 64 four-minute tracks, host PCM in and host
+            # predicted / residual out (Inst HQ 2's STFT, mdx.rs:36-93), separation time summed.
+            opts = dict(n_fft=6144, hop=1024, bins=c.dim_f, frames=c.dim_t, compensate=1.033, batch=4)
+            graph.separate_pcm(track(10.0, 7000 + rank), **opts)  # warm-up
+            total = 0.0
+            for i in range(tracks):
+                total += graph.separate_pcm(track(240.0, 7100 + 64 * rank + i), **opts)[2]
+            e2e_s = max_over_ranks(total)
+        graph.close()
+    if rank != 0:
+        return None
+    flops = forward_flops(c, 16)
+    new_audio = 16 * (1024 * (c.dim_t - 1) - 6144) / SR  # UVR default step: chunk − n_fft per tile
+    return {"workload": f"classic MDX-Net (TFC-TDF v1, synthetic ONNX, growth {c.growth}, {c.scales} scales) "
+                        f"forward, 16 tiles [4, {c.dim_f}, {c.dim_t}] per GPU as 4 calls of batch 4, x{world} GPU(s)",
+            "ms_per_16_tiles": ms, "tflop_per_16_tiles": flops / 1e12,
+            "tflops_per_gpu": {m: flops / (v / 1e3) / 1e12 for m, v in ms.items()},
+            "tflops_frac_bf16": flops / (ms["bf16"] / 1e3) / 1e12 / peaks()[1],
+            "x_realtime_model_only": {m: new_audio * world / (v / 1e3) for m, v in ms.items()},
+            "e2e": {"tracks": tracks * world, "seconds_each": 240.0, "slowest_rank_s": e2e_s,
+                    "x_realtime": tracks * world * 240.0 / e2e_s, "dtype": "bf16"},
+            "note": "conv_gemm mode; ConvTranspose layers run on the direct FFMA kernel"}
 
 
 def config3(local: int, world: int, rank: int, dist, steps: int = 2):
@@ -481,6 +551,10 @@ def main():
     if not a.no_config4:
         c4 = config4(local, world, rank, dist)
 
+    c5 = None
+    if a.config5:
+        c5 = config5(local, world, rank, dist)
+
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         _, one = cpu_oracle_chunk(a.package)
@@ -504,7 +578,8 @@ def main():
             "clocks": clk.summary(), "e2e": e2e,
             "gpu_launches": launches_per_step(chunks, effective_batch(chunks, a.batch),
                                               fused=a.precision != "f32") * a.steps,
-            "roofline": roofline, "attention": attention, "config3": c3, "config4": c4, "cpu_baseline": cpu,
+            "roofline": roofline, "attention": attention, "config3": c3, "config4": c4, "config5": c5,
+            "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
     model.close()
