@@ -100,8 +100,9 @@ public:
 
     // Graph::forward's conv_gemm (mdx.rs:472-530, spatial.rs:21-67): ungrouped, undilated
     // convolutions with constant weights in the patch-gather geometries (1×1, 3×3 with padding
-    // 1, 2×2 with stride 2) run as the weight matrix [co][ci·kh·kw] times a patch matrix, and a
-    // MatMul by a constant 2-D right operand runs as one GEMM. precision < 0: off, every op on
+    // 1, 2×2 with stride 2) run as the weight matrix [co][ci·kh·kw] times a patch matrix, 2×2 /
+    // stride-2 ConvTranspose layers as a GEMM with rows (co, dy, dx) plus a scatter (as the
+    // MDX23C decoder does), and a MatMul by a constant 2-D right operand as one GEMM. precision < 0: off, every op on
     // its direct kernel (the default). ANCHA_PRECISION_F32: those GEMMs on the FFMA kernel.
     // ANCHA_PRECISION_BF16 / _F16: on the tcgen05 kernel with 16-bit weights and operands
     // (patches; MatMul inputs cast once), fp32 accumulation and output. Uploads the converted
@@ -116,12 +117,17 @@ private:
     // Instruction k (an eligible Conv) on x as pack + GEMM + bias into y; ANCHA_E_UNSUPPORTED,
     // with nothing enqueued, when the patch gather does not take the shape.
     int conv_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c, cudaStream_t s);
+    // Instruction k (an eligible 2 × 2 / stride-2 ConvTranspose) as 1 × 1 gather + GEMM with rows
+    // (co, dy, dx) + scatter + bias into y; ANCHA_E_UNSUPPORTED as above.
+    int conv_transpose_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c,
+                               cudaStream_t s);
     // Instruction k (a MatMul by a constant [K][N]) on rows × K inputs a as cast + tcgen05 GEMM
     // into y; ANCHA_E_UNSUPPORTED, with nothing written to y, when the GEMM declines the shape.
     int matmul_as_tc(size_t k, const float* a, int64_t rows, int kk, int nn, float* y, cudaStream_t s);
     int gemm_elt_ = -1;             // ELT_* of the GEMMs, −1 = off
-    std::vector<DevBuf> gemm_w_;    // by instruction: Conv [co][kp] / MatMul [N][K] weights in gemm_elt_
-    std::vector<int64_t> gemm_kp_;  // by instruction: Conv ci·kh·kw rounded up to 8, MatMul K; 0 = none
+    // by instruction, in gemm_elt_: Conv [co][kp], ConvTranspose [(co, dy, dx)][kp], MatMul [N][K]
+    std::vector<DevBuf> gemm_w_;
+    std::vector<int64_t> gemm_kp_;  // by instruction: kp (ci·kh·kw or ci, rounded up to 8), MatMul K; 0 = none
     std::vector<DevBuf> constants_;          // by value id
     std::vector<DevBuf> bn_scale_, bn_shift_;  // by instruction (BatchNormalization only)
 };

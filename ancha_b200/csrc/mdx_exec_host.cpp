@@ -48,6 +48,14 @@ bool gemm_geometry(const MdxInstruction& ins, int64_t kh, int64_t kw) {
 // The patch matrix's GEMM takes oh·ow as an int column count.
 bool npos_fits(const MdxConvShape& c) { return (int64_t)c.oh * c.ow <= INT32_MAX; }
 
+// ConvTranspose 2 × 2, stride 2, no padding or output padding, ungrouped and undilated: one
+// GEMM over the input positions with rows (co, dy, dx), then a scatter (mdx_shuffle2x2).
+bool gemm_transpose_geometry(const MdxInstruction& ins, int64_t kh, int64_t kw) {
+    return ins.op == MdxOp::ConvTranspose && ins.groups == 1 && kh == 2 && kw == 2 && ins.stride[0] == 2 &&
+           ins.stride[1] == 2 && ins.padding[0] == 0 && ins.padding[1] == 0 && ins.padding_out[0] == 0 &&
+           ins.padding_out[1] == 0 && ins.dilation[0] == 1 && ins.dilation[1] == 1;
+}
+
 GemmEpilogue plain_f32_epilogue() {
     GemmEpilogue e{};
     e.act = ANCHA_ACT_NONE;
@@ -101,9 +109,24 @@ int MdxModel::set_gemm(int precision) {
     try {
         for (size_t k = 0; k < n; ++k) {
             const MdxInstruction& ins = graph.instructions[k];
-            if ((ins.op != MdxOp::Conv && ins.op != MdxOp::MatMul) || ins.inputs[1] >= (int)graph.constants.size())
+            if ((ins.op != MdxOp::Conv && ins.op != MdxOp::MatMul && ins.op != MdxOp::ConvTranspose) ||
+                ins.inputs[1] >= (int)graph.constants.size())
                 continue;
             const MdxConstant& wc = graph.constants[ins.inputs[1]];
+            if (ins.op == MdxOp::ConvTranspose) {
+                // [ci][co][2][2] (BatchNormalization folded in when optimized) as rows
+                // (co, dy, dx) over ci, padded to kp.
+                if (!gemm_transpose_geometry(ins, wc.shape[2], wc.shape[3])) continue;
+                const int64_t ci = wc.shape[0], co = wc.shape[1], p = (ci + 7) / 8 * 8;
+                std::vector<float> rows((size_t)(co * 4 * p), 0.f);
+                for (int64_t i = 0; i < ci; ++i)
+                    for (int64_t o = 0; o < co; ++o)
+                        for (int64_t t = 0; t < 4; ++t)
+                            rows[(size_t)((o * 4 + t) * p + i)] = wc.data[(size_t)((i * co + o) * 4 + t)];
+                upload_elt(w[k], rows, elt);
+                kp[k] = p;
+                continue;
+            }
             if (ins.op == MdxOp::MatMul) {
                 // A constant 2-D right operand [K][N] for the tensor cores: its transpose [N][K]
                 // (the NK operand) in the 16-bit type. f32 mode reads the constant as stored.
@@ -164,6 +187,45 @@ int MdxModel::conv_as_gemm(size_t k, const float* x, const float* bias, float* y
     }
     cudaFreeAsync(patches, s);
     if (st == ANCHA_OK && bias) st = mdx_channel_bias(y, bias, c.n, c.co, npos, s);
+    return st;
+}
+
+int MdxModel::conv_transpose_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c,
+                                     cudaStream_t s) {
+    const int64_t kp = gemm_kp_[k], npos = (int64_t)c.h * c.w;
+    const size_t es = elt_size(gemm_elt_);
+    if (c.ci > kp || c.oh != 2 * c.h || c.ow != 2 * c.w) return fail(ANCHA_E_INVALID, "mdx conv_gemm: transpose shape");
+    void* patches = nullptr;
+    float* raw = nullptr;
+    if (cudaMallocAsync(&patches, (size_t)c.n * npos * kp * es, s) != cudaSuccess)
+        return fail(ANCHA_E_CUDA, "cudaMallocAsync of an MDX patch matrix");
+    if (cudaMallocAsync(reinterpret_cast<void**>(&raw), (size_t)c.n * c.co * 4 * npos * sizeof(float), s) != cudaSuccess) {
+        cudaFreeAsync(patches, s);
+        return fail(ANCHA_E_CUDA, "cudaMallocAsync of an MDX transposed-convolution product");
+    }
+    PackArgs p{};  // 1 × 1 gather: the input as [image][position][channel]
+    p.a = PackSource{x, c.ci, nullptr, nullptr, nullptr};
+    p.b = PackSource{nullptr, 0, nullptr, nullptr, nullptr};
+    p.batch = c.n; p.h = c.h; p.w = c.w; p.ho_n = c.h; p.wo_n = c.w;
+    p.kh = p.kw = 1; p.sh = p.sw = 1; p.ph = p.pw = 0;
+    p.gelu = false; p.eps = 0.f; p.kp = kp; p.out = patches; p.out_type = gemm_elt_;
+    int st = mdx_pack(p, s);
+    const GemmEpilogue e = plain_f32_epilogue();
+    for (int i = 0; i < c.n && st == ANCHA_OK; ++i) {
+        // raw[i] [(co, dy, dx)][h·w] = W' [4·co][kp] · P[i] [h·w][kp]ᵀ
+        GemmGroup g{};
+        g.a = gemm_w_[k].p; g.lda = kp;
+        g.b = static_cast<const uint8_t*>(patches) + (size_t)i * npos * kp * es; g.ldb = kp;
+        g.out = raw + (size_t)i * c.co * 4 * npos; g.ldo = npos; g.ldr = npos;
+        g.m = 4 * c.co; g.n = (int)npos; g.k = (int)kp;
+        st = ANCHA_E_UNSUPPORTED;
+        if (gemm_elt_ != ELT_F32) st = gemm_tc(g, gemm_elt_, e, s);
+        if (st == ANCHA_E_UNSUPPORTED) st = gemm_ffma(g, nullptr, 1, g.m, g.n, gemm_elt_, gemm_elt_, 1, e, s);
+    }
+    if (st == ANCHA_OK) st = mdx_shuffle2x2(raw, c.n, c.co, c.h, c.w, y, c.co, 0, s);
+    cudaFreeAsync(patches, s);
+    cudaFreeAsync(raw, s);
+    if (st == ANCHA_OK && bias) st = mdx_channel_bias(y, bias, c.n, c.co, 4 * npos, s);
     return st;
 }
 
@@ -228,7 +290,9 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
                 mdx_conv_shape(ins, a, shapes[ins.inputs[1]], c, err);  // checked by infer
                 const float* bias = ins.inputs.size() == 3 ? values[ins.inputs[2]] : nullptr;
                 st = ANCHA_E_UNSUPPORTED;
-                if (gemm_elt_ >= 0 && gemm_kp_[k] && npos_fits(c)) st = conv_as_gemm(k, va, bias, y, c, s);
+                if (gemm_elt_ >= 0 && gemm_kp_[k] && npos_fits(c))
+                    st = ins.op == MdxOp::Conv ? conv_as_gemm(k, va, bias, y, c, s)
+                                               : conv_transpose_as_gemm(k, va, bias, y, c, s);
                 if (st == ANCHA_E_UNSUPPORTED)
                     st = mdx_conv2d(va, values[ins.inputs[1]], bias, y, c, ins.op == MdxOp::ConvTranspose, s);
                 break;

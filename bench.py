@@ -133,7 +133,7 @@ def config5(local: int, world: int, rank: int, dist, steps: int = 2):
             "x_realtime_model_only": {m: new_audio * world / (v / 1e3) for m, v in ms.items()},
             "e2e": {"tracks": tracks * world, "seconds_each": 240.0, "slowest_rank_s": e2e_s,
                     "x_realtime": tracks * world * 240.0 / e2e_s, "dtype": "bf16"},
-            "note": "conv_gemm mode; ConvTranspose layers run on the direct FFMA kernel"}
+            "note": "conv_gemm mode: convolutions, 2x2 transposed convolutions and TDF MatMuls as GEMMs"}
 
 
 def config3(local: int, world: int, rank: int, dist, steps: int = 2):

@@ -289,8 +289,9 @@ ANCHA_API int ancha_mdx_separate_pcm(ancha_mdx* graph, const ancha_mdx_task* tas
 /* Graph::forward's conv_gemm option (mdx.rs:472-530, spatial.rs:21-67; the reference's CUDA
  * default, backend.rs:63): ungrouped, undilated convolutions with constant weights in the
  * patch-gather geometries (1x1, 3x3 with padding 1, 2x2 with stride 2) run as the weights
- * [co][ci*kh*kw] times a patch matrix, and a MatMul by a constant 2-D right operand as one
- * GEMM, for every later ancha_mdx_forward / ancha_mdx_separate_pcm on this handle.
+ * [co][ci*kh*kw] times a patch matrix, 2x2 / stride-2 ConvTranspose layers as one GEMM with
+ * rows (co, dy, dx) plus a scatter, and a MatMul by a constant 2-D right operand as one GEMM,
+ * for every later ancha_mdx_forward / ancha_mdx_separate_pcm on this handle.
  * precision < 0: off (the default; every operation on its direct kernel).
  * ANCHA_PRECISION_F32: those GEMMs in fp32 on FFMA. ANCHA_PRECISION_BF16 / _F16: on the
  * tensor cores with 16-bit weights and operands (patches; MatMul inputs cast once) and fp32
