@@ -38,9 +38,11 @@ int mdx_conv2d(const float* x, const float* w, const float* bias, float* out, co
 int mdx_ewise(const float* a, const float* b, float* out, const MdxEwise& e, cudaStream_t s);
 int mdx_permute(const float* x, float* out, const MdxPermute& p, cudaStream_t s);
 int mdx_matmul(const float* a, const float* b, float* out, const MdxMatmul& m, cudaStream_t s);
-// y[i][c][·] += bias[c] for `batch` images of `channels` planes of `plane` elements (the bias
-// of a convolution run as a GEMM, whose epilogue bias runs along the other axis).
-int mdx_channel_bias(float* y, const float* bias, int64_t batch, int channels, int64_t plane, cudaStream_t s);
+// y[i][c][·] += bias[c] (bias may be null), then max(·, 0) when `relu`, for `batch` images of
+// `channels` planes of `plane` elements: the bias (and a following Relu) of a convolution run
+// as a GEMM, whose epilogue bias runs along the other axis.
+int mdx_channel_bias(float* y, const float* bias, int64_t batch, int channels, int64_t plane, bool relu,
+                     cudaStream_t s);
 
 // ---- The classic MDX task (src/mdx_runtime.rs) -------------------------------------------------
 
@@ -116,11 +118,13 @@ private:
     int infer(const Shape4& in, std::vector<Shape4>& shapes) const;
     // Instruction k (an eligible Conv) on x as pack + GEMM + bias into y; ANCHA_E_UNSUPPORTED,
     // with nothing enqueued, when the patch gather does not take the shape.
-    int conv_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c, cudaStream_t s);
+    // `relu`: apply the Relu that follows in the same pass.
+    int conv_as_gemm(size_t k, const float* x, const float* bias, bool relu, float* y, const MdxConvShape& c,
+                     cudaStream_t s);
     // Instruction k (an eligible 2 × 2 / stride-2 ConvTranspose) as 1 × 1 gather + GEMM with rows
     // (co, dy, dx) + scatter + bias into y; ANCHA_E_UNSUPPORTED as above.
-    int conv_transpose_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c,
-                               cudaStream_t s);
+    int conv_transpose_as_gemm(size_t k, const float* x, const float* bias, bool relu, float* y,
+                               const MdxConvShape& c, cudaStream_t s);
     // Instruction k (a MatMul by a constant [K][N]) on rows × K inputs a as cast + tcgen05 GEMM
     // into y; ANCHA_E_UNSUPPORTED, with nothing written to y, when the GEMM declines the shape.
     int matmul_as_tc(size_t k, const float* a, int64_t rows, int kk, int nn, float* y, cudaStream_t s);

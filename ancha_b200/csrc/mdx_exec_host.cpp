@@ -158,7 +158,7 @@ int MdxModel::set_gemm(int precision) {
     return ANCHA_OK;
 }
 
-int MdxModel::conv_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c,
+int MdxModel::conv_as_gemm(size_t k, const float* x, const float* bias, bool relu, float* y, const MdxConvShape& c,
                            cudaStream_t s) {
     const int64_t kp = gemm_kp_[k], npos = (int64_t)c.oh * c.ow;
     const size_t es = elt_size(gemm_elt_);
@@ -186,12 +186,12 @@ int MdxModel::conv_as_gemm(size_t k, const float* x, const float* bias, float* y
         if (st == ANCHA_E_UNSUPPORTED) st = gemm_ffma(g, nullptr, 1, g.m, g.n, gemm_elt_, gemm_elt_, 1, e, s);
     }
     cudaFreeAsync(patches, s);
-    if (st == ANCHA_OK && bias) st = mdx_channel_bias(y, bias, c.n, c.co, npos, s);
+    if (st == ANCHA_OK) st = mdx_channel_bias(y, bias, c.n, c.co, npos, relu, s);
     return st;
 }
 
-int MdxModel::conv_transpose_as_gemm(size_t k, const float* x, const float* bias, float* y, const MdxConvShape& c,
-                                     cudaStream_t s) {
+int MdxModel::conv_transpose_as_gemm(size_t k, const float* x, const float* bias, bool relu, float* y,
+                                     const MdxConvShape& c, cudaStream_t s) {
     const int64_t kp = gemm_kp_[k], npos = (int64_t)c.h * c.w;
     const size_t es = elt_size(gemm_elt_);
     if (c.ci > kp || c.oh != 2 * c.h || c.ow != 2 * c.w) return fail(ANCHA_E_INVALID, "mdx conv_gemm: transpose shape");
@@ -225,7 +225,7 @@ int MdxModel::conv_transpose_as_gemm(size_t k, const float* x, const float* bias
     if (st == ANCHA_OK) st = mdx_shuffle2x2(raw, c.n, c.co, c.h, c.w, y, c.co, 0, s);
     cudaFreeAsync(patches, s);
     cudaFreeAsync(raw, s);
-    if (st == ANCHA_OK && bias) st = mdx_channel_bias(y, bias, c.n, c.co, 4 * npos, s);
+    if (st == ANCHA_OK) st = mdx_channel_bias(y, bias, c.n, c.co, 4 * npos, relu, s);
     return st;
 }
 
@@ -269,10 +269,18 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
                 values[v] = nullptr;
             }
     };
+    // conv_gemm: a Relu that is the next instruction and the only consumer of a convolution run
+    // as a GEMM is applied in the convolution's bias pass, and its value is that buffer.
+    auto relu_follows = [&](size_t k) {
+        const MdxInstruction& ins = graph.instructions[k];
+        return k + 1 < graph.instructions.size() && graph.instructions[k + 1].op == MdxOp::Relu &&
+               graph.instructions[k + 1].inputs[0] == ins.output && graph.uses[ins.output] == 1;
+    };
     int st = ANCHA_OK;
     for (size_t k = 0; k < graph.instructions.size() && st == ANCHA_OK; ++k) {
         if (cancel && *cancel) { st = fail(ANCHA_E_CANCELLED, "task cancelled"); break; }
         const MdxInstruction& ins = graph.instructions[k];
+        bool relu_done = false;
         const Shape4& os = shapes[ins.output];
         float* y = nullptr;
         if (cudaMallocAsync(reinterpret_cast<void**>(&y), (size_t)numel(os) * sizeof(float), s) != cudaSuccess) {
@@ -290,9 +298,12 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
                 mdx_conv_shape(ins, a, shapes[ins.inputs[1]], c, err);  // checked by infer
                 const float* bias = ins.inputs.size() == 3 ? values[ins.inputs[2]] : nullptr;
                 st = ANCHA_E_UNSUPPORTED;
-                if (gemm_elt_ >= 0 && gemm_kp_[k] && npos_fits(c))
-                    st = ins.op == MdxOp::Conv ? conv_as_gemm(k, va, bias, y, c, s)
-                                               : conv_transpose_as_gemm(k, va, bias, y, c, s);
+                if (gemm_elt_ >= 0 && gemm_kp_[k] && npos_fits(c)) {
+                    const bool relu = relu_follows(k);
+                    st = ins.op == MdxOp::Conv ? conv_as_gemm(k, va, bias, relu, y, c, s)
+                                               : conv_transpose_as_gemm(k, va, bias, relu, y, c, s);
+                    relu_done = relu && st == ANCHA_OK;
+                }
                 if (st == ANCHA_E_UNSUPPORTED)
                     st = mdx_conv2d(va, values[ins.inputs[1]], bias, y, c, ins.op == MdxOp::ConvTranspose, s);
                 break;
@@ -371,6 +382,12 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
                 cudaFreeAsync(values[v], s);
                 values[v] = nullptr;
             }
+        if (relu_done) {  // the fused Relu (instruction k + 1): its value is this buffer
+            values[graph.instructions[k + 1].output] = values[ins.output];
+            values[ins.output] = nullptr;
+            --uses[ins.output];
+            ++k;
+        }
     }
     if (st == ANCHA_OK) {
         const Shape4& os = shapes[graph.output];
