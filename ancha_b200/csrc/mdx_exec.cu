@@ -159,21 +159,25 @@ int mdx_permute(const float* x, float* out, const MdxPermute& p, cudaStream_t s)
 }
 
 namespace {
-__global__ void channel_bias_kernel(float* __restrict__ y, const float* __restrict__ bias, int channels,
-                                    int64_t plane, int64_t total, bool relu) {
+// x and y may alias (each element is read, then written, by one thread): no __restrict__.
+__global__ void channel_affine_kernel(const float* x, const float* scale, const float* shift, float* y, int channels,
+                                      int64_t plane, int64_t total, bool relu) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const float v = y[i] + (bias ? bias[(i / plane) % channels] : 0.f);
+        const int c = (int)((i / plane) % channels);
+        float v = x[i];
+        if (scale) v *= scale[c];
+        if (shift) v += shift[c];
         y[i] = relu ? fmaxf(v, 0.f) : v;
     }
 }
 }  // namespace
 
-int mdx_channel_bias(float* y, const float* bias, int64_t batch, int channels, int64_t plane, bool relu,
-                     cudaStream_t s) {
+int mdx_channel_affine(const float* x, const float* scale, const float* shift, float* y, int64_t batch, int channels,
+                       int64_t plane, bool relu, cudaStream_t s) {
     const int64_t total = batch * channels * plane;
-    if (total <= 0 || (!bias && !relu)) return ANCHA_OK;
-    channel_bias_kernel<<<blocks_for(total), kThreads, 0, s>>>(y, bias, channels, plane, total, relu);
-    return check_launch("mdx_channel_bias");
+    if (total <= 0 || (x == y && !scale && !shift && !relu)) return ANCHA_OK;
+    channel_affine_kernel<<<blocks_for(total), kThreads, 0, s>>>(x, scale, shift, y, channels, plane, total, relu);
+    return check_launch("mdx_channel_affine");
 }
 
 int mdx_matmul(const float* a, const float* b, float* out, const MdxMatmul& m, cudaStream_t s) {

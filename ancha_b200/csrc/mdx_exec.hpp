@@ -38,11 +38,12 @@ int mdx_conv2d(const float* x, const float* w, const float* bias, float* out, co
 int mdx_ewise(const float* a, const float* b, float* out, const MdxEwise& e, cudaStream_t s);
 int mdx_permute(const float* x, float* out, const MdxPermute& p, cudaStream_t s);
 int mdx_matmul(const float* a, const float* b, float* out, const MdxMatmul& m, cudaStream_t s);
-// y[i][c][·] += bias[c] (bias may be null), then max(·, 0) when `relu`, for `batch` images of
-// `channels` planes of `plane` elements: the bias (and a following Relu) of a convolution run
-// as a GEMM, whose epilogue bias runs along the other axis.
-int mdx_channel_bias(float* y, const float* bias, int64_t batch, int channels, int64_t plane, bool relu,
-                     cudaStream_t s);
+// y[i][c][·] = x[i][c][·] · scale[c] + shift[c] (scale / shift may be null: 1 / 0), then
+// max(·, 0) when `relu`, for `batch` images of `channels` planes of `plane` elements; x may be
+// y. Serves the bias (and a following Relu) of a convolution run as a GEMM, whose epilogue bias
+// runs along the other axis, and a BatchNormalization with the Relu that follows it.
+int mdx_channel_affine(const float* x, const float* scale, const float* shift, float* y, int64_t batch, int channels,
+                       int64_t plane, bool relu, cudaStream_t s);
 
 // ---- The classic MDX task (src/mdx_runtime.rs) -------------------------------------------------
 

@@ -186,7 +186,7 @@ int MdxModel::conv_as_gemm(size_t k, const float* x, const float* bias, bool rel
         if (st == ANCHA_E_UNSUPPORTED) st = gemm_ffma(g, nullptr, 1, g.m, g.n, gemm_elt_, gemm_elt_, 1, e, s);
     }
     cudaFreeAsync(patches, s);
-    if (st == ANCHA_OK) st = mdx_channel_bias(y, bias, c.n, c.co, npos, relu, s);
+    if (st == ANCHA_OK) st = mdx_channel_affine(y, nullptr, bias, y, c.n, c.co, npos, relu, s);
     return st;
 }
 
@@ -225,7 +225,7 @@ int MdxModel::conv_transpose_as_gemm(size_t k, const float* x, const float* bias
     if (st == ANCHA_OK) st = mdx_shuffle2x2(raw, c.n, c.co, c.h, c.w, y, c.co, 0, s);
     cudaFreeAsync(patches, s);
     cudaFreeAsync(raw, s);
-    if (st == ANCHA_OK) st = mdx_channel_bias(y, bias, c.n, c.co, 4 * npos, relu, s);
+    if (st == ANCHA_OK) st = mdx_channel_affine(y, nullptr, bias, y, c.n, c.co, 4 * npos, relu, s);
     return st;
 }
 
@@ -270,7 +270,8 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
             }
     };
     // conv_gemm: a Relu that is the next instruction and the only consumer of a convolution run
-    // as a GEMM is applied in the convolution's bias pass, and its value is that buffer.
+    // as a GEMM, or of a BatchNormalization, is applied in that instruction's pass, and its value
+    // is that instruction's buffer.
     auto relu_follows = [&](size_t k) {
         const MdxInstruction& ins = graph.instructions[k];
         return k + 1 < graph.instructions.size() && graph.instructions[k + 1].op == MdxOp::Relu &&
@@ -312,6 +313,13 @@ int MdxModel::forward(const float* x, const Shape4& in, float* out, const volati
             case MdxOp::Add:
             case MdxOp::Mul:
             case MdxOp::Bn: {
+                if (ins.op == MdxOp::Bn && gemm_elt_ >= 0 && relu_follows(k)) {
+                    // conv_gemm: the BatchNormalization and the Relu after it in one pass.
+                    st = mdx_channel_affine(va, bn_scale_[k].as<float>(), bn_shift_[k].as<float>(), y, a[0], (int)a[1],
+                                            a[2] * a[3], true, s);
+                    relu_done = st == ANCHA_OK;
+                    break;
+                }
                 MdxEwise e{};
                 e.op = ins.op == MdxOp::Relu ? 0 : ins.op == MdxOp::Add ? 1 : ins.op == MdxOp::Mul ? 2 : 3;
                 const Shape4 sa = strides_of(a);
