@@ -109,7 +109,7 @@ def write_package(directory: str, config: dict, tensors: dict, model_id: str = "
 
 
 def inst_voc_hq2() -> dict:
-    """The ``Config::inst_voc_hq2`` preset (mdx23c.rs:56-74), BASELINE config 4's network."""
+    """The ``Config::inst_voc_hq2`` preset (mdx23c.rs:56-74), the benchmarked MDX23C network."""
     return dict(family="mdx23c", sample_rate=44100, n_fft=8192, hop=1024, bins=4096, frames=256, overlap=8,
                 subbands=4, channels=128, growth=128, scales=5, blocks_per_scale=2, bottleneck_factor=4,
                 scale=[2, 2], stems=["vocals", "instrumental"])

@@ -1,4 +1,5 @@
-"""Synthetic classic MDX-Net graphs (TFC-TDF v1 U-Net) as ONNX, for BASELINE config 5.
+"""Synthetic classic MDX-Net graphs (TFC-TDF v1 U-Net) as ONNX: the classic MDX-Net benchmark
+workload (n_fft 6144, tiles of 3072 bins × 256 frames).
 
 The registered classic MDX checkpoints (crates/ancha-models/src/mdx.rs:36-93) are not available
 here, so this module writes a graph of the same family with random weights: the TFC-TDF v1 U-Net
@@ -36,7 +37,7 @@ from .onnx_writer import Attr, Node, model
 
 @dataclass
 class MdxNetConfig:
-    dim_f: int = 3072      # frequency bins of a tile
+    dim_f: int = 3072      # frequency bins of a tile ("mdx-inst-hq-2")
     dim_t: int = 256       # frames of a tile
     channels: int = 4      # stereo complex input
     growth: int = 48       # channels added per encoder level (stand-in)

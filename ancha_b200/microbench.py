@@ -3,8 +3,8 @@
 The counterpart of the reference's CUDA examples ``crates/ancha-models/examples/
 fused_attention.rs`` (fused vs materialised attention, 13-75) and ``fused_linear.rs``
 (custom GEMM vs Burn matmul, 7-55), on this library's kernels. Shapes are the Mel-Band
-RoFormer's at one 8 s chunk (60 bands × 801 frames, dim 384, 8 × 64 heads) and BASELINE
-config 2 (time axis [B=60, H=8, T, 64] for T ∈ {801, 1601, 3201}; band axis
+RoFormer's at one 8 s chunk (60 bands × 801 frames, dim 384, 8 × 64 heads) and the attention
+benchmark's (time axis [B=60, H=8, T, 64] for T ∈ {801, 1601, 3201}; band axis
 [B=801, H=8, S=60, 64]). Times are CUDA-event averages after warm-up; FLOPs are algorithmic
 (attention 4·B·H·T²·D, GEMM 2·M·N·K with unpadded N).
 
@@ -112,7 +112,7 @@ def run_attention(dtype, reps):
 
 
 def run_mdx23c(dtype_name, reps):
-    """MDX23C inst_voc_hq2 forward (BASELINE config 4's network, synthetic seeded weights) on
+    """MDX23C inst_voc_hq2 forward (the benchmarked network, synthetic seeded weights) on
     one chunk: [1, 4, 4096, 256] → [1, 8, 4096, 256]."""
     import shutil
     import tempfile

@@ -68,7 +68,7 @@ def test_attention_rejects_narrow_heads():
 
 @pytest.mark.parametrize("axis", ["time", "band"])
 def test_config2_attention_with_rope(axis):
-    """non-causal attention with RoPE on q and k, q/k/v ~ N(0, 1).
+    """The attention benchmark: non-causal attention with RoPE on q and k, q/k/v ~ N(0, 1).
     Time axis [B=60, H=8, T=801]; band axis [B=801, H=8, S=60] (a 40-group slice is checked)."""
     rng = np.random.default_rng(7)
     groups, tokens = (60, 801) if axis == "time" else (40, 60)

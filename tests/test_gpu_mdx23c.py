@@ -141,7 +141,7 @@ def test_wide_network_matches_oracle(torch_cuda, tmp_path, precision):
 
 @pytest.mark.parametrize("precision", ["f16", "bf16"])
 def test_full_size_reduced_precision_against_f32(torch_cuda, tmp_path, precision):
-    """inst_voc_hq2 at its native size (BASELINE config 4's network, synthetic weights): the
+    """inst_voc_hq2 at its native size (the benchmarked network, synthetic weights): the
     16-bit implicit-GEMM forward against this library's f32 forward (FFMA GEMMs and patch
     matrices, checked against the oracle above), a size-independent SNR check."""
     from ancha_b200.mdx23c import inst_voc_hq2, random_tensors

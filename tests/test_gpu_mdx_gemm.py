@@ -77,7 +77,7 @@ def test_separate_task_with_gemm_matches_oracle(torch_cuda, mode):
 
 @pytest.mark.parametrize("mode", [None, "f32", "bf16"])
 def test_mdx_net_graph_matches_oracle(torch_cuda, mode):
-    """BASELINE config 5's network family at full depth (five scales) on a small tile."""
+    """The classic MDX-Net benchmark's network family at full depth (five scales) on a small tile."""
     from ancha_b200 import mdx_net as MN
     from ancha_b200.mdx import Graph
     c = MN.MdxNetConfig(dim_f=256, dim_t=64, growth=8, scales=5, layers=3, bottleneck=8)

@@ -3,7 +3,7 @@
 * The reference's hardware contracts on its fixture packages (tests/cuda_contracts.rs:52-104,
   403-461): full separations of the tiny (head_dim 4) and kernel (dim 128, 2×64 heads)
   packages, both families, f32 within 1e-5 of the CPU path.
-* the Mel-Band RoFormer (dim 384, depth 6, 60 mel bands) with seeded
+* The benchmark model: the Mel-Band RoFormer (dim 384, depth 6, 60 mel bands) with seeded
   N(0, 0.02) weights on Gaussian σ=0.1 stereo audio. Tolerances from the task: fp32 max-abs
   waveform error ≤ 1e-4 and SNR ≥ 80 dB; bf16 SNR ≥ 50 dB.
 """
@@ -199,7 +199,7 @@ def bs512_package(tmp_path_factory):
 
 
 def test_config3_bs_roformer_512_parity(bs512_package):
-    """BASELINE config 3's network (BS-RoFormer dim 512, depth 12, 8×64 heads, the 62-band
+    """The BS-RoFormer benchmark network (BS-RoFormer dim 512, depth 12, 8×64 heads, the 62-band
     partition, hop 512, seeded N(0,0.02) weights) on one 1 s chunk (custom context, so the float64
     oracle finishes in well under a minute): fp32 ≤ 1e-4 / ≥ 80 dB; f16 ≥ 50 dB; bf16 (the config's dtype)
     reported, with the operand-rounding floor the Mel model shows (≥ 40 dB here)."""

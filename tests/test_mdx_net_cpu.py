@@ -1,4 +1,4 @@
-"""The synthetic classic MDX-Net graph (ancha_b200/mdx_net.py, BASELINE config 5's workload) on
+"""The synthetic classic MDX-Net graph (ancha_b200/mdx_net.py, the classic MDX-Net benchmark workload) on
 the CPU: the library's graph builder and the oracle agree on its structure, the oracle runs it
 with bounded activations, BatchNormalization folding does not change it, and forward_flops
 equals the multiply-adds the oracle performs."""
