@@ -28,6 +28,9 @@ class Graph:
     def __init__(self, onnx: bytes, device: int = 0, optimized: bool = True, gemm: Optional[str] = None):
         """``gemm``: None runs every operation on its direct kernel; "f32", "bf16" or "f16" runs
         eligible convolutions and constant-weight MatMuls as GEMMs (``ancha_mdx_set_gemm``)."""
+        self._h = None
+        if gemm is not None and gemm not in N.PRECISIONS:
+            raise N.AnchaError(N.E_INVALID, f"unknown conv_gemm precision {gemm!r}")
         handle = C.c_void_p()
         buf = C.create_string_buffer(onnx, len(onnx))
         N.check(N.lib().ancha_mdx_load(buf, len(onnx), int(optimized), device, C.byref(handle)))

@@ -200,6 +200,14 @@ def test_mdx_separate_identity_graph_reconstructs_and_rejects_bad_options():
             M.separate(g, 512, 256, 16, 1.0, x, hop=128, **bad)
 
 
+def test_graph_rejects_unknown_gemm_precision_before_loading():
+    from ancha_b200 import _native as N
+    from ancha_b200.mdx import Graph
+    with pytest.raises(N.AnchaError) as e:
+        Graph(chain_graph(), 0, True, gemm="f8")
+    assert e.value.status == N.E_INVALID
+
+
 def test_reader_accepts_both_protobuf_encodings():
     """onnx.proto is proto2: INTS attributes arrive unpacked from most writers, packed from some,
     and initializers as raw_data or packed float_data. Every combination builds the same graph
