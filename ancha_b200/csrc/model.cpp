@@ -227,17 +227,20 @@ std::unique_ptr<Model> Model::load(const std::string& package, int device, int p
     if (precision != ANCHA_PRECISION_F32 && precision != ANCHA_PRECISION_BF16 &&
         precision != ANCHA_PRECISION_F16)
         bad("unknown precision");
+    std::unique_ptr<Model> m(new Model());
+    m->device = -1;  // no device yet: the destructor leaves the caller's current device alone
+    // The manifest first: an invalid package is rejected before any device work, and the
+    // configuration decides the norm fusion below.
+    m->manifest = Manifest::from_json(Json::parse(read_file(package + "/manifest.json")));
+    m->manifest.validate();
     cudaError_t e = cudaSetDevice(device);
     if (e != cudaSuccess) bad(std::string("cudaSetDevice: ") + cudaGetErrorString(e));
-    std::unique_ptr<Model> m(new Model());
     m->device = device;
     m->precision = precision;
     m->elt_ = precision == ANCHA_PRECISION_BF16 ? ELT_BF16 : precision == ANCHA_PRECISION_F16 ? ELT_F16 : ELT_F32;
     m->fuse_norms_ = m->elt_ != ELT_F32 && m->manifest.config.dim % 32 == 0;
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, device) == cudaSuccess) m->device_name = prop.name;
-    m->manifest = Manifest::from_json(Json::parse(read_file(package + "/manifest.json")));
-    m->manifest.validate();
     const std::string bytes = read_file(package + "/model.safetensors");
     // SHA-256 on another thread while the model is built (weights.rs:29-40).
     std::string digest;

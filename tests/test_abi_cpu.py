@@ -67,3 +67,18 @@ def test_invalid_arguments_are_rejected_before_any_launch():
     h = C.c_void_p()
     assert lib.ancha_model_load(b"/nonexistent-package", 0, 0, C.byref(h)) != N.OK
     assert not h.value
+
+
+def test_model_load_rejects_an_invalid_manifest_before_device_work(tmp_path):
+    """The manifest is read and validated before the device is touched, so without a GPU an
+    invalid package still reports its own error (not a CUDA one)."""
+    import json
+    from ancha_b200 import synthetic
+    pkg = tmp_path / "pkg"
+    synthetic.tiny_package(str(pkg), "mel-band-roformer")
+    m = json.loads((pkg / "manifest.json").read_text())
+    m["config"]["hop"] = 2048
+    (pkg / "manifest.json").write_text(json.dumps(m))
+    h = C.c_void_p()
+    assert N.lib().ancha_model_load(str(pkg).encode(), 0, N.PRECISION_F16, C.byref(h)) == N.E_INVALID
+    assert "hop" in N.last_error() and not h.value
