@@ -46,6 +46,97 @@ __device__ __forceinline__ uint32_t pack2(float a, float b) {
     }
 }
 
+// Packed f32x2 arithmetic (sm_100: one instruction issue for two lanes of work).
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// Softmax exponentials 2^(s·log2 e − m) of one row of scores, split between two pipes: the MUFU
+// unit (ex2.approx, 16 results per SM per clock) and the FMA pipe. With head width 64 a score
+// costs the tensor cores 256 flop, so MUFU alone delivers exponentials at half the rate the
+// tensor cores consume scores; of every 8 column pairs POLY_PAIRS take the FMA-pipe form.
+//
+// FMA-pipe exp2 (Cody–Waite style range reduction, polynomial fitted here): for x =
+// s·log2 e − m, t = x + 1.5·2^23 = 1.5·2^23 + j with j = round(x) (the sum's ulp is 1, so the
+// addition rounds x to an integer held in the low mantissa bits), f = x − (t − 1.5·2^23) = x − j
+// ∈ [−0.5, 0.5] exactly; 2^f ≈ P3(f), a degree-3 minimax fit of 2^f on [−0.5, 0.5] by Remez
+// exchange on the relative error (max 7.5e-5 in f32 Horner evaluation, below the 16-bit
+// rounding of P); and 2^j is added to the exponent field as bits(P) + (bits(t) << 23), the shift
+// keeping j's low 9 bits in two's complement. Scores are clamped to x ≥ −124 first so the
+// result stays a normal number; x ≤ 8 holds by the lazy rescale.
+#ifndef ANCHA_ATTN_POLY_PAIRS
+#define ANCHA_ATTN_POLY_PAIRS 2
+#endif
+constexpr int POLY_PAIRS = ANCHA_ATTN_POLY_PAIRS;
+constexpr float EXP2_ROUND = 12582912.f;  // 1.5·2^23
+constexpr float EXP2_C0 = 0.9999280571937561f, EXP2_C1 = 0.6932609677314758f, EXP2_C2 = 0.2426111251115799f,
+                EXP2_C3 = 0.0551716685295105f;
+
+__device__ __forceinline__ void exp2_fma_pair(uint64_t x, float& e0, float& e1) {
+    const uint64_t t = fadd2(x, f2(EXP2_ROUND, EXP2_ROUND));
+    const uint64_t f = fsub2(x, fsub2(t, f2(EXP2_ROUND, EXP2_ROUND)));
+    uint64_t p = ffma2(f, f2(EXP2_C3, EXP2_C3), f2(EXP2_C2, EXP2_C2));
+    p = ffma2(p, f, f2(EXP2_C1, EXP2_C1));
+    p = ffma2(p, f, f2(EXP2_C0, EXP2_C0));
+    float p0, p1, t0, t1;
+    f2_split(p, p0, p1);
+    f2_split(t, t0, t1);
+    e0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+    e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
+}
+
+// Columns [J0, J0 + 64) of one score row: P as 16-bit pairs into pk (one TMEM store of 32
+// columns), row sums into the packed accumulators sa / sb. s_lo clamps the scores of the
+// FMA-pipe columns to x ≥ −124.
+template <bool BF16, int J0>
+__device__ __forceinline__ void exp_columns(const uint32_t (&s)[4][32], uint32_t (&pk)[32], uint64_t& sa,
+                                            uint64_t& sb, float m_used, float s_lo) {
+    const uint64_t l2 = f2(LOG2E, LOG2E), nm2 = f2(-m_used, -m_used);
+#pragma unroll
+    for (int j = J0; j < J0 + 64; j += 2) {
+        const float s0 = __uint_as_float(s[j / 32][j % 32]), s1 = __uint_as_float(s[j / 32][j % 32 + 1]);
+        float e0, e1;
+        if ((j / 2) % 8 < POLY_PAIRS) {
+            exp2_fma_pair(ffma2(f2(fmaxf(s0, s_lo), fmaxf(s1, s_lo)), l2, nm2), e0, e1);
+        } else {
+            float x0, x1;
+            f2_split(ffma2(f2(s0, s1), l2, nm2), x0, x1);
+            e0 = ex2_approx(x0);
+            e1 = ex2_approx(x1);
+        }
+        if ((j / 2) & 1)
+            sb = fadd2(sb, f2(e0, e1));
+        else
+            sa = fadd2(sa, f2(e0, e1));
+        pk[(j - J0) / 2] = pack2<BF16>(e0, e1);
+    }
+}
+
 // Band-axis kernel (tokens ≤ 64). A persistent CTA walks tiles of two problems: inner groups
 // gi0 and gi0 + 1 of one outer group and head, 128 query rows against one 128-key block
 // whose cross-problem scores are ignored. Tiles stream through a 4-deep ring of Q | K | V
@@ -393,9 +484,18 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_V + (k % PP_KV_STAGES) * QKV_BYTES));
                 // Steps of 16 keys up to the last valid key: P is 0 beyond it.
                 const int steps = min(TILE / 16, (p.tokens - k * TILE + 15) / 16);
-                for (int kk = 0; kk < steps; ++kk)  // 16 keys = 16 rows of 128 bytes = 128 units
-                    umma_f16_ts(tmem + PP_O_COL, tmem + PP_P_COL + kk * 8, v_desc + 128 * kk, p.idesc_o,
-                                (k > 0 || kk > 0) ? 1u : 0u);
+                // 16 keys = 16 rows of 128 bytes = 128 descriptor units; the full-block case is
+                // unrolled (the issuing thread's loop overhead is comparable to an N = 64 UMMA).
+                if (steps == TILE / 16) {
+#pragma unroll
+                    for (int kk = 0; kk < TILE / 16; ++kk)
+                        umma_f16_ts(tmem + PP_O_COL, tmem + PP_P_COL + kk * 8, v_desc + 128 * kk, p.idesc_o,
+                                    (k > 0 || kk > 0) ? 1u : 0u);
+                } else {
+                    for (int kk = 0; kk < steps; ++kk)
+                        umma_f16_ts(tmem + PP_O_COL, tmem + PP_P_COL + kk * 8, v_desc + 128 * kk, p.idesc_o,
+                                    (k > 0 || kk > 0) ? 1u : 0u);
+                }
                 umma_commit(pv_done);
                 return true;
             };
@@ -416,11 +516,27 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
         const uint32_t s_addr = tmem + lane_off;
         const uint32_t o_addr = tmem + lane_off + PP_O_COL;
         const uint32_t p_addr = tmem + lane_off + PP_P_COL;
+        // A warp whose 32 query rows all lie past the last token (in the last tile of a group)
+        // has no output: it computes nothing and only keeps the barrier phases in step. Its
+        // TMEM lanes of P and O hold stale values, which reach only its own (discarded) rows.
+        const bool live = q0 + warp * 32 < p.tokens;
         float m_used = -INFINITY, l = 0.f;
+        float s_lo = 0.f;  // score clamp of the FMA-pipe exp2 columns
         bool ok = true;
         for (int kb = 0; kb < nkb; ++kb) {
             ok = __all_sync(0xffffffffu, mbar_wait(s_full, kb & 1, abort, p.err));
             if (!ok) break;
+            if (!live) {
+                mbar_arrive(s_free);
+                // P(kb − 1) is complete (so the arrival below counts toward P(kb)) once its
+                // product has finished.
+                if (kb > 0) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (kb - 1) & 1, abort, p.err));
+                    if (!ok) break;
+                }
+                mbar_arrive(p_ready);
+                continue;
+            }
             tc_fence_after();
             uint32_t s[4][32];
 #pragma unroll
@@ -430,7 +546,7 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             mbar_arrive(s_free);  // the tensor cores may compute S(kb + 1) now
             const int nvalid = min(TILE, p.tokens - kb * TILE);  // valid keys in this block
             // With at most 64 valid keys S holds keys 0..63 only (N = 64); the masking below
-            // covers the stale columns 64..127 as well.
+            // covers the stale columns 64..127 as well, and their exponentials are skipped.
             const bool half = nvalid <= TILE / 2;
             if (nvalid < TILE) {
 #pragma unroll
@@ -439,11 +555,11 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             }
             float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-            for (int c = 0; c < TILE; c += 4) {
-                mx0 = fmaxf(mx0, __uint_as_float(s[c / 32][c % 32]));
-                mx1 = fmaxf(mx1, __uint_as_float(s[c / 32][c % 32 + 1]));
-                mx2 = fmaxf(mx2, __uint_as_float(s[c / 32][c % 32 + 2]));
-                mx3 = fmaxf(mx3, __uint_as_float(s[c / 32][c % 32 + 3]));
+            for (int c = 0; c < TILE; c += 8) {
+                mx0 = fmax3(mx0, __uint_as_float(s[c / 32][c % 32]), __uint_as_float(s[c / 32][c % 32 + 1]));
+                mx1 = fmax3(mx1, __uint_as_float(s[c / 32][c % 32 + 2]), __uint_as_float(s[c / 32][c % 32 + 3]));
+                mx2 = fmax3(mx2, __uint_as_float(s[c / 32][c % 32 + 4]), __uint_as_float(s[c / 32][c % 32 + 5]));
+                mx3 = fmax3(mx3, __uint_as_float(s[c / 32][c % 32 + 6]), __uint_as_float(s[c / 32][c % 32 + 7]));
             }
             const float m_blk = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * LOG2E;
             float corr = 1.f;
@@ -451,42 +567,47 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 corr = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_blk);
                 m_used = m_blk;
                 l *= corr;
+                s_lo = (m_used - 124.f) * (1.f / LOG2E);
             }
-            // P = 2^(s·log2 e − m_used) as 16-bit pairs, all 128 keys in registers before the
-            // wait for P(kb − 1)·V, which then has had the whole exponential pass to finish.
-            float sum0 = 0.f, sum1 = 0.f;
-            uint32_t pk[2][32];
-#pragma unroll
-            for (int j = 0; j < TILE; j += 2) {
-                const float e0 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32]), LOG2E, -m_used));
-                const float e1 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32 + 1]), LOG2E, -m_used));
-                sum0 += e0;
-                sum1 += e1;
-                pk[j / 64][(j % 64) / 2] = pack2<BF16>(e0, e1);
-            }
-            if (kb > 0) {
-                // P(kb − 1)·V must have finished reading P before it is overwritten, and O must
-                // hold it before a rescale.
-                ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (kb - 1) & 1, abort, p.err));
-                if (!ok) break;
-                tc_fence_after();
-                if (__any_sync(0xffffffffu, corr != 1.f)) {
-                    uint32_t o[2][32];
-                    tmem_ld32(o_addr, o[0]);
-                    tmem_ld32(o_addr + 32, o[1]);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int d = 0; d < 32; ++d) {
-                        o[0][d] = __float_as_uint(__uint_as_float(o[0][d]) * corr);
-                        o[1][d] = __float_as_uint(__uint_as_float(o[1][d]) * corr);
-                    }
-                    tmem_st32(o_addr, o[0]);
-                    tmem_st32(o_addr + 32, o[1]);
+            // P = 2^(s·log2 e − m_used) as 16-bit pairs: keys 0..63 are computed before the wait
+            // for P(kb − 1)·V, which then has had that part of the exponential pass to finish,
+            // and stored; keys 64..127 follow (skipped when the block has at most 64 valid keys:
+            // P·V of such a block reads keys 0..63 only).
+            uint64_t sa = 0, sb = 0;
+            {
+                uint32_t pk[32];
+                exp_columns<BF16, 0>(s, pk, sa, sb, m_used, s_lo);
+                if (kb > 0) {
+                    // P(kb − 1)·V must have finished reading P before it is overwritten, and O
+                    // must hold it before a rescale.
+                    ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (kb - 1) & 1, abort, p.err));
+                    if (!ok) break;
+                    tc_fence_after();
                 }
+                tmem_st32(p_addr, pk);
             }
-            tmem_st32(p_addr, pk[0]);
-            if (!half) tmem_st32(p_addr + 32, pk[1]);  // P·V of a half block reads keys 0..63 only
-            l += sum0 + sum1;
+            if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+                uint32_t o[2][32];
+                tmem_ld32(o_addr, o[0]);
+                tmem_ld32(o_addr + 32, o[1]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int d = 0; d < 32; ++d) {
+                    o[0][d] = __float_as_uint(__uint_as_float(o[0][d]) * corr);
+                    o[1][d] = __float_as_uint(__uint_as_float(o[1][d]) * corr);
+                }
+                tmem_st32(o_addr, o[0]);
+                tmem_st32(o_addr + 32, o[1]);
+            }
+            if (!half) {
+                uint32_t pk[32];
+                exp_columns<BF16, TILE / 2>(s, pk, sa, sb, m_used, s_lo);
+                tmem_st32(p_addr + 32, pk);
+            }
+            float sum0, sum1, sum2, sum3;
+            f2_split(sa, sum0, sum1);
+            f2_split(sb, sum2, sum3);
+            l += (sum0 + sum2) + (sum1 + sum3);
             tmem_wait_st();
             tc_fence_before();
             mbar_arrive(p_ready);
