@@ -329,6 +329,8 @@ int ola_finish(const float* sums, const float* weights, int planes, int64_t leng
 // kernel reads was written by the frames kernel earlier in the same batch. The status word is
 // zeroed by the call itself. The buffer is shared by every call on a device, so calls that may
 // overlap in time (different streams, or different host threads without ordering) race on it.
+// The array belongs to this module's device code: it is resident on every device where the
+// module is loaded (any use of the DSP kernels), whether or not the static entry point is called.
 namespace {
 
 __device__ __align__(256) float g_static_scratch[kStaticIstftScratchFloats];

@@ -141,12 +141,13 @@ ANCHA_API int ancha_istft_masked(const float* packed, const float* masks, int ch
 /* ancha_istft_masked without caller scratch, for callers that cannot allocate device memory:
  * a host whose allocator owns the whole device (a caching pool or fixed arenas that hand
  * out no extra buffers), or a real-time audio thread that must not block on cudaMalloc,
- * which can synchronise the device. No counterpart in the reference (its iSTFT runs on the
- * host, dsp.rs:82-133); same arguments and results as ancha_istft_masked.
+ * which can synchronise the device. No counterpart in the reference; same arguments and
+ * results as ancha_istft_masked.
  *
  * The frames go through a fixed 24 MiB device array inside the library (6 Mi floats per
  * device), processed one chunk and as many stems as fit at a time; the call allocates
- * nothing. Limit: one chunk-stem needs 2·frames·2048 floats, so frames = samples / hop + 1
+ * nothing. The array is part of the library's device code, so it is resident on every device
+ * where the library's DSP kernels are loaded, whether or not this entry point is called. Limit: one chunk-stem needs 2·frames·2048 floats, so frames = samples / hop + 1
  * must be at most 1536; larger calls fail with ANCHA_E_INVALID and a message naming the
  * sizes. `status` is an optional DEVICE pointer to one int: the call sets it to 0, or to a
  * non-zero value if a sample had no window support; no other memory needs to start at zero.

@@ -3,9 +3,10 @@
 Both entry points run the same frame and overlap kernels; the static one feeds them through
 its fixed device scratch one chunk and as many stems as fit at a time. The comparison runs
 two calls in a row with different masks (the second call reuses the scratch the first left
-behind), once with several stems per batch and once at the Mel chunk size where each batch
-holds a single stem. The file name keeps it last in collection so it also runs after every
-other GPU test; it needs nothing from them.
+behind): with several stems in one batch, with a partial last batch of stems (15 + 2 per
+chunk, which checks the mask and output offsets of the second batch and of the second chunk),
+and at the Mel chunk size where each batch holds a single stem. The file name keeps it last in
+collection so it also runs after every other GPU test; it needs nothing from them.
 """
 
 import numpy as np
@@ -37,6 +38,7 @@ def _with_caller_scratch(packed, masks, chunks, stems, samples, hop, zero_dc):
 
 @pytest.mark.parametrize("chunks,stems,samples,hop,zero_dc",
                          [(3, 4, 44100, 441, 0),     # 101 frames: all 4 stems in one batch
+                          (2, 17, 44100, 441, 1),    # 15 + 2 stems per chunk: a partial second batch
                           (2, 2, 352800, 441, 1)])   # Mel chunk, 801 frames: one stem per batch
 def test_static_scratch_matches_caller_scratch(chunks, stems, samples, hop, zero_dc):
     rng = np.random.default_rng(11)
