@@ -32,7 +32,9 @@ def parser() -> argparse.ArgumentParser:
     s.add_argument("--duration", type=float, default=None)
     s.add_argument("--chunk-samples", type=int, default=None)
     s.add_argument("--overlap", type=int, default=None)
-    s.add_argument("--precision", default="bf16", choices=sorted(N.PRECISIONS))
+    # f16 operands meet the 16-bit parity bar (the model's GEMM inputs are unit-normed or bounded
+    # activations, so f16's range suffices); bf16's 8-bit mantissa does not on this model.
+    s.add_argument("--precision", default="f16", choices=sorted(N.PRECISIONS))
     s.add_argument("--batch-chunks", type=int, default=0, help="chunks per model call (0: balanced default)")
     return p
 

@@ -31,8 +31,10 @@ independent, so ranks shard the work with no collective ("scaling": "weak").
   and fp32: model-only ms and TFLOP/s for 16 tiles per GPU (4 calls of batch 4), and end to
   end 64 four-minute tracks sharded over the ranks through ``ancha_mdx_separate_pcm`` (bf16),
   aggregate ×realtime from the slowest rank's summed separation time.
-* ``cpu_baseline``: the numpy oracle (f32, all host cores) on one native chunk (rank 0, N=1).
-* ``--impl reference`` times that CPU port per step instead (the reference itself is Rust and
+* ``cpu_baseline``: the numpy oracle (f32, all host cores) on one native chunk, median of 3
+  after one warm-up (rank 0, N=1). It is a port of the reference CPU path, not the reference's
+  own Burn CPU backend, so ratios against it are ratios against the numpy port.
+* ``--impl reference`` times that CPU port the same way (the reference itself is Rust and
   cannot be built offline).
 """
 from __future__ import annotations
@@ -369,18 +371,20 @@ def run_reference(a):
     ensure_package(a.package, 0)
     _, one = cpu_oracle_chunk(a.package)
     advance = CHUNK / OVERLAP / SR  # new audio per native chunk (s)
-    # One native chunk takes ~30 s on 16 cores: at most 1 warm-up and 3 timed samples, so the
-    # arm ends within a few minutes whatever --steps / --warmup ask for (the line reports the
-    # counts actually run).
-    warmup, steps = min(a.warmup, 1), max(1, min(a.steps, 3))
+    # One native chunk takes ~30 s on 16 cores: one warm-up and 3 timed samples (the median is
+    # reported), so the arm ends within a few minutes whatever --steps / --warmup ask for (the
+    # line reports the counts actually run).
+    warmup, steps = 1, 3
     for _ in range(warmup):
         one()
     times = [one() for _ in range(steps)]
-    t = float(np.mean(times))
+    t = float(np.median(times))
     value = advance / t
     cores = os.cpu_count()
     sample = (f"one native-context chunk (8 s window, {advance:.0f} s of new audio) of the Mel-Band "
-              f"RoFormer per step through the numpy f32 port of the reference CPU path")
+              f"RoFormer per step through the numpy f32 port of the reference CPU path (not the "
+              f"reference's own Burn CPU backend, which cannot be built here); median of {steps} "
+              f"after {warmup} warm-up")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": value, "unit": "×realtime",
         "n_gpus": a.gpus, "steps": steps, "warmup": warmup, "ms_per_step": t * 1e3,
@@ -558,12 +562,15 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
         _, one = cpu_oracle_chunk(a.package)
-        one()
-        tcpu = one()
+        one()  # warm-up
+        times = [one() for _ in range(3)]
+        tcpu = float(np.median(times))
         cpu = {"value": (CHUNK / OVERLAP / SR) / tcpu, "unit": "×realtime", "cores": os.cpu_count(),
                "kind": "port",
                "sample": "one native-context chunk (8 s window, 2 s of new audio) through the numpy "
-                         f"f32 oracle, {tcpu:.1f} s"}
+                         f"f32 port of the reference CPU path (not the reference's Burn CPU backend); "
+                         f"median of 3 after 1 warm-up: {tcpu:.1f} s (samples "
+                         f"{', '.join(f'{x:.1f}' for x in times)} s)"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "×realtime", "n_gpus": world,

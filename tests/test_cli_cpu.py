@@ -23,7 +23,7 @@ def test_reference_flags_map_onto_separate_options():
                                 devices=[3])
     assert parse("a.wav", "--model", "p", "--output", "o", "--devices", "0,1,2").devices == [0, 1, 2]
     d = parse("a.wav", "--model", "p", "-o", "o")
-    assert (d.devices, d.precision, d.chunk_samples, d.overlap) == ([0], "bf16", None, None)
+    assert (d.devices, d.precision, d.chunk_samples, d.overlap) == ([0], "f16", None, None)
 
 
 @pytest.mark.parametrize("argv", [["--backend", "cpu"], ["--device", "0", "--devices", "1"], ["--devices", "x"],
