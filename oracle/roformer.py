@@ -73,7 +73,7 @@ def rope_apply(x: np.ndarray, cos: np.ndarray, sin: np.ndarray, heads: int) -> n
 class Transformer:
     """One axial transformer (``roformer.rs:374-459``) with its folded weights."""
 
-    def __init__(self, w: dict, p: str, c: dict, normalized: bool, dtype):
+    def __init__(self, w: dict, p: str, c: dict, normalized: bool, dtype, wround=None):
         dim, heads, hd = c["dim"], c["heads"], c["head_dim"]
         inner = heads * hd
         root = math.sqrt(dim)
@@ -96,6 +96,9 @@ class Transformer:
         self.out_scale = (w[f"{p}.norm.gamma"].astype(np.float64) * root).astype(dtype) \
             if normalized else None
         self.heads, self.hd, self.dtype = heads, hd, dtype
+        if wround is not None:  # precision study: the folded weights as a 16-bit kernel holds them
+            for name in ("wq", "wk", "wv", "wg", "wo", "w1", "w2"):
+                setattr(self, name, wround(getattr(self, name)).astype(dtype))
 
     def attention(self, x: np.ndarray, tokens_cos_sin) -> np.ndarray:
         """Gated attention block output before the residual (roformer.rs:258-270)."""
@@ -132,9 +135,14 @@ class Transformer:
 
 
 class Roformer:
-    """Band split → ``depth`` × (time, band) transformers → mask heads (network.rs:59-400)."""
+    """Band split → ``depth`` × (time, band) transformers → mask heads (network.rs:59-400).
 
-    def __init__(self, package: str, dtype=np.float64):
+    ``weight_round`` (precision studies only) maps every transformer and mask-head weight matrix,
+    after load-time folding, through a rounding function, e.g. to bf16 or f16 values: the error
+    of that model bounds what any kernel holding those weights in that format can reach.
+    """
+
+    def __init__(self, package: str, dtype=np.float64, weight_round=None):
         with open(os.path.join(package, "manifest.json")) as fh:
             self.manifest = json.load(fh)
         c = self.manifest["config"]
@@ -153,8 +161,8 @@ class Roformer:
             self.split.append((W.T.astype(dtype), wt[f"{p}.1.bias"].astype(dtype)))
         normalized = c["family"] == "mel-band-roformer"
         self.normalized = normalized
-        self.axes = [(Transformer(wt, f"layers.{i}.0", c, normalized, dtype),
-                      Transformer(wt, f"layers.{i}.1", c, normalized, dtype))
+        self.axes = [(Transformer(wt, f"layers.{i}.0", c, normalized, dtype, weight_round),
+                      Transformer(wt, f"layers.{i}.1", c, normalized, dtype, weight_round))
                      for i in range(c["depth"])]
         self.final_norm = None if normalized else \
             (wt["final_norm.gamma"].astype(np.float64) * math.sqrt(dim)).astype(dtype)
@@ -169,7 +177,11 @@ class Roformer:
                 width = len(bins) * 4
                 W = wt[f"{key(hidden_layers)}.weight"].astype(dtype)          # [2·width, in]
                 b = wt[f"{key(hidden_layers)}.bias"].astype(dtype)
-                heads.append((hid, W[:width].T, b[:width], W[width:].T, b[width:]))
+                wv, wg = W[:width].T, W[width:].T
+                if weight_round is not None:
+                    hid = [(weight_round(h).astype(dtype), bh) for h, bh in hid]
+                    wv, wg = weight_round(wv).astype(dtype), weight_round(wg).astype(dtype)
+                heads.append((hid, wv, b[:width], wg, b[width:]))
             self.masks.append(heads)
         unused = set(w) - self._used
         if unused:
