@@ -31,7 +31,8 @@ EXPORTS = ("ancha_last_error", "ancha_version", "ancha_available", "ancha_attent
            "ancha_mdx23c_plan", "ancha_mdx23c_free", "ancha_mdx_graph_inspect", "ancha_mdx_load",
            "ancha_mdx_output_shape", "ancha_mdx_forward", "ancha_mdx_separate_pcm", "ancha_mdx_set_gemm", "ancha_mdx_free",
            "ancha_separate", "ancha_separate_pcm", "ancha_separate_device",
-           "ancha_separate_status", "ancha_chunk_plan", "ancha_chunk_span", "ancha_separate_span",
+           "ancha_separate_status", "ancha_chunk_plan", "ancha_chunk_span", "ancha_chunk_pcm_range",
+           "ancha_separate_span", "ancha_separate_span_device", "ancha_span_add", "ancha_span_finish",
            "ancha_free_string")
 
 
@@ -127,7 +128,11 @@ def lib() -> C.CDLL:
             "ancha_separate_status": (i32, [vp, vp]),
             "ancha_chunk_plan": (i32, [i64, i64, i32, C.POINTER(i64), C.POINTER(i64), C.POINTER(i64)]),
             "ancha_chunk_span": (i32, [i64, i64, i32, i64, i64, C.POINTER(i64), C.POINTER(i64)]),
+            "ancha_chunk_pcm_range": (i32, [i64, i64, i32, i64, i64, C.POINTER(i64), C.POINTER(i64)]),
             "ancha_separate_span": (i32, [vp, fp, i64, i64, i32, i32, i64, i64, vp, fp, fp]),
+            "ancha_separate_span_device": (i32, [vp, vp, i64, i64, i64, i64, i32, i32, i64, i64, vp, vp, vp]),
+            "ancha_span_add": (i32, [vp, vp, i32, i64, i64, vp, i64, vp]),
+            "ancha_span_finish": (i32, [vp, vp, i32, i64, i64, i64, vp, i64, vp, vp]),
             "ancha_free_string": (None, [vp]),
         }
         for name, (res, args) in sig.items():

@@ -181,9 +181,10 @@ __global__ void istft_overlap_kernel(const float* __restrict__ scratch, int64_t 
 }
 
 // Chunk input with reflect / zero tail (runtime.rs:117-142): grid over chunks·2·chunk.
-__global__ void gather_chunks_kernel(const float* __restrict__ planes, int64_t samples,
-                                     ChunkStarts starts, int chunks, int chunk, int64_t border,
-                                     int64_t length, float* __restrict__ out) {
+// planes holds track samples [pcm_lo, pcm_lo + pcm_len) of each channel (row stride pcm_len).
+__global__ void gather_chunks_kernel(const float* __restrict__ planes, int64_t samples, int64_t pcm_lo,
+                                     int64_t pcm_len, ChunkStarts starts, int chunks, int chunk,
+                                     int64_t border, int64_t length, float* __restrict__ out) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)chunks * 2 * chunk) return;
     const int n = (int)(i % chunk);
@@ -194,7 +195,7 @@ __global__ void gather_chunks_kernel(const float* __restrict__ planes, int64_t s
     float v = 0.f;
     if (!(n >= remaining && remaining <= chunk / 2)) {
         const int64_t local = n < remaining ? n : reflect_dev(n, remaining);
-        v = planes[ch * samples + reflect_dev(start + local - border, samples)];
+        v = planes[ch * pcm_len + reflect_dev(start + local - border, samples) - pcm_lo];
     }
     out[i] = v;
 }
@@ -245,6 +246,32 @@ __global__ void finish_kernel(const float* __restrict__ sums, const float* __res
     if (residual && p < 2) residual[i] = input[i] - v;
 }
 
+// sums[p][offset + j] += piece[p][j], weights[offset + j] += piece[planes][j] (a received halo:
+// rows of `count` columns, the weights last).
+__global__ void span_add_kernel(float* __restrict__ sums, float* __restrict__ weights, int planes, int64_t span,
+                                int64_t offset, const float* __restrict__ piece, int64_t count) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)(planes + 1) * count) return;
+    const int p = (int)(i / count);
+    const int64_t j = i % count;
+    if (p < planes) sums[p * span + offset + j] += piece[i];
+    else weights[offset + j] += piece[i];
+}
+
+// out[p][n] = sums[p][offset + n] / weights[offset + n] for n < count (out row stride ld).
+__global__ void span_finish_kernel(const float* __restrict__ sums, const float* __restrict__ weights, int planes,
+                                   int64_t span, int64_t offset, int64_t count, float* __restrict__ out,
+                                   int64_t ld, int* __restrict__ flag) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= planes * count) return;
+    const int64_t p = i / count, n = i % count;
+    const float w = weights[offset + n];
+    if (!(w > 0.f)) atomicOr(flag, 4);
+    const float v = sums[p * span + offset + n] / w;
+    if (!isfinite(v)) atomicOr(flag, 1);
+    out[p * ld + n] = v;
+}
+
 }  // namespace
 
 int dsp_prepare(cudaStream_t s) {
@@ -289,13 +316,33 @@ int istft_masked(const float* packed, const float* masks, int chunks, int stems,
     return check_launch("istft_overlap");
 }
 
-int gather_chunks(const float* planes, int64_t samples, const ChunkStarts& starts, int chunks,
-                  int chunk, int64_t border, int64_t length, float* out, cudaStream_t s) {
+int gather_chunks(const float* planes, int64_t samples, int64_t pcm_lo, int64_t pcm_len, const ChunkStarts& starts,
+                  int chunks, int chunk, int64_t border, int64_t length, float* out, cudaStream_t s) {
     const int64_t n = (int64_t)chunks * 2 * chunk;
     if (n == 0) return ANCHA_OK;
-    gather_chunks_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(planes, samples, starts, chunks,
-                                                                    chunk, border, length, out);
+    gather_chunks_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(planes, samples, pcm_lo, pcm_len, starts,
+                                                                    chunks, chunk, border, length, out);
     return check_launch("gather_chunks");
+}
+
+int span_add(float* sums, float* weights, int planes, int64_t span, int64_t offset, const float* piece,
+             int64_t count, cudaStream_t s) {
+    if (count <= 0) return ANCHA_OK;
+    if (offset < 0 || offset + count > span) return fail(ANCHA_E_INVALID, "span_add: piece outside the span");
+    const int64_t n = (int64_t)(planes + 1) * count;
+    span_add_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(sums, weights, planes, span, offset, piece, count);
+    return check_launch("span_add");
+}
+
+int span_finish(const float* sums, const float* weights, int planes, int64_t span, int64_t offset, int64_t count,
+                float* out, int64_t ld, int* flag, cudaStream_t s) {
+    if (count <= 0) return ANCHA_OK;
+    if (offset < 0 || offset + count > span || ld < count)
+        return fail(ANCHA_E_INVALID, "span_finish: range outside the span");
+    const int64_t n = planes * count;
+    span_finish_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(sums, weights, planes, span, offset, count, out,
+                                                                  ld, flag);
+    return check_launch("span_finish");
 }
 
 int ola_add(const float* y, int chunks, int planes, int chunk, const ChunkStarts& starts,

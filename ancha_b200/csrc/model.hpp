@@ -89,7 +89,8 @@ struct PipelineBuffers {
     int batch = 0;
     int64_t chunk = 0;
     DevBuf audio, packed, masks, scratch, y, flag, acc;
-    DevBuf pcm, span;  // host-PCM separations: the uploaded track and the span accumulators
+    DevBuf pcm, span;  // host-PCM separations: the uploaded track samples and the span accumulators
+    DevBuf halo;       // multi-GPU separations: overlap-add columns received from other GPUs
     DevBuf stems;      // single-device host-PCM separations: the finished stems before the copy
 };
 

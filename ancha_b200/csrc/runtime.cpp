@@ -4,9 +4,12 @@
 // the outputs (float32 WAVs + run.json, atomically published, runtime.rs:240-397).
 //
 // Multi-GPU: the chunk starts are split into contiguous ranges, one host thread and model per
-// GPU. Each GPU overlap-adds its own chunks into a partial sum over its sample span; the
-// spans are added on the host in device order (only the chunk-overlap halos meet), then
-// divided by the summed weights. No collective runs on the compute path.
+// GPU. Each GPU uploads only the track samples its chunks read and overlap-adds its chunks into
+// a partial sum over its sample span, which stays on that GPU. GPU d owns the output samples
+// from the start of its span to the start of the next GPU's span; the columns of its span past
+// that point (the chunk-overlap halo, at most chunk − step samples) are peer-copied to the GPUs
+// that own them and added there. Each GPU then divides and crops its owned range on the device
+// and copies it into the caller's stems. No collective runs on the compute path.
 #include <cuda_runtime.h>
 #include <dirent.h>
 #include <sys/stat.h>
@@ -55,6 +58,37 @@ TrackPlan make_plan(int64_t samples, int64_t chunk, int overlap) {
     return p;
 }
 
+// Track samples [*lo, *hi) read by the reflect-padded chunk gather for padded samples [p0, p1)
+// (p0 < p1): the padded sample p reads track sample reflect(p − border), which is monotone on
+// each fold interval [k·(samples − 1), (k + 1)·(samples − 1)].
+void pcm_range(const TrackPlan& plan, int64_t p0, int64_t p1, int64_t* lo, int64_t* hi) {
+    const int64_t n = plan.samples;
+    if (n <= 1) {
+        *lo = 0;
+        *hi = n;
+        return;
+    }
+    const int64_t n1 = n - 1, period = 2 * n1;
+    auto reflect = [&](int64_t i) {
+        int64_t r = i % period;
+        if (r < 0) r += period;
+        return r < n ? r : period - r;
+    };
+    const int64_t a = p0 - plan.border, b = p1 - plan.border - 1;  // inclusive
+    int64_t mn = n, mx = -1;
+    int64_t k = a >= 0 ? a / n1 : -((-a + n1 - 1) / n1);
+    for (; k * n1 <= b; ++k) {
+        const int64_t q0 = std::max(a, k * n1), q1 = std::min(b, (k + 1) * n1);
+        if (q0 > q1) continue;
+        const int64_t r0 = reflect(q0), r1 = reflect(q1);
+        mn = std::min(mn, std::min(r0, r1));
+        mx = std::max(mx, std::max(r0, r1));
+        if (mn == 0 && mx == n - 1) break;
+    }
+    *lo = mn;
+    *hi = mx + 1;
+}
+
 // Chunks per model call when the caller passes 0: balanced batches of at most 8 (21 chunks run as
 // 3 × 7, 47 as 6 × 8). Bigger batches mean fewer tail waves in the GEMMs and no near-empty last
 // batch; 8 Mel chunks take ~6 GB of activations.
@@ -72,11 +106,12 @@ struct Partial {
     double model_seconds = 0.0;
 };
 
-// Chunks [i0, i1) of `plan` on the model's device: device PCM planes [2][samples] → the
-// weighted overlap-add of those chunks into the device span buffers sums [planes][span] /
-// weights [span] that start at padded-track sample `lo`. Buffers are cached on the model.
-int run_chunks(Model& model, const float* planes, const TrackPlan& plan, size_t i0, size_t i1,
-               int batch, int64_t lo, int64_t span, float* sums, float* weights,
+// Chunks [i0, i1) of `plan` on the model's device: device PCM planes [2][pcm_len] holding track
+// samples [pcm_lo, pcm_lo + pcm_len) → the weighted overlap-add of those chunks into the device
+// span buffers sums [planes][span] / weights [span] that start at padded-track sample `lo`.
+// Buffers are cached on the model.
+int run_chunks(Model& model, const float* planes, int64_t pcm_lo, int64_t pcm_len, const TrackPlan& plan,
+               size_t i0, size_t i1, int batch, int64_t lo, int64_t span, float* sums, float* weights,
                const volatile int* cancel, cudaStream_t s, double* model_seconds) {
     const ModelConfig& c = model.manifest.config;
     const int stems = (int)c.stems.size();
@@ -107,7 +142,7 @@ int run_chunks(Model& model, const float* planes, const TrackPlan& plan, size_t 
         const int nb = (int)std::min<size_t>(batch, i1 - b0);
         ChunkStarts cs{};
         for (int k = 0; k < nb; ++k) cs.v[k] = plan.starts[b0 + k];
-        ANCHA_TRY(gather_chunks(planes, plan.samples, cs, nb, (int)chunk, plan.border, plan.length,
+        ANCHA_TRY(gather_chunks(planes, plan.samples, pcm_lo, pcm_len, cs, nb, (int)chunk, plan.border, plan.length,
                                 p.audio.as<float>(), s));
         ANCHA_TRY(stft_forward(p.audio.as<float>(), nb, (int)chunk, c.hop, p.packed.as<float>(), s));
         auto t0 = Clock::now();
@@ -150,16 +185,20 @@ void run_device(Model& model, const float* planes, const TrackPlan& plan, size_t
         // Device copies of the track and the span accumulators are cached on the model (grown
         // as needed): a per-call cudaMalloc / cudaFree pair would synchronise the device.
         PipelineBuffers& pb = model.pipe;
-        if (pb.pcm.bytes < (size_t)(2 * plan.samples * 4)) pb.pcm.alloc(2 * plan.samples * 4);
+        int64_t pcm_lo = 0, pcm_hi = 0;
+        pcm_range(plan, out.lo, out.hi, &pcm_lo, &pcm_hi);
+        const int64_t pcm_len = pcm_hi - pcm_lo;
+        if (pb.pcm.bytes < (size_t)(2 * pcm_len * 4)) pb.pcm.alloc(2 * pcm_len * 4);
         if (pb.span.bytes < (size_t)(planes_n + 1) * span * 4) pb.span.alloc((size_t)(planes_n + 1) * span * 4);
         float* d_planes = pb.pcm.as<float>();
         float* d_sums = pb.span.as<float>();
         float* d_weights = d_sums + (size_t)planes_n * span;
-        st = cudaMemcpyAsync(d_planes, planes, 2 * plan.samples * 4, cudaMemcpyHostToDevice, s) == cudaSuccess
-                 ? ANCHA_OK : fail(ANCHA_E_CUDA, "upload PCM");
+        for (int ch = 0; ch < 2 && !st; ++ch)
+            st = cudaMemcpyAsync(d_planes + ch * pcm_len, planes + ch * plan.samples + pcm_lo, pcm_len * 4,
+                                 cudaMemcpyHostToDevice, s) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "upload PCM");
         if (!st) st = cudaMemsetAsync(d_sums, 0, (size_t)(planes_n + 1) * span * 4, s) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "memset");
-        if (!st) st = run_chunks(model, d_planes, plan, i0, i1, batch, out.lo, span, d_sums, d_weights, cancel, s,
-                                 &out.model_seconds);
+        if (!st) st = run_chunks(model, d_planes, pcm_lo, pcm_len, plan, i0, i1, batch, out.lo, span, d_sums,
+                                 d_weights, cancel, s, &out.model_seconds);
         if (!st) {
             out.sums.resize((size_t)planes_n * span);
             out.weights.resize((size_t)span);
@@ -209,8 +248,8 @@ PcmResult separate_single(Model& model, const float* planes, const TrackPlan& pl
         st = cudaMemcpyAsync(d_planes, planes, 2 * samples * 4, cudaMemcpyHostToDevice, s) == cudaSuccess
                  ? ANCHA_OK : fail(ANCHA_E_CUDA, "upload PCM");
         if (!st) st = cudaMemsetAsync(d_sums, 0, acc * 4, s) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "memset");
-        if (!st) st = run_chunks(model, d_planes, plan, 0, plan.starts.size(), batch, 0, plan.length, d_sums,
-                                 d_weights, cancel, s, &r.model_seconds);
+        if (!st) st = run_chunks(model, d_planes, 0, samples, plan, 0, plan.starts.size(), batch, 0, plan.length,
+                                 d_sums, d_weights, cancel, s, &r.model_seconds);
         if (!st) st = ola_finish(d_sums, d_weights, planes_n, plan.length, plan.border, samples, nullptr,
                                  pb.stems.as<float>(), nullptr, pb.flag.as<int>() + 1, s);
         if (!st) st = cudaMemcpyAsync(stems_out, pb.stems.p, (size_t)planes_n * samples * 4, cudaMemcpyDeviceToHost,
@@ -228,6 +267,194 @@ PcmResult separate_single(Model& model, const float* planes, const TrackPlan& pl
         st = fail(ANCHA_E_CUDA, ex.what());
     }
     cudaStreamDestroy(s);
+    r.status = st;
+    return r;
+}
+
+// One shard of a multi-GPU separation: chunks [i0, i1) on one GPU, the padded span [lo, hi) they
+// cover, and the padded samples [own_lo, own_hi) whose output this GPU produces.
+struct Shard {
+    Model* model = nullptr;
+    size_t i0 = 0, i1 = 0;
+    int64_t lo = 0, hi = 0, own_lo = 0, own_hi = 0;
+    cudaStream_t stream = nullptr;
+    int status = ANCHA_OK;
+    std::string error;
+    double model_seconds = 0.0;
+    float* sums() const { return model->pipe.span.as<float>(); }
+};
+
+// Chunks [i0, i1) of the shard from host PCM: upload the track samples they read, overlap-add
+// into the device span buffers (enqueued on the shard's stream; no host synchronisation).
+void run_shard(const float* planes, const TrackPlan& plan, int batch, const volatile int* cancel, Shard& sh) {
+    Model& model = *sh.model;
+    int st = cudaSetDevice(model.device) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "cudaSetDevice");
+    const int planes_n = (int)model.manifest.config.stems.size() * 2;
+    const int64_t span = sh.hi - sh.lo;
+    try {
+        PipelineBuffers& pb = model.pipe;
+        int64_t pcm_lo = 0, pcm_hi = 0;
+        pcm_range(plan, sh.lo, sh.hi, &pcm_lo, &pcm_hi);
+        const int64_t pcm_len = pcm_hi - pcm_lo;
+        if (!st && pb.pcm.bytes < (size_t)(2 * pcm_len * 4)) pb.pcm.alloc(2 * pcm_len * 4);
+        if (!st && pb.span.bytes < (size_t)(planes_n + 1) * span * 4) pb.span.alloc((size_t)(planes_n + 1) * span * 4);
+        float* d_planes = pb.pcm.as<float>();
+        float* d_sums = pb.span.as<float>();
+        for (int ch = 0; ch < 2 && !st; ++ch)
+            st = cudaMemcpyAsync(d_planes + ch * pcm_len, planes + ch * plan.samples + pcm_lo, pcm_len * 4,
+                                 cudaMemcpyHostToDevice, sh.stream) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "upload PCM");
+        if (!st) st = cudaMemsetAsync(d_sums, 0, (size_t)(planes_n + 1) * span * 4, sh.stream) == cudaSuccess
+                          ? ANCHA_OK : fail(ANCHA_E_CUDA, "memset");
+        if (!st) st = run_chunks(model, d_planes, pcm_lo, pcm_len, plan, sh.i0, sh.i1, batch, sh.lo, span, d_sums,
+                                 d_sums + (size_t)planes_n * span, cancel, sh.stream, &sh.model_seconds);
+    } catch (const std::exception& ex) {
+        st = fail(ANCHA_E_CUDA, ex.what());
+    }
+    if (st) { sh.status = st; sh.error = ancha_last_error(); }
+}
+
+// Several GPUs: shards of contiguous chunk ranges, then the halo exchange on the device
+// (chunk.rs:77-88 rule: the output is the sum of every chunk's weighted samples over the sum of
+// the weights, so partial spans can be added anywhere before the division).
+PcmResult separate_multi(Model* const* models, int n, const float* planes, const TrackPlan& plan, int batch,
+                         const volatile int* cancel, float* stems_out) {
+    PcmResult r;
+    r.chunks = plan.starts.size();
+    const int64_t samples = plan.samples;
+    const int planes_n = (int)models[0]->manifest.config.stems.size() * 2;
+    const int rows = planes_n + 1;  // sums rows, then the weights row
+    // Contiguous ranges of chunk starts, ceil(chunks / n) per device; empty trailing shards drop out.
+    const size_t per = (plan.starts.size() + n - 1) / n;
+    std::vector<Shard> sh;
+    for (int d = 0; d < n; ++d) {
+        Shard x;
+        x.model = models[d];
+        x.i0 = std::min(plan.starts.size(), d * per);
+        x.i1 = std::min(plan.starts.size(), (d + 1) * per);
+        if (x.i0 >= x.i1) continue;
+        x.lo = plan.starts[x.i0];
+        x.hi = std::min(plan.starts[x.i1 - 1] + plan.chunk, plan.length);
+        sh.push_back(x);
+    }
+    for (size_t k = 0; k < sh.size(); ++k) {
+        sh[k].own_lo = k == 0 ? 0 : sh[k].lo;
+        sh[k].own_hi = k + 1 < sh.size() ? sh[k + 1].lo : plan.length;
+    }
+    std::vector<cudaEvent_t> events;
+    auto cleanup = [&] {
+        for (auto& x : sh)
+            if (x.stream) {
+                cudaSetDevice(x.model->device);
+                cudaStreamSynchronize(x.stream);
+                cudaStreamDestroy(x.stream);
+                x.stream = nullptr;
+            }
+        for (cudaEvent_t e : events) cudaEventDestroy(e);
+        events.clear();
+    };
+    for (auto& x : sh) {
+        if (cudaSetDevice(x.model->device) != cudaSuccess ||
+            cudaStreamCreateWithFlags(&x.stream, cudaStreamNonBlocking) != cudaSuccess) {
+            r.status = fail(ANCHA_E_CUDA, "cudaStreamCreate");
+            cleanup();
+            return r;
+        }
+    }
+    // Phase 1 (one host thread per GPU, so kernel launches overlap): spans on the devices.
+    {
+        std::vector<std::thread> workers;
+        for (auto& x : sh) workers.emplace_back([&, px = &x] { run_shard(planes, plan, batch, cancel, *px); });
+        for (auto& w : workers) w.join();
+    }
+    for (auto& x : sh) {
+        r.model_seconds = std::max(r.model_seconds, x.model_seconds);
+        if (x.status != ANCHA_OK) {
+            r.status = fail(x.status, x.error);
+            cleanup();
+            return r;
+        }
+    }
+    int st = ANCHA_OK;
+    // Phase 2: each shard's span columns inside a later shard's owned range go to that shard's
+    // halo buffer (one peer copy per row, on the sender's stream), which adds them into its own
+    // span once the copies have landed (an event wait on the receiver's stream).
+    for (size_t q = 1; q < sh.size() && !st; ++q) {
+        Shard& rq = sh[q];
+        int64_t total = 0;
+        for (size_t p = 0; p < q; ++p)
+            total += std::max<int64_t>(0, std::min(sh[p].hi, rq.own_hi) - std::max(sh[p].lo, rq.own_lo));
+        if (total == 0) continue;
+        try {
+            cudaSetDevice(rq.model->device);
+            DevBuf& halo = rq.model->pipe.halo;
+            if (halo.bytes < (size_t)rows * total * 4) halo.alloc((size_t)rows * total * 4);
+        } catch (const std::exception& ex) {
+            st = fail(ANCHA_E_CUDA, ex.what());
+            break;
+        }
+        int64_t off = 0;
+        for (size_t p = 0; p < q && !st; ++p) {
+            Shard& sp = sh[p];
+            const int64_t a = std::max(sp.lo, rq.own_lo), b = std::min(sp.hi, rq.own_hi);
+            if (b <= a) continue;
+            const int64_t w = b - a, span_p = sp.hi - sp.lo;
+            float* piece = rq.model->pipe.halo.as<float>() + (size_t)rows * off;
+            cudaSetDevice(sp.model->device);
+            for (int row = 0; row < rows && !st; ++row)
+                st = cudaMemcpyPeerAsync(piece + (size_t)row * w, rq.model->device,
+                                         sp.sums() + (size_t)row * span_p + (a - sp.lo), sp.model->device,
+                                         (size_t)w * 4, sp.stream) == cudaSuccess
+                         ? ANCHA_OK : fail(ANCHA_E_CUDA, "halo peer copy");
+            cudaEvent_t e;
+            if (!st && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) st = fail(ANCHA_E_CUDA, "event");
+            if (st) break;
+            events.push_back(e);
+            if (cudaEventRecord(e, sp.stream) != cudaSuccess) { st = fail(ANCHA_E_CUDA, "event record"); break; }
+            cudaSetDevice(rq.model->device);
+            if (cudaStreamWaitEvent(rq.stream, e, 0) != cudaSuccess) { st = fail(ANCHA_E_CUDA, "event wait"); break; }
+            const int64_t span_q = rq.hi - rq.lo;
+            st = span_add(rq.sums(), rq.sums() + (size_t)planes_n * span_q, planes_n, span_q, a - rq.lo, piece, w,
+                          rq.stream);
+            off += w;
+        }
+    }
+    // Phase 3: each shard divides and crops its owned range and copies it into the caller's stems.
+    for (size_t k = 0; k < sh.size() && !st; ++k) {
+        Shard& x = sh[k];
+        const int64_t o0 = std::max(x.own_lo, plan.border), o1 = std::min(x.own_hi, plan.border + samples);
+        if (o1 <= o0) continue;
+        const int64_t count = o1 - o0, span = x.hi - x.lo;
+        cudaSetDevice(x.model->device);
+        PipelineBuffers& pb = x.model->pipe;
+        try {
+            if (pb.stems.bytes < (size_t)planes_n * count * 4) pb.stems.alloc((size_t)planes_n * count * 4);
+        } catch (const std::exception& ex) {
+            st = fail(ANCHA_E_CUDA, ex.what());
+            break;
+        }
+        st = span_finish(x.sums(), x.sums() + (size_t)planes_n * span, planes_n, span, o0 - x.lo, count,
+                         pb.stems.as<float>(), count, pb.flag.as<int>() + 1, x.stream);
+        for (int p = 0; p < planes_n && !st; ++p)
+            st = cudaMemcpyAsync(stems_out + (size_t)p * samples + (o0 - plan.border),
+                                 pb.stems.as<float>() + (size_t)p * count, (size_t)count * 4, cudaMemcpyDeviceToHost,
+                                 x.stream) == cudaSuccess ? ANCHA_OK : fail(ANCHA_E_CUDA, "download stems");
+    }
+    // Phase 4: status words of every shard.
+    for (auto& x : sh) {
+        if (st) break;
+        cudaSetDevice(x.model->device);
+        int flags[2] = {0, 0};
+        if (cudaMemcpyAsync(flags, x.model->pipe.flag.p, 8, cudaMemcpyDeviceToHost, x.stream) != cudaSuccess) {
+            st = fail(ANCHA_E_CUDA, "read status");
+            break;
+        }
+        int mflag = 0;
+        st = x.model->read_flag(x.stream, &mflag);  // synchronises the stream
+        if (!st && (mflag || (flags[1] & 1))) st = fail(ANCHA_E_NONFINITE, "non-finite chunk output");
+        if (!st && flags[0]) st = fail(ANCHA_E_NONFINITE, "iSTFT has an uncovered sample");
+        if (!st && (flags[1] & 4)) st = fail(ANCHA_E_INVALID, "uncovered overlap-add sample");
+    }
+    cleanup();
     r.status = st;
     return r;
 }
@@ -257,47 +484,7 @@ PcmResult separate_pcm(Model* const* models, int n, const float* planes, int64_t
     if (batch <= 0) batch = default_batch((plan.starts.size() + n - 1) / n);
     batch = std::min(batch, kMaxChunksPerCall);
     if (n == 1) return separate_single(*models[0], planes, plan, batch, cancel, stems_out);
-    const int stems = (int)c.stems.size();
-    const int planes_n = stems * 2;
-    // Contiguous ranges of chunk starts, ceil(chunks / n) per device.
-    const size_t per = (plan.starts.size() + n - 1) / n;
-    std::vector<Partial> parts(n);
-    std::vector<std::thread> workers;
-    for (int d = 0; d < n; ++d) {
-        const size_t i0 = std::min(plan.starts.size(), d * per);
-        const size_t i1 = std::min(plan.starts.size(), (d + 1) * per);
-        workers.emplace_back([&, d, i0, i1] {
-            run_device(*models[d], planes, plan, i0, i1, batch, cancel, parts[d]);
-        });
-    }
-    for (auto& w : workers) w.join();
-    for (auto& p : parts) {
-        r.model_seconds = std::max(r.model_seconds, p.model_seconds);
-        if (p.status != ANCHA_OK) {
-            r.status = fail(p.status, p.error);
-            return r;
-        }
-    }
-    // Add the partial spans in device order, then divide and crop (chunk.rs:77-88,
-    // runtime.rs:210-225).
-    std::vector<float> sums((size_t)planes_n * plan.length, 0.f), weights((size_t)plan.length, 0.f);
-    for (auto& p : parts) {
-        const int64_t span = p.hi - p.lo;
-        if (span <= 0) continue;
-        for (int64_t j = 0; j < span; ++j) weights[p.lo + j] += p.weights[j];
-        for (int q = 0; q < planes_n; ++q)
-            for (int64_t j = 0; j < span; ++j)
-                sums[(size_t)q * plan.length + p.lo + j] += p.sums[(size_t)q * span + j];
-    }
-    for (int64_t j = 0; j < plan.length; ++j)
-        if (!(weights[j] > 0.f)) { r.status = fail(ANCHA_E_INVALID, "uncovered overlap-add sample"); return r; }
-    for (int q = 0; q < planes_n; ++q)
-        for (int64_t i = 0; i < samples; ++i) {
-            const float v = sums[(size_t)q * plan.length + plan.border + i] / weights[plan.border + i];
-            if (!std::isfinite(v)) { r.status = fail(ANCHA_E_NONFINITE, "non-finite chunk output"); return r; }
-            stems_out[(size_t)q * samples + i] = v;
-        }
-    return r;
+    return separate_multi(models, n, planes, plan, batch, cancel, stems_out);
 }
 
 std::string output_stem(const std::string& name) {  // report.rs:24-30
@@ -470,6 +657,71 @@ extern "C" int ancha_separate_span(ancha_model* model, const float* planes, int6
     return ANCHA_OK;
 }
 
+extern "C" int ancha_chunk_pcm_range(int64_t samples, int64_t chunk_samples, int overlap, int64_t first,
+                                     int64_t last, int64_t* lo, int64_t* hi) {
+    if (samples <= 0 || !lo || !hi) return fail(ANCHA_E_INVALID, "chunk_pcm_range: invalid arguments");
+    try {
+        const TrackPlan plan = make_plan(samples, chunk_samples, overlap);
+        const int64_t n = (int64_t)plan.starts.size();
+        if (first < 0 || last > n || first > last)
+            return fail(ANCHA_E_INVALID, "chunk_pcm_range: chunk range outside the plan");
+        if (first == last) {
+            *lo = *hi = 0;
+        } else {
+            pcm_range(plan, plan.starts[first], std::min(plan.starts[last - 1] + plan.chunk, plan.length), lo, hi);
+        }
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
+    }
+    return ANCHA_OK;
+}
+
+extern "C" int ancha_separate_span_device(ancha_model* model, const float* pcm, int64_t pcm_lo, int64_t pcm_len,
+                                          int64_t samples, int64_t chunk_samples, int overlap, int batch_chunks,
+                                          int64_t first, int64_t last, float* sums, float* weights, void* stream) {
+    if (!model || !pcm || !sums || !weights) return fail(ANCHA_E_INVALID, "separate_span_device: null argument");
+    Model& m = *model->impl;
+    const ModelConfig& c = m.manifest.config;
+    TrackPlan plan;
+    try {
+        plan = make_plan(samples, chunk_samples > 0 ? chunk_samples : c.chunk_samples,
+                         overlap > 0 ? overlap : c.overlap);
+    } catch (const std::exception& e) {
+        return fail(ANCHA_E_INVALID, e.what());
+    }
+    if (samples <= 0 || plan.chunk <= c.n_fft / 2) return fail(ANCHA_E_INVALID, "invalid chunk settings");
+    if (first < 0 || last > (int64_t)plan.starts.size() || first >= last)
+        return fail(ANCHA_E_INVALID, "separate_span_device: empty chunk range or outside the plan");
+    const int64_t lo = plan.starts[first], hi = std::min(plan.starts[last - 1] + plan.chunk, plan.length);
+    int64_t need_lo = 0, need_hi = 0;
+    pcm_range(plan, lo, hi, &need_lo, &need_hi);
+    if (pcm_lo < 0 || pcm_len <= 0 || pcm_lo > need_lo || pcm_lo + pcm_len < need_hi || pcm_lo + pcm_len > samples)
+        return fail(ANCHA_E_INVALID, "separate_span_device: the PCM slice does not hold samples [" +
+                                         std::to_string(need_lo) + ", " + std::to_string(need_hi) + ")");
+    const int batch = batch_chunks > 0 ? std::min(batch_chunks, kMaxChunksPerCall) : default_batch((size_t)(last - first));
+    cudaStream_t s = as_stream(stream);
+    ANCHA_CUDA(cudaSetDevice(m.device));
+    const int planes_n = (int)c.stems.size() * 2;
+    ANCHA_CUDA(cudaMemsetAsync(sums, 0, (size_t)planes_n * (hi - lo) * 4, s));
+    ANCHA_CUDA(cudaMemsetAsync(weights, 0, (size_t)(hi - lo) * 4, s));
+    return run_chunks(m, pcm, pcm_lo, pcm_len, plan, (size_t)first, (size_t)last, batch, lo, hi - lo, sums, weights,
+                      nullptr, s, nullptr);
+}
+
+extern "C" int ancha_span_add(float* sums, float* weights, int planes, int64_t span, int64_t offset,
+                              const float* piece, int64_t count, void* stream) {
+    if (!sums || !weights || !piece || planes <= 0 || span <= 0 || count < 0)
+        return fail(ANCHA_E_INVALID, "span_add: invalid arguments");
+    return span_add(sums, weights, planes, span, offset, piece, count, as_stream(stream));
+}
+
+extern "C" int ancha_span_finish(const float* sums, const float* weights, int planes, int64_t span, int64_t offset,
+                                 int64_t count, float* out, int64_t ld, int* flag, void* stream) {
+    if (!sums || !weights || !out || !flag || planes <= 0 || span <= 0 || count < 0)
+        return fail(ANCHA_E_INVALID, "span_finish: invalid arguments");
+    return span_finish(sums, weights, planes, span, offset, count, out, ld, flag, as_stream(stream));
+}
+
 extern "C" int ancha_separate_device(ancha_model* model, const float* planes, int64_t samples,
                                      int64_t chunk_samples, int overlap, int batch_chunks,
                                      float* stems, void* stream) {
@@ -499,7 +751,7 @@ extern "C" int ancha_separate_device(ancha_model* model, const float* planes, in
     float* sums = p.acc.as<float>();
     float* weights = sums + (size_t)planes_n * plan.length;
     ANCHA_CUDA(cudaMemsetAsync(sums, 0, (size_t)(planes_n + 1) * plan.length * 4, s));
-    ANCHA_TRY(run_chunks(m, planes, plan, 0, plan.starts.size(), batch, 0, plan.length, sums, weights,
+    ANCHA_TRY(run_chunks(m, planes, 0, samples, plan, 0, plan.starts.size(), batch, 0, plan.length, sums, weights,
                          nullptr, s, nullptr));
     ANCHA_TRY(ola_finish(sums, weights, planes_n, plan.length, plan.border, samples, nullptr, stems,
                          nullptr, p.flag.as<int>() + 1, s));

@@ -2,21 +2,26 @@
 
 The reference separates a track chunk by chunk on one device (``src/runtime.rs:103-225``);
 the chunks are independent until the weighted overlap-add (``chunk.rs:37-88``), so the plan
-shards cleanly: rank r runs a contiguous range of chunk starts on its GPU
-(``ancha_separate_span``) and returns the overlap-add of those chunks over the samples they
-cover. The only exchange is the sum of those partial spans, which overlap where two ranks'
-chunks overlap: each rank places its span in a zero track-length buffer, one ``reduce``
-(SUM) brings them to the destination rank, which divides by the summed weights and crops the
-reflect border exactly as the single-process path does (``runtime.cpp::separate_pcm``).
+shards cleanly: rank r runs a contiguous range of chunk starts on its GPU and keeps the
+overlap-add of those chunks over the samples they cover (its span) in device memory. Each rank
+uploads only the track samples its chunks read (``ancha_chunk_pcm_range``).
 
-The span step is a parameter (``span_fn``) so the sharding and the exchange can run on CPU
-ranks (``gloo``) in tests, with a stand-in for the GPU step.
+Rank r owns the output samples from the start of its span to the start of the next rank's span.
+The only exchange is the chunk-overlap halo: the columns of a rank's span that fall in a later
+rank's owned range (at most chunk − step samples, times stems·2 + 1 rows) are sent to that rank
+(point-to-point, NCCL on GPUs, gloo on CPU) and added into its span there. Each rank then divides
+and crops its owned range on its own device, and one gather brings the stems to the destination
+rank, which is the single-process result (``runtime.cpp::separate_pcm``).
+
+The per-rank steps are an object (``ShardOps``) so the sharding and the exchange can run on CPU
+ranks (``gloo``) in tests, with a stand-in for the GPU steps.
 """
 from __future__ import annotations
 
+import abc
 import ctypes as C
 from dataclasses import dataclass
-from typing import Callable, Optional, Tuple
+from typing import List, Optional, Tuple
 
 import numpy as np
 
@@ -39,6 +44,13 @@ class ChunkPlan:
         N.check(N.lib().ancha_chunk_plan(samples, chunk_samples, overlap, C.byref(n), C.byref(b), C.byref(l)))
         return ChunkPlan(samples, chunk_samples, overlap, n.value, b.value, l.value)
 
+    def pcm_range(self, first: int, last: int) -> Tuple[int, int]:
+        """Track samples ``[lo, hi)`` read by chunks ``[first, last)`` (reflect padding)."""
+        lo, hi = C.c_int64(), C.c_int64()
+        N.check(N.lib().ancha_chunk_pcm_range(self.samples, self.chunk_samples, self.overlap, first, last,
+                                              C.byref(lo), C.byref(hi)))
+        return lo.value, hi.value
+
     def span(self, first: int, last: int) -> Tuple[int, int]:
         """Padded-track samples ``[lo, hi)`` covered by chunks ``[first, last)``."""
         lo, hi = C.c_int64(), C.c_int64()
@@ -57,58 +69,179 @@ def shard(chunks: int, rank: int, world: int) -> Tuple[int, int]:
     return first, min(chunks, first + per)
 
 
-SpanFn = Callable[[np.ndarray, ChunkPlan, int, int], Tuple[np.ndarray, np.ndarray]]
+def ownership(plan: ChunkPlan, world: int) -> List[Optional[Tuple[int, int]]]:
+    """Padded-track samples ``[lo, hi)`` whose output each rank produces (None: empty shard):
+    from the start of the rank's span to the start of the next non-empty rank's span."""
+    ranks = [r for r in range(world) if shard(plan.chunks, r, world)[1] > shard(plan.chunks, r, world)[0]]
+    own: List[Optional[Tuple[int, int]]] = [None] * world
+    for k, r in enumerate(ranks):
+        lo = 0 if k == 0 else plan.span(*shard(plan.chunks, r, world))[0]
+        hi = plan.span(*shard(plan.chunks, ranks[k + 1], world))[0] if k + 1 < len(ranks) else plan.length
+        own[r] = (lo, hi)
+    return own
 
 
-def gpu_span(model, batch_chunks: int = 0, cancel: Optional[C.c_int] = None) -> SpanFn:
-    """The GPU step: ``ancha_separate_span`` of ``model`` (an :class:`ancha_b200.model.Roformer`)."""
+class ShardOps(abc.ABC):
+    """The per-rank steps of :func:`separate_distributed` (tensors on ``device``)."""
 
-    def run(planes: np.ndarray, plan: ChunkPlan, first: int, last: int):
+    device = None
+
+    @abc.abstractmethod
+    def span(self, planes: np.ndarray, plan: ChunkPlan, first: int, last: int):
+        """Overlap-add of chunks ``[first, last)``: sums ``[planes_out, hi − lo]`` and weights
+        ``[hi − lo]`` over ``plan.span(first, last)``."""
+
+    @abc.abstractmethod
+    def add(self, sums, weights, offset: int, piece) -> None:
+        """Add a received ``[planes_out + 1, w]`` piece at span column ``offset``."""
+
+    @abc.abstractmethod
+    def finish(self, sums, weights, offset: int, count: int):
+        """``sums[:, offset:offset + count] / weights[offset:offset + count]``."""
+
+    def check(self) -> None:
+        """Raise if a device status word reports an error (synchronises)."""
+
+
+class GpuShard(ShardOps):
+    """The GPU steps for a :class:`ancha_b200.model.Roformer` on the current CUDA device:
+    ``ancha_separate_span_device``, ``ancha_span_add`` and ``ancha_span_finish`` on torch's
+    current stream (which the process group's collectives follow)."""
+
+    def __init__(self, model, batch_chunks: int = 0):
+        import torch
+        self.model, self.batch = model, batch_chunks
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.planes_out = model.stems * 2
+
+    def _stream(self):
+        import torch
+        return C.c_void_p(torch.cuda.current_stream(self.device).cuda_stream)
+
+    def span(self, planes, plan, first, last):
+        import torch
         lo, hi = plan.span(first, last)
-        sums = np.zeros((model.stems * 2, hi - lo), dtype=np.float32)
-        weights = np.zeros(hi - lo, dtype=np.float32)
-        if last > first:
-            fp = C.POINTER(C.c_float)
-            N.check(N.lib().ancha_separate_span(
-                model.handle, planes.ctypes.data_as(fp), plan.samples, plan.chunk_samples, plan.overlap,
-                batch_chunks, first, last, None if cancel is None else C.byref(cancel),
-                sums.ctypes.data_as(fp), weights.ctypes.data_as(fp)))
+        plo, phi = plan.pcm_range(first, last)
+        pcm = torch.from_numpy(np.ascontiguousarray(planes[:, plo:phi])).to(self.device)
+        sums = torch.empty((self.planes_out, hi - lo), dtype=torch.float32, device=self.device)
+        weights = torch.empty(hi - lo, dtype=torch.float32, device=self.device)
+        N.check(N.lib().ancha_separate_span_device(
+            self.model.handle, pcm.data_ptr(), plo, phi - plo, plan.samples, plan.chunk_samples, plan.overlap,
+            self.batch, first, last, sums.data_ptr(), weights.data_ptr(), self._stream()))
+        self._pcm = pcm  # kept alive until the enqueued work has read it
         return sums, weights
 
-    return run
+    def add(self, sums, weights, offset, piece):
+        N.check(N.lib().ancha_span_add(sums.data_ptr(), weights.data_ptr(), self.planes_out, sums.shape[1],
+                                       offset, piece.data_ptr(), piece.shape[1], self._stream()))
+
+    def finish(self, sums, weights, offset, count):
+        import torch
+        out = torch.empty((self.planes_out, count), dtype=torch.float32, device=self.device)
+        N.check(N.lib().ancha_span_finish(sums.data_ptr(), weights.data_ptr(), self.planes_out, sums.shape[1],
+                                          offset, count, out.data_ptr(), count, self.flag.data_ptr(),
+                                          self._stream()))
+        return out
+
+    def check(self):
+        N.check(N.lib().ancha_separate_status(self.model.handle, self._stream()))
+        bits = int(self.flag.item())
+        self.flag.zero_()
+        if bits & 1:
+            raise N.AnchaError(N.E_NONFINITE, "non-finite chunk output")
+        if bits & 4:
+            raise N.AnchaError(N.E_INVALID, "uncovered overlap-add sample")
 
 
-def separate_distributed(planes: np.ndarray, plan: ChunkPlan, span_fn: SpanFn, planes_out: int,
-                         group=None, dst: int = 0) -> Optional[np.ndarray]:
+def separate_distributed(planes: np.ndarray, plan: ChunkPlan, ops: ShardOps, planes_out: int,
+                         group=None, dst: int = 0, to_host: bool = True):
     """Stems ``[planes_out // 2, 2, samples]`` of host PCM ``planes [2, samples]`` on rank
-    ``dst`` (None on the other ranks). Every rank of ``group`` must call it with the same
-    ``planes`` and ``plan``; each runs ``span_fn`` on its own chunk range."""
+    ``dst`` (None on the other ranks; a device tensor when ``to_host`` is False). Every rank of
+    ``group`` must call it with the same ``planes`` and ``plan``; each runs ``ops`` on its own
+    chunk range."""
     import torch
     import torch.distributed as dist
-    planes = np.ascontiguousarray(planes, dtype=np.float32)
+    planes = np.asarray(planes, dtype=np.float32)
     if planes.ndim != 2 or planes.shape[0] != 2 or planes.shape[1] != plan.samples:
         raise N.AnchaError(N.E_INVALID, "planes must be [2, samples] of the plan's track")
     rank, world = dist.get_rank(group), dist.get_world_size(group)
-    first, last = shard(plan.chunks, rank, world)
-    lo, hi = plan.span(first, last)
-    sums, weights = span_fn(planes, plan, first, last)
-    if sums.shape != (planes_out, hi - lo) or weights.shape != (hi - lo,):
-        raise N.AnchaError(N.E_INVALID, "span step returned the wrong shape")
-    # One buffer [planes_out + 1, length]: the partial sums, then the weights.
-    dev = torch.device("cuda", torch.cuda.current_device()) \
-        if dist.get_backend(group) == "nccl" else torch.device("cpu")
-    acc = torch.zeros((planes_out + 1, plan.length), dtype=torch.float32, device=dev)
-    if hi > lo:
-        acc[:planes_out, lo:hi] = torch.from_numpy(sums).to(dev)
-        acc[planes_out, lo:hi] = torch.from_numpy(weights).to(dev)
-    dist.reduce(acc, dst=dst, op=dist.ReduceOp.SUM, group=group)
+    shards = [shard(plan.chunks, r, world) for r in range(world)]
+    spans = [plan.span(f, l) for f, l in shards]
+    own = ownership(plan, world)
+    first, last = shards[rank]
+    lo, hi = spans[rank]
+    dev = ops.device
+    # Every rank enters the exchange through one collective (the first point-to-point batch of
+    # an NCCL group must not be its first collective), which also reports a rank that failed
+    # before it as an error on its peers.
+    dist.barrier(group=group)
+    sums = weights = None
+    if own[rank] is not None:
+        sums, weights = ops.span(planes, plan, first, last)
+        if tuple(sums.shape) != (planes_out, hi - lo) or tuple(weights.shape) != (hi - lo,):
+            raise N.AnchaError(N.E_INVALID, "span step returned the wrong shape")
+    # Halo exchange: the columns of rank p's span inside rank q's owned range go from p to q.
+    ops_list, received = [], []
+    for q in range(world):
+        if q == rank or own[q] is None or own[rank] is None:
+            continue
+        if q > rank:  # send to later owners
+            a, b = max(lo, own[q][0]), min(hi, own[q][1])
+            if b > a:
+                piece = torch.cat([sums[:, a - lo:b - lo], weights[None, a - lo:b - lo]]).contiguous()
+                ops_list.append(dist.P2POp(dist.isend, piece, q, group))
+        else:  # receive from earlier ranks
+            plo, phi = spans[q]
+            a, b = max(plo, own[rank][0]), min(phi, own[rank][1])
+            if b > a:
+                piece = torch.empty((planes_out + 1, b - a), dtype=torch.float32, device=dev)
+                ops_list.append(dist.P2POp(dist.irecv, piece, q, group))
+                received.append((a, piece))
+    for req in (dist.batch_isend_irecv(ops_list) if ops_list else []):
+        req.wait()
+    for a, piece in received:
+        ops.add(sums, weights, a - lo, piece)
+    # Division and crop of the owned range, then one gather of the stems at dst.
+    pieces = []
+    for r in range(world):
+        if own[r] is None:
+            pieces.append(None)
+            continue
+        o0, o1 = max(own[r][0], plan.border), min(own[r][1], plan.border + plan.samples)
+        pieces.append((o0, o1) if o1 > o0 else None)
+    mine = None
+    if pieces[rank] is not None:
+        o0, o1 = pieces[rank]
+        mine = ops.finish(sums, weights, o0 - lo, o1 - o0)
+    ops.check()
+    out = None
+    gather_ops = []
+    if rank == dst:
+        out = torch.empty((planes_out, plan.samples), dtype=torch.float32, device=dev)
+        parts = []
+        for r in range(world):
+            if pieces[r] is None:
+                continue
+            o0, o1 = pieces[r]
+            if r == rank:
+                out[:, o0 - plan.border:o1 - plan.border] = mine
+            else:
+                buf = torch.empty((planes_out, o1 - o0), dtype=torch.float32, device=dev)
+                gather_ops.append(dist.P2POp(dist.irecv, buf, r, group))
+                parts.append((o0, buf))
+    elif mine is not None:
+        gather_ops.append(dist.P2POp(dist.isend, mine.contiguous(), dst, group))
+    for req in (dist.batch_isend_irecv(gather_ops) if gather_ops else []):
+        req.wait()
     if rank != dst:
         return None
-    acc = acc.cpu().numpy()
-    if not np.all(acc[planes_out] > 0.0):
-        raise N.AnchaError(N.E_INVALID, "uncovered overlap-add sample")
-    w = acc[planes_out, plan.border:plan.border + plan.samples]
-    out = acc[:planes_out, plan.border:plan.border + plan.samples] / w
-    if not np.all(np.isfinite(out)):
+    for o0, buf in parts:
+        out[:, o0 - plan.border:o0 - plan.border + buf.shape[1]] = buf
+    out = out.reshape(planes_out // 2, 2, plan.samples)
+    if not to_host:
+        return out
+    res = out.cpu().numpy()
+    if not np.all(np.isfinite(res)):
         raise N.AnchaError(N.E_NONFINITE, "non-finite chunk output")
-    return out.reshape(planes_out // 2, 2, plan.samples)
+    return res

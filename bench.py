@@ -18,10 +18,15 @@ independent, so ranks shard the work with no collective ("scaling": "weak").
 * ``roofline``: the dominant kernel re-launched alone with CUDA events.
 * ``attention``: BASELINE config 2, the fused attention alone (time axis T = 801 / 1601 / 3201
   and the band axis S = 60) in the bench dtype, and the fp32 (FFMA) variant at T = 801.
+* ``strong_track``: the same Mel-Band RoFormer on ONE 180 s track (96 chunks) split over the
+  ranks (``ancha_b200.distributed``: each rank separates its chunk range from the PCM slice it
+  needs, sends only the chunk-overlap halo of its span to the rank that owns those samples,
+  divides its owned range on its GPU, then one gather of the stems to rank 0), host PCM in and
+  host stems out on rank 0, CUDA events per rank around the whole call, max over ranks,
+  ``"scaling": "strong"``. At N=1 it runs ``ancha_separate_pcm``.
 * ``config3``: BASELINE config 3, BS-RoFormer dim 512, depth 12, 8×64 heads, 62 bands, hop 512,
-  bf16, one 180 s track (chunk 352800, overlap 2 → 47 chunks) sharded over the ranks
-  (``ancha_b200.distributed``: each rank separates its chunk range, one reduce of the spans);
-  host PCM in, host stems out on rank 0, wall clock, ``"scaling": "strong"``.
+  bf16, one 180 s track (chunk 352800, overlap 2 → 47 chunks) split over the ranks the same way,
+  ``"scaling": "strong"``.
 * ``config4``: BASELINE config 4, the MDX23C inst_voc_hq2 forward in bf16, 16 chunks per GPU
   (4 calls of batch 4) on spectra in HBM: ms, TFLOP/s against the measured bf16 peak, and
   model-only ×realtime (0.74 s of new audio per chunk at overlap 8).
@@ -138,35 +143,54 @@ def config5(local: int, world: int, rank: int, dist, steps: int = 2):
             "note": "conv_gemm mode: convolutions, 2x2 transposed convolutions and TDF MatMuls as GEMMs"}
 
 
+def one_track(model, planes, chunk: int, overlap: int, local: int, world: int, dist, steps: int):
+    """One track split over the ranks (``ancha_b200.distributed``: each rank separates its chunk
+    range from the PCM slice it needs, the chunk-overlap halos go to their owners over NCCL, each
+    rank divides its owned range on its GPU, one gather brings the stems to rank 0), or on one GPU
+    through ``ancha_separate_pcm``. Host PCM in, host stems out on rank 0. Returns the median over
+    ``steps`` of the per-step time (s), each step timed with CUDA events on the rank's stream around
+    the whole call, max over ranks, and rank 0's stems."""
+    import torch
+
+    from ancha_b200.distributed import ChunkPlan, GpuShard, separate_distributed
+    from ancha_b200.model import separate_pcm
+    plan = ChunkPlan.of(planes.shape[1], chunk, overlap)
+    ops = GpuShard(model) if dist else None
+
+    def run():
+        if dist:
+            return separate_distributed(planes, plan, ops, model.stems * 2)
+        return separate_pcm([model], planes, chunk, overlap)[0]
+
+    out = run()
+    times = []
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(steps):
+        if dist:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        out = run()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / 1e3], device=f"cuda:{local}")
+        if dist:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        times.append(float(t.item()))
+    return float(np.median(times)), out, plan
+
+
 def config3(local: int, world: int, rank: int, dist, steps: int = 2):
     """BASELINE config 3 (see the module docstring); returns the JSON block on rank 0."""
     from ancha_b200.config import ModelConfig
-    from ancha_b200.distributed import ChunkPlan, gpu_span, separate_distributed
     from ancha_b200.model import Roformer
     pkg = "/tmp/ancha_bench/bs512-seed0"
     ensure_package(pkg, rank if world == 1 else int(os.environ.get("LOCAL_RANK", "0")),
                    ModelConfig.bs_roformer_512())
     model = Roformer(pkg, local, "bf16")
     planes = track(180.0, 3000)
-    plan = ChunkPlan.of(planes.shape[1], model.chunk_samples, model.overlap)
-    span = gpu_span(model, batch_chunks=0)
-
-    def run():
-        if dist:
-            return separate_distributed(planes, plan, span, model.stems * 2)
-        sums, weights = span(planes, plan, 0, plan.chunks)
-        return (sums / weights)[:, plan.border:plan.border + plan.samples]
-
-    run()
-    times = []
-    for _ in range(steps):
-        if dist:
-            dist.barrier()
-        t0 = time.perf_counter()
-        out = run()
-        times.append(time.perf_counter() - t0)
+    t, out, plan = one_track(model, planes, model.chunk_samples, model.overlap, local, world, dist, steps)
     model.close()
-    t = float(np.median(times))  # rank 0's clock includes the reduce, i.e. the slowest rank
     if rank != 0:
         return None
     assert out is not None and np.all(np.isfinite(out))
@@ -174,7 +198,25 @@ def config3(local: int, world: int, rank: int, dist, steps: int = 2):
                         f"chunk {plan.chunk_samples}, overlap {plan.overlap} ({plan.chunks} chunks) sharded "
                         f"over {world} GPU(s)", "value": 180.0 / t, "unit": "×realtime",
             "seconds_per_track": t, "steps": steps, "scaling": "strong", "dtype": "bf16",
-            "timing": "wall clock, host PCM in, host stems out on rank 0, median of steps"}
+            "timing": "CUDA events per rank around the whole call (host PCM in, host stems out on rank 0), "
+                      "max over ranks, median of steps"}
+
+
+def mel_track(model, local: int, world: int, rank: int, dist, precision: str, steps: int = 3):
+    """The Mel-Band RoFormer on ONE 180 s track split over the ranks (strong scaling of the
+    headline model at native context: chunk 352800, overlap 4, 96 chunks)."""
+    planes = track(180.0, 4000)
+    t, out, plan = one_track(model, planes, CHUNK, OVERLAP, local, world, dist, steps)
+    if rank != 0:
+        return None
+    assert out is not None and np.all(np.isfinite(out))
+    return {"workload": f"mel-band-roformer dim384 depth6, {precision}, one 180 s track, chunk {CHUNK}, "
+                        f"overlap {OVERLAP} ({plan.chunks} chunks) sharded over {world} GPU(s)",
+            "value": 180.0 / t, "unit": "×realtime", "seconds_per_track": t, "steps": steps, "scaling": "strong",
+            "dtype": precision, "h2d_bytes_per_step": int(planes.nbytes),
+            "d2h_bytes_per_step": int(model.stems * 2 * planes.shape[1] * 4),
+            "timing": "CUDA events per rank around the whole call (host PCM in, host stems out on rank 0), "
+                      "max over ranks, median of steps"}
 
 
 def config4(local: int, world: int, rank: int, dist, steps: int = 3):
@@ -479,9 +521,8 @@ def main():
     if dist:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_s = float(te.item())
-    span_planes = model.stems * 2 + 1
     e2e = {"value": world * audio_s / e2e_s, "unit": "×realtime",
-           "h2d_bytes_per_step": int(planes.nbytes), "d2h_bytes_per_step": int(span_planes * length * 4)}
+           "h2d_bytes_per_step": int(planes.nbytes), "d2h_bytes_per_step": int(model.stems * 2 * samples * 4)}
 
     # Dominant kernel alone: the FFN-in projection (rows = 60·801, 384 → 1536, GELU epilogue).
     hbm, tc_peak, tc_sus, peak_kind = peaks()
@@ -547,6 +588,8 @@ def main():
                   "gbs": moved / (ms_t / 1e3) / 1e9, "hbm_frac": moved / (ms_t / 1e3) / 1e9 / hbm})
     attention = dict(sweep[0], sweep=sweep[1:])
 
+    strong = mel_track(model, local, world, rank, dist, a.precision)
+
     c3 = None
     if not a.no_config3:
         c3 = config3(local, world, rank, dist)
@@ -585,7 +628,8 @@ def main():
             "clocks": clk.summary(), "e2e": e2e,
             "gpu_launches": launches_per_step(chunks, effective_batch(chunks, a.batch),
                                               fused=a.precision != "f32") * a.steps,
-            "roofline": roofline, "attention": attention, "config3": c3, "config4": c4, "config5": c5,
+            "roofline": roofline, "attention": attention, "strong_track": strong, "config3": c3, "config4": c4,
+            "config5": c5,
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

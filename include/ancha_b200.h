@@ -354,6 +354,37 @@ ANCHA_API int ancha_separate_span(ancha_model* model, const float* planes, int64
                         int64_t chunk_samples, int overlap, int batch_chunks, int64_t first,
                         int64_t last, const volatile int* cancel, float* sums, float* weights);
 
+/* Track samples [*lo, *hi) that chunks [first, last) of the plan read (their reflect-padded
+ * gather; both 0 for an empty range). A process separating that shard needs only this slice
+ * of the PCM. Host-only; no reference counterpart beyond the padding rule of runtime.rs:103-116
+ * and chunk.rs:1-23. */
+ANCHA_API int ancha_chunk_pcm_range(int64_t samples, int64_t chunk_samples, int overlap, int64_t first,
+                          int64_t last, int64_t* lo, int64_t* hi);
+
+/* Device-resident shard of one track (one process per GPU): chunks [first, last) of the plan of a
+ * track of `samples` samples per channel, read from `pcm` (device [2][pcm_len], holding track
+ * samples [pcm_lo, pcm_lo + pcm_len), which must contain ancha_chunk_pcm_range's slice), overlap-
+ * added into device sums[stems·2][hi − lo] and weights[hi − lo] over the span [lo, hi) of
+ * ancha_chunk_span (the call zeroes them). Enqueued on `stream` without a host synchronisation;
+ * ancha_separate_status reports the model's status words. Spans of different shards meet only in
+ * their chunk-overlap columns: adding those (ancha_span_add), dividing and cropping
+ * (ancha_span_finish) gives the stems (chunk.rs:77-88, runtime.rs:210-225). */
+ANCHA_API int ancha_separate_span_device(ancha_model* model, const float* pcm, int64_t pcm_lo, int64_t pcm_len,
+                               int64_t samples, int64_t chunk_samples, int overlap, int batch_chunks,
+                               int64_t first, int64_t last, float* sums, float* weights, void* stream);
+
+/* sums[p][offset + j] += piece[p][j] and weights[offset + j] += piece[planes][j] for j < count:
+ * add overlap-add columns received from another shard (piece: device [planes + 1][count], the
+ * sums rows then the weights row) into a span (device sums[planes][span], weights[span]). */
+ANCHA_API int ancha_span_add(float* sums, float* weights, int planes, int64_t span, int64_t offset,
+                   const float* piece, int64_t count, void* stream);
+
+/* out[p][n] = sums[p][offset + n] / weights[offset + n] for n < count (out: device, row stride
+ * ld): the stems of a span's owned, cropped range. `flag` (device int) gets bit 4 for a zero
+ * weight and bit 1 for a non-finite value (runtime.rs:210-225). */
+ANCHA_API int ancha_span_finish(const float* sums, const float* weights, int planes, int64_t span, int64_t offset,
+                      int64_t count, float* out, int64_t ld, int* flag, void* stream);
+
 /* Device-resident form for one model: planes[2][samples] (device) → stems[stems][2][samples]
  * (device), everything enqueued on `stream` without a host synchronisation (the model's
  * pipeline buffers are allocated on the first call and reused). Status words (non-finite

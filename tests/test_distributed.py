@@ -1,10 +1,12 @@
 """Multi-process separation of one track (ancha_b200.distributed) on CPU ranks (gloo).
 
-Rank r runs a contiguous chunk range; the partial overlap-add spans are summed onto rank 0
-with one reduce. The GPU step is replaced by an identity separation (each chunk's output is
-its own input), so the combined result must reproduce the input track (the fades sum to the
-overlap-add weights), and must equal the single-process overlap-add of the oracle. A rank
-that fails before the exchange must make the others fail with an error, not hang.
+Rank r runs a contiguous chunk range over the PCM slice it needs; the chunk-overlap halos of
+the spans go point to point to the ranks that own those samples, each rank divides its own
+range and one gather brings the stems to rank 0. The GPU steps are replaced by an identity
+separation (each chunk's output is its own input), so the combined result must reproduce the
+input track (the fades sum to the overlap-add weights), and must equal the single-process
+overlap-add of the oracle. A rank that fails before the exchange must make the others fail with
+an error, not hang.
 """
 import os
 import socket
@@ -53,6 +55,27 @@ def test_chunk_plan_rejects_invalid():
         plan.span(3, 2)
 
 
+def test_pcm_range_covers_every_sample_the_gather_reads():
+    from ancha_b200.distributed import ownership
+    from oracle.runtime import chunk_layout
+    for samples, chunk, overlap in [(44100, 8192, 4), (5000, 4096, 2), (3000, 2048, 4), (30000, 6000, 3),
+                                    (1, 4096, 4), (2, 1024, 1)]:
+        plan = ChunkPlan.of(samples, chunk, overlap)
+        _, border, length, starts = chunk_layout(samples, chunk, overlap)
+        period = max(1, 2 * (samples - 1))
+        for first in range(len(starts)):
+            for last in range(first + 1, min(len(starts), first + 4) + 1):
+                lo, hi = plan.span(first, last)
+                q = np.arange(lo, hi) - border
+                r = np.mod(q, period)
+                r = np.where(r < samples, r, period - r) if samples > 1 else np.zeros_like(r)
+                assert plan.pcm_range(first, last) == (int(r.min()), int(r.max()) + 1)
+        for world in (1, 2, 3, 5):
+            own = [o for o in ownership(plan, world) if o is not None]
+            assert own[0][0] == 0 and own[-1][1] == plan.length
+            assert all(a[1] == b[0] for a, b in zip(own, own[1:]))
+
+
 def test_shards_partition_the_plan():
     for chunks in range(0, 40):
         for world in range(1, 9):
@@ -83,7 +106,10 @@ def _oracle_identity(planes, samples, chunk, overlap):
 
 
 @pytest.mark.parametrize("world,samples,chunk,overlap", [(2, 44100, 8192, 4), (2, 30000, 6000, 3),
-                                                         (3, 20000, 4096, 4)])
+                                                         (3, 20000, 4096, 4),
+                                                         # two chunks per rank, a 1536-sample halo: rank
+                                                         # 0's span reaches into rank 2's owned range
+                                                         (4, 3000, 2048, 4)])
 def test_ranks_reproduce_single_process_overlap_add(world, samples, chunk, overlap):
     out = _spawn(world, samples, chunk, overlap)
     for r in range(world):

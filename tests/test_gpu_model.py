@@ -155,40 +155,91 @@ def test_separate_task_writes_reference_outputs(tmp_path, mel_package):
 
 
 def test_span_shards_combine_to_separate_pcm(mel_package):
-    """ancha_separate_span on two chunk ranges, placed at their spans and summed, gives the
-    single-call result; through a one-rank process group separate_distributed is identical."""
+    """Device spans of two chunk ranges (each from only the PCM slice it needs), placed at their
+    spans and summed, give the single-call result; two models sharing the work in one process
+    (the device halo exchange of ancha_separate_pcm) and a one-rank process group through
+    separate_distributed give it too."""
     import datetime
     import socket
 
     import torch.distributed as dist
 
-    from ancha_b200.distributed import ChunkPlan, gpu_span, separate_distributed, shard
+    from ancha_b200.distributed import ChunkPlan, GpuShard, separate_distributed, shard
     rng = np.random.default_rng(12)
     planes = (rng.standard_normal((2, 132300)) * 0.1).astype(np.float32)
     model = Roformer(mel_package, 0, "f16")
     whole, _ = separate_pcm([model], planes, chunk_samples=22050, overlap=2, batch_chunks=3)
+    scale = max(1.0, float(np.max(np.abs(whole))))
     plan = ChunkPlan.of(planes.shape[1], 22050, 2)
-    span = gpu_span(model, batch_chunks=3)
+    ops = GpuShard(model, batch_chunks=3)
     sums = np.zeros((2, plan.length), np.float64)
     weights = np.zeros(plan.length, np.float64)
     for r in range(2):
         first, last = shard(plan.chunks, r, 2)
-        s, w = span(planes, plan, first, last)
+        s, w = ops.span(planes, plan, first, last)
         lo, hi = plan.span(first, last)
-        sums[:, lo:hi] += s
-        weights[lo:hi] += w
+        sums[:, lo:hi] += s.cpu().numpy()
+        weights[lo:hi] += w.cpu().numpy()
+    ops.check()
     got = (sums / weights)[:, plan.border:plan.border + plan.samples]
-    assert np.max(np.abs(got - whole[0])) <= 1e-6 * max(1.0, np.max(np.abs(whole)))
+    assert np.max(np.abs(got - whole[0])) <= 1e-6 * scale
+    # In-process sharding over two models (here on one GPU: the halo copy is a device copy).
+    second = Roformer(mel_package, 0, "f16")
+    for n_chunks in (3, 1):
+        pair, _ = separate_pcm([model, second], planes, chunk_samples=22050, overlap=2, batch_chunks=n_chunks)
+        assert np.max(np.abs(pair - whole)) <= 1e-6 * scale
+    second.close()
     with socket.socket() as sk:
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1,
                             timeout=datetime.timedelta(seconds=60))
     try:
-        one = separate_distributed(planes, plan, span, 2)
+        one = separate_distributed(planes, plan, ops, 2)
     finally:
         dist.destroy_process_group()
     assert np.array_equal(one, whole)
+
+
+def _two_gpu_worker(rank, port, package, out_dir):
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from ancha_b200.distributed import ChunkPlan, GpuShard, separate_distributed
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        rng = np.random.default_rng(13)
+        planes = (rng.standard_normal((2, 441000)) * 0.1).astype(np.float32)
+        model = Roformer(package, rank, "f16")
+        plan = ChunkPlan.of(planes.shape[1], 88200, 4)
+        out = separate_distributed(planes, plan, GpuShard(model, batch_chunks=4), 2)
+        if rank == 0:
+            np.save(f"{out_dir}/two.npy", out)
+            whole, _ = separate_pcm([model], planes, chunk_samples=88200, overlap=4, batch_chunks=4)
+            np.save(f"{out_dir}/whole.npy", whole)
+        model.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_ranks_nccl_halo_exchange(mel_package, tmp_path):
+    """Two processes, one GPU each, NCCL: the device halo exchange and the gather of the stems
+    give the single-GPU result of the same track (10 s, chunk 2 s, overlap 4: 27 chunks)."""
+    import socket
+
+    import torch.multiprocessing as mp
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    mp.start_processes(_two_gpu_worker, args=(port, mel_package, str(tmp_path)), nprocs=2, join=True,
+                       start_method="spawn")
+    two, whole = np.load(tmp_path / "two.npy"), np.load(tmp_path / "whole.npy")
+    assert np.max(np.abs(two - whole)) <= 1e-6 * max(1.0, float(np.max(np.abs(whole))))
 
 
 @pytest.fixture(scope="session")
