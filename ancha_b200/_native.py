@@ -24,7 +24,7 @@ STATUS_NAMES = {OK: "ok", E_UNSUPPORTED: "unsupported", E_INVALID: "invalid", E_
                 E_NONFINITE: "non-finite"}
 
 # Every symbol the header declares (checked by the CPU test suite).
-EXPORTS = ("ancha_last_error", "ancha_version", "ancha_available", "ancha_attention_fwd",
+EXPORTS = ("ancha_last_error", "ancha_version", "ancha_available", "ancha_wait_selftest", "ancha_attention_fwd",
            "ancha_linear_fwd", "ancha_stft_fwd", "ancha_istft_masked", "ancha_istft_masked_static", "ancha_ola_add",
            "ancha_model_load", "ancha_model_info", "ancha_model_forward", "ancha_model_free",
            "ancha_mdx23c_load", "ancha_mdx23c_info", "ancha_mdx23c_forward", "ancha_mdx23c_separate_pcm",
@@ -95,6 +95,7 @@ def lib() -> C.CDLL:
             "ancha_last_error": (C.c_char_p, []),
             "ancha_version": (C.c_char_p, []),
             "ancha_available": (i32, [i32]),
+            "ancha_wait_selftest": (i32, [i64, vp]),
             "ancha_attention_fwd": (i32, [C.POINTER(AttnDesc), vp, vp, vp, vp, vp, vp]),
             "ancha_linear_fwd": (i32, [C.POINTER(LinearDesc), vp, vp, vp, vp, vp, vp, vp]),
             "ancha_stft_fwd": (i32, [vp, i32, i32, i32, vp, vp]),

@@ -13,6 +13,7 @@
 #include "mdx_exec.hpp"
 #include "onnx.hpp"
 #include "model.hpp"
+#include "tc.cuh"
 
 namespace ancha {
 
@@ -44,6 +45,10 @@ extern "C" {
 const char* ancha_last_error(void) { return g_last_error.c_str(); }
 
 const char* ancha_version(void) { return "ancha-b200 0.1.0 (sm_100a)"; }
+
+int ancha_wait_selftest(int64_t budget_cycles, void* stream) {
+    return wait_selftest((long long)budget_cycles, as_stream(stream));
+}
 
 int ancha_available(int device) {
     int count = 0;

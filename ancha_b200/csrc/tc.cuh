@@ -22,6 +22,11 @@ int* device_error_word();
 // Read and clear the device error word (synchronises `s`); ANCHA_E_TIMEOUT if it was set.
 int take_device_error(cudaStream_t s);
 
+// Watchdog self-test: one CTA waits, with a budget of `budget_cycles`, on an mbarrier that
+// nothing arrives at, through the same bounded wait as the tensor-core kernels; returns the
+// status the host reads back (ANCHA_E_TIMEOUT when the watchdog works).
+int wait_selftest(long long budget_cycles, cudaStream_t s);
+
 // Encode a 3-D tiled tensor map over a row-major [depth][rows][cols] array of 2-byte
 // elements (row stride `ld`, depth stride `depth_stride`, in elements) with a
 // {64, box_rows, 1} box and 128-byte swizzle; zero fill out of bounds.
@@ -90,14 +95,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for the phase of `bar` with parity `parity`; false on timeout or when another thread
-// of the CTA aborted (then `abort` is set and the device error word records the timeout).
+// Wait for the phase of `bar` with parity `parity`; false on timeout (after `budget` clock
+// cycles) or when another thread of the CTA aborted (then `abort` is set and the device error
+// word records the timeout).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          int* err) {
+                                          int* err, long long budget = kWaitCycles) {
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
         if (*abort) return false;
-        if (clock64() - t0 > kWaitCycles) {
+        if (clock64() - t0 > budget) {
             *abort = 1;
             if (err) atomicOr(err, ANCHA_DEVICE_TIMEOUT);
             return false;

@@ -53,6 +53,40 @@ int take_device_error(cudaStream_t s) {
     return ANCHA_OK;
 }
 
+namespace {
+// An mbarrier expecting one arrival that never comes: thread 0 waits for its first phase with
+// the given budget, gives up, raises the abort flag and records the timeout in the error word;
+// the other threads of the warp wait on the flag as the kernels' consumer warps do.
+__global__ void wait_selftest_kernel(long long budget, int* err) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort_flag = 0;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    volatile int* abort = &abort_flag;
+    if (threadIdx.x == 0) {
+        mbar_wait(&bar, 0, abort, err, budget);
+    } else {
+        const long long t0 = clock64();
+        while (!*abort && clock64() - t0 < 4 * budget + 1000000) {
+        }
+    }
+}
+}  // namespace
+
+int wait_selftest(long long budget_cycles, cudaStream_t s) {
+    if (budget_cycles < 0 || budget_cycles > kWaitCycles)
+        return fail(ANCHA_E_INVALID, "wait_selftest: budget outside [0, the kernels' budget]");
+    int* w = device_error_word();
+    if (!w) return fail(ANCHA_E_CUDA, "device error word unavailable");
+    wait_selftest_kernel<<<1, 32, 0, s>>>(budget_cycles, w);
+    ANCHA_TRY(check_launch("wait_selftest"));
+    return take_device_error(s);
+}
+
 int make_tma_3d(CUtensorMap* map, const void* base, int elt, int64_t cols, int64_t rows,
                 int64_t depth, int64_t ld, int64_t depth_stride, int box_rows) {
     auto fn = encode_fn();

@@ -123,7 +123,11 @@ class GpuShard(ShardOps):
         import torch
         lo, hi = plan.span(first, last)
         plo, phi = plan.pcm_range(first, last)
-        pcm = torch.from_numpy(np.ascontiguousarray(planes[:, plo:phi])).to(self.device)
+        # One copy per channel row: each row of the slice is contiguous in the caller's array
+        # (asynchronous when that array is in pinned memory).
+        pcm = torch.empty((2, phi - plo), dtype=torch.float32, device=self.device)
+        for ch in range(2):
+            pcm[ch].copy_(torch.from_numpy(planes[ch, plo:phi]), non_blocking=True)
         sums = torch.empty((self.planes_out, hi - lo), dtype=torch.float32, device=self.device)
         weights = torch.empty(hi - lo, dtype=torch.float32, device=self.device)
         N.check(N.lib().ancha_separate_span_device(
@@ -155,11 +159,13 @@ class GpuShard(ShardOps):
 
 
 def separate_distributed(planes: np.ndarray, plan: ChunkPlan, ops: ShardOps, planes_out: int,
-                         group=None, dst: int = 0, to_host: bool = True):
+                         group=None, dst: int = 0, to_host: bool = True, out: Optional[np.ndarray] = None):
     """Stems ``[planes_out // 2, 2, samples]`` of host PCM ``planes [2, samples]`` on rank
     ``dst`` (None on the other ranks; a device tensor when ``to_host`` is False). Every rank of
     ``group`` must call it with the same ``planes`` and ``plan``; each runs ``ops`` on its own
-    chunk range."""
+    chunk range. ``out`` (rank ``dst``, optional) is a C-contiguous float32 host array of the
+    stems' shape to copy into, e.g. a view of pinned memory for a faster download. Non-finite
+    stems are reported by ``ops.check`` from the device status words."""
     import torch
     import torch.distributed as dist
     planes = np.asarray(planes, dtype=np.float32)
@@ -217,6 +223,10 @@ def separate_distributed(planes: np.ndarray, plan: ChunkPlan, ops: ShardOps, pla
     ops.check()
     out = None
     gather_ops = []
+    host_out = out
+    if host_out is not None and (host_out.dtype != np.float32 or not host_out.flags.c_contiguous or
+                                 host_out.shape != (planes_out // 2, 2, plan.samples)):
+        raise N.AnchaError(N.E_INVALID, "out must be a C-contiguous float32 [stems, 2, samples] array")
     if rank == dst:
         out = torch.empty((planes_out, plan.samples), dtype=torch.float32, device=dev)
         parts = []
@@ -241,7 +251,7 @@ def separate_distributed(planes: np.ndarray, plan: ChunkPlan, ops: ShardOps, pla
     out = out.reshape(planes_out // 2, 2, plan.samples)
     if not to_host:
         return out
-    res = out.cpu().numpy()
-    if not np.all(np.isfinite(res)):
-        raise N.AnchaError(N.E_NONFINITE, "non-finite chunk output")
-    return res
+    if host_out is None:
+        return out.cpu().numpy()
+    torch.from_numpy(host_out).copy_(out)
+    return host_out

@@ -25,9 +25,11 @@ def inspect(onnx: bytes, optimized: bool = True) -> dict:
 class Graph:
     """A classic MDX ONNX graph on one GPU (not re-entrant)."""
 
-    def __init__(self, onnx: bytes, device: int = 0, optimized: bool = True, gemm: Optional[str] = None):
-        """``gemm``: None runs every operation on its direct kernel; "f32", "bf16" or "f16" runs
-        eligible convolutions and constant-weight MatMuls as GEMMs (``ancha_mdx_set_gemm``)."""
+    def __init__(self, onnx: bytes, device: int = 0, optimized: bool = True, gemm: Optional[str] = "f32"):
+        """``gemm``: "f32" (the default, as the reference's CUDA path runs ``Graph::forward`` with
+        conv_gemm, mdx.rs:472-530), "bf16" or "f16" runs eligible convolutions and constant-weight
+        MatMuls as GEMMs in that precision (``ancha_mdx_set_gemm``); None runs every operation on
+        its direct kernel."""
         self._h = None
         if gemm is not None and gemm not in N.PRECISIONS:
             raise N.AnchaError(N.E_INVALID, f"unknown conv_gemm precision {gemm!r}")

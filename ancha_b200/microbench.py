@@ -8,7 +8,7 @@ benchmark's (time axis [B=60, H=8, T, 64] for T ∈ {801, 1601, 3201}; band axis
 [B=801, H=8, S=60, 64]). Times are CUDA-event averages after warm-up; FLOPs are algorithmic
 (attention 4·B·H·T²·D, GEMM 2·M·N·K with unpadded N).
 
-    python -m ancha_b200.microbench [--kernel all|gemm|attention|mdx23c] [--reps N] [--dtype f16]
+    python -m ancha_b200.microbench [--kernel all|gemm|attention|mdx23c|mdxnet] [--reps N] [--dtype f16]
 """
 from __future__ import annotations
 
@@ -135,14 +135,31 @@ def run_mdx23c(dtype_name, reps):
              "ms": ms, "tflops": flops / (ms / 1e3) / 1e12, "x_realtime_model_only": step_s / (ms / 1e3)}]
 
 
+def run_mdxnet(dtype_name, reps):
+    """BASELINE config 5's synthetic classic MDX-Net (TFC-TDF v1 ONNX graph, n_fft 6144, dim_f
+    3072, dim_t 256) through the classic MDX executor with conv_gemm in ``dtype_name``: one call of
+    batch 4, [4, 4, 3072, 256]."""
+    import torch
+
+    from .mdx import Graph
+    from .mdx_net import MdxNetConfig, forward_flops, tfc_tdf_v1
+    c = MdxNetConfig()
+    g = Graph(tfc_tdf_v1(c, seed=0), 0, True, gemm=dtype_name)
+    x = torch.randn(4, 4, c.dim_f, c.dim_t, device="cuda") * 0.1
+    ms = _time(lambda: g.forward(x), reps, warmup=2)
+    g.close()
+    return [{"kernel": "mdx_graph_forward", "case": "tfc-tdf v1 batch 4", "dtype": dtype_name, "ms": ms,
+             "tflops": forward_flops(c, 4) / (ms / 1e3) / 1e12}]
+
+
 def main(argv=None):
     import torch
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("--kernel", default="all", choices=["all", "gemm", "attention", "mdx23c"])
+    p.add_argument("--kernel", default="all", choices=["all", "gemm", "attention", "mdx23c", "mdxnet"])
     p.add_argument("--reps", type=int, default=20)
-    p.add_argument("--dtype", default="f16", choices=["f16", "bf16"])
+    p.add_argument("--dtype", default="f16", choices=["f16", "bf16", "f32"])
     a = p.parse_args(argv)
-    dt = torch.float16 if a.dtype == "f16" else torch.bfloat16
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[a.dtype]
     res = []
     if a.kernel in ("all", "gemm"):
         res += run_gemm(dt, a.reps)
@@ -150,6 +167,8 @@ def main(argv=None):
         res += run_attention(dt, a.reps)
     if a.kernel == "mdx23c":
         res += run_mdx23c(a.dtype, a.reps)
+    if a.kernel == "mdxnet":
+        res += run_mdxnet(a.dtype, a.reps)
     for r in res:
         print(json.dumps(r))
 

@@ -71,14 +71,20 @@ class Roformer:
 
 
 def separate_pcm(models: Sequence[Roformer], planes: np.ndarray, chunk_samples: int = 0,
-                 overlap: int = 0, batch_chunks: int = 0, cancel: Optional[C.c_int] = None):
+                 overlap: int = 0, batch_chunks: int = 0, cancel: Optional[C.c_int] = None,
+                 out: Optional[np.ndarray] = None):
     """Stems ``[stems, 2, samples]`` (host f32) for host PCM ``[2, samples]`` on ``models``
-    (one per GPU; chunks are sharded in contiguous ranges). Returns ``(stems, seconds)``."""
+    (one per GPU; chunks are sharded in contiguous ranges). Returns ``(stems, seconds)``.
+    ``out`` (optional) is a C-contiguous float32 array of that shape to write into, e.g. a view
+    of pinned host memory."""
     planes = np.ascontiguousarray(planes, dtype=np.float32)
     if planes.ndim != 2 or planes.shape[0] != 2:
         raise N.AnchaError(N.E_INVALID, "planes must be [2, samples]")
     samples = planes.shape[1]
-    out = np.empty((models[0].stems, 2, samples), dtype=np.float32)
+    if out is None:
+        out = np.empty((models[0].stems, 2, samples), dtype=np.float32)
+    elif out.dtype != np.float32 or not out.flags.c_contiguous or out.shape != (models[0].stems, 2, samples):
+        raise N.AnchaError(N.E_INVALID, "out must be a C-contiguous float32 [stems, 2, samples] array")
     handles = (C.c_void_p * len(models))(*[m.handle for m in models])
     secs = C.c_double()
     fp = C.POINTER(C.c_float)

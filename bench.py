@@ -30,11 +30,11 @@ independent, so ranks shard the work with no collective ("scaling": "weak").
 * ``config4``: BASELINE config 4, the MDX23C inst_voc_hq2 forward in bf16, 16 chunks per GPU
   (4 calls of batch 4) on spectra in HBM: ms, TFLOP/s against the measured bf16 peak, and
   model-only ×realtime (0.74 s of new audio per chunk at overlap 8).
-* ``config5`` (only with ``--config5``; its conv_gemm path has not yet run on a GPU): BASELINE
-  config 5, a synthetic classic MDX-Net (TFC-TDF v1) ONNX graph (``ancha_b200.mdx_net``; n_fft
-  6144, hop 1024, dim_f 3072, dim_t 256) through the classic MDX executor with conv_gemm, bf16
-  and fp32: model-only ms and TFLOP/s for 16 tiles per GPU (4 calls of batch 4), and end to
-  end 64 four-minute tracks sharded over the ranks through ``ancha_mdx_separate_pcm`` (bf16),
+* ``config5`` (``--no-config5`` skips it): BASELINE config 5, a synthetic classic MDX-Net
+  (TFC-TDF v1) ONNX graph (``ancha_b200.mdx_net``; n_fft 6144, hop 1024, dim_f 3072, dim_t 256)
+  through the classic MDX executor with conv_gemm, bf16 and fp32: model-only ms and TFLOP/s for
+  16 tiles per GPU (4 calls of batch 4), and end to end four-minute tracks through
+  ``ancha_mdx_separate_pcm`` (bf16): each rank's share of 64 tracks, at most 8 of them timed,
   aggregate ×realtime from the slowest rank's summed separation time.
 * ``cpu_baseline``: the numpy oracle (f32, all host cores) on one native chunk, median of 3
   after one warm-up (rank 0, N=1). It is a port of the reference CPU path, not the reference's
@@ -74,7 +74,7 @@ def parse():
     p.add_argument("--package", default=os.environ.get("ANCHA_BENCH_PACKAGE", "/tmp/ancha_bench/mel-seed0"))
     p.add_argument("--no-config3", action="store_true")
     p.add_argument("--no-config4", action="store_true")
-    p.add_argument("--config5", action="store_true", help="also run BASELINE config 5 (classic MDX-Net)")
+    p.add_argument("--no-config5", action="store_true")
     p.add_argument("--pipeline-only", action="store_true",
                    help="run only the warm-up and timed pipeline steps (for launch-list captures)")
     return p.parse_args()
@@ -98,7 +98,9 @@ def config5(local: int, world: int, rank: int, dist, steps: int = 2):
             v = float(t.item())
         return v
 
-    ms, e2e_s, tracks = {}, None, 64 // world
+    # End to end: this rank's share of the 64 tracks, at most 8 of them timed (one 4-minute
+    # track takes about a second on one GPU), so the leg stays near ten seconds at any N.
+    ms, e2e_s, tracks = {}, None, min(8, 64 // world)
     for mode in ("bf16", "f32"):
         graph = Graph(onnx, local, True, gemm=mode)
 
@@ -138,8 +140,10 @@ def config5(local: int, world: int, rank: int, dist, steps: int = 2):
             "tflops_per_gpu": {m: flops / (v / 1e3) / 1e12 for m, v in ms.items()},
             "tflops_frac_bf16": flops / (ms["bf16"] / 1e3) / 1e12 / peaks()[1],
             "x_realtime_model_only": {m: new_audio * world / (v / 1e3) for m, v in ms.items()},
-            "e2e": {"tracks": tracks * world, "seconds_each": 240.0, "slowest_rank_s": e2e_s,
-                    "x_realtime": tracks * world * 240.0 / e2e_s, "dtype": "bf16"},
+            "e2e": {"tracks_timed": tracks * world, "of_tracks": 64, "seconds_each": 240.0, "slowest_rank_s": e2e_s,
+                    "x_realtime": tracks * world * 240.0 / e2e_s, "dtype": "bf16",
+                    "timing": "summed separation time per rank (ancha_mdx_separate_pcm, host PCM in, host "
+                              "outputs out), max over ranks"},
             "note": "conv_gemm mode: convolutions, 2x2 transposed convolutions and TDF MatMuls as GEMMs"}
 
 
@@ -156,11 +160,13 @@ def one_track(model, planes, chunk: int, overlap: int, local: int, world: int, d
     from ancha_b200.model import separate_pcm
     plan = ChunkPlan.of(planes.shape[1], chunk, overlap)
     ops = GpuShard(model) if dist else None
+    rank = dist.get_rank() if dist else 0
+    stems = pinned((model.stems, 2, planes.shape[1])) if rank == 0 else None
 
     def run():
         if dist:
-            return separate_distributed(planes, plan, ops, model.stems * 2)
-        return separate_pcm([model], planes, chunk, overlap)[0]
+            return separate_distributed(planes, plan, ops, model.stems * 2, out=stems)
+        return separate_pcm([model], planes, chunk, overlap, out=stems)[0]
 
     out = run()
     times = []
@@ -188,7 +194,7 @@ def config3(local: int, world: int, rank: int, dist, steps: int = 2):
     ensure_package(pkg, rank if world == 1 else int(os.environ.get("LOCAL_RANK", "0")),
                    ModelConfig.bs_roformer_512())
     model = Roformer(pkg, local, "bf16")
-    planes = track(180.0, 3000)
+    planes = pinned_track(180.0, 3000)
     t, out, plan = one_track(model, planes, model.chunk_samples, model.overlap, local, world, dist, steps)
     model.close()
     if rank != 0:
@@ -205,7 +211,7 @@ def config3(local: int, world: int, rank: int, dist, steps: int = 2):
 def mel_track(model, local: int, world: int, rank: int, dist, precision: str, steps: int = 3):
     """The Mel-Band RoFormer on ONE 180 s track split over the ranks (strong scaling of the
     headline model at native context: chunk 352800, overlap 4, 96 chunks)."""
-    planes = track(180.0, 4000)
+    planes = pinned_track(180.0, 4000)
     t, out, plan = one_track(model, planes, CHUNK, OVERLAP, local, world, dist, steps)
     if rank != 0:
         return None
@@ -312,6 +318,19 @@ def ensure_package(path: str, rank: int, config=None):
 def track(seconds: float, seed: int):
     n = int(round(seconds * SR))
     return (np.random.default_rng(seed).standard_normal((2, n)) * 0.1).astype(np.float32)
+
+
+def pinned(shape):
+    """A float32 host array in page-locked memory (the host side of the end-to-end legs)."""
+    import torch
+    return torch.empty(shape, dtype=torch.float32, pin_memory=True).numpy()
+
+
+def pinned_track(seconds: float, seed: int):
+    planes = track(seconds, seed)
+    buf = pinned(planes.shape)
+    buf[...] = planes
+    return buf
 
 
 def plan_chunks(samples: int, chunk=CHUNK, overlap=OVERLAP):
@@ -509,14 +528,20 @@ def main():
     audio_s = samples / SR
     value = world * audio_s / (ms / 1e3)
 
-    # End to end through the public host API (host PCM in, host stems out).
+    # End to end through the public host API (pinned host PCM in, pinned host stems out).
+    h_planes, h_stems = pinned(planes.shape), pinned((model.stems, 2, samples))
+    h_planes[...] = planes
     for _ in range(2):
-        separate_pcm([model], planes, CHUNK, OVERLAP, a.batch)
+        separate_pcm([model], h_planes, CHUNK, OVERLAP, a.batch, out=h_stems)
     barrier()
-    t0 = time.perf_counter()
+    torch.cuda.synchronize()
+    x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    x0.record()
     for _ in range(a.steps):
-        _, secs = separate_pcm([model], planes, CHUNK, OVERLAP, a.batch)
-    e2e_s = (time.perf_counter() - t0) / a.steps
+        _, secs = separate_pcm([model], h_planes, CHUNK, OVERLAP, a.batch, out=h_stems)
+    x1.record()
+    torch.cuda.synchronize()
+    e2e_s = x0.elapsed_time(x1) / 1e3 / a.steps  # CUDA events around the blocking host calls
     te = torch.tensor([e2e_s], device=f"cuda:{local}")
     if dist:
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
@@ -599,7 +624,7 @@ def main():
         c4 = config4(local, world, rank, dist)
 
     c5 = None
-    if a.config5:
+    if not a.no_config5:
         c5 = config5(local, world, rank, dist)
 
     cpu = None

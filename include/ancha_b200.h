@@ -59,6 +59,15 @@ ANCHA_API const char* ancha_version(void);
  * Replaces fused::available::<B>() (fused/mod.rs:249-255) and src/cuda.rs::probe (19-46). */
 ANCHA_API int ancha_available(int device);
 
+/* Watchdog self-test of the current device: one kernel waits, with a budget of `budget_cycles`
+ * SM clock cycles (0 to the kernels' own ~1 s budget), on an mbarrier that nothing arrives at,
+ * through the same bounded wait every tensor-core kernel uses; the kernel gives up, records the
+ * timeout in the library's device error word and returns. Returns ANCHA_E_TIMEOUT (with a
+ * message) when the watchdog works; the device stays usable and the error word is cleared.
+ * Diagnostics of the failure path that src/device.rs:11-41 and tests/cuda_device_failure.rs
+ * cover in the reference; synchronises `stream`. */
+ANCHA_API int ancha_wait_selftest(int64_t budget_cycles, void* stream);
+
 /* ------------------------------------------------------------------------------------ *
  * Kernel plug-in API (replaces crates/ancha-models/src/fused/mod.rs)                   *
  * ------------------------------------------------------------------------------------ */

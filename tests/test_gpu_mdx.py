@@ -23,7 +23,7 @@ def torch_cuda():
 
 def run(torch, onnx, x, optimized=True):
     from ancha_b200.mdx import Graph
-    g = Graph(onnx, 0, optimized)
+    g = Graph(onnx, 0, optimized, gemm=None)  # the direct kernels (conv_gemm: test_gpu_mdx_gemm.py)
     return g.forward(torch.from_numpy(np.asarray(x, np.float32)).cuda()).cpu().numpy().astype(np.float64)
 
 
@@ -143,7 +143,7 @@ def test_separate_task_matches_oracle(torch_cuda, n_fft, hop, bins, opts):
     onnx = shape_preserving_graph()
     x = (np.random.default_rng(7).standard_normal((2, 4000)) * 0.1).astype(np.float32)
     ref_p, ref_r = M.separate(M.Graph(onnx, True), n_fft, bins, 16, 1.035, x.astype(np.float64), hop=hop, **opts)
-    p, r, secs = Graph(onnx).separate_pcm(x, n_fft=n_fft, hop=hop, bins=bins, frames=16, compensate=1.035, **opts)
+    p, r, secs = Graph(onnx, gemm=None).separate_pcm(x, n_fft=n_fft, hop=hop, bins=bins, frames=16, compensate=1.035, **opts)
     err = np.abs(p - ref_p).max() / np.abs(ref_p).max()
     print(f"classic MDX task n_fft {n_fft} {opts}: max |d| / max |ref| {err:.2e}, {secs * 1e3:.1f} ms")
     assert err < 2e-5

@@ -2,10 +2,7 @@
 crates/ancha-models/src/mdx.rs:472-530): eligible convolutions as patch gather + GEMM and
 constant-weight MatMuls as one GEMM, in f32 (FFMA) and with 16-bit operands on the tensor
 cores, against the numpy oracle and against the direct kernels.
-
-These tests have not yet run on a GPU; they run when ANCHA_GPU_PENDING=1 is set.
 """
-import os
 
 import numpy as np
 import pytest
@@ -13,9 +10,7 @@ import pytest
 from ancha_b200 import _native as N
 from oracle import mdx as M
 
-pytestmark = [pytest.mark.gpu,
-              pytest.mark.skipif(os.environ.get("ANCHA_GPU_PENDING") != "1",
-                                 reason="conv_gemm mode not yet run on a GPU (set ANCHA_GPU_PENDING=1)")]
+pytestmark = pytest.mark.gpu
 
 # max |Δ| / max |ref| per mode: f32 as the direct kernels; 16-bit operands on every
 # convolution of a ~10-layer graph. Rounding the operands of exactly the GEMM-run operations
@@ -55,7 +50,7 @@ def test_gemm_off_restores_direct_kernels(torch_cuda):
     from test_gpu_mdx import tfc_tdf_graph
     onnx, _ = tfc_tdf_graph()
     x = np.random.default_rng(4).standard_normal((1, 4, 64, 32))
-    direct = run(torch_cuda, Graph(onnx), x)
+    direct = run(torch_cuda, Graph(onnx, gemm=None), x)
     g = Graph(onnx, 0, True, gemm="f16")
     assert not np.array_equal(run(torch_cuda, g, x), direct)  # the 16-bit path did run
     N.check(N.lib().ancha_mdx_set_gemm(g._h, -1))
