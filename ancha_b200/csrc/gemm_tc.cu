@@ -111,24 +111,32 @@ struct Smem {
     static constexpr int BYTES = 1024 + TILES + STAGING + STAGING16 + 8 * (2 * STAGES + 4) + 16;
 };
 
+// v[j], v[j + 1] = f2 result (the register pairs of the packed arithmetic below).
+__device__ __forceinline__ void put2(float (&v)[32], int j, uint64_t x) { f2_split(x, v[j], v[j + 1]); }
+
 // Bias, activation, RoPE and residual for 32 consecutive accumulator columns c0.. of one
 // row, in registers. Returns the number of output values (32, or 16 for GLU). All indexing
-// of the register arrays is static.
+// of the register arrays is static. The element-wise arithmetic runs on packed f32x2 pairs
+// (one instruction issue per two values): these epilogues are issue-bound.
 __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, bool live, int c0, int n_g,
                                           const uint32_t (&r)[32], float (&v)[32], float row_scale,
                                           float res_scale) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * row_scale;
     const int nv = min(32, n_g - c0);  // valid columns (> 0)
-    if (p.bias) {
+    const uint64_t rs2 = f2(row_scale, row_scale);
+    if (p.bias && nv == 32) {  // v = acc · row_scale + bias
         const float* b = p.bias + (int64_t)(g % p.b_groups) * p.bias_group_stride + c0;
-        if (nv == 32) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const float4 q = *reinterpret_cast<const float4*>(b + j);
-                v[j] += q.x; v[j + 1] += q.y; v[j + 2] += q.z; v[j + 3] += q.w;
-            }
-        } else {
+        for (int j = 0; j < 32; j += 4) {
+            const float4 q = *reinterpret_cast<const float4*>(b + j);
+            put2(v, j, ffma2(f2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), rs2, f2(q.x, q.y)));
+            put2(v, j + 2, ffma2(f2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])), rs2, f2(q.z, q.w)));
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2)
+            put2(v, j, fmul2(f2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), rs2));
+        if (p.bias) {
+            const float* b = p.bias + (int64_t)(g % p.b_groups) * p.bias_group_stride + c0;
 #pragma unroll
             for (int j = 0; j < 32; ++j)
                 if (j < nv) v[j] += b[j];
@@ -136,10 +144,10 @@ __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, boo
     }
     if (p.act == ANCHA_ACT_GELU) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = gelu_fast(v[j]);
+        for (int j = 0; j < 32; j += 2) gelu_fast2(v[j], v[j + 1]);
     } else if (p.act == ANCHA_ACT_TANH) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = tanh_fast(v[j]);
+        for (int j = 0; j < 32; j += 2) tanh_fast2(v[j], v[j + 1]);
     }
     if (p.rope_pairs && c0 < 2 * p.rope_width) {
         const int key = c0 >= p.rope_width;
@@ -147,11 +155,9 @@ __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, boo
         const float2* t = p.rope_pairs +
                           ((int64_t)key * (p.rope_hd / 2) + (c0 % p.rope_hd) / 2) * p.rope_tokens + token;
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
+        for (int j = 0; j < 32; j += 2) {  // (x0·c − x1·s, x1·c + x0·s), packed
             const float2 cs = t[(int64_t)(j / 2) * p.rope_tokens];
-            const float x0 = v[j], x1 = v[j + 1];
-            v[j] = x0 * cs.x - x1 * cs.y;
-            v[j + 1] = x1 * cs.x + x0 * cs.y;
+            put2(v, j, ffma2(f2(v[j + 1], v[j]), f2(-cs.y, cs.y), fmul2(f2(v[j], v[j + 1]), f2(cs.x, cs.x))));
         }
     } else if (p.rope && c0 < 2 * p.rope_width) {
         const int key = c0 >= p.rope_width;
@@ -177,16 +183,15 @@ __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, boo
     }
     if (p.residual && live) {
         const float* rr = p.residual + (int64_t)row * p.ldr + c0;
+        const uint64_t sc2 = f2(res_scale, res_scale);
         if (p.res_col && nv == 32) {
             const float* rc = p.res_col + c0;
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
                 const float4 q = *reinterpret_cast<const float4*>(rr + j);
                 const float4 w = *reinterpret_cast<const float4*>(rc + j);
-                v[j] = fmaf(q.x * res_scale, w.x, v[j]);
-                v[j + 1] = fmaf(q.y * res_scale, w.y, v[j + 1]);
-                v[j + 2] = fmaf(q.z * res_scale, w.z, v[j + 2]);
-                v[j + 3] = fmaf(q.w * res_scale, w.w, v[j + 3]);
+                put2(v, j, ffma2(fmul2(f2(q.x, q.y), sc2), f2(w.x, w.y), f2(v[j], v[j + 1])));
+                put2(v, j + 2, ffma2(fmul2(f2(q.z, q.w), sc2), f2(w.z, w.w), f2(v[j + 2], v[j + 3])));
             }
         } else if (p.res_col) {
 #pragma unroll
@@ -196,10 +201,8 @@ __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, boo
 #pragma unroll
             for (int j = 0; j < 32; j += 4) {
                 const float4 q = *reinterpret_cast<const float4*>(rr + j);
-                v[j] = fmaf(q.x, res_scale, v[j]);
-                v[j + 1] = fmaf(q.y, res_scale, v[j + 1]);
-                v[j + 2] = fmaf(q.z, res_scale, v[j + 2]);
-                v[j + 3] = fmaf(q.w, res_scale, v[j + 3]);
+                put2(v, j, ffma2(f2(q.x, q.y), sc2, f2(v[j], v[j + 1])));
+                put2(v, j + 2, ffma2(f2(q.z, q.w), sc2, f2(v[j + 2], v[j + 3])));
             }
         } else {
 #pragma unroll
@@ -224,9 +227,23 @@ __device__ __forceinline__ float inv_norm(const float* ss, int n, int64_t rows) 
 __device__ __forceinline__ void store_ss(float* ss, const TcParams& p, int row, bool live, int c0, int nv,
                                          const float (&v)[32]) {
     float q = 0.f;
+    if (nv == 32) {  // two packed accumulators
+        uint64_t qa = 0, qb = 0;
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-        if (j < nv) q = fmaf(v[j], v[j], q);
+        for (int j = 0; j < 32; j += 4) {
+            const uint64_t x = f2(v[j], v[j + 1]), y = f2(v[j + 2], v[j + 3]);
+            qa = ffma2(x, x, qa);
+            qb = ffma2(y, y, qb);
+        }
+        float a0, a1, b0, b1;
+        f2_split(qa, a0, a1);
+        f2_split(qb, b0, b1);
+        q = (a0 + b0) + (a1 + b1);
+    } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+            if (j < nv) q = fmaf(v[j], v[j], q);
+    }
     if (live) ss[(int64_t)(c0 / 32) * p.m + row] = q;
 }
 
@@ -236,7 +253,8 @@ __device__ __forceinline__ void scale_cols(const float* col, int c0, int nv, flo
 #pragma unroll
         for (int j = 0; j < 32; j += 4) {
             const float4 c = *reinterpret_cast<const float4*>(col + c0 + j);
-            v[j] *= c.x; v[j + 1] *= c.y; v[j + 2] *= c.z; v[j + 3] *= c.w;
+            f2_split(fmul2(f2(v[j], v[j + 1]), f2(c.x, c.y)), v[j], v[j + 1]);
+            f2_split(fmul2(f2(v[j + 2], v[j + 3]), f2(c.z, c.w)), v[j + 2], v[j + 3]);
         }
     } else {
 #pragma unroll

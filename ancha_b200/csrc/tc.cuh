@@ -282,6 +282,41 @@ __device__ __forceinline__ float rcp_approx(float x) {
     return y;
 }
 
+// Packed f32x2 arithmetic (sm_100: one instruction issue for two lanes of work).
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& a, float& b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fmul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 // Activations of the tensor-core epilogues (f16 / bf16 outputs), built from the MUFU ex2 and
 // rcp instructions plus a few FMAs instead of the libm-accurate erff / tanhf, whose
 // instruction count made the GEMM epilogues issue-bound.
@@ -308,6 +343,32 @@ __device__ __forceinline__ float gelu_fast(float x) {
 __device__ __forceinline__ float tanh_fast(float x) {
     const float e = ex2_approx(2.0f * 1.4426950408889634f * fabsf(x));
     return copysignf(fmaf(-2.0f, rcp_approx(e + 1.0f), 1.0f), x);
+}
+// gelu_fast on two values with the polynomial on packed f32x2 FMAs (same coefficients).
+__device__ __forceinline__ void gelu_fast2(float& x0, float& x1) {
+    const uint64_t v = ffma2(f2(fminf(fabsf(x0), 5.5f), fminf(fabsf(x1), 5.5f)), f2(2.0f / 5.5f, 2.0f / 5.5f),
+                             f2(-1.0f, -1.0f));
+    uint64_t r = ffma2(f2(-0.0022850772365927696f, -0.0022850772365927696f), v,
+                       f2(0.011377031914889812f, 0.011377031914889812f));
+    r = ffma2(r, v, f2(-0.03212796524167061f, -0.03212796524167061f));
+    r = ffma2(r, v, f2(0.07807064056396484f, 0.07807064056396484f));
+    r = ffma2(r, v, f2(-0.1830366849899292f, -0.1830366849899292f));
+    r = ffma2(r, v, f2(-5.023968696594238f, -5.023968696594238f));
+    r = ffma2(r, v, f2(-12.107662200927734f, -12.107662200927734f));
+    r = ffma2(r, v, f2(-8.390584945678711f, -8.390584945678711f));
+    float r0, r1;
+    f2_split(r, r0, r1);
+    x0 = fmaf(-fabsf(x0), ex2_approx(r0), fmaxf(x0, 0.f));
+    x1 = fmaf(-fabsf(x1), ex2_approx(r1), fmaxf(x1, 0.f));
+}
+// tanh(x) = 1 − 2 / (e^(2x) + 1) on two values, packed: the form needs no sign handling (e^(2x)
+// → 0 gives −1, → ∞ gives 1); absolute error ~2e-7, as tanh_fast.
+__device__ __forceinline__ void tanh_fast2(float& x0, float& x1) {
+    float t0, t1;
+    f2_split(fmul2(f2(x0, x1), f2(2.0f * 1.4426950408889634f, 2.0f * 1.4426950408889634f)), t0, t1);
+    float e0, e1;
+    f2_split(fadd2(f2(ex2_approx(t0), ex2_approx(t1)), f2(1.0f, 1.0f)), e0, e1);
+    f2_split(ffma2(f2(-2.0f, -2.0f), f2(rcp_approx(e0), rcp_approx(e1)), f2(1.0f, 1.0f)), x0, x1);
 }
 // σ(x) = 1 / (1 + e^(−x)).
 __device__ __forceinline__ float sigmoid_fast(float x) {

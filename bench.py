@@ -24,6 +24,8 @@ independent, so ranks shard the work with no collective ("scaling": "weak").
   divides its owned range on its GPU, then one gather of the stems to rank 0), host PCM in and
   host stems out on rank 0, CUDA events per rank around the whole call, max over ranks,
   ``"scaling": "strong"``. At N=1 it runs ``ancha_separate_pcm``.
+* ``fp32``: the ``value`` pipeline and track in fp32, the reference's arithmetic and BASELINE
+  config 1's dtype (FFMA kernels), PCM in HBM, CUDA events, max over ranks.
 * ``config3``: BASELINE config 3, BS-RoFormer dim 512, depth 12, 8×64 heads, 62 bands, hop 512,
   in f16 (the config names bf16, which misses the 50 dB tolerance on this network), one 180 s track (chunk 352800, overlap 2 → 47 chunks) split over the ranks the same way,
   ``"scaling": "strong"``.
@@ -208,6 +210,50 @@ def config3(local: int, world: int, rank: int, dist, steps: int = 2):
             "seconds_per_track": t, "steps": steps, "scaling": "strong", "dtype": "f16",
             "timing": "CUDA events per rank around the whole call (host PCM in, host stems out on rank 0), "
                       "max over ranks, median of steps"}
+
+
+def fp32_leg(package: str, local: int, world: int, rank: int, dist, planes, d_planes, steps: int = 2):
+    """The same pipeline and track as ``value`` in fp32 (the reference's arithmetic and BASELINE
+    config 1's dtype): PCM in HBM, CUDA events, max over ranks."""
+    import ctypes as C
+
+    import torch
+
+    from ancha_b200 import _native as N
+    from ancha_b200.model import Roformer
+    model = Roformer(package, local, "f32")
+    samples = planes.shape[1]
+    d_stems = torch.empty((model.stems, 2, samples), dtype=torch.float32, device=f"cuda:{local}")
+    stream = torch.cuda.Stream()
+    L = N.lib()
+
+    def step():
+        N.check(L.ancha_separate_device(model.handle, d_planes.data_ptr(), samples, CHUNK, OVERLAP, 0,
+                                        d_stems.data_ptr(), C.c_void_p(stream.cuda_stream)))
+
+    with torch.cuda.stream(stream):
+        step()
+        N.check(L.ancha_separate_status(model.handle, C.c_void_p(stream.cuda_stream)))
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        N.check(L.ancha_separate_status(model.handle, C.c_void_p(stream.cuda_stream)))
+    t = torch.tensor([e0.elapsed_time(e1) / 1e3 / steps], device=f"cuda:{local}")
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    model.close()
+    if rank != 0:
+        return None
+    sec = float(t.item())
+    return {"workload": "the value workload (mel-band-roformer, native context, one 30 s track per GPU) in fp32",
+            "value": world * samples / SR / sec, "unit": "×realtime", "ms_per_step": sec * 1e3, "steps": steps,
+            "dtype": "f32", "scaling": "weak",
+            "kernels": "GEMMs and time-axis attention on the FFMA (SIMT) kernels; band axis FFMA"}
 
 
 def mel_track(model, local: int, world: int, rank: int, dist, precision: str, steps: int = 3):
@@ -616,6 +662,7 @@ def main():
     attention = dict(sweep[0], sweep=sweep[1:])
 
     strong = mel_track(model, local, world, rank, dist, a.precision)
+    f32 = fp32_leg(a.package, local, world, rank, dist, planes, d_planes) if a.precision != "f32" else None
 
     c3 = None
     if not a.no_config3:
@@ -655,7 +702,7 @@ def main():
             "clocks": clk.summary(), "e2e": e2e,
             "gpu_launches": launches_per_step(chunks, effective_batch(chunks, a.batch),
                                               fused=a.precision != "f32") * a.steps,
-            "roofline": roofline, "attention": attention, "strong_track": strong, "config3": c3, "config4": c4,
+            "roofline": roofline, "attention": attention, "strong_track": strong, "fp32": f32, "config3": c3, "config4": c4,
             "config5": c5,
             "cpu_baseline": cpu,
         }
