@@ -98,12 +98,14 @@ __device__ __forceinline__ void flush_stats(double2* stats, int plane, double& s
 constexpr int STAGE_BYTES = 4096;    // one 32-row × 128-byte epilogue staging buffer
 constexpr int STAGE16_BYTES = 2048;  // one 32-row × 64-byte buffer for the 16-bit copy
 // One buffer per warp: a chunk waits for every store of the previous chunk (the output and the
-// 16-bit copy) to have read its source before it overwrites either buffer.
+// 16-bit copy) to have read its source before it overwrites either buffer. (Alternating two
+// halves for 16-bit outputs measured within ±1 %.)
 static_assert(STAGE_BUFS == 1, "the row-norm copy shares the single-buffer wait");
 
-template <int BN, int STAGES, int EPI_WARPS>
+// PAIR: a CTA of a two-CTA pair holds half of the tile's B columns.
+template <int BN, int STAGES, int EPI_WARPS, bool PAIR = false>
 struct Smem {
-    static constexpr int B_BYTES = BN * BK * 2;
+    static constexpr int B_BYTES = (PAIR ? BN / 2 : BN) * BK * 2;
     static constexpr int TILES = STAGES * (A_BYTES + B_BYTES);
     static constexpr int STAGING = EPI_WARPS * STAGE_BUFS * STAGE_BYTES;
     // The row-norm fusion's 16-bit copy: only the plain (residual) epilogues write one.
@@ -310,23 +312,31 @@ struct TileCoord {
     int g, m0, n0, n_g;
 };
 
-__device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int t, int bn) {
+__device__ __forceinline__ TileCoord tile_coord(const TcParams& p, int t, int bn, int bm = BM) {
     TileCoord c;
     const int per_group = p.m_tiles * p.n_tiles;
     c.g = t / per_group;
     const int r = t % per_group;
-    c.m0 = (r / p.n_tiles) * BM;
+    c.m0 = (r / p.n_tiles) * bm;
     c.n0 = (r % p.n_tiles) * bn;
     c.n_g = p.group_n ? p.group_n[c.g % p.b_groups] : p.n;
     return c;
 }
 
-template <int BN, int STAGES, int EPI_WARPS>
+// PAIR: the kernel runs as clusters of two CTAs on two SMs. A tile is 256 × BN: CTA rank r
+// loads A rows m0 + 128·r .. and B columns n0 + (BN / 2)·r .. of each K slab into its own
+// shared memory (both completing on the even CTA's full barrier), the even CTA's issuer runs
+// M = 256 UMMAs over both CTAs' operands (cta_group::2) into both CTAs' TMEM, and its commits
+// arrive on both CTAs' barriers; each CTA's epilogue drains its own 128 rows and arrives on the
+// even CTA's accumulator barrier. Per SM this halves the B slab loaded per tile (the GEMMs with
+// K = 384 are limited by the operand traffic from L2).
+template <int BN, int STAGES, int EPI_WARPS, bool PAIR>
 __global__ void __launch_bounds__(threads_of<EPI_WARPS>(), 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
                const __grid_constant__ CUtensorMap tma_out, const __grid_constant__ CUtensorMap tma_out16,
                const TcParams p) {
-    using S = Smem<BN, STAGES, EPI_WARPS>;
+    using S = Smem<BN, STAGES, EPI_WARPS, PAIR>;
+    constexpr int BMT = PAIR ? 2 * BM : BM;  // rows of a tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* a_tiles = smem;
@@ -341,6 +351,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     constexpr uint32_t TMEM_COLS = 2 * BN <= 256 ? 256 : 512;
 
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const uint32_t rank = PAIR ? cluster_ctarank() : 0;
+    const int tile0 = PAIR ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+    const int tstep = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
             mbar_init(&full[s], 1);
@@ -348,7 +361,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&tfull[b], 1);
-            mbar_init(&tempty[b], EPI_WARPS);
+            mbar_init(&tempty[b], PAIR ? 2 * EPI_WARPS : EPI_WARPS);
         }
         *abort = 0;
         fence_barrier_init();
@@ -359,11 +372,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         if (p.out16) prefetch_tma(&tma_out16);
     }
     if (warp == 1) {
-        tmem_alloc(tmem_slot, TMEM_COLS);
-        tmem_relinquish();
+        if (PAIR) {
+            tmem_alloc_pair(tmem_slot, TMEM_COLS);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(tmem_slot, TMEM_COLS);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if (PAIR) cluster_sync();  // the peer's barriers exist before anything arrives on them
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int kblocks = (p.k + BK - 1) / BK;
@@ -372,13 +391,22 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         if (lane == 0) {
             // TMA producer.
             uint32_t it = 0;
-            for (int t = blockIdx.x; t < p.tiles && !*abort; t += gridDim.x) {
-                const TileCoord c = tile_coord(p, t, BN);
+            for (int t = tile0; t < p.tiles && !*abort; t += tstep) {
+                const TileCoord c = tile_coord(p, t, BN, BMT);
                 if (c.n0 >= c.n_g) continue;
                 const int bg = c.g % p.b_groups;
                 for (int kb = 0; kb < kblocks; ++kb, ++it) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort, p.err)) break;
+                    if (PAIR) {
+                        // Both CTAs' slabs complete on the even CTA's barrier, which expects both.
+                        const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
+                        if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (A_BYTES + S::B_BYTES));
+                        tma_load_3d_pair(a_tiles + s * A_BYTES, &tma_a, fb, kb * BK, c.m0 + (int)rank * BM, c.g);
+                        tma_load_3d_pair(b_tiles + s * S::B_BYTES, &tma_b, fb, kb * BK, c.n0 + (int)rank * (BN / 2),
+                                         bg);
+                        continue;
+                    }
                     mbar_arrive_expect_tx(&full[s], A_BYTES + S::B_BYTES);
                     tma_load_3d(a_tiles + s * A_BYTES, &tma_a, &full[s], kb * BK, c.m0, c.g);
                     if (p.conv_taps) {
@@ -393,7 +421,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                     }
                 }
             }
-            if (*abort) {  // let copies in flight land before the CTA exits (bounded)
+            if (*abort && rank == 0) {  // let copies in flight land before the CTA exits (bounded;
+                // with a pair the even CTA's barriers also count the peer's copies)
                 const long long c0 = clock64();
                 for (uint32_t j = it > (uint32_t)STAGES ? it - STAGES : 0; j < it; ++j)
                     while (!mbar_try_wait(&full[j % STAGES], (j / STAGES) & 1) && clock64() - c0 < kWaitCycles) {
@@ -401,11 +430,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             }
         }
     } else if (warp == 1) {
-        if (lane == 0) {
-            // UMMA issuer.
+        if (lane == 0 && rank == 0) {
+            // UMMA issuer (the even CTA of a pair issues for both).
             uint32_t it = 0, local = 0;
-            for (int t = blockIdx.x; t < p.tiles && !*abort; t += gridDim.x) {
-                const TileCoord c = tile_coord(p, t, BN);
+            for (int t = tile0; t < p.tiles && !*abort; t += tstep) {
+                const TileCoord c = tile_coord(p, t, BN, BMT);
                 if (c.n0 >= c.n_g) continue;
                 const int b = local & 1;
                 if (!mbar_wait(&tempty[b], ((local >> 1) & 1) ^ 1, abort, p.err)) break;
@@ -417,13 +446,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                     tc_fence_after();
                     const uint32_t a_addr = smem_u32(a_tiles + s * A_BYTES);
                     const uint32_t b_addr = smem_u32(b_tiles + s * S::B_BYTES);
+                    if (PAIR) {
 #pragma unroll
-                    for (int kk = 0; kk < BK / 16; ++kk)
-                        umma_f16(acc, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), p.idesc,
-                                 (kb | kk) != 0);
-                    umma_commit(&empty[s]);
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            umma_f16_pair(acc, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
+                                          p.idesc, (kb | kk) != 0);
+                        umma_commit_pair(&empty[s], 0x3);
+                    } else {
+#pragma unroll
+                        for (int kk = 0; kk < BK / 16; ++kk)
+                            umma_f16(acc, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32),
+                                     p.idesc, (kb | kk) != 0);
+                        umma_commit(&empty[s]);
+                    }
                 }
-                umma_commit(&tfull[b]);
+                if (PAIR)
+                    umma_commit_pair(&tfull[b], 0x3);
+                else
+                    umma_commit(&tfull[b]);
                 ++local;
             }
         }
@@ -441,14 +481,14 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
         // usually keeps its rows) and flushed when the plane changes.
         double st_sum = 0.0, st_sq = 0.0;
         int st_plane = -1;
-        for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
-            const TileCoord c = tile_coord(p, t, BN);
+        for (int t = tile0; t < p.tiles; t += tstep) {
+            const TileCoord c = tile_coord(p, t, BN, BMT);
             if (c.n0 >= c.n_g) continue;
             const int b = local & 1;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[b], (local >> 1) & 1, abort, p.err));
             if (!ok) break;
             tc_fence_after();
-            const int row0 = c.m0 + quarter * 32;
+            const int row0 = c.m0 + (int)rank * BM + quarter * 32;
             const int row = row0 + lane;
             const bool live = row < p.m;
             if (p.stats) {
@@ -510,7 +550,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[b]);
+            if (lane == 0) {
+                if (PAIR)
+                    mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[b]), 0));
+                else
+                    mbar_arrive(&tempty[b]);
+            }
             ++local;
         }
         if (p.stats) flush_stats(p.stats, st_plane, st_sum, st_sq, lane);
@@ -519,29 +564,57 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     }
     tc_fence_before();
     __syncthreads();
+    // With a pair, neither CTA releases TMEM or exits while the other may still use its
+    // shared memory (the even CTA's UMMAs read the peer's slabs) or its barriers.
+    if (PAIR) cluster_sync();
     if (warp == 1) {
         __syncwarp();
-        tmem_dealloc(tmem, TMEM_COLS);
+        if (PAIR)
+            tmem_dealloc_pair(tmem, TMEM_COLS);
+        else
+            tmem_dealloc(tmem, TMEM_COLS);
     }
 }
 
-template <int BN, int STAGES, int EPI_WARPS>
+template <int BN, int STAGES, int EPI_WARPS, bool PAIR = false>
 int launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const CUtensorMap& to16,
            const TcParams& p, cudaStream_t s) {
-    using S = Smem<BN, STAGES, EPI_WARPS>;
+    using S = Smem<BN, STAGES, EPI_WARPS, PAIR>;
+    auto kernel = gemm_tc_kernel<BN, STAGES, EPI_WARPS, PAIR>;
     static bool configured[64] = {};
-    static int sms[64] = {};
+    static int slots[64] = {};  // co-resident CTAs (one CTA per SM) or CTA pairs
     int dev = 0;
     cudaGetDevice(&dev);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(threads_of<EPI_WARPS>(), 1, 1);
+    cfg.dynamicSmemBytes = S::BYTES;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
     if (!configured[dev & 63]) {
-        ANCHA_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, STAGES, EPI_WARPS>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES));
-        ANCHA_CUDA(cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev));
+        ANCHA_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S::BYTES));
+        if (PAIR) {
+            cfg.gridDim = dim3(2, 1, 1);
+            ANCHA_CUDA(cudaOccupancyMaxActiveClusters(&slots[dev & 63], (void*)kernel, &cfg));
+            if (slots[dev & 63] < 1) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: no CTA pair fits an SM pair");
+        } else {
+            ANCHA_CUDA(cudaDeviceGetAttribute(&slots[dev & 63], cudaDevAttrMultiProcessorCount, dev));
+        }
         configured[dev & 63] = true;
     }
-    const int grid = std::max(1, std::min(p.tiles, sms[dev & 63]));
-    gemm_tc_kernel<BN, STAGES, EPI_WARPS><<<grid, threads_of<EPI_WARPS>(), S::BYTES, s>>>(ta, tb, to, to16, p);
-    return check_launch("gemm_tc");
+    const int units = std::max(1, std::min(p.tiles, slots[dev & 63]));
+    if (!PAIR) {
+        kernel<<<units, threads_of<EPI_WARPS>(), S::BYTES, s>>>(ta, tb, to, to16, p);
+        return check_launch("gemm_tc");
+    }
+    cfg.gridDim = dim3(2 * units, 1, 1);
+    cfg.stream = s;
+    ANCHA_CUDA(cudaLaunchKernelEx(&cfg, kernel, ta, tb, to, to16, p));
+    return check_launch("gemm_tc (CTA pairs)");
 }
 
 // Output tile width: the widest of 256 / 192 / 128 whose padded N is within 1/6 of the least
@@ -555,12 +628,24 @@ int pick_bn(int n) {
     return 128;
 }
 
+#ifndef ANCHA_GEMM_PAIRS
+#define ANCHA_GEMM_PAIRS 1
+#endif
+
 int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64_t ldb,
         int64_t b_group_stride, TcParams p, int ab_type, cudaStream_t s) {
     const int bn = p.group_n ? 128 : pick_bn(p.n);
+    // CTA pairs (256-row tiles over two SMs) for single problems with at least two 128-row tiles
+    // and a long K loop: measured on the model's GEMMs, pairs take 12.5 % off the K = 1536
+    // FFN-out and 7 % off the K = 1536 mask layer, where the operand traffic per SM limits the
+    // main loop, but add 6-9 % at K = 384 / 512, where each SM's epilogue is the limit and a pair
+    // must wait for both CTAs' epilogues before reusing an accumulator. Grouped problems and the
+    // implicit-GEMM convolution keep one CTA per tile.
+    const bool pair = ANCHA_GEMM_PAIRS && p.groups == 1 && !p.group_n && !p.conv_taps && p.m >= 2 * BM &&
+                      p.k >= 1024;
     CUtensorMap ta, tb, to;
     ANCHA_TRY(make_tma_3d(&ta, a, ab_type, p.k, p.m, p.groups, lda, a_group_stride, BM));
-    ANCHA_TRY(make_tma_3d(&tb, b, ab_type, p.k, p.n, p.b_groups, ldb, b_group_stride, bn));
+    ANCHA_TRY(make_tma_3d(&tb, b, ab_type, p.k, p.n, p.b_groups, ldb, b_group_stride, pair ? bn / 2 : bn));
     const bool glu = p.act == ANCHA_ACT_GLU;
     if (glu && p.out_type != ELT_F32) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: GLU output must be f32");
     const int64_t out_cols = glu ? p.n / 2 : p.n;
@@ -572,15 +657,22 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
         if (p.groups != 1) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: row-norm fusion on grouped problems");
         ANCHA_TRY(make_tma_store_3d(&to16, p.out16, ab_type, p.n, p.m, 1, p.n, (int64_t)p.m * p.n, 32, 32));
     }
-    p.idesc = umma_idesc_f16(ab_type == ELT_BF16, BM, bn);
+    p.idesc = umma_idesc_f16(ab_type == ELT_BF16, pair ? 2 * BM : BM, bn);
     p.err = device_error_word();
-    p.m_tiles = (int)ceil_div(p.m, BM);
+    p.m_tiles = (int)ceil_div(p.m, pair ? 2 * BM : BM);
     p.n_tiles = (int)ceil_div(p.n, bn);
     const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles * p.groups;
     if (tiles > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: too many tiles");
     p.tiles = (int)tiles;
     const bool act = p.act == ANCHA_ACT_GELU || p.act == ANCHA_ACT_TANH;
     if (act && p.out16) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: no 16-bit copy after an activation");
+    if (pair) {
+        switch (bn) {
+            case 256: return act ? launch<256, 4, EPI_ACT, true>(ta, tb, to, to16, p, s) : launch<256, 4, EPI_PLAIN, true>(ta, tb, to, to16, p, s);
+            case 192: return act ? launch<192, 4, EPI_ACT, true>(ta, tb, to, to16, p, s) : launch<192, 5, EPI_PLAIN, true>(ta, tb, to, to16, p, s);
+            default: return act ? launch<128, 6, EPI_ACT, true>(ta, tb, to, to16, p, s) : launch<128, 6, EPI_PLAIN, true>(ta, tb, to, to16, p, s);
+        }
+    }
     switch (bn) {
         case 256: return act ? launch<256, 3, EPI_ACT>(ta, tb, to, to16, p, s) : launch<256, 3, EPI_PLAIN>(ta, tb, to, to16, p, s);
         case 192: return act ? launch<192, 3, EPI_ACT>(ta, tb, to, to16, p, s) : launch<192, 3, EPI_PLAIN>(ta, tb, to, to16, p, s);
