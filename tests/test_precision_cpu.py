@@ -15,8 +15,6 @@ GEMM by the same relative amount whatever the sequence length.
 import numpy as np
 import pytest
 
-from ancha_b200 import synthetic
-from ancha_b200.config import ModelConfig
 from oracle import roformer as oracle_model
 from tests._util import bf16_round, snr_db
 
@@ -29,14 +27,8 @@ def bf16_weights(x):
     return bf16_round(np.asarray(x, dtype=np.float32)).astype(np.float64)
 
 
-@pytest.fixture(scope="module")
-def mel(tmp_path_factory):
-    d = str(tmp_path_factory.mktemp("mel") / "pkg")
-    synthetic.seeded_package(d, ModelConfig.mel_karaoke())
-    return d
-
-
-def test_bf16_weights_bound_the_16_bit_mode_below_50_db(mel):
+def test_bf16_weights_bound_the_16_bit_mode_below_50_db(mel_seeded_package):
+    mel = mel_seeded_package
     rng = np.random.default_rng(0)
     frames = 201
     spectrum = (rng.standard_normal((frames, 1025 * 4)) * 0.5).astype(np.float32)
