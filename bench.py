@@ -623,7 +623,7 @@ def main():
                 "peak_kind": peak_kind,
                 # DRAM bytes of one launch from an ncu capture of the same shape (cold cache);
                 # profiles/gemm_tc_ffn_in_gelu.md has the command and the counters.
-                "traffic": 138.39e6, "traffic_unit": "bytes per launch (dram read + write, ncu)",
+                "traffic": 134.10e6, "traffic_unit": "bytes per launch (dram read + write, ncu)",
                 "algorithmic": f"2·{rows}·384·1536 flop per launch"}
 
     # Fused attention alone: time axis T = 801 / 1601 / 3201, band axis S = 60
