@@ -58,7 +58,7 @@ class LinearDesc(C.Structure):
                 ("out_dtype", C.c_int), ("weight_layout", C.c_int), ("ldx", C.c_int64),
                 ("ldw", C.c_int64), ("ldout", C.c_int64), ("ldres", C.c_int64),
                 ("act", C.c_int), ("rope_width", C.c_int), ("rope_tokens", C.c_int),
-                ("rope_div", C.c_int)]
+                ("rope_div", C.c_int), ("row_scale", C.c_void_p)]
 
 
 class SeparateOpts(C.Structure):

@@ -138,6 +138,9 @@ int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, c
     e.rope_tokens = d->rope_tokens > 0 ? d->rope_tokens : 1;
     e.rope_div = d->rope_div > 0 ? d->rope_div : 1;
     e.rope_hd = 64;
+    e.row_mul = d->row_scale;
+    if (d->row_scale && reinterpret_cast<uintptr_t>(d->row_scale) % 4)
+        return fail(ANCHA_E_INVALID, "linear: row_scale not 4-byte aligned");
     cudaStream_t s = as_stream(stream);
     if (d->dtype != ANCHA_F32 && wl == ANCHA_W_NK) {
         int st = gemm_tc(g, d->dtype, e, s);

@@ -52,6 +52,9 @@ struct GemmEpilogue {
     // r are added (f64 atomics) into stats[r / stats_div]; the caller zeroes them. Null = off.
     double2* stats;
     int stats_div;
+    // Per-row multiplier of A·Bᵀ (row_mul[r], applied before the bias; null = 1), the plug-in
+    // API's row_scale. Both paths; the row-norm fusion's row_ss takes precedence.
+    const float* row_mul;
 };
 
 // FFMA GEMM (fp32 accumulation). `groups` is a device array of `count` problems when

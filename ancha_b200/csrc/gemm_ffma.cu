@@ -21,6 +21,11 @@ __device__ __forceinline__ float ld_elem(const void* base, int64_t idx) {
 __device__ __forceinline__ void finish4(const GemmGroup& g, const GemmEpilogue& e, int row,
                                         int c0, float v[4]) {
     if (row >= g.m) return;
+    if (e.row_mul) {
+        const float r = e.row_mul[row];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) v[j] *= r;
+    }
     if (g.bias) {
 #pragma unroll
         for (int j = 0; j < 4; ++j)

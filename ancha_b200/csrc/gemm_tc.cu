@@ -47,6 +47,7 @@ struct TcParams {
     const float* rope;
     const float2* rope_pairs;
     int rope_width, rope_tokens, rope_div, rope_hd;
+    const float* row_mul;    // per-row multiplier (GemmEpilogue::row_mul)
     const float* row_ss;     // row-norm fusion, see GemmEpilogue
     int row_ss_n;
     const float* res_ss;
@@ -499,7 +500,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 }
             }
             const uint32_t base = tmem + b * BN + ((uint32_t)(quarter * 32) << 16);
-            const float row_scale = p.row_ss && live ? inv_norm(p.row_ss + row, p.row_ss_n, p.m) : 1.f;
+            const float row_scale = !live ? 1.f
+                                    : p.row_ss ? inv_norm(p.row_ss + row, p.row_ss_n, p.m)
+                                    : p.row_mul ? p.row_mul[row] : 1.f;
             const float res_scale = p.res_ss && live ? inv_norm(p.res_ss + row, p.res_ss_n, p.m) : 1.f;
 #pragma unroll 1
             for (int col = first * 32; col < BN; col += PER_QUARTER * 32) {
@@ -705,6 +708,7 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     p.rope_pairs = reinterpret_cast<const float2*>(e.rope_pairs);
     p.rope_div = e.rope_div; p.rope_hd = e.rope_hd;
     p.row_ss = e.row_ss; p.row_ss_n = e.row_ss_n; p.res_ss = e.res_ss; p.res_ss_n = e.res_ss_n;
+    p.row_mul = e.row_mul;
     p.res_col = e.res_col; p.out16 = e.out16; p.out16_col = e.out16_col;
     p.ss_out = e.ss_out; p.ss16_out = e.ss16_out; p.ab16 = ab_type;
     p.stats = e.stats; p.stats_div = e.stats_div > 0 ? e.stats_div : 1;

@@ -97,11 +97,14 @@ def gated_attention(packed, heads: int):
 class Epilogue:
     """Work fused into the output pass of :func:`linear`, applied in field order
     (fused/mod.rs:57-79): bias ``[m]``, erf-GELU, interleaved RoPE (``(table [4, tokens, 64],
-    width)``), residual ``[n, m]``."""
+    width)``), residual ``[n, m]``. ``row_scale`` ``[n]`` (this engine's addition, before the
+    bias) multiplies each row of the product, e.g. by 1 / ‖x_row‖ so a unit norm of the input
+    rows needs no separate pass."""
     bias: Optional[object] = None
     gelu: bool = False
     rotary: Optional[tuple] = None
     residual: Optional[object] = None
+    row_scale: Optional[object] = None
 
 
 def linear_supported(k: int, m: int) -> bool:
@@ -125,7 +128,7 @@ def linear(x, weight, epilogue: Epilogue = Epilogue(), weight_layout: int = N.W_
     if rows != k or k == 0 or k % 8 or m == 0:
         return None
     empty = epilogue.bias is None and not epilogue.gelu and epilogue.rotary is None \
-        and epilogue.residual is None
+        and epilogue.residual is None and epilogue.row_scale is None
     if m % 128 and not empty:
         return None
     rope, width, tokens = None, 0, 1
@@ -137,6 +140,8 @@ def linear(x, weight, epilogue: Epilogue = Epilogue(), weight_layout: int = N.W_
         rope = table.contiguous().float()
     if epilogue.residual is not None and tuple(epilogue.residual.shape) != (n, m):
         return None
+    if epilogue.row_scale is not None and tuple(epilogue.row_scale.shape) != (n,):
+        return None
     xs = x if x.stride(-1) == 1 else x.contiguous()
     ws = weight if weight.stride(-1) == 1 else weight.contiguous()
     out = torch.empty((n, m), dtype=torch.float32 if x.dtype == torch.float32 else x.dtype,
@@ -146,9 +151,11 @@ def linear(x, weight, epilogue: Epilogue = Epilogue(), weight_layout: int = N.W_
         res = res.float()
         res = res if res.stride(-1) == 1 else res.contiguous()
     bias = None if epilogue.bias is None else epilogue.bias.float().contiguous()
+    rs = None if epilogue.row_scale is None else epilogue.row_scale.float().contiguous()
     d = N.LinearDesc(n, m, k, _dtype_code(xs), _dtype_code(out), weight_layout,
                      xs.stride(0), ws.stride(0), m, res.stride(0) if res is not None else 0,
-                     N.ACT_GELU if epilogue.gelu else N.ACT_NONE, width, tokens, 1)
+                     N.ACT_GELU if epilogue.gelu else N.ACT_NONE, width, tokens, 1,
+                     None if rs is None else rs.data_ptr())
     ptr = lambda t: None if t is None else t.data_ptr()
     N.check(N.lib().ancha_linear_fwd(C.byref(d), xs.data_ptr(), ws.data_ptr(), ptr(bias),
                                      ptr(res), ptr(rope), out.data_ptr(), _stream()))

@@ -120,6 +120,9 @@ typedef struct {
     int64_t ldx, ldw, ldout, ldres;
     int act;
     int rope_width, rope_tokens, rope_div;  /* rope_width = 0: no rotary epilogue */
+    const float* row_scale;  /* optional device [m]: row r of x·w is multiplied by row_scale[r]
+                                before the bias (the unit-norm of rows, applied after the GEMM
+                                instead of to x); null = 1 */
 } ancha_linear_desc;
 
 ANCHA_API int ancha_linear_fwd(const ancha_linear_desc* desc, const void* x, const void* w,

@@ -46,8 +46,34 @@ def test_version_and_status_without_gpu():
 def test_struct_layouts_match_header():
     # The ctypes mirrors must match the C layout (sizes of the packed descriptors).
     assert C.sizeof(N.AttnDesc) == 5 * 4 + 4 + 6 * 8 + 5 * 4 + 4  # + padding to 8
-    assert C.sizeof(N.LinearDesc) == 6 * 4 + 4 * 8 + 4 * 4
+    assert C.sizeof(N.LinearDesc) == 6 * 4 + 4 * 8 + 4 * 4 + 8
     assert C.sizeof(N.SeparateOpts) == 3 * 8 + 8 + 4 * 4 + 2 * 8
+
+
+def test_struct_layouts_match_the_c_compiler(tmp_path):
+    """Sizes and field offsets of the descriptors as gcc lays out include/ancha_b200.h."""
+    import shutil
+    import subprocess
+    if not shutil.which("gcc"):
+        pytest.skip("no gcc")
+    structs = {"ancha_attn_desc": N.AttnDesc, "ancha_linear_desc": N.LinearDesc,
+               "ancha_separate_opts": N.SeparateOpts}
+    lines = ['#include <stddef.h>', '#include <stdio.h>', '#include "ancha_b200.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append(f'printf("{cname} %zu\\n", sizeof({cname}));')
+        for field, _ in py._fields_:
+            lines.append(f'printf("{cname}.{field} %zu\\n", offsetof({cname}, {field}));')
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    for cname, py in structs.items():
+        assert int(got[cname]) == C.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert int(got[f"{cname}.{field}"]) == getattr(py, field).offset, f"{cname}.{field}"
 
 
 def test_invalid_arguments_are_rejected_before_any_launch():

@@ -117,6 +117,26 @@ def test_gemm_epilogues_match_reference_ops():
     assert max_abs(t64(got), expected) < 1e-5
 
 
+@pytest.mark.parametrize("dt", ["f32", "f16"])
+def test_linear_row_scale(dt):
+    """The plug-in API's row_scale: unit_norm of the input rows applied after the product
+    (roformer.rs:16-24 then the Linear), on the FFMA (f32) and tcgen05 (f16) paths."""
+    rows, k, m = 300, 384, 512
+    x = wave([rows, k], 0.7) * np.float32(3.0)
+    w = wave([m, k], 1.9) * np.float32(0.05)
+    b = wave([m], 2.5)
+    inv = (1.0 / np.maximum(np.linalg.norm(x.astype(np.float64), axis=1), 1e-12)).astype(np.float32)
+    td = torch.float32 if dt == "f32" else torch.float16
+    xd, wd = dev(x).to(td), dev(w).to(td)
+    got = t64(fused.linear(xd, wd, fused.Epilogue(bias=dev(b), gelu=True, row_scale=dev(inv)),
+                           weight_layout=N.W_NK))
+    xe, we = xd.double().cpu().numpy(), wd.double().cpu().numpy()
+    pre = (xe @ we.T) * inv[:, None].astype(np.float64) + b
+    ref = 0.5 * pre * (1.0 + np.vectorize(math.erf)(pre / math.sqrt(2.0)))
+    tol = 1e-5 if dt == "f32" else 2e-3 * np.abs(ref).max()
+    assert max_abs(got, ref) < tol
+
+
 @pytest.mark.parametrize("rows,k,m,bias,strided", [
     (1, 8, 128, True, False), (127, 256, 256, False, False), (129, 64, 384, True, True),
     (300, 1024, 128, True, False)])
