@@ -14,6 +14,11 @@ struct GemmGroup {
     void* out;              // [m, n] (n/2 for GLU), row stride ldo
     int m, n, k;
     int64_t lda, ldb, ldr, ldo;
+    // Tensor-core fp32 (gemm_tc, bf16 operands): a and b each hold three bf16 planes
+    // [3][m][lda] / [3][n][ldb] of a three-way split (split3_rows), and the product is the sum
+    // of the six significant plane products hi·hi, hi·mid, mid·hi, hi·lo, lo·hi, mid·mid, run
+    // as one K loop of 6·k (the dropped terms are below 2^-24 of the product).
+    bool split3;
 };
 
 // Epilogue shared by every group of one launch.

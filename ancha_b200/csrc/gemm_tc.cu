@@ -24,6 +24,9 @@ namespace ancha {
 namespace {
 
 constexpr int BM = 128, BK = 64;
+// split3: the six significant products of (hi, mid, lo) planes: hh, hm, mh, hl, lh, mm.
+__constant__ int kSplitA[6] = {0, 0, 1, 0, 2, 1};
+__constant__ int kSplitB[6] = {0, 1, 0, 2, 0, 1};
 constexpr int A_BYTES = BM * BK * 2;
 // Epilogue warps per CTA (a multiple of 4: EPI / 4 warps per TMEM lane quarter): 16 for the
 // GELU / tanh epilogues, whose long dependent chains need the extra latency hiding, 8 for the
@@ -48,6 +51,7 @@ struct TcParams {
     const float2* rope_pairs;
     int rope_width, rope_tokens, rope_div, rope_hd;
     const float* row_mul;    // per-row multiplier (GemmEpilogue::row_mul)
+    int split3;              // three-plane bf16 operands, six plane products (GemmGroup::split3)
     const float* row_ss;     // row-norm fusion, see GemmEpilogue
     int row_ss_n;
     const float* res_ss;
@@ -387,6 +391,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int kblocks = (p.k + BK - 1) / BK;
+    const int kb_total = kblocks * (p.split3 ? 6 : 1);  // K steps per tile
 
     if (warp == 0) {
         if (lane == 0) {
@@ -396,20 +401,23 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 const TileCoord c = tile_coord(p, t, BN, BMT);
                 if (c.n0 >= c.n_g) continue;
                 const int bg = c.g % p.b_groups;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kt = 0; kt < kb_total; ++kt, ++it) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort, p.err)) break;
+                    // split3: K step kt is slab kb of plane product `term` (A plane, B plane).
+                    const int term = kt / kblocks, kb = kt - term * kblocks;
+                    const int az = p.split3 ? kSplitA[term] : c.g, bz = p.split3 ? kSplitB[term] : bg;
                     if (PAIR) {
                         // Both CTAs' slabs complete on the even CTA's barrier, which expects both.
                         const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
                         if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * (A_BYTES + S::B_BYTES));
-                        tma_load_3d_pair(a_tiles + s * A_BYTES, &tma_a, fb, kb * BK, c.m0 + (int)rank * BM, c.g);
+                        tma_load_3d_pair(a_tiles + s * A_BYTES, &tma_a, fb, kb * BK, c.m0 + (int)rank * BM, az);
                         tma_load_3d_pair(b_tiles + s * S::B_BYTES, &tma_b, fb, kb * BK, c.n0 + (int)rank * (BN / 2),
-                                         bg);
+                                         bz);
                         continue;
                     }
                     mbar_arrive_expect_tx(&full[s], A_BYTES + S::B_BYTES);
-                    tma_load_3d(a_tiles + s * A_BYTES, &tma_a, &full[s], kb * BK, c.m0, c.g);
+                    tma_load_3d(a_tiles + s * A_BYTES, &tma_a, &full[s], kb * BK, c.m0, az);
                     if (p.conv_taps) {
                         // The tap's shifted window; rows or columns outside the image load as
                         // zeros (the convolution's padding).
@@ -418,7 +426,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                         const int y0 = c.n0 / p.conv_w, x0 = c.n0 - y0 * p.conv_w;
                         tma_load_4d(b_tiles + s * S::B_BYTES, &tma_b, &full[s], cb * BK, x0 + dx, y0 + dy, p.conv_b);
                     } else {
-                        tma_load_3d(b_tiles + s * S::B_BYTES, &tma_b, &full[s], kb * BK, c.n0, bg);
+                        tma_load_3d(b_tiles + s * S::B_BYTES, &tma_b, &full[s], kb * BK, c.n0, bz);
                     }
                 }
             }
@@ -441,7 +449,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                 if (!mbar_wait(&tempty[b], ((local >> 1) & 1) ^ 1, abort, p.err)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + b * BN;
-                for (int kb = 0; kb < kblocks; ++kb, ++it) {
+                for (int kb = 0; kb < kb_total; ++kb, ++it) {
                     const int s = it % STAGES;
                     if (!mbar_wait(&full[s], (it / STAGES) & 1, abort, p.err)) break;
                     tc_fence_after();
@@ -645,10 +653,12 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
     // must wait for both CTAs' epilogues before reusing an accumulator. Grouped problems and the
     // implicit-GEMM convolution keep one CTA per tile.
     const bool pair = ANCHA_GEMM_PAIRS && p.groups == 1 && !p.group_n && !p.conv_taps && p.m >= 2 * BM &&
-                      p.k >= 1024;
+                      p.k * (p.split3 ? 6 : 1) >= 1024;
     CUtensorMap ta, tb, to;
-    ANCHA_TRY(make_tma_3d(&ta, a, ab_type, p.k, p.m, p.groups, lda, a_group_stride, BM));
-    ANCHA_TRY(make_tma_3d(&tb, b, ab_type, p.k, p.n, p.b_groups, ldb, b_group_stride, pair ? bn / 2 : bn));
+    // split3 operands are three planes along the depth coordinate of each map.
+    ANCHA_TRY(make_tma_3d(&ta, a, ab_type, p.k, p.m, p.split3 ? 3 : p.groups, lda, a_group_stride, BM));
+    ANCHA_TRY(make_tma_3d(&tb, b, ab_type, p.k, p.n, p.split3 ? 3 : p.b_groups, ldb, b_group_stride,
+                          pair ? bn / 2 : bn));
     const bool glu = p.act == ANCHA_ACT_GLU;
     if (glu && p.out_type != ELT_F32) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: GLU output must be f32");
     const int64_t out_cols = glu ? p.n / 2 : p.n;
@@ -709,6 +719,8 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     p.rope_div = e.rope_div; p.rope_hd = e.rope_hd;
     p.row_ss = e.row_ss; p.row_ss_n = e.row_ss_n; p.res_ss = e.res_ss; p.res_ss_n = e.res_ss_n;
     p.row_mul = e.row_mul;
+    p.split3 = g.split3 ? 1 : 0;
+    if (g.split3 && ab_type != ELT_BF16) return fail(ANCHA_E_INVALID, "gemm_tc: split operands are bf16");
     p.res_col = e.res_col; p.out16 = e.out16; p.out16_col = e.out16_col;
     p.ss_out = e.ss_out; p.ss16_out = e.ss16_out; p.ab16 = ab_type;
     p.stats = e.stats; p.stats_div = e.stats_div > 0 ? e.stats_div : 1;

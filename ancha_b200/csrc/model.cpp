@@ -21,6 +21,10 @@
 #include "dsp.cuh"
 #include "rowops.cuh"
 
+#ifndef ANCHA_FP32_SPLIT
+#define ANCHA_FP32_SPLIT 1
+#endif
+
 namespace ancha {
 
 void DevBuf::release() {
@@ -425,6 +429,30 @@ std::unique_ptr<Model> Model::load(const std::string& package, int device, int p
     }
     hasher.join();
     if (digest != m->manifest.weights_sha256) bad("model checksum mismatch");
+    if (m->elt_ == ELT_F32 && ANCHA_FP32_SPLIT) {
+        // fp32 on the tensor cores: three-plane bf16 splits of the transformer weights (the
+        // GEMMs that carry ~90 % of the model's FLOPs; the grouped band-split and mask-head
+        // GEMMs stay on the FFMA kernel).
+        const ModelConfig& c = m->manifest.config;
+        const int dim = c.dim, inner = c.heads * c.head_dim, hidden = c.dim * c.ff_mult;
+        const int ncols = 3 * inner + c.heads;
+        auto split = [&](const DevBuf& w, int n, int k) {
+            if (k % 8) return;  // the tensor-core GEMM needs 16-byte operand rows
+            DevBuf d;
+            d.alloc((size_t)3 * n * k * 2);
+            if (split3_rows(w.as<float>(), k, d.p, n, k, nullptr) != ANCHA_OK) bad("weight split");
+            m->split_w_[w.p] = std::move(d);
+        };
+        for (auto& pair : m->layers_)
+            for (auto& t : pair) {
+                split(t.wqkvg, ncols, dim);
+                split(t.wout, dim, inner);
+                split(t.w1, hidden, dim);
+                split(t.w2, dim, hidden);
+            }
+        if (cudaDeviceSynchronize() != cudaSuccess) bad("weight split");
+        m->split_ = true;
+    }
     return m;
 }
 
@@ -449,6 +477,7 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
         w.z.alloc((int64_t)chunks * frames * total_width * 4);
         if (split_kp_) w.z16.alloc(R * split_kp_ * 2);
         w.glu.alloc(R * max_width * 4);
+        if (split_) w.a3.alloc((size_t)3 * R * std::max(std::max(c.dim, inner), hidden) * 2);
         if (fuse_norms_) {
             w.ss_x.alloc(R * (c.dim / 32) * 4);
             w.ss_y.alloc(R * (c.dim / 32) * 4);
@@ -604,6 +633,22 @@ int Model::linear_fused(const void* x, int64_t ldx, const DevBuf& w, const float
     e.ss_out = nf.ss_out;
     e.ss16_out = nf.ss16_out;
     const bool fused = nf.row_ss || nf.res_ss || nf.out16 || nf.ss_out;
+    if (elt_ == ELT_F32 && split_ && !fused) {
+        // fp32 on the tensor cores: A split into three bf16 planes, the six significant plane
+        // products in one K loop against the weight's planes, f32 accumulation and epilogue.
+        const auto it = split_w_.find(w.p);
+        if (it != split_w_.end()) {
+            ANCHA_TRY(split3_rows(static_cast<const float*>(x), ldx, ws_.a3.p, m, k, s));
+            GemmGroup g3 = g;
+            g3.a = ws_.a3.p;
+            g3.lda = k;
+            g3.b = it->second.p;
+            g3.ldb = k;
+            g3.split3 = true;
+            const int st = gemm_tc(g3, ELT_BF16, e, s);
+            if (st != ANCHA_E_UNSUPPORTED) return st;
+        }
+    }
     if (elt_ != ELT_F32) {
         const int st = gemm_tc(g, elt_, e, s);
         if (st != ANCHA_E_UNSUPPORTED) return st;

@@ -79,6 +79,7 @@ struct Workspace {
     // SourceNorm scale (ss_yg).
     DevBuf ss_x, ss_y, ss_yg;
     DevBuf split_groups, mask_groups, glu_groups;
+    DevBuf a3;  // fp32 mode: the three bf16 planes of a GEMM's A operand [3][rows][k]
     std::vector<DevBuf> rope;        // per rope set: [time table, band table], [4, tokens, hd]
     std::vector<DevBuf> rope_pairs;  // the same tables pair-major: [2, hd / 2, tokens] × float2
 };
@@ -165,6 +166,10 @@ private:
     Workspace ws_;
     DevBuf flag_;  // non-finite model output (sticky until reset_flag)
     int elt_ = ELT_F32;  // operand type of the GEMMs and attention (ELT_*)
+    // fp32 mode on the tensor cores: the transformer weights' three-plane bf16 splits
+    // ([3][n][k], keyed by the f32 weight's device pointer) for the split3 GEMM.
+    bool split_ = false;
+    std::map<const void*, DevBuf> split_w_;
     int cur_chunks_ = 0;  // chunks of the forward in progress
 };
 

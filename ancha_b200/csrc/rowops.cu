@@ -172,6 +172,32 @@ int cast_rows(const float* x, int64_t ldx, void* y, int y_type, int64_t ldy, int
     return check_launch("cast_rows");
 }
 
+namespace {
+__global__ void split3_kernel(const float* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ y,
+                              int64_t rows, int dim) {
+    const int64_t n = rows * dim;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int64_t r = i / dim, c = i % dim;
+    const float v = x[r * ldx + c];
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    const float r1 = v - __bfloat162float(h);
+    const __nv_bfloat16 m = __float2bfloat16_rn(r1);
+    const float r2 = r1 - __bfloat162float(m);
+    y[i] = h;
+    y[n + i] = m;
+    y[2 * n + i] = __float2bfloat16_rn(r2);
+}
+}  // namespace
+
+int split3_rows(const float* x, int64_t ldx, void* y, int64_t rows, int dim, cudaStream_t s) {
+    const int64_t n = rows * dim;
+    if (n == 0) return ANCHA_OK;
+    split3_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(x, ldx, reinterpret_cast<__nv_bfloat16*>(y), rows,
+                                                             dim);
+    return check_launch("split3_rows");
+}
+
 int band_gather(const float* spec, int chunks, int frames, int columns, const int* cols,
                 const int* offsets, int bands, int total, float* z, cudaStream_t s) {
     const int64_t units = (int64_t)chunks * frames * bands;

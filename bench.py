@@ -25,7 +25,8 @@ independent, so ranks shard the work with no collective ("scaling": "weak").
   host stems out on rank 0, CUDA events per rank around the whole call, max over ranks,
   ``"scaling": "strong"``. At N=1 it runs ``ancha_separate_pcm``.
 * ``fp32``: the ``value`` pipeline and track in fp32, the reference's arithmetic and BASELINE
-  config 1's dtype (FFMA kernels), PCM in HBM, CUDA events, max over ranks.
+  config 1's dtype (transformer GEMMs on the tensor cores through three-plane bf16 splits, the
+  rest on FFMA kernels), PCM in HBM, CUDA events, max over ranks.
 * ``config3``: BASELINE config 3, BS-RoFormer dim 512, depth 12, 8×64 heads, 62 bands, hop 512,
   in f16 (the config names bf16, which misses the 50 dB tolerance on this network), one 180 s track (chunk 352800, overlap 2 → 47 chunks) split over the ranks the same way,
   ``"scaling": "strong"``.
@@ -253,7 +254,8 @@ def fp32_leg(package: str, local: int, world: int, rank: int, dist, planes, d_pl
     return {"workload": "the value workload (mel-band-roformer, native context, one 30 s track per GPU) in fp32",
             "value": world * samples / SR / sec, "unit": "×realtime", "ms_per_step": sec * 1e3, "steps": steps,
             "dtype": "f32", "scaling": "weak",
-            "kernels": "GEMMs and time-axis attention on the FFMA (SIMT) kernels; band axis FFMA"}
+            "kernels": "transformer GEMMs on the tensor cores with three-plane bf16 operand splits (six plane "
+                       "products, f32 accumulation); attention, band split and mask heads on the FFMA kernels"}
 
 
 def mel_track(model, local: int, world: int, rank: int, dist, precision: str, steps: int = 3):
