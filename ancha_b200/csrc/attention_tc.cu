@@ -80,16 +80,17 @@ __device__ __forceinline__ void exp2_fma_pair(uint64_t x, float& e0, float& e1) 
     e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-// Columns [J0, J0 + 64) of one score row: P as 16-bit pairs into pk (one TMEM store of 32
+// Columns [J0, J0 + NCOL) of one score row: P as 16-bit pairs into pk (NCOL / 2 TMEM
 // columns), row sums into the packed accumulators sa / sb. s_lo clamps the scores of the
 // FMA-pipe columns to x ≥ −124.
-template <bool BF16, int J0>
-__device__ __forceinline__ void exp_columns(const uint32_t (&s)[4][32], uint32_t (&pk)[32], uint64_t& sa,
+template <bool BF16, int J0, int NCOL, int NS, int W, int NP, int WP>
+__device__ __forceinline__ void exp_columns(const uint32_t (&s)[NS][W], uint32_t (&pk)[NP][WP], uint64_t& sa,
                                             uint64_t& sb, float m_used, float s_lo) {
+    static_assert(NP * WP == NCOL / 2, "P of NCOL columns is NCOL / 2 packed words");
     const uint64_t l2 = f2(LOG2E, LOG2E), nm2 = f2(-m_used, -m_used);
 #pragma unroll
-    for (int j = J0; j < J0 + 64; j += 2) {
-        const float s0 = __uint_as_float(s[j / 32][j % 32]), s1 = __uint_as_float(s[j / 32][j % 32 + 1]);
+    for (int j = J0; j < J0 + NCOL; j += 2) {
+        const float s0 = __uint_as_float(s[j / W][j % W]), s1 = __uint_as_float(s[j / W][j % W + 1]);
         float e0, e1;
         if ((j / 2) % 8 < POLY_PAIRS) {
             exp2_fma_pair(ffma2(f2(fmaxf(s0, s_lo), fmaxf(s1, s_lo)), l2, nm2), e0, e1);
@@ -103,7 +104,7 @@ __device__ __forceinline__ void exp_columns(const uint32_t (&s)[4][32], uint32_t
             sb = fadd2(sb, f2(e0, e1));
         else
             sa = fadd2(sa, f2(e0, e1));
-        pk[(j - J0) / 2] = pack2<BF16>(e0, e1);
+        pk[(j - J0) / 2 / WP][(j - J0) / 2 % WP] = pack2<BF16>(e0, e1);
     }
 }
 
@@ -338,8 +339,8 @@ attention_band_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
 }
 
 // Time-axis kernel (tokens > 64): one 128-row query tile per CTA and two CTAs per SM. Warps
-// 0–3 run the softmax (one query row per thread), warp 4 issues TMA (Q once, then K / V blocks
-// through a 2-deep ring), warp 5 issues UMMA. A tcgen05.mma issue costs a fixed ~80 cycles
+// 0–3 run the softmax (one query row per thread), warp 4 issues TMA (Q once, then K and V blocks
+// through two 2-deep rings), warp 5 issues UMMA. A tcgen05.mma issue costs a fixed ~80 cycles
 // whatever its N, so one issuing thread cannot keep the tensor cores busy with these small
 // (N = 128 / 64, K = 16) instructions; two co-resident CTAs give each SM two independent issue
 // streams, and the tensor cores interleave them (measured: 18–20 % faster than two query tiles
@@ -355,7 +356,7 @@ attention_band_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
 constexpr int PP_KV_STAGES = 2;
 constexpr int PP_OFF_Q = 0, PP_OFF_K = QKV_BYTES, PP_OFF_V = PP_OFF_K + PP_KV_STAGES * QKV_BYTES;
 constexpr int PP_OFF_BAR = PP_OFF_V + PP_KV_STAGES * QKV_BYTES;
-constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + 12 * 8 + 16;
+constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + 16 * 8 + 16;
 constexpr int PP_THREADS = 192;
 constexpr float PP_RESCALE_LOG2 = 8.f;
 constexpr uint32_t PP_TMEM_COLS = 256, PP_O_COL = 128, PP_P_COL = 192;
@@ -363,17 +364,23 @@ constexpr uint32_t PP_TMEM_COLS = 256, PP_O_COL = 128, PP_P_COL = 192;
 template <bool BF16>
 __global__ void __launch_bounds__(PP_THREADS, 2)
 attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams p) {
+    constexpr int SOFT = 128;  // softmax threads
+    constexpr int TMA_WARP = 4, MMA_WARP = 5;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + PP_OFF_BAR);
     uint64_t* q_full = bars;
-    uint64_t* kv_full = bars + 1;                  // [stage]
-    uint64_t* kv_empty = bars + 1 + PP_KV_STAGES;  // [stage]
-    uint64_t* s_full = bars + 5;                   // S(kb) computed
-    uint64_t* s_free = bars + 6;                   // S(kb) copied to registers (128 arrivals)
-    uint64_t* p_ready = bars + 7;                  // P(kb) written (128 arrivals)
-    uint64_t* pv_done = bars + 8;                  // O += P(kb)·V(kb) completed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+    // K and V run through separate rings: a K stage is free once S(kb) is done, a V stage once
+    // P·V(kb) is, so the load of K(kb + 2) starts a block earlier than with shared K | V stages.
+    uint64_t* k_full = bars + 1;                   // [stage]
+    uint64_t* k_empty = bars + 1 + PP_KV_STAGES;   // [stage]
+    uint64_t* v_full = bars + 1 + 2 * PP_KV_STAGES;
+    uint64_t* v_empty = bars + 1 + 3 * PP_KV_STAGES;
+    uint64_t* s_full = bars + 9;                   // S(kb) computed
+    uint64_t* s_free = bars + 10;                  // S(kb) copied to registers (128 arrivals)
+    uint64_t* p_ready = bars + 11;                 // P(kb) written (128 arrivals)
+    uint64_t* pv_done = bars + 12;                 // O += P(kb)·V(kb) completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tile = blockIdx.x % p.tiles_per_group;
@@ -383,22 +390,24 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
     const int q0 = tile * TILE;  // first query token of the tile
 
-    if (threadIdx.x == 128) {
+    if (threadIdx.x == SOFT) {
         mbar_init(q_full, 1);
         for (int s = 0; s < PP_KV_STAGES; ++s) {
-            mbar_init(&kv_full[s], 1);
-            mbar_init(&kv_empty[s], 1);
+            mbar_init(&k_full[s], 1);
+            mbar_init(&k_empty[s], 1);
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
         }
         mbar_init(s_full, 1);
-        mbar_init(s_free, 128);
-        mbar_init(p_ready, 128);
+        mbar_init(s_free, SOFT);
+        mbar_init(p_ready, SOFT);
         mbar_init(pv_done, 1);
         *abort = 0;
         fence_barrier_init();
         fence_proxy_async();
         prefetch_tma(&tmap);
     }
-    if (warp == 5) {
+    if (warp == MMA_WARP) {
         tmem_alloc(tmem_slot, PP_TMEM_COLS);
         tmem_relinquish();
     }
@@ -407,30 +416,38 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
-        if (lane == 0) {
-            mbar_arrive_expect_tx(q_full, QKV_BYTES);
-            tma_load_4d(smem + PP_OFF_Q, &tmap, q_full, p.q_col + head * HD, q0, gi, go);
+    if (warp == TMA_WARP) {
+        // Lane 0 loads Q and the K ring, lane 1 the V ring.
+        if (lane < 2) {
+            const bool is_k = lane == 0;
+            uint64_t* full = is_k ? k_full : v_full;
+            uint64_t* empty = is_k ? k_empty : v_empty;
+            const int off = is_k ? PP_OFF_K : PP_OFF_V;
+            const int col = (is_k ? p.k_col : p.v_col) + head * HD;
+            if (is_k) {
+                mbar_arrive_expect_tx(q_full, QKV_BYTES);
+                tma_load_4d(smem + PP_OFF_Q, &tmap, q_full, p.q_col + head * HD, q0, gi, go);
+            }
             int issued = 0;
             for (int kb = 0; kb < nkb; ++kb) {
                 const int s = kb % PP_KV_STAGES;
-                if (!mbar_wait(&kv_empty[s], ((kb / PP_KV_STAGES) & 1) ^ 1, abort, p.err)) break;
-                mbar_arrive_expect_tx(&kv_full[s], 2 * QKV_BYTES);
-                tma_load_4d(smem + PP_OFF_K + s * QKV_BYTES, &tmap, &kv_full[s], p.k_col + head * HD, kb * TILE, gi, go);
-                tma_load_4d(smem + PP_OFF_V + s * QKV_BYTES, &tmap, &kv_full[s], p.v_col + head * HD, kb * TILE, gi, go);
+                if (!mbar_wait(&empty[s], ((kb / PP_KV_STAGES) & 1) ^ 1, abort, p.err)) break;
+                mbar_arrive_expect_tx(&full[s], QKV_BYTES);
+                tma_load_4d(smem + off + s * QKV_BYTES, &tmap, &full[s], col, kb * TILE, gi, go);
                 ++issued;
             }
             if (*abort) {  // let copies in flight land before the CTA exits (bounded)
                 const long long c0 = clock64();
-                while (!mbar_try_wait(q_full, 0) && clock64() - c0 < kWaitCycles) {
-                }
+                if (is_k)
+                    while (!mbar_try_wait(q_full, 0) && clock64() - c0 < kWaitCycles) {
+                    }
                 for (int kb = max(0, issued - PP_KV_STAGES); kb < issued; ++kb)
-                    while (!mbar_try_wait(&kv_full[kb % PP_KV_STAGES], (kb / PP_KV_STAGES) & 1) &&
+                    while (!mbar_try_wait(&full[kb % PP_KV_STAGES], (kb / PP_KV_STAGES) & 1) &&
                            clock64() - c0 < kWaitCycles) {
                     }
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == MMA_WARP) {
         if (lane == 0) {
             // Per key block j: S(j + 1) once the softmax has copied S(j) out, then P(j)·V(j) once
             // it has written P(j).
@@ -469,13 +486,16 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 umma_commit(pv_done);
                 return true;
             };
-            bool ok = mbar_wait(q_full, 0, abort, p.err) && mbar_wait(&kv_full[0], 0, abort, p.err) && issue_s(0);
+            bool ok = mbar_wait(q_full, 0, abort, p.err) && mbar_wait(&k_full[0], 0, abort, p.err) && issue_s(0);
+            if (ok) umma_commit(&k_empty[0]);  // fires once S(0) is done
             for (int j = 0; ok && j < nkb; ++j) {
-                if (j + 1 < nkb)
-                    ok = mbar_wait(&kv_full[(j + 1) % PP_KV_STAGES], ((j + 1) / PP_KV_STAGES) & 1, abort, p.err) &&
-                         issue_s(j + 1);
-                if (ok) ok = issue_pv(j);
-                if (ok) umma_commit(&kv_empty[j % PP_KV_STAGES]);  // fires once P·V(j) is done
+                if (j + 1 < nkb) {
+                    const int s1 = (j + 1) % PP_KV_STAGES;
+                    ok = mbar_wait(&k_full[s1], ((j + 1) / PP_KV_STAGES) & 1, abort, p.err) && issue_s(j + 1);
+                    if (ok) umma_commit(&k_empty[s1]);
+                }
+                if (ok) ok = mbar_wait(&v_full[j % PP_KV_STAGES], (j / PP_KV_STAGES) & 1, abort, p.err) && issue_pv(j);
+                if (ok) umma_commit(&v_empty[j % PP_KV_STAGES]);  // fires once P·V(j) is done
             }
         }
     } else {
@@ -545,8 +565,8 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             // P·V of such a block reads keys 0..63 only).
             uint64_t sa = 0, sb = 0;
             {
-                uint32_t pk[32];
-                exp_columns<BF16, 0>(s, pk, sa, sb, m_used, s_lo);
+                uint32_t pk[1][32];
+                exp_columns<BF16, 0, 64>(s, pk, sa, sb, m_used, s_lo);
                 if (kb > 0) {
                     // P(kb − 1)·V must have finished reading P before it is overwritten, and O
                     // must hold it before a rescale.
@@ -554,7 +574,7 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                     if (!ok) break;
                     tc_fence_after();
                 }
-                tmem_st32(p_addr, pk);
+                tmem_st32(p_addr, pk[0]);
             }
             if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
                 uint32_t o[2][32];
@@ -570,9 +590,9 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 tmem_st32(o_addr + 32, o[1]);
             }
             if (!half) {
-                uint32_t pk[32];
-                exp_columns<BF16, TILE / 2>(s, pk, sa, sb, m_used, s_lo);
-                tmem_st32(p_addr + 32, pk);
+                uint32_t pk[1][32];
+                exp_columns<BF16, TILE / 2, 64>(s, pk, sa, sb, m_used, s_lo);
+                tmem_st32(p_addr + 32, pk[0]);
             }
             float sum0, sum1, sum2, sum3;
             f2_split(sa, sum0, sum1);
@@ -613,7 +633,7 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == MMA_WARP) {
         __syncwarp();
         tmem_dealloc(tmem, PP_TMEM_COLS);
     }
