@@ -353,10 +353,14 @@ attention_band_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
 // running maximum is updated lazily: it moves (and O, l are rescaled in TMEM) only when a row's
 // block maximum exceeds it by more than 2^8, so P stays ≤ 256 and the rescale is rare.
 // Interior key blocks skip masking.
-constexpr int PP_KV_STAGES = 2;
-constexpr int PP_OFF_Q = 0, PP_OFF_K = QKV_BYTES, PP_OFF_V = PP_OFF_K + PP_KV_STAGES * QKV_BYTES;
-constexpr int PP_OFF_BAR = PP_OFF_V + PP_KV_STAGES * QKV_BYTES;
-constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + 16 * 8 + 16;
+#ifndef ANCHA_ATTN_K_STAGES
+#define ANCHA_ATTN_K_STAGES 2
+#endif
+constexpr int PP_K_STAGES = ANCHA_ATTN_K_STAGES, PP_V_STAGES = 2;
+constexpr int PP_OFF_Q = 0, PP_OFF_K = QKV_BYTES, PP_OFF_V = PP_OFF_K + PP_K_STAGES * QKV_BYTES;
+constexpr int PP_OFF_BAR = PP_OFF_V + PP_V_STAGES * QKV_BYTES;
+constexpr int PP_NBARS = 1 + 2 * PP_K_STAGES + 2 * PP_V_STAGES + 4;
+constexpr int PP_SMEM_BYTES = 1024 + PP_OFF_BAR + PP_NBARS * 8 + 16;
 constexpr int PP_THREADS = 192;
 constexpr float PP_RESCALE_LOG2 = 8.f;
 constexpr uint32_t PP_TMEM_COLS = 256, PP_O_COL = 128, PP_P_COL = 192;
@@ -372,15 +376,15 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
     uint64_t* q_full = bars;
     // K and V run through separate rings: a K stage is free once S(kb) is done, a V stage once
     // P·V(kb) is, so the load of K(kb + 2) starts a block earlier than with shared K | V stages.
-    uint64_t* k_full = bars + 1;                   // [stage]
-    uint64_t* k_empty = bars + 1 + PP_KV_STAGES;   // [stage]
-    uint64_t* v_full = bars + 1 + 2 * PP_KV_STAGES;
-    uint64_t* v_empty = bars + 1 + 3 * PP_KV_STAGES;
-    uint64_t* s_full = bars + 9;                   // S(kb) computed
-    uint64_t* s_free = bars + 10;                  // S(kb) copied to registers (128 arrivals)
-    uint64_t* p_ready = bars + 11;                 // P(kb) written (128 arrivals)
-    uint64_t* pv_done = bars + 12;                 // O += P(kb)·V(kb) completed
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+    uint64_t* k_full = bars + 1;                                  // [K stage]
+    uint64_t* k_empty = k_full + PP_K_STAGES;                     // [K stage]
+    uint64_t* v_full = k_empty + PP_K_STAGES;                     // [V stage]
+    uint64_t* v_empty = v_full + PP_V_STAGES;                     // [V stage]
+    uint64_t* s_full = v_empty + PP_V_STAGES;                     // S(kb) computed
+    uint64_t* s_free = s_full + 1;                                // S(kb) copied to registers (128 arrivals)
+    uint64_t* p_ready = s_full + 2;                               // P(kb) written (128 arrivals)
+    uint64_t* pv_done = s_full + 3;                               // O += P(kb)·V(kb) completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + PP_NBARS);
     volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
     const int tile = blockIdx.x % p.tiles_per_group;
@@ -392,9 +396,11 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
 
     if (threadIdx.x == SOFT) {
         mbar_init(q_full, 1);
-        for (int s = 0; s < PP_KV_STAGES; ++s) {
+        for (int s = 0; s < PP_K_STAGES; ++s) {
             mbar_init(&k_full[s], 1);
             mbar_init(&k_empty[s], 1);
+        }
+        for (int s = 0; s < PP_V_STAGES; ++s) {
             mbar_init(&v_full[s], 1);
             mbar_init(&v_empty[s], 1);
         }
@@ -424,14 +430,15 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             uint64_t* empty = is_k ? k_empty : v_empty;
             const int off = is_k ? PP_OFF_K : PP_OFF_V;
             const int col = (is_k ? p.k_col : p.v_col) + head * HD;
+            const int stages = is_k ? PP_K_STAGES : PP_V_STAGES;
             if (is_k) {
                 mbar_arrive_expect_tx(q_full, QKV_BYTES);
                 tma_load_4d(smem + PP_OFF_Q, &tmap, q_full, p.q_col + head * HD, q0, gi, go);
             }
             int issued = 0;
             for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % PP_KV_STAGES;
-                if (!mbar_wait(&empty[s], ((kb / PP_KV_STAGES) & 1) ^ 1, abort, p.err)) break;
+                const int s = kb % stages;
+                if (!mbar_wait(&empty[s], ((kb / stages) & 1) ^ 1, abort, p.err)) break;
                 mbar_arrive_expect_tx(&full[s], QKV_BYTES);
                 tma_load_4d(smem + off + s * QKV_BYTES, &tmap, &full[s], col, kb * TILE, gi, go);
                 ++issued;
@@ -441,8 +448,8 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 if (is_k)
                     while (!mbar_try_wait(q_full, 0) && clock64() - c0 < kWaitCycles) {
                     }
-                for (int kb = max(0, issued - PP_KV_STAGES); kb < issued; ++kb)
-                    while (!mbar_try_wait(&full[kb % PP_KV_STAGES], (kb / PP_KV_STAGES) & 1) &&
+                for (int kb = max(0, issued - stages); kb < issued; ++kb)
+                    while (!mbar_try_wait(&full[kb % stages], (kb / stages) & 1) &&
                            clock64() - c0 < kWaitCycles) {
                     }
             }
@@ -455,7 +462,7 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             auto issue_s = [&](int j) -> bool {
                 if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, abort, p.err)) return false;
                 tc_fence_after();
-                const uint64_t k_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_K + (j % PP_KV_STAGES) * QKV_BYTES));
+                const uint64_t k_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_K + (j % PP_K_STAGES) * QKV_BYTES));
                 // A key block with at most 64 valid keys (the last one) computes only S[:, 0:64];
                 // the softmax then reads only those columns.
                 const uint32_t idesc = p.tokens - j * TILE <= TILE / 2 ? p.idesc_s_half : p.idesc_s;
@@ -468,7 +475,7 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             auto issue_pv = [&](int k) -> bool {
                 if (!mbar_wait(p_ready, k & 1, abort, p.err)) return false;
                 tc_fence_after();
-                const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_V + (k % PP_KV_STAGES) * QKV_BYTES));
+                const uint64_t v_desc = umma_desc_sw128(smem_u32(smem + PP_OFF_V + (k % PP_V_STAGES) * QKV_BYTES));
                 // Steps of 16 keys up to the last valid key: P is 0 beyond it.
                 const int steps = min(TILE / 16, (p.tokens - k * TILE + 15) / 16);
                 // 16 keys = 16 rows of 128 bytes = 128 descriptor units; the full-block case is
@@ -490,12 +497,12 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             if (ok) umma_commit(&k_empty[0]);  // fires once S(0) is done
             for (int j = 0; ok && j < nkb; ++j) {
                 if (j + 1 < nkb) {
-                    const int s1 = (j + 1) % PP_KV_STAGES;
-                    ok = mbar_wait(&k_full[s1], ((j + 1) / PP_KV_STAGES) & 1, abort, p.err) && issue_s(j + 1);
+                    const int s1 = (j + 1) % PP_K_STAGES;
+                    ok = mbar_wait(&k_full[s1], ((j + 1) / PP_K_STAGES) & 1, abort, p.err) && issue_s(j + 1);
                     if (ok) umma_commit(&k_empty[s1]);
                 }
-                if (ok) ok = mbar_wait(&v_full[j % PP_KV_STAGES], (j / PP_KV_STAGES) & 1, abort, p.err) && issue_pv(j);
-                if (ok) umma_commit(&v_empty[j % PP_KV_STAGES]);  // fires once P·V(j) is done
+                if (ok) ok = mbar_wait(&v_full[j % PP_V_STAGES], (j / PP_V_STAGES) & 1, abort, p.err) && issue_pv(j);
+                if (ok) umma_commit(&v_empty[j % PP_V_STAGES]);  // fires once P·V(j) is done
             }
         }
     } else {

@@ -29,8 +29,9 @@ __constant__ int kSplitA[6] = {0, 0, 1, 0, 2, 1};
 __constant__ int kSplitB[6] = {0, 1, 0, 2, 0, 1};
 constexpr int A_BYTES = BM * BK * 2;
 // Epilogue warps per CTA (a multiple of 4: EPI / 4 warps per TMEM lane quarter): 16 for the
-// GELU / tanh epilogues, whose long dependent chains need the extra latency hiding, 8 for the
-// others, which need the registers (10 warps allow 168 registers a thread, 18 warps 96).
+// GELU / tanh epilogues, whose long dependent chains need the extra latency hiding, and for RoPE
+// (its table loads wait on L2), 8 for the others, which need the registers (10 warps allow 168
+// registers a thread, 18 warps 96).
 constexpr int EPI_ACT = 16, EPI_PLAIN = 8;
 constexpr int STAGE_BUFS = 1;       // staging buffers per epilogue warp
 template <int EPI>
@@ -677,8 +678,11 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
     const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles * p.groups;
     if (tiles > 0x7fffffff) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: too many tiles");
     p.tiles = (int)tiles;
-    const bool act = p.act == ANCHA_ACT_GELU || p.act == ANCHA_ACT_TANH;
-    if (act && p.out16) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: no 16-bit copy after an activation");
+    if ((p.act == ANCHA_ACT_GELU || p.act == ANCHA_ACT_TANH) && p.out16)
+        return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: no 16-bit copy after an activation");
+    // Sixteen epilogue warps for the activations and for RoPE (whose table loads wait on L2),
+    // eight for the plain and residual epilogues.
+    const bool act = p.act == ANCHA_ACT_GELU || p.act == ANCHA_ACT_TANH || ((p.rope || p.rope_pairs) && !p.out16);
     if (pair) {
         switch (bn) {
             case 256: return act ? launch<256, 4, EPI_ACT, true>(ta, tb, to, to16, p, s) : launch<256, 4, EPI_PLAIN, true>(ta, tb, to, to16, p, s);
