@@ -2,11 +2,17 @@
 // reference's rules (fused/mod.rs:20-176), status codes and the per-thread last error.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <string>
 
+#ifndef ANCHA_FP32_SPLIT
+#define ANCHA_FP32_SPLIT 1  // fp32 operands on the tensor cores as three-plane bf16 splits
+#endif
+
 #include "attention.cuh"
+#include "rowops.cuh"
 #include "dsp.cuh"
 #include "gemm.cuh"
 #include "mdx23c_model.hpp"
@@ -99,6 +105,24 @@ int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, 
         int st = attention_tc(a, s);
         if (st != ANCHA_E_UNSUPPORTED) return st;
     }
+#if ANCHA_FP32_SPLIT
+    // fp32 time axis on the tensor cores: the used q | k | v columns of every row up to the last
+    // one the groups reach, split into three bf16 planes in a stream-ordered scratch buffer.
+    if (a.elt == ELT_F32 && q == k && q == v && a.tokens > 64 && a.groups > 0 && a.groups % a.group_inner == 0) {
+        const int64_t outer = a.groups / a.group_inner;
+        const int64_t rows = (outer - 1) * a.group_outer_stride + (a.group_inner - 1) * a.group_inner_stride +
+                             (int64_t)(a.tokens - 1) * a.token_stride + 1;
+        const int64_t cols = std::max(std::max(a.q_col, a.k_col), a.v_col) + span;
+        const int64_t pld = (cols + 7) / 8 * 8;
+        void* planes = nullptr;
+        if (cudaMallocAsync(&planes, (size_t)(3 * rows * pld * 2), s) != cudaSuccess)
+            return fail(ANCHA_E_CUDA, "attention: cudaMallocAsync of the operand planes");
+        int st = split3_rows_strided(static_cast<const float*>(q), a.ld, planes, pld, rows * pld, rows, (int)cols, s);
+        if (st == ANCHA_OK) st = attention_tc_split(a, planes, pld, rows * pld, s);
+        cudaFreeAsync(planes, s);
+        if (st != ANCHA_E_UNSUPPORTED) return st;
+    }
+#endif
     return attention_ffma(a, s);
 }
 

@@ -13,6 +13,8 @@
 // Two kernels: attention_pp_kernel for tokens > 64 (the time axis, online softmax over key
 // blocks, one query tile per CTA, two CTAs per SM) and attention_band_kernel for tokens ≤ 64
 // (the band axis, two problems per tile, persistent and pipelined across tiles).
+#include <algorithm>
+
 #include "attention.cuh"
 #include "tc.cuh"
 
@@ -678,6 +680,325 @@ int launch_band(const CUtensorMap& map, const CUtensorMap& omap, const AttnTcPar
     return check_launch("attention_band");
 }
 
+// fp32 mode, time axis (tokens > 64), on the tensor cores. The f32 q / k / v arrive split into
+// three bf16 planes, x = hi + mid + lo with hi = bf16(x), mid = bf16(x − hi), lo = bf16(x − hi −
+// mid) (24 significant bits), and each product runs as the six plane products whose weight is at
+// least 2^-24 of the leading one (mm, lh, hl, mh, hm, hh, in that order), accumulated in f32 in TMEM:
+// S = Q·Kᵀ as 6 × 4 UMMAs per key block, O += P·V as 6 × 8, with P (f32 probabilities ≤ 2^8)
+// split into three bf16 planes by the softmax and stored to TMEM as the A operand. The
+// exponentials are MUFU ex2.approx only (no polynomial columns). One CTA per SM: TMEM holds S
+// (128 columns), O (64) and the three P planes (3 × 64) in 512 columns. Shared memory holds the
+// three Q planes, one K stage and two V stages (three planes each). Warp roles, barriers and
+// the lazy rescale are those of attention_pp_kernel.
+constexpr int SP_PLANE = QKV_BYTES;  // one 128 × 64 bf16 tile
+constexpr int SP_V_STAGES = 2;
+constexpr int SP_OFF_Q = 0, SP_OFF_K = 3 * SP_PLANE, SP_OFF_V = SP_OFF_K + 3 * SP_PLANE;
+constexpr int SP_OFF_BAR = SP_OFF_V + SP_V_STAGES * 3 * SP_PLANE;
+constexpr int SP_NBARS = 3 + 2 * SP_V_STAGES + 4;
+constexpr int SP_SMEM_BYTES = 1024 + SP_OFF_BAR + SP_NBARS * 8 + 16;
+constexpr uint32_t SP_TMEM_COLS = 512, SP_O_COL = 128, SP_P_COL = 256;
+
+// Plane of the A and B operands in each of the six products, smallest weight first (mm, lh, hl,
+// mh, hm, hh): each product is added to the f32 accumulator with one rounding at the
+// accumulator's magnitude, so the small products are summed before the large one arrives.
+__device__ __forceinline__ int split_a(int t) { return t == 0 || t == 3 ? 1 : t == 1 ? 2 : 0; }
+__device__ __forceinline__ int split_b(int t) { return t == 0 || t == 4 ? 1 : t == 2 ? 2 : 0; }
+
+struct PlaneMaps {
+    CUtensorMap plane[3];  // {columns, tokens, inner groups, outer groups} over each bf16 plane
+};
+
+// Splits a pair of f32 probabilities into the hi / mid / lo bf16 pairs of the three P planes.
+__device__ __forceinline__ void split_pair(float e0, float e1, uint32_t& h, uint32_t& m, uint32_t& l) {
+    const __nv_bfloat162 hh = __floats2bfloat162_rn(e0, e1);
+    const float r0 = e0 - __low2float(hh), r1 = e1 - __high2float(hh);
+    const __nv_bfloat162 mm = __floats2bfloat162_rn(r0, r1);
+    const __nv_bfloat162 ll = __floats2bfloat162_rn(r0 - __low2float(mm), r1 - __high2float(mm));
+    h = *reinterpret_cast<const uint32_t*>(&hh);
+    m = *reinterpret_cast<const uint32_t*>(&mm);
+    l = *reinterpret_cast<const uint32_t*>(&ll);
+}
+
+// Exponentials of score columns [J0, J0 + 64) (MUFU), the three P planes of those columns
+// (32 packed words each) and the row sum in f32.
+template <int J0>
+__device__ __forceinline__ void exp_planes(const uint32_t (&s)[4][32], uint32_t (&ph)[32], uint32_t (&pm)[32],
+                                           uint32_t (&pl)[32], float& sum, float m_used) {
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+    for (int j = J0; j < J0 + 64; j += 2) {
+        const float e0 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32]), LOG2E, -m_used));
+        const float e1 = ex2_approx(fmaf(__uint_as_float(s[j / 32][j % 32 + 1]), LOG2E, -m_used));
+        acc0 += e0;
+        acc1 += e1;
+        split_pair(e0, e1, ph[(j - J0) / 2], pm[(j - J0) / 2], pl[(j - J0) / 2]);
+    }
+    sum += acc0 + acc1;
+}
+
+__global__ void __launch_bounds__(PP_THREADS, 1)
+attention_split_kernel(const __grid_constant__ PlaneMaps maps, const AttnTcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SP_OFF_BAR);
+    uint64_t* q_full = bars;
+    uint64_t* k_full = bars + 1;
+    uint64_t* k_empty = bars + 2;
+    uint64_t* v_full = bars + 3;                 // [V stage]
+    uint64_t* v_empty = v_full + SP_V_STAGES;    // [V stage]
+    uint64_t* s_full = v_empty + SP_V_STAGES;    // S(kb) computed
+    uint64_t* s_free = s_full + 1;               // S(kb) copied to registers (128 arrivals)
+    uint64_t* p_ready = s_full + 2;              // P(kb) planes written (128 arrivals)
+    uint64_t* pv_done = s_full + 3;              // O += P(kb)·V(kb) completed
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + SP_NBARS);
+    volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int tile = blockIdx.x % p.tiles_per_group;
+    const int gi = blockIdx.x / p.tiles_per_group;
+    const int go = blockIdx.z, head = blockIdx.y;
+    const int nkb = p.tiles_per_group;
+    const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+    const int q0 = tile * TILE;
+
+    if (threadIdx.x == 128) {
+        mbar_init(q_full, 1);
+        mbar_init(k_full, 1);
+        mbar_init(k_empty, 1);
+        for (int s = 0; s < SP_V_STAGES; ++s) {
+            mbar_init(&v_full[s], 1);
+            mbar_init(&v_empty[s], 1);
+        }
+        mbar_init(s_full, 1);
+        mbar_init(s_free, 128);
+        mbar_init(p_ready, 128);
+        mbar_init(pv_done, 1);
+        *abort = 0;
+        fence_barrier_init();
+        fence_proxy_async();
+        for (int pl = 0; pl < 3; ++pl) prefetch_tma(&maps.plane[pl]);
+    }
+    if (warp == 5) {
+        tmem_alloc(tmem_slot, SP_TMEM_COLS);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        if (lane == 0) {
+            // Q once; per key block K(kb) into the one K stage (free once S(kb − 1) is done),
+            // then V(kb) into stage kb mod 2 (free once P·V(kb − 2) is done, which precedes
+            // S(kb) in the UMMA stream, so the V wait never holds up the next K load).
+            mbar_arrive_expect_tx(q_full, 3 * SP_PLANE);
+            for (int pl = 0; pl < 3; ++pl)
+                tma_load_4d(smem + SP_OFF_Q + pl * SP_PLANE, &maps.plane[pl], q_full, p.q_col + head * HD, q0, gi, go);
+            int nk = 0, nv = 0;
+            for (int kb = 0; kb < nkb; ++kb) {
+                if (!mbar_wait(k_empty, (kb & 1) ^ 1, abort, p.err)) break;
+                mbar_arrive_expect_tx(k_full, 3 * SP_PLANE);
+                for (int pl = 0; pl < 3; ++pl)
+                    tma_load_4d(smem + SP_OFF_K + pl * SP_PLANE, &maps.plane[pl], k_full, p.k_col + head * HD,
+                                kb * TILE, gi, go);
+                ++nk;
+                const int sv = kb % SP_V_STAGES;
+                if (!mbar_wait(&v_empty[sv], ((kb / SP_V_STAGES) & 1) ^ 1, abort, p.err)) break;
+                mbar_arrive_expect_tx(&v_full[sv], 3 * SP_PLANE);
+                for (int pl = 0; pl < 3; ++pl)
+                    tma_load_4d(smem + SP_OFF_V + (sv * 3 + pl) * SP_PLANE, &maps.plane[pl], &v_full[sv],
+                                p.v_col + head * HD, kb * TILE, gi, go);
+                ++nv;
+            }
+            if (*abort) {  // let copies in flight land before the CTA exits (bounded)
+                const long long c0 = clock64();
+                while (!mbar_try_wait(q_full, 0) && clock64() - c0 < kWaitCycles) {
+                }
+                if (nk > 0)
+                    while (!mbar_try_wait(k_full, (nk - 1) & 1) && clock64() - c0 < kWaitCycles) {
+                    }
+                for (int kb = max(0, nv - SP_V_STAGES); kb < nv; ++kb)
+                    while (!mbar_try_wait(&v_full[kb % SP_V_STAGES], (kb / SP_V_STAGES) & 1) &&
+                           clock64() - c0 < kWaitCycles) {
+                    }
+            }
+        }
+    } else if (warp == 5) {
+        if (lane == 0) {
+            const uint32_t q_base = smem_u32(smem + SP_OFF_Q), k_base = smem_u32(smem + SP_OFF_K);
+            auto issue_s = [&](int j) -> bool {
+                if (!mbar_wait(k_full, j & 1, abort, p.err)) return false;
+                if (j >= 1 && !mbar_wait(s_free, (j - 1) & 1, abort, p.err)) return false;
+                tc_fence_after();
+                const uint32_t idesc = p.tokens - j * TILE <= TILE / 2 ? p.idesc_s_half : p.idesc_s;
+#pragma unroll
+                for (int t = 0; t < 6; ++t) {
+                    const uint64_t qd = umma_desc_sw128(q_base + split_a(t) * SP_PLANE);
+                    const uint64_t kd = umma_desc_sw128(k_base + split_b(t) * SP_PLANE);
+#pragma unroll
+                    for (int kk = 0; kk < HD / 16; ++kk)
+                        umma_f16(tmem, qd + 2 * kk, kd + 2 * kk, idesc, (t | kk) != 0);
+                }
+                umma_commit(s_full);
+                umma_commit(k_empty);
+                return true;
+            };
+            auto issue_pv = [&](int k) -> bool {
+                const int sv = k % SP_V_STAGES;
+                if (!mbar_wait(&v_full[sv], (k / SP_V_STAGES) & 1, abort, p.err)) return false;
+                if (!mbar_wait(p_ready, k & 1, abort, p.err)) return false;
+                tc_fence_after();
+                const uint32_t v_base = smem_u32(smem + SP_OFF_V + sv * 3 * SP_PLANE);
+                const int steps = min(TILE / 16, (p.tokens - k * TILE + 15) / 16);
+                for (int t = 0; t < 6; ++t) {
+                    const uint64_t vd = umma_desc_sw128(v_base + split_b(t) * SP_PLANE);
+                    const uint32_t pa = tmem + SP_P_COL + split_a(t) * (TILE / 2);
+                    for (int kk = 0; kk < steps; ++kk)
+                        umma_f16_ts(tmem + SP_O_COL, pa + kk * 8, vd + 128 * kk, p.idesc_o,
+                                    (k > 0 || t > 0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(pv_done);
+                umma_commit(&v_empty[sv]);
+                return true;
+            };
+            bool ok = mbar_wait(q_full, 0, abort, p.err) && issue_s(0);
+            for (int j = 0; ok && j < nkb; ++j) {
+                if (j + 1 < nkb) ok = issue_s(j + 1);
+                if (ok) ok = issue_pv(j);
+            }
+        }
+    } else {
+        const int row = threadIdx.x;  // query row of the tile (warps 0–3)
+        const int tok = q0 + row;
+        const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+        const uint32_t s_addr = tmem + lane_off;
+        const uint32_t o_addr = tmem + lane_off + SP_O_COL;
+        const uint32_t p_addr = tmem + lane_off + SP_P_COL;
+        const bool live = q0 + warp * 32 < p.tokens;
+        float m_used = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int kb = 0; kb < nkb; ++kb) {
+            ok = __all_sync(0xffffffffu, mbar_wait(s_full, kb & 1, abort, p.err));
+            if (!ok) break;
+            if (!live) {
+                mbar_arrive(s_free);
+                if (kb > 0) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (kb - 1) & 1, abort, p.err));
+                    if (!ok) break;
+                }
+                mbar_arrive(p_ready);
+                continue;
+            }
+            tc_fence_after();
+            uint32_t s[4][32];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, s[c]);
+            tmem_wait_ld();
+            tc_fence_before();
+            mbar_arrive(s_free);
+            const int nvalid = min(TILE, p.tokens - kb * TILE);
+            const bool half = nvalid <= TILE / 2;
+            if (nvalid < TILE) {
+#pragma unroll
+                for (int c = 0; c < TILE; ++c)
+                    if (c >= nvalid) s[c / 32][c % 32] = __float_as_uint(-INFINITY);
+            }
+            float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < TILE; c += 4) {
+                mx0 = fmax3(mx0, __uint_as_float(s[c / 32][c % 32]), __uint_as_float(s[c / 32][c % 32 + 1]));
+                mx1 = fmax3(mx1, __uint_as_float(s[c / 32][c % 32 + 2]), __uint_as_float(s[c / 32][c % 32 + 3]));
+            }
+            const float m_blk = fmaxf(mx0, mx1) * LOG2E;
+            float corr = 1.f;
+            if (m_blk > m_used + PP_RESCALE_LOG2) {
+                corr = m_used == -INFINITY ? 0.f : ex2_approx(m_used - m_blk);
+                m_used = m_blk;
+                l *= corr;
+            }
+            {
+                uint32_t ph[32], pm[32], pl[32];
+                exp_planes<0>(s, ph, pm, pl, l, m_used);
+                if (kb > 0) {
+                    ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (kb - 1) & 1, abort, p.err));
+                    if (!ok) break;
+                    tc_fence_after();
+                }
+                tmem_st32(p_addr, ph);
+                tmem_st32(p_addr + TILE / 2, pm);
+                tmem_st32(p_addr + TILE, pl);
+            }
+            if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
+                uint32_t o[2][32];
+                tmem_ld32(o_addr, o[0]);
+                tmem_ld32(o_addr + 32, o[1]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int d = 0; d < 32; ++d) {
+                    o[0][d] = __float_as_uint(__uint_as_float(o[0][d]) * corr);
+                    o[1][d] = __float_as_uint(__uint_as_float(o[1][d]) * corr);
+                }
+                tmem_st32(o_addr, o[0]);
+                tmem_st32(o_addr + 32, o[1]);
+            }
+            if (!half) {
+                uint32_t ph[32], pm[32], pl[32];
+                exp_planes<TILE / 2>(s, ph, pm, pl, l, m_used);
+                tmem_st32(p_addr + 32, ph);
+                tmem_st32(p_addr + TILE / 2 + 32, pm);
+                tmem_st32(p_addr + TILE + 32, pl);
+            }
+            tmem_wait_st();
+            tc_fence_before();
+            mbar_arrive(p_ready);
+        }
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (nkb - 1) & 1, abort, p.err));
+        if (ok && live) {
+            tc_fence_after();
+            uint32_t o[2][32];
+            tmem_ld32(o_addr, o[0]);
+            tmem_ld32(o_addr + 32, o[1]);
+            tmem_wait_ld();
+            if (tok < p.tokens) {
+                const int64_t orow = (int64_t)go * p.group_outer_stride + (int64_t)gi * p.group_inner_stride +
+                                     (int64_t)tok * p.token_stride;
+                float scale = 1.f / l;
+                if (p.gate_col >= 0) {
+                    const float gl = reinterpret_cast<const float*>(p.q)[orow * p.ld + p.gate_col + head];
+                    scale /= 1.f + expf(-gl);
+                }
+                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + orow * p.out_ld + p.out_col +
+                                                        head * HD);
+#pragma unroll
+                for (int q = 0; q < HD / 4; ++q)
+                    dst[q] = make_float4(__uint_as_float(o[q / 8][(q % 8) * 4]) * scale,
+                                         __uint_as_float(o[q / 8][(q % 8) * 4 + 1]) * scale,
+                                         __uint_as_float(o[q / 8][(q % 8) * 4 + 2]) * scale,
+                                         __uint_as_float(o[q / 8][(q % 8) * 4 + 3]) * scale);
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        __syncwarp();
+        tmem_dealloc(tmem, SP_TMEM_COLS);
+    }
+}
+
+int launch_split(const PlaneMaps& maps, const AttnTcParams& p, dim3 grid, cudaStream_t s) {
+    static bool configured[64] = {};
+    int dev = 0;
+    ANCHA_CUDA(cudaGetDevice(&dev));
+    if (!configured[dev & 63]) {
+        ANCHA_CUDA(cudaFuncSetAttribute(attention_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SP_SMEM_BYTES));
+        configured[dev & 63] = true;
+    }
+    attention_split_kernel<<<grid, PP_THREADS, SP_SMEM_BYTES, s>>>(maps, p);
+    return check_launch("attention_split");
+}
+
 }  // namespace
 
 int attention_tc(const AttnArgs& a, cudaStream_t stream) {
@@ -743,6 +1064,60 @@ int attention_tc(const AttnArgs& a, cudaStream_t stream) {
                           BT, BG));
     return a.elt == ELT_BF16 ? launch_band<true>(map, omap, p, (int)pairs, a.heads, (int)total, stream)
                              : launch_band<false>(map, omap, p, (int)pairs, a.heads, (int)total, stream);
+}
+
+
+int attention_tc_split(const AttnArgs& a, const void* planes, int64_t plane_ld, int64_t plane_stride,
+                       cudaStream_t stream) {
+    if (a.elt != ELT_F32 || a.head_dim != HD || a.tokens <= 64)
+        return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: f32 time axis with head_dim 64 only");
+    if (a.groups == 0) return ANCHA_OK;
+    if (a.q != a.k || a.q != a.v) return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: q, k, v must share one buffer");
+    const uintptr_t pb = reinterpret_cast<uintptr_t>(planes);
+    const int64_t span = (int64_t)a.heads * HD;
+    if (plane_ld < std::max(std::max(a.q_col, a.k_col), a.v_col) + span)
+        return fail(ANCHA_E_INVALID, "attention_tc_split: plane rows too short");
+    if (pb % 16 || (plane_ld * 2) % 16 || (plane_stride * 2) % 16 || (a.q_col * 2) % 16 || (a.k_col * 2) % 16 ||
+        (a.v_col * 2) % 16)
+        return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: planes not 16-byte aligned");
+    const uintptr_t ob = reinterpret_cast<uintptr_t>(a.out);
+    if (ob % 16 || (a.out_ld * 4) % 16 || (a.out_col * 4) % 16)
+        return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: output not 16-byte aligned");
+    AttnTcParams p{};
+    p.tokens = a.tokens;
+    p.group_inner = (int)a.group_inner;
+    p.group_outer = (int)ceil_div(a.groups, a.group_inner);
+    if ((int64_t)p.group_outer * a.group_inner != a.groups)
+        return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: groups must be a multiple of group_inner");
+    p.tiles_per_group = (int)ceil_div(a.tokens, TILE);
+    p.q_col = a.q_col; p.k_col = a.k_col; p.v_col = a.v_col;
+    p.gate_col = a.gate ? a.gate_col : -1;
+    p.out_col = a.out_col;
+    p.q = a.gate ? a.gate : a.q;  // f32 gate logits
+    p.out = a.out;
+    p.ld = a.ld; p.out_ld = a.out_ld;
+    p.group_inner_stride = a.group_inner_stride;
+    p.group_outer_stride = a.group_outer_stride;
+    p.token_stride = a.token_stride;
+    p.idesc_s = umma_idesc_f16(1, TILE, TILE, 0);
+    p.idesc_o = umma_idesc_f16(1, TILE, HD, 1);
+    p.idesc_s_half = umma_idesc_f16(1, TILE, TILE / 2, 0);
+    p.err = device_error_word();
+    // The planes keep the source's row indexing (row stride plane_ld elements), plane p at
+    // planes + p · plane_stride elements.
+    const int64_t s1 = a.token_stride * plane_ld;
+    const int64_t s2 = a.group_inner_stride * plane_ld;
+    const int64_t s3 = p.group_outer > 1 ? a.group_outer_stride * plane_ld : plane_ld;
+    PlaneMaps maps;
+    for (int pl = 0; pl < 3; ++pl)
+        ANCHA_TRY(make_tma_4d(&maps.plane[pl], reinterpret_cast<const __nv_bfloat16*>(planes) + pl * plane_stride,
+                              ELT_BF16, plane_ld, a.tokens, a.group_inner, p.group_outer, s1 > 0 ? s1 : plane_ld,
+                              s2 > 0 ? s2 : plane_ld, s3 > 0 ? s3 : plane_ld, TILE, 1));
+    const int64_t gx = (int64_t)p.tiles_per_group * a.group_inner;
+    if (gx > 0x7fffffff || a.heads > 65535 || p.group_outer > 65535)
+        return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: grid too large");
+    dim3 grid((unsigned)gx, (unsigned)a.heads, (unsigned)p.group_outer);
+    return launch_split(maps, p, grid, stream);
 }
 
 }  // namespace ancha

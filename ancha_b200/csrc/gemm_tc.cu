@@ -24,9 +24,10 @@ namespace ancha {
 namespace {
 
 constexpr int BM = 128, BK = 64;
-// split3: the six significant products of (hi, mid, lo) planes: hh, hm, mh, hl, lh, mm.
-__constant__ int kSplitA[6] = {0, 0, 1, 0, 2, 1};
-__constant__ int kSplitB[6] = {0, 1, 0, 2, 0, 1};
+// split3: the six significant products of (hi, mid, lo) planes, smallest weight first (mm, lh, hl,
+// mh, hm, hh) so that the small products accumulate before the large one sets the magnitude.
+__constant__ int kSplitA[6] = {1, 2, 0, 1, 0, 0};
+__constant__ int kSplitB[6] = {1, 0, 2, 0, 1, 0};
 constexpr int A_BYTES = BM * BK * 2;
 // Epilogue warps per CTA (a multiple of 4: EPI / 4 warps per TMEM lane quarter): 16 for the
 // GELU / tanh epilogues, whose long dependent chains need the extra latency hiding, and for RoPE

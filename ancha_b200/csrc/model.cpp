@@ -477,7 +477,9 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
         w.z.alloc((int64_t)chunks * frames * total_width * 4);
         if (split_kp_) w.z16.alloc(R * split_kp_ * 2);
         w.glu.alloc(R * max_width * 4);
-        if (split_) w.a3.alloc((size_t)3 * R * std::max(std::max(c.dim, inner), hidden) * 2);
+        // The three bf16 planes of a GEMM's A operand, or of the q | k | v rows for the time-axis
+        // attention (3 · inner columns).
+        if (split_) w.a3.alloc((size_t)3 * R * std::max(std::max(c.dim, 3 * inner), hidden) * 2);
         if (fuse_norms_) {
             w.ss_x.alloc(R * (c.dim / 32) * 4);
             w.ss_y.alloc(R * (c.dim / 32) * 4);
@@ -709,7 +711,14 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
         a.group_outer_stride = (int64_t)bands * T;
         a.token_stride = T;
     }
-    int ast = bf != ELT_F32 ? attention_tc(a, s) : ANCHA_E_UNSUPPORTED;
+    int ast = ANCHA_E_UNSUPPORTED;
+    if (bf != ELT_F32) {
+        ast = attention_tc(a, s);
+    } else if (split_ && time_axis && a.tokens > 64) {
+        // fp32 on the tensor cores: the q | k | v | gate rows split into three bf16 planes.
+        ANCHA_TRY(split3_rows(ws_.qkvg.as<float>(), ldq, ws_.a3.p, R, 3 * inner, s));
+        ast = attention_tc_split(a, ws_.a3.p, 3 * inner, R * 3 * inner, s);
+    }
     if (ast == ANCHA_E_UNSUPPORTED) ast = attention_ffma(a, s);
     ANCHA_TRY(ast);
     // Output projection + residual (with the SourceNorm the previous block deferred), then the

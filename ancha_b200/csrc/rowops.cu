@@ -173,8 +173,8 @@ int cast_rows(const float* x, int64_t ldx, void* y, int y_type, int64_t ldy, int
 }
 
 namespace {
-__global__ void split3_kernel(const float* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ y,
-                              int64_t rows, int dim) {
+__global__ void split3_kernel(const float* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ y, int64_t ldy,
+                              int64_t plane, int64_t rows, int dim) {
     const int64_t n = rows * dim;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= n) return;
@@ -184,18 +184,24 @@ __global__ void split3_kernel(const float* __restrict__ x, int64_t ldx, __nv_bfl
     const float r1 = v - __bfloat162float(h);
     const __nv_bfloat16 m = __float2bfloat16_rn(r1);
     const float r2 = r1 - __bfloat162float(m);
-    y[i] = h;
-    y[n + i] = m;
-    y[2 * n + i] = __float2bfloat16_rn(r2);
+    const int64_t o = r * ldy + c;
+    y[o] = h;
+    y[plane + o] = m;
+    y[2 * plane + o] = __float2bfloat16_rn(r2);
 }
 }  // namespace
 
-int split3_rows(const float* x, int64_t ldx, void* y, int64_t rows, int dim, cudaStream_t s) {
+int split3_rows_strided(const float* x, int64_t ldx, void* y, int64_t ldy, int64_t plane, int64_t rows, int dim,
+                        cudaStream_t s) {
     const int64_t n = rows * dim;
     if (n == 0) return ANCHA_OK;
-    split3_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(x, ldx, reinterpret_cast<__nv_bfloat16*>(y), rows,
-                                                             dim);
+    split3_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(x, ldx, reinterpret_cast<__nv_bfloat16*>(y), ldy, plane,
+                                                             rows, dim);
     return check_launch("split3_rows");
+}
+
+int split3_rows(const float* x, int64_t ldx, void* y, int64_t rows, int dim, cudaStream_t s) {
+    return split3_rows_strided(x, ldx, y, dim, rows * dim, rows, dim, s);
 }
 
 int band_gather(const float* spec, int chunks, int frames, int columns, const int* cols,

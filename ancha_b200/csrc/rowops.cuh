@@ -13,6 +13,10 @@ int cast_rows(const float* x, int64_t ldx, void* y, int y_type, int64_t ldy, int
 // within 2^-24 relative; written as planes y[p][r][c] (p = 0, 1, 2; plane stride rows·dim, row
 // stride dim).
 int split3_rows(const float* x, int64_t ldx, void* y, int64_t rows, int dim, cudaStream_t s);
+// The same split of columns [0, dim) of each row into planes with row stride ldy, plane p at
+// y + p · plane elements.
+int split3_rows_strided(const float* x, int64_t ldx, void* y, int64_t ldy, int64_t plane, int64_t rows, int dim,
+                        cudaStream_t s);
 int band_gather(const float* spec, int chunks, int frames, int columns, const int* cols,
                 const int* offsets, int bands, int total, float* z, cudaStream_t s);
 // band_gather in f16 with each band's row zero-padded to kp features, rows ordered

@@ -44,8 +44,10 @@ enum {
 /* Element types of kernel operands. */
 enum { ANCHA_F32 = 0, ANCHA_BF16 = 1, ANCHA_F16 = 2 };
 
-/* Model arithmetic: F32 = fp32 FFMA kernels throughout; BF16 / F16 = bf16 / f16 operands
- * on the tcgen05 tensor cores (GEMMs and attention) with fp32 accumulation; the residual
+/* Model arithmetic: F32 = fp32 operands, the transformer GEMMs and the time-axis attention
+ * on the tcgen05 tensor cores as three-plane bf16 splits (hi + mid + lo, 24 significant bits;
+ * six plane products accumulated in fp32), the rest on fp32 FFMA kernels; BF16 / F16 = bf16 /
+ * f16 operands on the tensor cores (GEMMs and attention) with fp32 accumulation; the residual
  * stream, norms, softmax statistics and DSP stay fp32 in every mode. */
 enum { ANCHA_PRECISION_F32 = 0, ANCHA_PRECISION_BF16 = 1, ANCHA_PRECISION_F16 = 2 };
 
@@ -92,7 +94,11 @@ typedef struct {
 
 /* softmax(q·kᵀ)·v per (group, head), non-causal, q pre-scaled by 1/sqrt(64); optionally
  * gated. Replaces fused::attention (fused/mod.rs:20-41) and fused::gated_attention
- * (fused/mod.rs:43-55), whose kernel is fused/attention.rs:24-298. */
+ * (fused/mod.rs:43-55), whose kernel is fused/attention.rs:24-298. With q, k and v in one
+ * buffer (q == k == v) and tokens > 64 the tensor cores run it: BF16 / F16 directly, F32 from
+ * a three-plane bf16 split of the used columns, written to a stream-ordered scratch buffer
+ * (cudaMallocAsync, 3 · rows · columns · 2 bytes) that is freed on `stream`; other forms run
+ * on the FFMA kernel. */
 ANCHA_API int ancha_attention_fwd(const ancha_attn_desc* desc, const void* q, const void* k,
                         const void* v, const void* gate, void* out, void* stream);
 

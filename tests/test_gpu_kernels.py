@@ -365,3 +365,44 @@ def test_tensor_core_attention_matches_ffma(dt, min_db, axis, gated):
     print(f"attention tc vs ffma {axis} {dt} gated={gated}: {snr:.1f} dB")
     assert np.all(np.isfinite(tc)) and np.abs(ref).max() > 0 and snr >= min_db
     assert snr < 200.0  # the two kernels really differ (P is rounded to 16 bits on the tensor path)
+
+
+@pytest.mark.parametrize("axis", ["time", "t129", "t200", "t300"])
+@pytest.mark.parametrize("gated", [False, True])
+def test_fp32_split_attention_matches_ffma(axis, gated):
+    """fp32 attention on the tensor cores (q, k, v split into three bf16 planes, six plane
+    products for S and for P·V, P split in the softmax) against the FFMA attention on the same
+    f32 operands, which is held to the oracle at 1e-5: the time axis of the model (60 bands ×
+    801 frames) and time axes whose last key block holds 1, 72 or 44 valid keys."""
+    chunks, bands, frames, heads = {"time": (1, 60, 801, 8), "t129": (1, 4, 129, 2),
+                                    "t200": (1, 3, 200, 2), "t300": (2, 3, 300, 2)}[axis]
+    ld = (3 * heads * 64 + heads + 7) // 8 * 8
+    rows = chunks * bands * frames
+    g = torch.Generator(device="cuda").manual_seed(11)
+    buf = torch.randn(rows, ld, device="cuda", generator=g) * 0.7
+    kw = dict(groups=chunks * bands, tokens=frames, group_inner=chunks * bands, inner_stride=frames,
+              outer_stride=0, token_stride=1, heads=heads, gated=gated)
+    tc = attention_abi(buf, kw).double().cpu().numpy()
+    ffma = attention_abi(buf, kw, separate_kv=True).double().cpu().numpy()
+    # float64 attention of the first (up to) four groups from the same f32 operands
+    b = buf.double().cpu().numpy()
+    ng = min(4, chunks * bands)
+    exact = np.zeros((ng * frames, heads * 64))
+    for gi in range(ng):
+        r = slice(gi * frames, (gi + 1) * frames)
+        for h in range(heads):
+            q, k, v = (b[r, c + h * 64:c + (h + 1) * 64] for c in (0, heads * 64, 2 * heads * 64))
+            sc = q @ k.T
+            pr = np.exp(sc - sc.max(axis=1, keepdims=True))
+            o = (pr / pr.sum(axis=1, keepdims=True)) @ v
+            if gated:
+                o = o / (1.0 + np.exp(-b[r, 3 * heads * 64 + h]))[:, None]
+            exact[gi * frames:(gi + 1) * frames, h * 64:(h + 1) * 64] = o
+    n = ng * frames
+    e_tc, e_ffma = np.abs(tc[:n] - exact).max(), np.abs(ffma[:n] - exact).max()
+    scale = np.abs(exact).max()
+    snr = snr_db(ffma, tc)
+    print(f"fp32 split attention {axis} gated={gated}: vs float64 max abs {e_tc:.2e}, FFMA vs float64 "
+          f"{e_ffma:.2e} (|o| ≤ {scale:.2f}); split vs FFMA {snr:.1f} dB")
+    assert np.all(np.isfinite(tc)) and scale > 0
+    assert e_tc <= 1e-5 * max(scale, 1.0) and snr >= 100.0
