@@ -87,6 +87,10 @@ struct GroupedGemm {
     int64_t bias_group_stride;
     void* out;
     int64_t ldo, out_group_stride;
+    // Three-plane bf16 operands (see GemmGroup::split3), plane-major over the groups: A plane p
+    // of group g at a + (p · groups + g) · a_group_stride, B plane p of group g at
+    // b + (p · b_groups + g) · b_group_stride.
+    bool split3 = false;
 };
 
 int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& epi, cudaStream_t stream);

@@ -408,7 +408,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant_
                     if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort, p.err)) break;
                     // split3: K step kt is slab kb of plane product `term` (A plane, B plane).
                     const int term = kt / kblocks, kb = kt - term * kblocks;
-                    const int az = p.split3 ? kSplitA[term] : c.g, bz = p.split3 ? kSplitB[term] : bg;
+                    const int az = p.split3 ? kSplitA[term] * p.groups + c.g : c.g;
+                    const int bz = p.split3 ? kSplitB[term] * p.b_groups + bg : bg;
                     if (PAIR) {
                         // Both CTAs' slabs complete on the even CTA's barrier, which expects both.
                         const uint32_t fb = mapa_shared(smem_u32(&full[s]), 0);
@@ -657,9 +658,10 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
     const bool pair = ANCHA_GEMM_PAIRS && p.groups == 1 && !p.group_n && !p.conv_taps && p.m >= 2 * BM &&
                       p.k * (p.split3 ? 6 : 1) >= 1024;
     CUtensorMap ta, tb, to;
-    // split3 operands are three planes along the depth coordinate of each map.
-    ANCHA_TRY(make_tma_3d(&ta, a, ab_type, p.k, p.m, p.split3 ? 3 : p.groups, lda, a_group_stride, BM));
-    ANCHA_TRY(make_tma_3d(&tb, b, ab_type, p.k, p.n, p.split3 ? 3 : p.b_groups, ldb, b_group_stride,
+    // split3 operands are three planes along the depth coordinate of each map, plane-major over
+    // the groups.
+    ANCHA_TRY(make_tma_3d(&ta, a, ab_type, p.k, p.m, (p.split3 ? 3 : 1) * p.groups, lda, a_group_stride, BM));
+    ANCHA_TRY(make_tma_3d(&tb, b, ab_type, p.k, p.n, (p.split3 ? 3 : 1) * p.b_groups, ldb, b_group_stride,
                           pair ? bn / 2 : bn));
     const bool glu = p.act == ANCHA_ACT_GLU;
     if (glu && p.out_type != ELT_F32) return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: GLU output must be f32");
@@ -787,6 +789,8 @@ int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& e, cu
     p.residual = nullptr; p.ldr = 0;
     p.act = e.act; p.out_type = e.out_type;
     p.rope = nullptr; p.rope_pairs = nullptr; p.rope_width = 0; p.rope_tokens = 1; p.rope_div = 1; p.rope_hd = 64;
+    p.split3 = q.split3 ? 1 : 0;
+    if (q.split3 && ab_type != ELT_BF16) return fail(ANCHA_E_INVALID, "gemm_tc: split operands are bf16");
     return run(q.a, q.lda, q.a_group_stride, q.b, q.ldb, q.b_group_stride, p, ab_type, s);
 }
 

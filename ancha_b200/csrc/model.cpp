@@ -430,9 +430,8 @@ std::unique_ptr<Model> Model::load(const std::string& package, int device, int p
     hasher.join();
     if (digest != m->manifest.weights_sha256) bad("model checksum mismatch");
     if (m->elt_ == ELT_F32 && ANCHA_FP32_SPLIT) {
-        // fp32 on the tensor cores: three-plane bf16 splits of the transformer weights (the
-        // GEMMs that carry ~90 % of the model's FLOPs; the grouped band-split and mask-head
-        // GEMMs stay on the FFMA kernel).
+        // fp32 on the tensor cores: three-plane bf16 splits of the transformer and mask-head
+        // weights (the grouped band split, a small share of the FLOPs, stays on the FFMA kernel).
         const ModelConfig& c = m->manifest.config;
         const int dim = c.dim, inner = c.heads * c.head_dim, hidden = c.dim * c.ff_mult;
         const int ncols = 3 * inner + c.heads;
@@ -450,6 +449,12 @@ std::unique_ptr<Model> Model::load(const std::string& package, int device, int p
                 split(t.w1, hidden, dim);
                 split(t.w2, dim, hidden);
             }
+        // Mask heads: [bands][rows][in] per layer, split as bands · rows rows (plane-major).
+        const int mh = c.dim * c.mask_expansion;
+        for (auto& mw : m->masks_) {
+            for (size_t l = 0; l < mw.w.size(); ++l) split(mw.w[l], m->bands * mh, l == 0 ? dim : mh);
+            split(mw.glu_w, m->bands * 2 * m->max_width, mh);
+        }
         if (cudaDeviceSynchronize() != cudaSuccess) bad("weight split");
         m->split_ = true;
     }
@@ -479,7 +484,7 @@ int Model::ensure_workspace(int chunks, int frames, cudaStream_t s) {
         w.glu.alloc(R * max_width * 4);
         // The three bf16 planes of a GEMM's A operand, or of the q | k | v rows for the time-axis
         // attention (3 · inner columns).
-        if (split_) w.a3.alloc((size_t)3 * R * std::max(std::max(c.dim, 3 * inner), hidden) * 2);
+        if (split_) w.a3.alloc((size_t)3 * R * std::max(std::max(c.dim, 3 * inner), std::max(hidden, mh)) * 2);
         if (fuse_norms_) {
             w.ss_x.alloc(R * (c.dim / 32) * 4);
             w.ss_y.alloc(R * (c.dim / 32) * 4);
@@ -865,12 +870,19 @@ int Model::forward(const float* spectrum, int chunks, int frames, float* masks,
             e.act = glu ? ANCHA_ACT_GLU : ANCHA_ACT_TANH;
             e.out_type = glu ? ELT_F32 : elt_;
             int gst = ANCHA_E_UNSUPPORTED;
-            if (elt_ != ELT_F32) {
-                // One tcgen05 launch over every (chunk, band) problem of this layer.
-                const MaskWeights& mw = masks_[st];
+            const MaskWeights& mw = masks_[st];
+            const auto wsplit = split_ ? split_w_.find(glu ? mw.glu_w.p : mw.w[l].p) : split_w_.end();
+            if (elt_ != ELT_F32 || wsplit != split_w_.end()) {
+                // One tcgen05 launch over every (chunk, band) problem of this layer; in fp32 mode
+                // on the three-plane splits of the f32 input rows and of the weights.
                 const int in = l == 0 ? c.dim : mh;
-                const void* a = l == 0 ? ws_.xn.p : (l % 2 == 1 ? ws_.hidden.p : ws_.h2.p);
+                const void* a = l == 0 ? (elt_ != ELT_F32 ? ws_.xn.p : ws_.x.p) : (l % 2 == 1 ? ws_.hidden.p : ws_.h2.p);
                 GroupedGemm q{};
+                if (elt_ == ELT_F32) {
+                    ANCHA_TRY(split3_rows(static_cast<const float*>(a), in, ws_.a3.p, R, in, s));
+                    a = ws_.a3.p;
+                    q.split3 = true;
+                }
                 q.a = a;
                 q.lda = in;
                 q.a_group_stride = (int64_t)frames * in;
@@ -897,7 +909,8 @@ int Model::forward(const float* spectrum, int chunks, int frames, float* masks,
                 q.b_group_stride = (int64_t)q.n * in;
                 q.bias_group_stride = q.n;
                 q.out_group_stride = (int64_t)frames * q.ldo;
-                gst = gemm_tc_grouped(q, elt_, e, s);
+                if (q.split3) q.b = wsplit->second.p;
+                gst = gemm_tc_grouped(q, q.split3 ? ELT_BF16 : elt_, e, s);
             }
             if (gst == ANCHA_E_UNSUPPORTED) {
                 const GemmGroup* gl = groups + ((size_t)st * (hidden_layers + 1) + l) * (size_t)ws_.chunks * bands;

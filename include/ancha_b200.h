@@ -44,8 +44,8 @@ enum {
 /* Element types of kernel operands. */
 enum { ANCHA_F32 = 0, ANCHA_BF16 = 1, ANCHA_F16 = 2 };
 
-/* Model arithmetic: F32 = fp32 operands, the transformer GEMMs and the time-axis attention
- * on the tcgen05 tensor cores as three-plane bf16 splits (hi + mid + lo, 24 significant bits;
+/* Model arithmetic: F32 = fp32 operands, the transformer and mask-head GEMMs and the time-axis
+ * attention on the tcgen05 tensor cores as three-plane bf16 splits (hi + mid + lo, 24 significant bits;
  * six plane products accumulated in fp32), the rest on fp32 FFMA kernels; BF16 / F16 = bf16 /
  * f16 operands on the tensor cores (GEMMs and attention) with fp32 accumulation; the residual
  * stream, norms, softmax statistics and DSP stay fp32 in every mode. */
