@@ -4,6 +4,8 @@
 // assembly (network.rs:382-396). One warp per row; reductions in fp32 with a fixed order.
 #include "rowops.cuh"
 
+#include <algorithm>
+
 namespace ancha {
 namespace {
 
@@ -189,12 +191,49 @@ __global__ void split3_kernel(const float* __restrict__ x, int64_t ldx, __nv_bfl
     y[plane + o] = m;
     y[2 * plane + o] = __float2bfloat16_rn(r2);
 }
+// Eight consecutive columns per thread (threadIdx.x over 8-column groups of a row, the y
+// dimension over rows, grid-striding when rows exceed the grid).
+__global__ void split3_vec_kernel(const float* __restrict__ x, int64_t ldx, __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                  int64_t plane, int64_t rows, int groups) {
+    const int gcol = blockIdx.x * blockDim.x + threadIdx.x;
+    if (gcol >= groups) return;
+    for (int64_t r = (int64_t)blockIdx.y * blockDim.y + threadIdx.y; r < rows; r += (int64_t)gridDim.y * blockDim.y) {
+        const float4* src = reinterpret_cast<const float4*>(x + r * ldx + gcol * 8);
+        const float4 a = src[0], b = src[1];
+        const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        uint32_t h[4], m[4], l[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const __nv_bfloat162 hh = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+            const float r0 = v[2 * i] - __low2float(hh), r1 = v[2 * i + 1] - __high2float(hh);
+            const __nv_bfloat162 mm = __floats2bfloat162_rn(r0, r1);
+            const __nv_bfloat162 ll = __floats2bfloat162_rn(r0 - __low2float(mm), r1 - __high2float(mm));
+            h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+            m[i] = *reinterpret_cast<const uint32_t*>(&mm);
+            l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+        }
+        __nv_bfloat16* o = y + r * ldy + gcol * 8;
+        *reinterpret_cast<uint4*>(o) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(o + plane) = make_uint4(m[0], m[1], m[2], m[3]);
+        *reinterpret_cast<uint4*>(o + 2 * plane) = make_uint4(l[0], l[1], l[2], l[3]);
+    }
+}
 }  // namespace
 
 int split3_rows_strided(const float* x, int64_t ldx, void* y, int64_t ldy, int64_t plane, int64_t rows, int dim,
                         cudaStream_t s) {
     const int64_t n = rows * dim;
     if (n == 0) return ANCHA_OK;
+    const uintptr_t xa = reinterpret_cast<uintptr_t>(x), ya = reinterpret_cast<uintptr_t>(y);
+    if (dim % 8 == 0 && ldx % 4 == 0 && ldy % 8 == 0 && plane % 8 == 0 && xa % 16 == 0 && ya % 16 == 0) {
+        // Eight columns per thread: two 16-byte loads, three 16-byte stores.
+        const int groups = dim / 8;
+        const dim3 block(32, 8);
+        const dim3 grid((unsigned)ceil_div(groups, 32), (unsigned)std::min<int64_t>(ceil_div(rows, 8), 65535));
+        split3_vec_kernel<<<grid, block, 0, s>>>(x, ldx, reinterpret_cast<__nv_bfloat16*>(y), ldy, plane, rows,
+                                                  groups);
+        return check_launch("split3_rows");
+    }
     split3_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(x, ldx, reinterpret_cast<__nv_bfloat16*>(y), ldy, plane,
                                                              rows, dim);
     return check_launch("split3_rows");
