@@ -167,7 +167,22 @@ int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, c
         return fail(ANCHA_E_INVALID, "linear: row_scale not 4-byte aligned");
     cudaStream_t s = as_stream(stream);
     if (d->dtype != ANCHA_F32 && wl == ANCHA_W_NK) {
-        int st = gemm_tc(g, d->dtype, e, s);
+        int st;
+        if (e.rope) {
+            // The tensor-core epilogue reads the table in its pair-major general form (same
+            // arithmetic, coalesced loads), built in a stream-ordered scratch buffer.
+            void* quads = nullptr;
+            if (cudaMallocAsync(&quads, (size_t)2 * 32 * e.rope_tokens * 16, s) != cudaSuccess)
+                return fail(ANCHA_E_CUDA, "linear: cudaMallocAsync of the rotary table");
+            GemmEpilogue eq = e;
+            eq.rope = nullptr;
+            eq.rope_quads = static_cast<const float*>(quads);
+            st = rope_quads_from_table(e.rope, e.rope_tokens, 64, quads, s);
+            if (st == ANCHA_OK) st = gemm_tc(g, d->dtype, eq, s);
+            cudaFreeAsync(quads, s);
+        } else {
+            st = gemm_tc(g, d->dtype, e, s);
+        }
         if (st != ANCHA_E_UNSUPPORTED) return st;
     }
     return gemm_ffma(g, nullptr, 1, d->m, d->n, d->dtype, d->dtype, wl == ANCHA_W_NK, e, s);

@@ -35,6 +35,11 @@ struct GemmEpilogue {
     // columns share the cosine and carry ∓sin. Lanes of a warp hold consecutive rows, so a
     // token-fastest table makes their loads coalesce. Null: the tensor-core path reads `rope`.
     const float* rope_pairs;
+    // Optional pair-major general form of a [4, tokens, hd] table for the tensor-core epilogue:
+    // [2][rope_hd / 2][rope_tokens] × (C0, C1, S0, S1) float4, the cosine-row and sine-row entries
+    // of a pair's two columns (rope_quads_from_table); the columns rotate as
+    // (x0·C0 + x1·S0, x1·C1 + x0·S1), exactly the `rope` table's arithmetic, with coalesced loads.
+    const float* rope_quads;
     // Row-norm fusion (tensor-core path only; null / 0 = off). Sums of squares are kept per
     // 32-column chunk, chunk-major: ss[c / 32][r] for an m-row output.
     //   row_ss / row_ss_n: scale row r of A·Bᵀ by 1 / max(√Σ row_ss[r][·], 1e-12) before the
@@ -92,6 +97,10 @@ struct GroupedGemm {
     // b + (p · b_groups + g) · b_group_stride.
     bool split3 = false;
 };
+
+// The general pair-major (C0, C1, S0, S1) form of a [4, tokens, hd] rotary table (see
+// GemmEpilogue::rope_quads): quads[key][pair][token], 2 · (hd / 2) · tokens float4.
+int rope_quads_from_table(const float* table, int tokens, int hd, void* quads, cudaStream_t stream);
 
 int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& epi, cudaStream_t stream);
 

@@ -51,6 +51,7 @@ struct TcParams {
     int act, out_type;
     const float* rope;
     const float2* rope_pairs;
+    const float4* rope_quads;
     int rope_width, rope_tokens, rope_div, rope_hd;
     const float* row_mul;    // per-row multiplier (GemmEpilogue::row_mul)
     int split3;              // three-plane bf16 operands, six plane products (GemmGroup::split3)
@@ -158,7 +159,17 @@ __device__ __forceinline__ int epilogue32(const TcParams& p, int g, int row, boo
 #pragma unroll
         for (int j = 0; j < 32; j += 2) tanh_fast2(v[j], v[j + 1]);
     }
-    if (p.rope_pairs && c0 < 2 * p.rope_width) {
+    if (p.rope_quads && c0 < 2 * p.rope_width) {
+        const int key = c0 >= p.rope_width;
+        const int token = (row / p.rope_div) % p.rope_tokens;
+        const float4* t = p.rope_quads +
+                          ((int64_t)key * (p.rope_hd / 2) + (c0 % p.rope_hd) / 2) * p.rope_tokens + token;
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {  // (x0·C0 + x1·S0, x1·C1 + x0·S1), packed
+            const float4 q = t[(int64_t)(j / 2) * p.rope_tokens];
+            put2(v, j, ffma2(f2(v[j + 1], v[j]), f2(q.z, q.w), fmul2(f2(v[j], v[j + 1]), f2(q.x, q.y))));
+        }
+    } else if (p.rope_pairs && c0 < 2 * p.rope_width) {
         const int key = c0 >= p.rope_width;
         const int token = (row / p.rope_div) % p.rope_tokens;
         const float2* t = p.rope_pairs +
@@ -685,7 +696,8 @@ int run(const void* a, int64_t lda, int64_t a_group_stride, const void* b, int64
         return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: no 16-bit copy after an activation");
     // Sixteen epilogue warps for the activations and for RoPE (whose table loads wait on L2),
     // eight for the plain and residual epilogues.
-    const bool act = p.act == ANCHA_ACT_GELU || p.act == ANCHA_ACT_TANH || ((p.rope || p.rope_pairs) && !p.out16);
+    const bool act = p.act == ANCHA_ACT_GELU || p.act == ANCHA_ACT_TANH ||
+                     ((p.rope || p.rope_pairs || p.rope_quads) && !p.out16);
     if (pair) {
         switch (bn) {
             case 256: return act ? launch<256, 4, EPI_ACT, true>(ta, tb, to, to16, p, s) : launch<256, 4, EPI_PLAIN, true>(ta, tb, to, to16, p, s);
@@ -711,6 +723,7 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     if (!aligned16(g.out) || (g.ldo * oe) % 16 || (g.residual && (!aligned16(g.residual) || (g.ldr * 4) % 16)) ||
         (g.bias && !aligned16(g.bias)) || (e.rope && (!aligned16(e.rope) || e.rope_hd % 32)) ||
         (e.rope_pairs && (!aligned16(e.rope_pairs) || e.rope_hd % 32)) ||
+        (e.rope_quads && (!aligned16(e.rope_quads) || e.rope_hd % 32)) ||
         (e.out16 && (!aligned16(e.out16) || g.n % 8)) || (e.res_col && !aligned16(e.res_col)))
         return fail(ANCHA_E_UNSUPPORTED, "gemm_tc: epilogue operands not 16-byte aligned");
     if ((e.res_ss && !g.residual) || e.act == ANCHA_ACT_GLU && (e.out16 || e.ss_out))
@@ -723,6 +736,7 @@ int gemm_tc(const GemmGroup& g, int ab_type, const GemmEpilogue& e, cudaStream_t
     p.act = e.act; p.out_type = e.out_type;
     p.rope = e.rope; p.rope_width = e.rope_width; p.rope_tokens = e.rope_tokens;
     p.rope_pairs = reinterpret_cast<const float2*>(e.rope_pairs);
+    p.rope_quads = reinterpret_cast<const float4*>(e.rope_quads);
     p.rope_div = e.rope_div; p.rope_hd = e.rope_hd;
     p.row_ss = e.row_ss; p.row_ss_n = e.row_ss_n; p.res_ss = e.res_ss; p.res_ss_n = e.res_ss_n;
     p.row_mul = e.row_mul;
@@ -747,7 +761,7 @@ int gemm_tc_conv(const ConvGemm& q, int ab_type, const GemmEpilogue& e, cudaStre
     const size_t oe = elt_size(e.out_type);
     if (!aligned16(q.out) || (q.ldo * oe) % 16 || (q.residual && (!aligned16(q.residual) || (q.ldo * 4) % 16)))
         return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: output not 16-byte aligned");
-    if (e.act != ANCHA_ACT_NONE || e.rope || e.rope_pairs || e.row_ss || e.res_ss || e.out16 || e.ss_out)
+    if (e.act != ANCHA_ACT_NONE || e.rope || e.rope_pairs || e.rope_quads || e.row_ss || e.res_ss || e.out16 || e.ss_out)
         return fail(ANCHA_E_UNSUPPORTED, "gemm_tc_conv: epilogue");
     TcParams p{};
     p.m = q.co; p.n = q.h * q.w; p.k = q.taps * q.channels; p.groups = 1; p.b_groups = 1; p.group_n = nullptr;
@@ -792,6 +806,30 @@ int gemm_tc_grouped(const GroupedGemm& q, int ab_type, const GemmEpilogue& e, cu
     p.split3 = q.split3 ? 1 : 0;
     if (q.split3 && ab_type != ELT_BF16) return fail(ANCHA_E_INVALID, "gemm_tc: split operands are bf16");
     return run(q.a, q.lda, q.a_group_stride, q.b, q.ldb, q.b_group_stride, p, ab_type, s);
+}
+
+
+namespace {
+__global__ void rope_quads_kernel(const float* __restrict__ tab, int tokens, int hd, float4* __restrict__ quads,
+                                  int64_t total) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= total) return;
+    const int64_t per_key = (int64_t)(hd / 2) * tokens;
+    const int key = (int)(i / per_key);
+    const int64_t rem = i - key * per_key;
+    const int pair = (int)(rem / tokens), t = (int)(rem - (int64_t)pair * tokens);
+    const float* c = tab + ((int64_t)(2 * key) * tokens + t) * hd + 2 * pair;
+    const float* sn = tab + ((int64_t)(2 * key + 1) * tokens + t) * hd + 2 * pair;
+    quads[i] = make_float4(c[0], c[1], sn[0], sn[1]);
+}
+}  // namespace
+
+int rope_quads_from_table(const float* table, int tokens, int hd, void* quads, cudaStream_t s) {
+    const int64_t total = (int64_t)2 * (hd / 2) * tokens;
+    if (total == 0) return ANCHA_OK;
+    rope_quads_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, s>>>(table, tokens, hd,
+                                                                      reinterpret_cast<float4*>(quads), total);
+    return check_launch("rope_quads");
 }
 
 }  // namespace ancha

@@ -119,7 +119,10 @@ enum { ANCHA_ACT_NONE = 0, ANCHA_ACT_GELU = 1, ANCHA_ACT_TANH = 2, ANCHA_ACT_GLU
  * (value, gate) and writes value·sigmoid(gate) to column j (n_out = n / 2).
  * Replaces fused::linear + Epilogue (fused/mod.rs:57-176, kernel fused/gemm.rs:84-311).
  * x, w: `dtype` (F32 → fp32 FFMA kernel; BF16 / F16 → tcgen05 kernel with ANCHA_W_NK);
- * bias, residual, rope: f32; out: out_dtype. `workspace` may be NULL (none is needed). */
+ * bias, residual, rope: f32; out: out_dtype. `workspace` may be NULL (none is needed). On the
+ * tensor-core path the rotary table is first rewritten pair-major ([2][32][tokens] × (cos, cos,
+ * sin, sin) entries of each column pair, the same arithmetic with coalesced loads) into a
+ * stream-ordered scratch buffer (cudaMallocAsync, 1 KiB per token) freed on `stream`. */
 typedef struct {
     int m, n, k;
     int dtype, out_dtype, weight_layout;
