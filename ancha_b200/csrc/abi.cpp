@@ -106,9 +106,9 @@ int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, 
         if (st != ANCHA_E_UNSUPPORTED) return st;
     }
 #if ANCHA_FP32_SPLIT
-    // fp32 time axis on the tensor cores: the used q | k | v columns of every row up to the last
-    // one the groups reach, split into three bf16 planes in a stream-ordered scratch buffer.
-    if (a.elt == ELT_F32 && q == k && q == v && a.tokens > 64 && a.groups > 0 && a.groups % a.group_inner == 0) {
+    // fp32 on the tensor cores: the used q | k | v columns of every row up to the last one the
+    // groups reach, split into three bf16 planes in a stream-ordered scratch buffer.
+    if (a.elt == ELT_F32 && q == k && q == v && a.tokens > 0 && a.groups > 0 && a.groups % a.group_inner == 0) {
         const int64_t outer = a.groups / a.group_inner;
         const int64_t rows = (outer - 1) * a.group_outer_stride + (a.group_inner - 1) * a.group_inner_stride +
                              (int64_t)(a.tokens - 1) * a.token_stride + 1;

@@ -24,7 +24,7 @@ __host__ __device__ __forceinline__ int64_t attn_group_row(const AttnArgs& a, in
 
 int attention_ffma(const AttnArgs& a, cudaStream_t stream);
 int attention_tc(const AttnArgs& a, cudaStream_t stream);
-// fp32 operands (a.elt == ELT_F32, time axis) on the tensor cores from their three-plane bf16
+// fp32 operands (a.elt == ELT_F32) on the tensor cores from their three-plane bf16
 // split: `planes` holds hi, mid, lo of the q / k / v source rows (same row indexing and column
 // offsets as the source, row stride plane_ld elements), plane p at planes + p · plane_stride
 // elements (see split3_rows_strided); the gate logits (read from a.gate with a.ld) and out are f32.

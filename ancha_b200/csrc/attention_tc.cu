@@ -680,7 +680,8 @@ int launch_band(const CUtensorMap& map, const CUtensorMap& omap, const AttnTcPar
     return check_launch("attention_band");
 }
 
-// fp32 mode, time axis (tokens > 64), on the tensor cores. The f32 q / k / v arrive split into
+// fp32 mode on the tensor cores (both axes: a band-axis problem of ≤ 64 tokens is one tile with
+// one key block). The f32 q / k / v arrive split into
 // three bf16 planes, x = hi + mid + lo with hi = bf16(x), mid = bf16(x − hi), lo = bf16(x − hi −
 // mid) (24 significant bits), and each product runs as the six plane products whose weight is at
 // least 2^-24 of the leading one (mm, lh, hl, mh, hm, hh, in that order), accumulated in f32 in TMEM:
@@ -1069,8 +1070,8 @@ int attention_tc(const AttnArgs& a, cudaStream_t stream) {
 
 int attention_tc_split(const AttnArgs& a, const void* planes, int64_t plane_ld, int64_t plane_stride,
                        cudaStream_t stream) {
-    if (a.elt != ELT_F32 || a.head_dim != HD || a.tokens <= 64)
-        return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: f32 time axis with head_dim 64 only");
+    if (a.elt != ELT_F32 || a.head_dim != HD)
+        return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: f32 with head_dim 64 only");
     if (a.groups == 0) return ANCHA_OK;
     if (a.q != a.k || a.q != a.v) return fail(ANCHA_E_UNSUPPORTED, "attention_tc_split: q, k, v must share one buffer");
     const uintptr_t pb = reinterpret_cast<uintptr_t>(planes);

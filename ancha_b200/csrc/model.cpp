@@ -719,8 +719,8 @@ int Model::transformer(const TransformerWeights& t, bool time_axis, cudaStream_t
     int ast = ANCHA_E_UNSUPPORTED;
     if (bf != ELT_F32) {
         ast = attention_tc(a, s);
-    } else if (split_ && time_axis && a.tokens > 64) {
-        // fp32 on the tensor cores: the q | k | v | gate rows split into three bf16 planes.
+    } else if (split_) {
+        // fp32 on the tensor cores: the q | k | v rows split into three bf16 planes.
         ANCHA_TRY(split3_rows(ws_.qkvg.as<float>(), ldq, ws_.a3.p, R, 3 * inner, s));
         ast = attention_tc_split(a, ws_.a3.p, 3 * inner, R * 3 * inner, s);
     }

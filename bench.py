@@ -254,9 +254,9 @@ def fp32_leg(package: str, local: int, world: int, rank: int, dist, planes, d_pl
     return {"workload": "the value workload (mel-band-roformer, native context, one 30 s track per GPU) in fp32",
             "value": world * samples / SR / sec, "unit": "×realtime", "ms_per_step": sec * 1e3, "steps": steps,
             "dtype": "f32", "scaling": "weak",
-            "kernels": "transformer and mask-head GEMMs and time-axis attention on the tensor cores with "
-                       "three-plane bf16 operand splits (six plane products, f32 accumulation); band-axis "
-                       "attention and band split on the FFMA kernels"}
+            "kernels": "transformer and mask-head GEMMs and the attention of both axes on the tensor cores "
+                       "with three-plane bf16 operand splits (six plane products, f32 accumulation); band split "
+                       "on the FFMA kernel"}
 
 
 def mel_track(model, local: int, world: int, rank: int, dist, precision: str, steps: int = 3):

@@ -95,10 +95,10 @@ typedef struct {
 /* softmax(q·kᵀ)·v per (group, head), non-causal, q pre-scaled by 1/sqrt(64); optionally
  * gated. Replaces fused::attention (fused/mod.rs:20-41) and fused::gated_attention
  * (fused/mod.rs:43-55), whose kernel is fused/attention.rs:24-298. With q, k and v in one
- * buffer (q == k == v) and tokens > 64 the tensor cores run it: BF16 / F16 directly, F32 from
- * a three-plane bf16 split of the used columns, written to a stream-ordered scratch buffer
- * (cudaMallocAsync, 3 · rows · columns · 2 bytes) that is freed on `stream`; other forms run
- * on the FFMA kernel. */
+ * buffer (q == k == v) the tensor cores run it: BF16 / F16 directly, F32 from a three-plane
+ * bf16 split of the used columns, written to a stream-ordered scratch buffer (cudaMallocAsync,
+ * 3 · rows · columns · 2 bytes) that is freed on `stream`; separate buffers run on the FFMA
+ * kernel. */
 ANCHA_API int ancha_attention_fwd(const ancha_attn_desc* desc, const void* q, const void* k,
                         const void* v, const void* gate, void* out, void* stream);
 

@@ -367,29 +367,38 @@ def test_tensor_core_attention_matches_ffma(dt, min_db, axis, gated):
     assert snr < 200.0  # the two kernels really differ (P is rounded to 16 bits on the tensor path)
 
 
-@pytest.mark.parametrize("axis", ["time", "t129", "t200", "t300"])
+@pytest.mark.parametrize("axis", ["time", "t129", "t200", "t300", "band", "band2"])
 @pytest.mark.parametrize("gated", [False, True])
 def test_fp32_split_attention_matches_ffma(axis, gated):
     """fp32 attention on the tensor cores (q, k, v split into three bf16 planes, six plane
     products for S and for P·V, P split in the softmax) against the FFMA attention on the same
-    f32 operands, which is held to the oracle at 1e-5: the time axis of the model (60 bands ×
-    801 frames) and time axes whose last key block holds 1, 72 or 44 valid keys."""
-    chunks, bands, frames, heads = {"time": (1, 60, 801, 8), "t129": (1, 4, 129, 2),
-                                    "t200": (1, 3, 200, 2), "t300": (2, 3, 300, 2)}[axis]
+    f32 operands, which is held to the oracle at 1e-5, and against float64: the time axis of the
+    model (60 bands × 801 frames), time axes whose last key block holds 1, 72 or 44 valid keys,
+    and the band axis (801 frames × 60 bands, tokens 801 rows apart; two chunks of 51 frames ×
+    33 bands)."""
+    chunks, bands, frames, heads = {"time": (1, 60, 801, 8), "t129": (1, 4, 129, 2), "t200": (1, 3, 200, 2),
+                                    "t300": (2, 3, 300, 2), "band": (1, 60, 801, 8),
+                                    "band2": (2, 33, 51, 3)}[axis]
     ld = (3 * heads * 64 + heads + 7) // 8 * 8
     rows = chunks * bands * frames
     g = torch.Generator(device="cuda").manual_seed(11)
     buf = torch.randn(rows, ld, device="cuda", generator=g) * 0.7
-    kw = dict(groups=chunks * bands, tokens=frames, group_inner=chunks * bands, inner_stride=frames,
-              outer_stride=0, token_stride=1, heads=heads, gated=gated)
+    if not axis.startswith("band"):
+        kw = dict(groups=chunks * bands, tokens=frames, group_inner=chunks * bands, inner_stride=frames,
+                  outer_stride=0, token_stride=1)
+    else:
+        kw = dict(groups=chunks * frames, tokens=bands, group_inner=frames, inner_stride=1,
+                  outer_stride=bands * frames, token_stride=frames)
+    kw.update(heads=heads, gated=gated)
     tc = attention_abi(buf, kw).double().cpu().numpy()
     ffma = attention_abi(buf, kw, separate_kv=True).double().cpu().numpy()
     # float64 attention of the first (up to) four groups from the same f32 operands
     b = buf.double().cpu().numpy()
-    ng = min(4, chunks * bands)
-    exact = np.zeros((ng * frames, heads * 64))
-    for gi in range(ng):
-        r = slice(gi * frames, (gi + 1) * frames)
+    tokens = kw["tokens"]
+    got_tc, got_ffma, exact = [], [], []
+    for gi in range(min(4, kw["groups"])):
+        r0 = (gi // kw["group_inner"]) * kw["outer_stride"] + (gi % kw["group_inner"]) * kw["inner_stride"]
+        r = r0 + np.arange(tokens) * kw["token_stride"]
         for h in range(heads):
             q, k, v = (b[r, c + h * 64:c + (h + 1) * 64] for c in (0, heads * 64, 2 * heads * 64))
             sc = q @ k.T
@@ -397,9 +406,11 @@ def test_fp32_split_attention_matches_ffma(axis, gated):
             o = (pr / pr.sum(axis=1, keepdims=True)) @ v
             if gated:
                 o = o / (1.0 + np.exp(-b[r, 3 * heads * 64 + h]))[:, None]
-            exact[gi * frames:(gi + 1) * frames, h * 64:(h + 1) * 64] = o
-    n = ng * frames
-    e_tc, e_ffma = np.abs(tc[:n] - exact).max(), np.abs(ffma[:n] - exact).max()
+            exact.append(o)
+            got_tc.append(tc[r, h * 64:(h + 1) * 64])
+            got_ffma.append(ffma[r, h * 64:(h + 1) * 64])
+    exact, got_tc, got_ffma = np.stack(exact), np.stack(got_tc), np.stack(got_ffma)
+    e_tc, e_ffma = np.abs(got_tc - exact).max(), np.abs(got_ffma - exact).max()
     scale = np.abs(exact).max()
     snr = snr_db(ffma, tc)
     print(f"fp32 split attention {axis} gated={gated}: vs float64 max abs {e_tc:.2e}, FFMA vs float64 "
