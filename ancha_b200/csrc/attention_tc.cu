@@ -82,17 +82,16 @@ __device__ __forceinline__ void exp2_fma_pair(uint64_t x, float& e0, float& e1) 
     e1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-// Columns [J0, J0 + NCOL) of one score row: P as 16-bit pairs into pk (NCOL / 2 TMEM
+// Columns [J0, J0 + 64) of one score row: P as 16-bit pairs into pk (one TMEM store of 32
 // columns), row sums into the packed accumulators sa / sb. s_lo clamps the scores of the
 // FMA-pipe columns to x ≥ −124.
-template <bool BF16, int J0, int NCOL, int NS, int W, int NP, int WP>
-__device__ __forceinline__ void exp_columns(const uint32_t (&s)[NS][W], uint32_t (&pk)[NP][WP], uint64_t& sa,
+template <bool BF16, int J0>
+__device__ __forceinline__ void exp_columns(const uint32_t (&s)[4][32], uint32_t (&pk)[32], uint64_t& sa,
                                             uint64_t& sb, float m_used, float s_lo) {
-    static_assert(NP * WP == NCOL / 2, "P of NCOL columns is NCOL / 2 packed words");
     const uint64_t l2 = f2(LOG2E, LOG2E), nm2 = f2(-m_used, -m_used);
 #pragma unroll
-    for (int j = J0; j < J0 + NCOL; j += 2) {
-        const float s0 = __uint_as_float(s[j / W][j % W]), s1 = __uint_as_float(s[j / W][j % W + 1]);
+    for (int j = J0; j < J0 + 64; j += 2) {
+        const float s0 = __uint_as_float(s[j / 32][j % 32]), s1 = __uint_as_float(s[j / 32][j % 32 + 1]);
         float e0, e1;
         if ((j / 2) % 8 < POLY_PAIRS) {
             exp2_fma_pair(ffma2(f2(fmaxf(s0, s_lo), fmaxf(s1, s_lo)), l2, nm2), e0, e1);
@@ -106,7 +105,7 @@ __device__ __forceinline__ void exp_columns(const uint32_t (&s)[NS][W], uint32_t
             sb = fadd2(sb, f2(e0, e1));
         else
             sa = fadd2(sa, f2(e0, e1));
-        pk[(j - J0) / 2 / WP][(j - J0) / 2 % WP] = pack2<BF16>(e0, e1);
+        pk[(j - J0) / 2] = pack2<BF16>(e0, e1);
     }
 }
 
@@ -574,8 +573,8 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
             // P·V of such a block reads keys 0..63 only).
             uint64_t sa = 0, sb = 0;
             {
-                uint32_t pk[1][32];
-                exp_columns<BF16, 0, 64>(s, pk, sa, sb, m_used, s_lo);
+                uint32_t pk[32];
+                exp_columns<BF16, 0>(s, pk, sa, sb, m_used, s_lo);
                 if (kb > 0) {
                     // P(kb − 1)·V must have finished reading P before it is overwritten, and O
                     // must hold it before a rescale.
@@ -583,7 +582,7 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                     if (!ok) break;
                     tc_fence_after();
                 }
-                tmem_st32(p_addr, pk[0]);
+                tmem_st32(p_addr, pk);
             }
             if (kb > 0 && __any_sync(0xffffffffu, corr != 1.f)) {
                 uint32_t o[2][32];
@@ -599,9 +598,9 @@ attention_pp_kernel(const __grid_constant__ CUtensorMap tmap, const AttnTcParams
                 tmem_st32(o_addr + 32, o[1]);
             }
             if (!half) {
-                uint32_t pk[1][32];
-                exp_columns<BF16, TILE / 2, 64>(s, pk, sa, sb, m_used, s_lo);
-                tmem_st32(p_addr + 32, pk[0]);
+                uint32_t pk[32];
+                exp_columns<BF16, TILE / 2>(s, pk, sa, sb, m_used, s_lo);
+                tmem_st32(p_addr + 32, pk);
             }
             float sum0, sum1, sum2, sum3;
             f2_split(sa, sum0, sum1);
