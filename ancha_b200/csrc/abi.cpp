@@ -115,12 +115,15 @@ int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, 
         const int64_t cols = std::max(std::max(a.q_col, a.k_col), a.v_col) + span;
         const int64_t pld = (cols + 7) / 8 * 8;
         void* planes = nullptr;
-        if (cudaMallocAsync(&planes, (size_t)(3 * rows * pld * 2), s) != cudaSuccess)
-            return fail(ANCHA_E_CUDA, "attention: cudaMallocAsync of the operand planes");
-        int st = split3_rows_strided(static_cast<const float*>(q), a.ld, planes, pld, rows * pld, rows, (int)cols, s);
-        if (st == ANCHA_OK) st = attention_tc_split(a, planes, pld, rows * pld, s);
-        cudaFreeAsync(planes, s);
-        if (st != ANCHA_E_UNSUPPORTED) return st;
+        if (cudaMallocAsync(&planes, (size_t)(3 * rows * pld * 2), s) == cudaSuccess) {
+            int st = split3_rows_strided(static_cast<const float*>(q), a.ld, planes, pld, rows * pld, rows,
+                                         (int)cols, s);
+            if (st == ANCHA_OK) st = attention_tc_split(a, planes, pld, rows * pld, s);
+            cudaFreeAsync(planes, s);
+            if (st != ANCHA_E_UNSUPPORTED) return st;
+        } else {
+            cudaGetLastError();  // no room for the planes: the FFMA kernel needs no scratch
+        }
     }
 #endif
     return attention_ffma(a, s);
@@ -168,12 +171,10 @@ int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, c
     cudaStream_t s = as_stream(stream);
     if (d->dtype != ANCHA_F32 && wl == ANCHA_W_NK) {
         int st;
-        if (e.rope) {
+        void* quads = nullptr;
+        if (e.rope && cudaMallocAsync(&quads, (size_t)2 * 32 * e.rope_tokens * 16, s) == cudaSuccess) {
             // The tensor-core epilogue reads the table in its pair-major general form (same
             // arithmetic, coalesced loads), built in a stream-ordered scratch buffer.
-            void* quads = nullptr;
-            if (cudaMallocAsync(&quads, (size_t)2 * 32 * e.rope_tokens * 16, s) != cudaSuccess)
-                return fail(ANCHA_E_CUDA, "linear: cudaMallocAsync of the rotary table");
             GemmEpilogue eq = e;
             eq.rope = nullptr;
             eq.rope_quads = static_cast<const float*>(quads);
@@ -181,6 +182,7 @@ int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, c
             if (st == ANCHA_OK) st = gemm_tc(g, d->dtype, eq, s);
             cudaFreeAsync(quads, s);
         } else {
+            if (e.rope) cudaGetLastError();  // no room for the rewrite: read the table as given
             st = gemm_tc(g, d->dtype, e, s);
         }
         if (st != ANCHA_E_UNSUPPORTED) return st;
