@@ -97,8 +97,8 @@ typedef struct {
  * (fused/mod.rs:43-55), whose kernel is fused/attention.rs:24-298. With q, k and v in one
  * buffer (q == k == v) the tensor cores run it: BF16 / F16 directly, F32 from a three-plane
  * bf16 split of the used columns, written to a stream-ordered scratch buffer (cudaMallocAsync,
- * 3 · rows · columns · 2 bytes) that is freed on `stream`; separate buffers run on the FFMA
- * kernel. */
+ * 3 · rows · columns · 2 bytes) that is freed on `stream`; separate buffers, or a scratch that
+ * cannot be allocated, run on the FFMA kernel. */
 ANCHA_API int ancha_attention_fwd(const ancha_attn_desc* desc, const void* q, const void* k,
                         const void* v, const void* gate, void* out, void* stream);
 
@@ -122,7 +122,8 @@ enum { ANCHA_ACT_NONE = 0, ANCHA_ACT_GELU = 1, ANCHA_ACT_TANH = 2, ANCHA_ACT_GLU
  * bias, residual, rope: f32; out: out_dtype. `workspace` may be NULL (none is needed). On the
  * tensor-core path the rotary table is first rewritten pair-major ([2][32][tokens] × (cos, cos,
  * sin, sin) entries of each column pair, the same arithmetic with coalesced loads) into a
- * stream-ordered scratch buffer (cudaMallocAsync, 1 KiB per token) freed on `stream`. */
+ * stream-ordered scratch buffer (cudaMallocAsync, 1 KiB per token) freed on `stream`; without
+ * room for it the epilogue reads the table as given. */
 typedef struct {
     int m, n, k;
     int dtype, out_dtype, weight_layout;
