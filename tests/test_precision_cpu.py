@@ -39,3 +39,42 @@ def test_bf16_weights_bound_the_16_bit_mode_below_50_db(mel_seeded_package):
     print(f"mask SNR with rounded weights: bf16 {db_bf16:.1f} dB, f16 {db_f16:.1f} dB")
     assert db_bf16 < 50.0
     assert db_f16 > 60.0
+
+
+def split3(x):
+    """The fp32 mode's operand split (split3_rows): hi = bf16(x), mid = bf16(x − hi),
+    lo = bf16(x − hi − mid), every difference formed in f32."""
+    x = np.asarray(x, dtype=np.float32)
+    hi = bf16_round(x)
+    r1 = (x - hi).astype(np.float32)
+    mid = bf16_round(r1)
+    lo = bf16_round((r1 - mid).astype(np.float32))
+    return hi, mid, lo
+
+
+def test_three_plane_split_is_exact_and_six_products_carry_f32():
+    """The fp32 mode runs f32 GEMMs and attention on bf16 tensor cores as three-plane splits.
+    The split is exact: hi + mid + lo reproduces every f32 value bit for bit (three 8-bit
+    significands cover f32's 24), both differences are exact in f32, and the planes fall by
+    2^-8 per step. Of the nine plane products, the six the kernels keep (mm, lh, hl, mh, hm, hh:
+    weight ≥ 2^-24 of the leading one) reproduce a float64 dot product of the f32 operands to
+    within the f32 accumulation error; the three dropped ones (ml, lm, ll) lie below 2^-24."""
+    rng = np.random.default_rng(3)
+    for scale in (1e-3, 1.0, 1e3):
+        x = (rng.standard_normal(200_000) * scale).astype(np.float32)
+        hi, mid, lo = split3(x)
+        assert np.array_equal((hi.astype(np.float64) + mid + lo).astype(np.float32), x)
+        nz = np.abs(hi) > 0
+        assert np.all(np.abs(mid[nz]) <= np.abs(hi[nz]) * 2.0 ** -8)
+        assert np.all(np.abs(lo[nz]) <= np.abs(hi[nz]) * 2.0 ** -16)
+    k = 1536
+    a = rng.standard_normal((64, k)).astype(np.float32)
+    b = rng.standard_normal((k, 64)).astype(np.float32)
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    pa, pb = split3(a), split3(b)
+    terms = [(1, 1), (2, 0), (0, 2), (1, 0), (0, 1), (0, 0)]  # smallest first, as the kernels
+    kept = sum(pa[i].astype(np.float64) @ pb[j].astype(np.float64) for i, j in terms)
+    dropped = sum(pa[i].astype(np.float64) @ pb[j].astype(np.float64) for i, j in [(1, 2), (2, 1), (2, 2)])
+    mag = np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64)
+    assert np.max(np.abs(kept - exact) / mag) < 2.0 ** -22
+    assert np.max(np.abs(dropped) / mag) < 2.0 ** -24
