@@ -25,7 +25,8 @@ STATUS_NAMES = {OK: "ok", E_UNSUPPORTED: "unsupported", E_INVALID: "invalid", E_
 
 # Every symbol the header declares (checked by the CPU test suite).
 EXPORTS = ("ancha_last_error", "ancha_version", "ancha_available", "ancha_wait_selftest", "ancha_attention_fwd",
-           "ancha_linear_fwd", "ancha_stft_fwd", "ancha_istft_masked", "ancha_istft_masked_static", "ancha_ola_add",
+           "ancha_attention_workspace", "ancha_attention_fwd_ws", "ancha_linear_fwd", "ancha_linear_workspace",
+           "ancha_linear_fwd_ws", "ancha_stft_fwd", "ancha_istft_masked", "ancha_istft_masked_static", "ancha_ola_add",
            "ancha_model_load", "ancha_model_info", "ancha_model_forward", "ancha_model_free",
            "ancha_mdx23c_load", "ancha_mdx23c_info", "ancha_mdx23c_forward", "ancha_mdx23c_separate_pcm",
            "ancha_mdx23c_plan", "ancha_mdx23c_free", "ancha_mdx_graph_inspect", "ancha_mdx_load",
@@ -97,7 +98,11 @@ def lib() -> C.CDLL:
             "ancha_available": (i32, [i32]),
             "ancha_wait_selftest": (i32, [i64, vp]),
             "ancha_attention_fwd": (i32, [C.POINTER(AttnDesc), vp, vp, vp, vp, vp, vp]),
+            "ancha_attention_workspace": (i32, [C.POINTER(AttnDesc), C.POINTER(C.c_size_t)]),
+            "ancha_attention_fwd_ws": (i32, [C.POINTER(AttnDesc), vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),
             "ancha_linear_fwd": (i32, [C.POINTER(LinearDesc), vp, vp, vp, vp, vp, vp, vp]),
+            "ancha_linear_workspace": (i32, [C.POINTER(LinearDesc), C.POINTER(C.c_size_t)]),
+            "ancha_linear_fwd_ws": (i32, [C.POINTER(LinearDesc), vp, vp, vp, vp, vp, vp, vp, C.c_size_t, vp]),
             "ancha_stft_fwd": (i32, [vp, i32, i32, i32, vp, vp]),
             "ancha_istft_masked": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp]),
             "ancha_istft_masked_static": (i32, [vp, vp, i32, i32, i32, i32, i32, vp, vp, vp]),

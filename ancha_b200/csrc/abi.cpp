@@ -76,8 +76,24 @@ int ancha_available(int device) {
     return 1;
 }
 
-int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, const void* v,
-                        const void* gate, void* out, void* stream) {
+namespace {
+// Rows up to the last one the attention's groups reach and the used q | k | v columns, rounded
+// to 16-byte plane rows: the fp32 split's planes are 3 · rows · pld bf16.
+void attention_plane_shape(const AttnArgs& a, int64_t* rows, int64_t* cols, int64_t* pld) {
+    const int64_t outer = a.groups / a.group_inner;
+    *rows = (outer - 1) * a.group_outer_stride + (a.group_inner - 1) * a.group_inner_stride +
+            (int64_t)(a.tokens - 1) * a.token_stride + 1;
+    *cols = std::max(std::max(a.q_col, a.k_col), a.v_col) + (int64_t)a.heads * 64;
+    *pld = (*cols + 7) / 8 * 8;
+}
+
+bool attention_split_applies(const AttnArgs& a, const void* q, const void* k, const void* v) {
+    return ANCHA_FP32_SPLIT && a.elt == ELT_F32 && q == k && q == v && a.tokens > 0 && a.groups > 0 &&
+           a.groups % a.group_inner == 0;
+}
+
+int attention_args(const ancha_attn_desc* d, const void* q, const void* k, const void* v, const void* gate,
+                   void* out, AttnArgs* a) {
     if (!d || !q || !k || !v || !out) return fail(ANCHA_E_INVALID, "attention: null argument");
     if (d->head_dim != 64) return fail(ANCHA_E_UNSUPPORTED, "attention: head_dim must be 64");
     if (d->groups < 0 || d->tokens < 0 || d->heads <= 0)
@@ -91,46 +107,73 @@ int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, 
         d->q_col + span > d->ld || d->k_col + span > d->ld || d->v_col + span > d->ld ||
         d->out_col + span > d->out_ld || (gate && (d->gate_col < 0 || d->gate_col + d->heads > d->ld)))
         return fail(ANCHA_E_INVALID, "attention: q / k / v column ranges do not fit the rows");
+    *a = AttnArgs{};
+    a->q = q; a->k = k; a->v = v; a->gate = gate; a->out = out;
+    a->groups = d->groups; a->tokens = d->tokens; a->heads = d->heads; a->head_dim = 64;
+    a->ld = d->ld; a->out_ld = d->out_ld;
+    a->group_inner = d->group_inner; a->group_inner_stride = d->group_inner_stride;
+    a->group_outer_stride = d->group_outer_stride; a->token_stride = d->token_stride;
+    a->q_col = d->q_col; a->k_col = d->k_col; a->v_col = d->v_col;
+    a->gate_col = gate ? d->gate_col : 0; a->out_col = d->out_col;
+    a->elt = d->dtype;
+    return ANCHA_OK;
+}
+}  // namespace
+
+int ancha_attention_workspace(const ancha_attn_desc* d, size_t* bytes) {
+    if (!d || !bytes) return fail(ANCHA_E_INVALID, "attention_workspace: null argument");
+    *bytes = 0;
+    if (d->dtype != ANCHA_F32 || d->groups <= 0 || d->tokens <= 0 || d->group_inner <= 0 ||
+        d->groups % d->group_inner != 0)
+        return ANCHA_OK;
     AttnArgs a{};
-    a.q = q; a.k = k; a.v = v; a.gate = gate; a.out = out;
-    a.groups = d->groups; a.tokens = d->tokens; a.heads = d->heads; a.head_dim = 64;
-    a.ld = d->ld; a.out_ld = d->out_ld;
-    a.group_inner = d->group_inner; a.group_inner_stride = d->group_inner_stride;
-    a.group_outer_stride = d->group_outer_stride; a.token_stride = d->token_stride;
-    a.q_col = d->q_col; a.k_col = d->k_col; a.v_col = d->v_col;
-    a.gate_col = gate ? d->gate_col : 0; a.out_col = d->out_col;
-    a.elt = d->dtype;
+    a.groups = d->groups; a.tokens = d->tokens; a.heads = d->heads; a.group_inner = d->group_inner;
+    a.group_inner_stride = d->group_inner_stride; a.group_outer_stride = d->group_outer_stride;
+    a.token_stride = d->token_stride; a.q_col = d->q_col; a.k_col = d->k_col; a.v_col = d->v_col;
+    int64_t rows, cols, pld;
+    attention_plane_shape(a, &rows, &cols, &pld);
+    *bytes = (size_t)(3 * rows * pld * 2);
+    return ANCHA_OK;
+}
+
+int ancha_attention_fwd_ws(const ancha_attn_desc* d, const void* q, const void* k, const void* v,
+                           const void* gate, void* out, void* workspace, size_t workspace_bytes, void* stream) {
+    AttnArgs a{};
+    ANCHA_TRY(attention_args(d, q, k, v, gate, out, &a));
     cudaStream_t s = as_stream(stream);
     if (a.elt != ELT_F32) {
         int st = attention_tc(a, s);
         if (st != ANCHA_E_UNSUPPORTED) return st;
     }
-#if ANCHA_FP32_SPLIT
     // fp32 on the tensor cores: the used q | k | v columns of every row up to the last one the
-    // groups reach, split into three bf16 planes in a stream-ordered scratch buffer.
-    if (a.elt == ELT_F32 && q == k && q == v && a.tokens > 0 && a.groups > 0 && a.groups % a.group_inner == 0) {
-        const int64_t outer = a.groups / a.group_inner;
-        const int64_t rows = (outer - 1) * a.group_outer_stride + (a.group_inner - 1) * a.group_inner_stride +
-                             (int64_t)(a.tokens - 1) * a.token_stride + 1;
-        const int64_t cols = std::max(std::max(a.q_col, a.k_col), a.v_col) + span;
-        const int64_t pld = (cols + 7) / 8 * 8;
-        void* planes = nullptr;
-        if (cudaMallocAsync(&planes, (size_t)(3 * rows * pld * 2), s) == cudaSuccess) {
-            int st = split3_rows_strided(static_cast<const float*>(q), a.ld, planes, pld, rows * pld, rows,
+    // groups reach, split into three bf16 planes in the caller's workspace.
+    if (attention_split_applies(a, q, k, v) && workspace) {
+        int64_t rows, cols, pld;
+        attention_plane_shape(a, &rows, &cols, &pld);
+        if (workspace_bytes >= (size_t)(3 * rows * pld * 2)) {
+            int st = split3_rows_strided(static_cast<const float*>(q), a.ld, workspace, pld, rows * pld, rows,
                                          (int)cols, s);
-            if (st == ANCHA_OK) st = attention_tc_split(a, planes, pld, rows * pld, s);
-            cudaFreeAsync(planes, s);
+            if (st == ANCHA_OK) st = attention_tc_split(a, workspace, pld, rows * pld, s);
             if (st != ANCHA_E_UNSUPPORTED) return st;
-        } else {
-            cudaGetLastError();  // no room for the planes: the FFMA kernel needs no scratch
         }
     }
-#endif
     return attention_ffma(a, s);
 }
 
-int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, const float* bias,
-                     const float* residual, const float* rope, void* out, void* stream) {
+int ancha_attention_fwd(const ancha_attn_desc* d, const void* q, const void* k, const void* v,
+                        const void* gate, void* out, void* stream) {
+    return ancha_attention_fwd_ws(d, q, k, v, gate, out, nullptr, 0, stream);
+}
+
+int ancha_linear_workspace(const ancha_linear_desc* d, size_t* bytes) {
+    if (!d || !bytes) return fail(ANCHA_E_INVALID, "linear_workspace: null argument");
+    *bytes = d->rope_width && d->rope_tokens > 0 && d->dtype != ANCHA_F32 ? (size_t)2 * 32 * d->rope_tokens * 16 : 0;
+    return ANCHA_OK;
+}
+
+int ancha_linear_fwd_ws(const ancha_linear_desc* d, const void* x, const void* w, const float* bias,
+                        const float* residual, const float* rope, void* out, void* workspace,
+                        size_t workspace_bytes, void* stream) {
     if (!d || !x || !w || !out) return fail(ANCHA_E_INVALID, "linear: null argument");
     if (d->m < 0 || d->n <= 0 || d->k <= 0) return fail(ANCHA_E_UNSUPPORTED, "linear: empty shape");
     if (d->dtype != ANCHA_F32 && d->dtype != ANCHA_BF16 && d->dtype != ANCHA_F16)
@@ -171,23 +214,26 @@ int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, c
     cudaStream_t s = as_stream(stream);
     if (d->dtype != ANCHA_F32 && wl == ANCHA_W_NK) {
         int st;
-        void* quads = nullptr;
-        if (e.rope && cudaMallocAsync(&quads, (size_t)2 * 32 * e.rope_tokens * 16, s) == cudaSuccess) {
+        const size_t qbytes = (size_t)2 * 32 * e.rope_tokens * 16;
+        if (e.rope && workspace && workspace_bytes >= qbytes && reinterpret_cast<uintptr_t>(workspace) % 16 == 0) {
             // The tensor-core epilogue reads the table in its pair-major general form (same
-            // arithmetic, coalesced loads), built in a stream-ordered scratch buffer.
+            // arithmetic, coalesced loads), rewritten into the caller's workspace.
             GemmEpilogue eq = e;
             eq.rope = nullptr;
-            eq.rope_quads = static_cast<const float*>(quads);
-            st = rope_quads_from_table(e.rope, e.rope_tokens, 64, quads, s);
+            eq.rope_quads = static_cast<const float*>(workspace);
+            st = rope_quads_from_table(e.rope, e.rope_tokens, 64, workspace, s);
             if (st == ANCHA_OK) st = gemm_tc(g, d->dtype, eq, s);
-            cudaFreeAsync(quads, s);
         } else {
-            if (e.rope) cudaGetLastError();  // no room for the rewrite: read the table as given
             st = gemm_tc(g, d->dtype, e, s);
         }
         if (st != ANCHA_E_UNSUPPORTED) return st;
     }
     return gemm_ffma(g, nullptr, 1, d->m, d->n, d->dtype, d->dtype, wl == ANCHA_W_NK, e, s);
+}
+
+int ancha_linear_fwd(const ancha_linear_desc* d, const void* x, const void* w, const float* bias,
+                     const float* residual, const float* rope, void* out, void* stream) {
+    return ancha_linear_fwd_ws(d, x, w, bias, residual, rope, out, nullptr, 0, stream);
 }
 
 int ancha_stft_fwd(const float* audio, int chunks, int samples, int hop, float* packed, void* stream) {

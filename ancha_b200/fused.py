@@ -54,6 +54,18 @@ def _rows_view(t, name: str):
     return t.stride(-2) if t.dim() >= 2 else t.shape[-1]
 
 
+def _workspace(query, desc, device):
+    """A device workspace of the size the library asks for ``desc`` (the caller's allocation,
+    through torch's caching allocator), or ``(None, 0)`` when none helps."""
+    torch = _torch()
+    n = C.c_size_t(0)
+    N.check(query(C.byref(desc), C.byref(n)))
+    if n.value == 0:
+        return None, 0
+    buf = torch.empty(n.value, dtype=torch.uint8, device=device)
+    return buf, n.value
+
+
 def attention(q, k, v):
     """``softmax(q·kᵀ)·v`` over ``[groups, tokens, heads, 64]`` with ``q`` pre-scaled
     (fused/mod.rs:20-41). Returns ``None`` unless the head width is 64 and shapes match."""
@@ -68,8 +80,11 @@ def attention(q, k, v):
         flat = [t.contiguous() for t in flat]
     d = N.AttnDesc(groups, tokens, heads, 64, _dtype_code(q), heads * 64, heads * 64, groups,
                    tokens, 0, 1, 0, 0, 0, -1, 0)
-    N.check(N.lib().ancha_attention_fwd(C.byref(d), flat[0].data_ptr(), flat[1].data_ptr(),
-                                        flat[2].data_ptr(), None, out.data_ptr(), _stream()))
+    L = N.lib()
+    ws, nbytes = _workspace(L.ancha_attention_workspace, d, q.device)
+    N.check(L.ancha_attention_fwd_ws(C.byref(d), flat[0].data_ptr(), flat[1].data_ptr(), flat[2].data_ptr(),
+                                     None, out.data_ptr(), None if ws is None else ws.data_ptr(), nbytes,
+                                     _stream()))
     return out
 
 
@@ -89,7 +104,10 @@ def gated_attention(packed, heads: int):
     d = N.AttnDesc(groups, tokens, heads, 64, _dtype_code(p), ld, inner, groups, tokens, 0, 1,
                    0, inner, 2 * inner, 3 * inner, 0)
     ptr = p.data_ptr()
-    N.check(N.lib().ancha_attention_fwd(C.byref(d), ptr, ptr, ptr, ptr, out.data_ptr(), _stream()))
+    L = N.lib()
+    ws, nbytes = _workspace(L.ancha_attention_workspace, d, packed.device)
+    N.check(L.ancha_attention_fwd_ws(C.byref(d), ptr, ptr, ptr, ptr, out.data_ptr(),
+                                     None if ws is None else ws.data_ptr(), nbytes, _stream()))
     return out
 
 
@@ -157,6 +175,8 @@ def linear(x, weight, epilogue: Epilogue = Epilogue(), weight_layout: int = N.W_
                      N.ACT_GELU if epilogue.gelu else N.ACT_NONE, width, tokens, 1,
                      None if rs is None else rs.data_ptr())
     ptr = lambda t: None if t is None else t.data_ptr()
-    N.check(N.lib().ancha_linear_fwd(C.byref(d), xs.data_ptr(), ws.data_ptr(), ptr(bias),
-                                     ptr(res), ptr(rope), out.data_ptr(), _stream()))
+    L = N.lib()
+    wk, nbytes = _workspace(L.ancha_linear_workspace, d, x.device)
+    N.check(L.ancha_linear_fwd_ws(C.byref(d), xs.data_ptr(), ws.data_ptr(), ptr(bias), ptr(res), ptr(rope),
+                                  out.data_ptr(), ptr(wk), nbytes, _stream()))
     return out

@@ -67,7 +67,8 @@ def run_gemm(dtype, reps):
 
 
 def _abi_linear(x, w, act, rope=None):
-    """ancha_linear_fwd with NK weights and a bias (and the RoPE epilogue when given)."""
+    """ancha_linear_fwd_ws with NK weights, a bias and the workspace the library asks for (the
+    RoPE epilogue when given)."""
     import ctypes as C
 
     import torch
@@ -80,8 +81,11 @@ def _abi_linear(x, w, act, rope=None):
     tokens = rope.shape[1] if rope is not None else 1
     d = N.LinearDesc(m, n, k, code, code, N.W_NK, k, k, n, 0, act, 512 if rope is not None else 0, tokens, 1)
     rp = None if rope is None else rope.data_ptr()
-    return lambda: N.check(N.lib().ancha_linear_fwd(C.byref(d), x.data_ptr(), w.data_ptr(), b.data_ptr(),
-                                                    None, rp, y.data_ptr(), None))
+    nbytes = C.c_size_t(0)
+    N.check(N.lib().ancha_linear_workspace(C.byref(d), C.byref(nbytes)))
+    ws = torch.empty(max(nbytes.value, 16), dtype=torch.uint8, device="cuda")
+    return lambda: N.check(N.lib().ancha_linear_fwd_ws(C.byref(d), x.data_ptr(), w.data_ptr(), b.data_ptr(),
+                                                       None, rp, y.data_ptr(), ws.data_ptr(), nbytes.value, None))
 
 
 def run_attention(dtype, reps):

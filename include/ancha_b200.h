@@ -94,13 +94,24 @@ typedef struct {
 
 /* softmax(q·kᵀ)·v per (group, head), non-causal, q pre-scaled by 1/sqrt(64); optionally
  * gated. Replaces fused::attention (fused/mod.rs:20-41) and fused::gated_attention
- * (fused/mod.rs:43-55), whose kernel is fused/attention.rs:24-298. With q, k and v in one
- * buffer (q == k == v) the tensor cores run it: BF16 / F16 directly, F32 from a three-plane
- * bf16 split of the used columns, written to a stream-ordered scratch buffer (cudaMallocAsync,
- * 3 · rows · columns · 2 bytes) that is freed on `stream`; separate buffers, or a scratch that
- * cannot be allocated, run on the FFMA kernel. */
+ * (fused/mod.rs:43-55), whose kernel is fused/attention.rs:24-298. No allocation: BF16 / F16
+ * with q, k and v in one buffer (q == k == v) run on the tensor cores, everything else (F32
+ * included) on the FFMA kernel. */
 ANCHA_API int ancha_attention_fwd(const ancha_attn_desc* desc, const void* q, const void* k,
                         const void* v, const void* gate, void* out, void* stream);
+
+/* Device workspace bytes ancha_attention_fwd_ws can use for `desc` (0: none helps): for F32,
+ * the three-plane bf16 split of the used q / k / v columns of every row the groups reach. */
+ANCHA_API int ancha_attention_workspace(const ancha_attn_desc* desc, size_t* bytes);
+
+/* ancha_attention_fwd with a caller-owned device workspace (16-byte aligned, at least the
+ * ancha_attention_workspace bytes; NULL or smaller = the ancha_attention_fwd paths). With it an
+ * F32 call with q == k == v runs on the tensor cores: the used columns split into hi / mid / lo
+ * bf16 planes in the workspace and six plane products per S = q·kᵀ and per P·v, with f32
+ * accumulation (max abs error against float64 on par with the FFMA kernel's). */
+ANCHA_API int ancha_attention_fwd_ws(const ancha_attn_desc* desc, const void* q, const void* k,
+                           const void* v, const void* gate, void* out, void* workspace,
+                           size_t workspace_bytes, void* stream);
 
 /* Weight layouts accepted by ancha_linear_fwd. */
 enum {
@@ -119,11 +130,7 @@ enum { ANCHA_ACT_NONE = 0, ANCHA_ACT_GELU = 1, ANCHA_ACT_TANH = 2, ANCHA_ACT_GLU
  * (value, gate) and writes value·sigmoid(gate) to column j (n_out = n / 2).
  * Replaces fused::linear + Epilogue (fused/mod.rs:57-176, kernel fused/gemm.rs:84-311).
  * x, w: `dtype` (F32 → fp32 FFMA kernel; BF16 / F16 → tcgen05 kernel with ANCHA_W_NK);
- * bias, residual, rope: f32; out: out_dtype. `workspace` may be NULL (none is needed). On the
- * tensor-core path the rotary table is first rewritten pair-major ([2][32][tokens] × (cos, cos,
- * sin, sin) entries of each column pair, the same arithmetic with coalesced loads) into a
- * stream-ordered scratch buffer (cudaMallocAsync, 1 KiB per token) freed on `stream`; without
- * room for it the epilogue reads the table as given. */
+ * bias, residual, rope: f32; out: out_dtype. No allocation. */
 typedef struct {
     int m, n, k;
     int dtype, out_dtype, weight_layout;
@@ -138,6 +145,19 @@ typedef struct {
 ANCHA_API int ancha_linear_fwd(const ancha_linear_desc* desc, const void* x, const void* w,
                      const float* bias, const float* residual, const float* rope,
                      void* out, void* stream);
+
+/* Device workspace bytes ancha_linear_fwd_ws can use for `desc`: with a rotary epilogue on the
+ * tensor-core path (BF16 / F16), 1 KiB per table token; otherwise 0. */
+ANCHA_API int ancha_linear_workspace(const ancha_linear_desc* desc, size_t* bytes);
+
+/* ancha_linear_fwd with a caller-owned device workspace (16-byte aligned, at least the
+ * ancha_linear_workspace bytes; NULL or smaller = the ancha_linear_fwd path). With it the
+ * tensor-core rotary epilogue reads the table rewritten pair-major into the workspace
+ * ([2][32][tokens] × the (cos, cos, sin, sin) entries of each column pair: the same arithmetic,
+ * coalesced loads) instead of the [4, tokens, 64] rows. */
+ANCHA_API int ancha_linear_fwd_ws(const ancha_linear_desc* desc, const void* x, const void* w,
+                        const float* bias, const float* residual, const float* rope, void* out,
+                        void* workspace, size_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------------------------------ *
  * Spectral DSP (replaces crates/ancha-audio/src/dsp.rs and chunk.rs on the device)     *

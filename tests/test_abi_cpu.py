@@ -76,6 +76,24 @@ def test_struct_layouts_match_the_c_compiler(tmp_path):
             assert int(got[f"{cname}.{field}"]) == getattr(py, field).offset, f"{cname}.{field}"
 
 
+def test_workspace_queries():
+    """The workspace variants say how many bytes help (pure host arithmetic, no GPU)."""
+    lib = N.lib()
+    n = C.c_size_t(7)
+    # f32 time axis over a packed [60 · 801, 1544] buffer: three bf16 planes of the used
+    # 3 · 512 q | k | v columns of all 48 060 rows.
+    d = N.AttnDesc(60, 801, 8, 64, N.F32, 1544, 512, 60, 801, 0, 1, 0, 512, 1024, 1536, 0)
+    assert lib.ancha_attention_workspace(C.byref(d), C.byref(n)) == N.OK
+    assert n.value == 3 * 60 * 801 * 1536 * 2
+    d16 = N.AttnDesc(60, 801, 8, 64, N.F16, 1544, 512, 60, 801, 0, 1, 0, 512, 1024, 1536, 0)
+    assert lib.ancha_attention_workspace(C.byref(d16), C.byref(n)) == N.OK and n.value == 0
+    ld = N.LinearDesc(8010, 1544, 384, N.F16, N.F16, N.W_NK, 384, 384, 1544, 0, N.ACT_NONE, 512, 801, 1)
+    assert lib.ancha_linear_workspace(C.byref(ld), C.byref(n)) == N.OK and n.value == 2 * 32 * 801 * 16
+    ld0 = N.LinearDesc(8010, 1536, 384, N.F16, N.F16, N.W_NK, 384, 384, 1536, 0, N.ACT_GELU, 0, 1, 1)
+    assert lib.ancha_linear_workspace(C.byref(ld0), C.byref(n)) == N.OK and n.value == 0
+    assert lib.ancha_attention_workspace(None, C.byref(n)) == N.E_INVALID
+
+
 def test_invalid_arguments_are_rejected_before_any_launch():
     lib = N.lib()
     assert lib.ancha_attention_fwd(None, None, None, None, None, None, None) == N.E_INVALID

@@ -256,8 +256,9 @@ def test_overlap_add_matches_oracle():
 
 
 def linear_abi(x, w_nk, act=N.ACT_NONE, bias=None, residual=None, rope=None, rope_width=0,
-               rope_tokens=1, rope_div=1, layout=N.W_NK, out_dtype=None):
-    """Call ancha_linear_fwd directly; w_nk is [n, k] (transposed here for W_KN)."""
+               rope_tokens=1, rope_div=1, layout=N.W_NK, out_dtype=None, workspace=False):
+    """Call ancha_linear_fwd directly (ancha_linear_fwd_ws with the workspace the library asks
+    for when `workspace`); w_nk is [n, k] (transposed here for W_KN)."""
     import ctypes as C
     m, k = x.shape
     n = w_nk.shape[0]
@@ -270,8 +271,15 @@ def linear_abi(x, w_nk, act=N.ACT_NONE, bias=None, residual=None, rope=None, rop
                      out.stride(0), residual.stride(0) if residual is not None else 0, act,
                      rope_width, rope_tokens, rope_div)
     p = lambda t: None if t is None else t.data_ptr()
-    N.check(N.lib().ancha_linear_fwd(C.byref(d), x.data_ptr(), w.data_ptr(), p(bias), p(residual),
-                                     p(rope), out.data_ptr(), None))
+    if workspace:
+        nbytes = C.c_size_t(0)
+        N.check(N.lib().ancha_linear_workspace(C.byref(d), C.byref(nbytes)))
+        ws = torch.empty(max(nbytes.value, 16), dtype=torch.uint8, device="cuda")
+        N.check(N.lib().ancha_linear_fwd_ws(C.byref(d), x.data_ptr(), w.data_ptr(), p(bias), p(residual),
+                                            p(rope), out.data_ptr(), ws.data_ptr(), nbytes.value, None))
+    else:
+        N.check(N.lib().ancha_linear_fwd(C.byref(d), x.data_ptr(), w.data_ptr(), p(bias), p(residual),
+                                         p(rope), out.data_ptr(), None))
     torch.cuda.synchronize()
     return out
 
@@ -306,17 +314,22 @@ def test_tensor_core_gemm_matches_ffma(dt, case, shape):
         kc, ks_ = roformer.rope_tables(freqs, tokens, 1.0)
         kw["rope"] = dev(np.stack([qc, qs_, kc, ks_]).astype(np.float32))
         kw.update(rope_width=512, rope_tokens=tokens, rope_div=1)
-    tc = linear_abi(x, w, layout=N.W_NK, **kw).double()
     ref = linear_abi(x, w, layout=N.W_KN, **kw).double()
     scale = ref.abs().max().item()
-    err = (tc - ref).abs().max().item()
-    # 16-bit outputs may differ by one rounding step; f32 outputs only by summation order.
-    assert err <= (8e-3 if kw.get("out_dtype") is None and case != "glu" else 1e-4) * max(scale, 1.0), (case, err, scale)
+    # The tensor-core path with and without a workspace (the rotary table read as given, or
+    # rewritten pair-major into the workspace).
+    for ws in (False, True):
+        tc = linear_abi(x, w, layout=N.W_NK, workspace=ws, **kw).double()
+        err = (tc - ref).abs().max().item()
+        # 16-bit outputs may differ by one rounding step; f32 outputs only by summation order.
+        assert err <= (8e-3 if kw.get("out_dtype") is None and case != "glu" else 1e-4) * max(scale, 1.0), \
+            (case, ws, err, scale)
 
 
-def attention_abi(buf, desc_kw, separate_kv=False, out_dtype=None):
-    """ancha_attention_fwd on a packed [rows, ld] buffer; separate_kv copies k / v into their
-    own buffers (which routes 16-bit inputs to the FFMA kernel)."""
+def attention_abi(buf, desc_kw, separate_kv=False, out_dtype=None, workspace=True):
+    """ancha_attention_fwd_ws (with the workspace the library asks for) or, with
+    workspace=False, ancha_attention_fwd on a packed [rows, ld] buffer; separate_kv copies k / v
+    into their own buffers (which routes the call to the FFMA kernel)."""
     import ctypes as C
     rows, ld = buf.shape
     heads = desc_kw["heads"]
@@ -329,8 +342,16 @@ def attention_abi(buf, desc_kw, separate_kv=False, out_dtype=None):
     k = buf.clone() if separate_kv else buf
     v = buf.clone() if separate_kv else buf
     gate = buf if desc_kw.get("gated") else None
-    N.check(N.lib().ancha_attention_fwd(C.byref(d), buf.data_ptr(), k.data_ptr(), v.data_ptr(),
-                                        None if gate is None else gate.data_ptr(), out.data_ptr(), None))
+    g = None if gate is None else gate.data_ptr()
+    if workspace:
+        nbytes = C.c_size_t(0)
+        N.check(N.lib().ancha_attention_workspace(C.byref(d), C.byref(nbytes)))
+        ws = torch.empty(max(nbytes.value, 16), dtype=torch.uint8, device="cuda")
+        N.check(N.lib().ancha_attention_fwd_ws(C.byref(d), buf.data_ptr(), k.data_ptr(), v.data_ptr(), g,
+                                               out.data_ptr(), ws.data_ptr(), nbytes.value, None))
+    else:
+        N.check(N.lib().ancha_attention_fwd(C.byref(d), buf.data_ptr(), k.data_ptr(), v.data_ptr(), g,
+                                            out.data_ptr(), None))
     torch.cuda.synchronize()
     return out
 
@@ -392,6 +413,9 @@ def test_fp32_split_attention_matches_ffma(axis, gated):
     kw.update(heads=heads, gated=gated)
     tc = attention_abi(buf, kw).double().cpu().numpy()
     ffma = attention_abi(buf, kw, separate_kv=True).double().cpu().numpy()
+    # Without a workspace the same call runs the FFMA kernel (no allocation inside the call).
+    plain = attention_abi(buf, kw, workspace=False).double().cpu().numpy()
+    assert np.array_equal(plain, ffma)
     # float64 attention of the first (up to) four groups from the same f32 operands
     b = buf.double().cpu().numpy()
     tokens = kw["tokens"]
