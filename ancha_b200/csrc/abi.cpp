@@ -42,40 +42,6 @@ int check_launch(const char* what) {
     return ANCHA_OK;
 }
 
-}  // namespace ancha
-
-using namespace ancha;
-
-extern "C" {
-
-const char* ancha_last_error(void) { return g_last_error.c_str(); }
-
-const char* ancha_version(void) { return "ancha-b200 0.1.0 (sm_100a)"; }
-
-int ancha_wait_selftest(int64_t budget_cycles, void* stream) {
-    return wait_selftest((long long)budget_cycles, as_stream(stream));
-}
-
-int ancha_available(int device) {
-    int count = 0;
-    cudaError_t e = cudaGetDeviceCount(&count);
-    if (e != cudaSuccess) {
-        cudaGetLastError();
-        fail(ANCHA_E_CUDA, std::string("no CUDA device: ") + cudaGetErrorString(e));
-        return 0;
-    }
-    if (device < 0 || device >= count) {
-        fail(ANCHA_E_INVALID, "CUDA device " + std::to_string(device) + " not found");
-        return 0;
-    }
-    cudaDeviceProp p;
-    if (cudaGetDeviceProperties(&p, device) != cudaSuccess || p.major != 10) {
-        fail(ANCHA_E_UNSUPPORTED, "device is not an sm_100 (B200-class) GPU");
-        return 0;
-    }
-    return 1;
-}
-
 namespace {
 // Rows up to the last one the attention's groups reach and the used q | k | v columns, rounded
 // to 16-byte plane rows: the fp32 split's planes are 3 · rows · pld bf16.
@@ -119,6 +85,41 @@ int attention_args(const ancha_attn_desc* d, const void* q, const void* k, const
     return ANCHA_OK;
 }
 }  // namespace
+
+}  // namespace ancha
+
+using namespace ancha;
+
+extern "C" {
+
+const char* ancha_last_error(void) { return g_last_error.c_str(); }
+
+const char* ancha_version(void) { return "ancha-b200 0.1.0 (sm_100a)"; }
+
+int ancha_wait_selftest(int64_t budget_cycles, void* stream) {
+    return wait_selftest((long long)budget_cycles, as_stream(stream));
+}
+
+int ancha_available(int device) {
+    int count = 0;
+    cudaError_t e = cudaGetDeviceCount(&count);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(ANCHA_E_CUDA, std::string("no CUDA device: ") + cudaGetErrorString(e));
+        return 0;
+    }
+    if (device < 0 || device >= count) {
+        fail(ANCHA_E_INVALID, "CUDA device " + std::to_string(device) + " not found");
+        return 0;
+    }
+    cudaDeviceProp p;
+    if (cudaGetDeviceProperties(&p, device) != cudaSuccess || p.major != 10) {
+        fail(ANCHA_E_UNSUPPORTED, "device is not an sm_100 (B200-class) GPU");
+        return 0;
+    }
+    return 1;
+}
+
 
 int ancha_attention_workspace(const ancha_attn_desc* d, size_t* bytes) {
     if (!d || !bytes) return fail(ANCHA_E_INVALID, "attention_workspace: null argument");
