@@ -354,10 +354,7 @@ attention_band_kernel(const __grid_constant__ CUtensorMap tmap, const __grid_con
 // running maximum is updated lazily: it moves (and O, l are rescaled in TMEM) only when a row's
 // block maximum exceeds it by more than 2^8, so P stays ≤ 256 and the rescale is rare.
 // Interior key blocks skip masking.
-#ifndef ANCHA_ATTN_K_STAGES
-#define ANCHA_ATTN_K_STAGES 2
-#endif
-constexpr int PP_K_STAGES = ANCHA_ATTN_K_STAGES, PP_V_STAGES = 2;
+constexpr int PP_K_STAGES = 2, PP_V_STAGES = 2;  // deeper rings measured no faster
 constexpr int PP_OFF_Q = 0, PP_OFF_K = QKV_BYTES, PP_OFF_V = PP_OFF_K + PP_K_STAGES * QKV_BYTES;
 constexpr int PP_OFF_BAR = PP_OFF_V + PP_V_STAGES * QKV_BYTES;
 constexpr int PP_NBARS = 1 + 2 * PP_K_STAGES + 2 * PP_V_STAGES + 4;
