@@ -24,7 +24,9 @@ from . import _native as N
 class Roformer:
     """A model package resident on one GPU (not re-entrant; one per device and thread)."""
 
-    def __init__(self, package: str, device: int = 0, precision: str = "bf16"):
+    def __init__(self, package: str, device: int = 0, precision: str = "f16"):
+        """``precision``: "f16" (the default: 16-bit tensor-core operands within the 16-bit mode's
+        50 dB bar), "bf16" (below it on these models) or "f32" (the reference's arithmetic)."""
         self.precision = N.PRECISIONS[precision]
         handle = C.c_void_p()
         N.check(N.lib().ancha_model_load(package.encode(), device, self.precision, C.byref(handle)))
@@ -103,7 +105,7 @@ class SeparateOptions:
     output: str
     chunk_samples: Optional[int] = None
     overlap: Optional[int] = None
-    precision: str = "bf16"
+    precision: str = "f16"
     batch_chunks: int = 0
     start_seconds: float = 0.0
     duration_seconds: Optional[float] = None
